@@ -1,0 +1,152 @@
+/*
+ * ugb.h -- C ABI of libugb, the B200 (sm_100a) quantized linear-layer hot path of the
+ * nodnarbrox/uefi-gpu GGUF runtime.
+ *
+ * Drop-in boundary.  The reference drives its kernels from Rust through QMD/GPFIFO
+ * submission (gpu_graph.rs:24-80, gpu_prefill.rs:10-30, frontier_gpu.rs:6-34,
+ * frontier_batch.rs:19-72) and exposes them to the model code as Gpu::matvec / Gpu::batch
+ * (llm.rs:226-273) and trait Weights::{linear,batch} (frontier_forward.rs:14-22).  Each
+ * entry point below names the reference interface it replaces.  A Rust host binds them with
+ * `extern "C"`; the CUDA stream argument replaces the GPFIFO channel.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  Pointers named `*_dev` or documented as device memory
+ *    are CUDA device pointers; `*_host` pointers are host memory.
+ *  - Buffers are caller-owned and must stay live until the work on `stream` completes
+ *    (the reference holds its leases until the fence, frontier_backend.rs:211-213).
+ *  - Calls are asynchronous on `stream` unless the name ends in a host-buffer form
+ *    (ugb_linear / ugb_linear_batch), which synchronise and check results like the
+ *    reference's Gpu::matvec (llm.rs:246-273).
+ *  - Errors: ugb_status.  Shape / alignment / kind problems are caught on the host before
+ *    anything is launched.  Device-side conditions (non-finite values, a timed-out wait)
+ *    set bits in the context's status word, read with ugb_status_read().
+ *  - One ugb_ctx per device; a context may be used from one host thread at a time.
+ *  - `ugb_stream` is a CUstream / cudaStream_t (NULL = the legacy default stream).
+ */
+#ifndef UGB_H
+#define UGB_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ugb_stream;
+typedef struct ugb_ctx ugb_ctx;
+
+/* Status codes.  Mirrors the reference's Error{Backend,Shape,NonFinite,Context}
+ * (frontier_forward.rs:10) plus alignment / quant-kind / timeout detail. */
+typedef enum ugb_status {
+  UGB_OK = 0,
+  UGB_ESHAPE = 1,     /* a size or count is out of range (Error::Shape) */
+  UGB_ENONFINITE = 2, /* non-finite input or output (Error::NonFinite) */
+  UGB_ETIMEOUT = 3,   /* a bounded device-side wait gave up (the reference's poll timeout) */
+  UGB_EBACKEND = 4,   /* a CUDA call failed (Error::Backend) */
+  UGB_EALIGN = 5,     /* a pointer or stride breaks the documented alignment */
+  UGB_EQUANT = 6,     /* unsupported quant kind (frontier_core::Error::QuantType) */
+  UGB_ECONTEXT = 7    /* bad or missing context / not initialised (Error::Context) */
+} ugb_status;
+
+/* GGML type ids, the same numbers the reference uses for `kind` (frontier_core.rs:146-151). */
+enum {
+  UGB_F32 = 0,
+  UGB_Q8_0 = 8,
+  UGB_Q3_K = 11,
+  UGB_Q4_K = 12
+};
+
+/* Device status-word bits reported by ugb_status_read(). */
+enum {
+  UGB_STATUS_NONFINITE_IN = 1u << 0,
+  UGB_STATUS_NONFINITE_OUT = 1u << 1,
+  UGB_STATUS_TIMEOUT = 1u << 2,
+  UGB_STATUS_BADARG = 1u << 3
+};
+
+/* Largest number of activation vectors one matvec launch multiplies (decode batch). */
+#define UGB_MAX_BATCH 8
+/* Largest row length K accepted.  The reference caps n at 16384 because of its 64 KiB input
+ * window (frontier_backend.rs:245); the 7B-shaped configs need K = 18944, so this is larger. */
+#define UGB_MAX_K 65536
+
+/* ---- context --------------------------------------------------------------------------- */
+
+/* Create a context on CUDA device `device`: queries the SM count, allocates the 4-byte
+ * device status word and prepares every kernel's launch attributes.  Replaces the
+ * reference's channel / compute-object setup (m4.rs:6-105). */
+ugb_status ugb_init(int device, ugb_ctx **out);
+ugb_status ugb_destroy(ugb_ctx *ctx);
+const char *ugb_status_string(ugb_status s);
+
+/* Synchronise `stream`, return the device status bits accumulated since the last read in
+ * *bits, and clear them.  Returns UGB_ENONFINITE / UGB_ETIMEOUT when the corresponding bits
+ * are set (TIMEOUT wins), UGB_OK otherwise. */
+ugb_status ugb_status_read(ugb_ctx *ctx, ugb_stream stream, uint32_t *bits);
+
+/* ---- formats ----------------------------------------------------------------------------- */
+
+/* Bytes of one row of n elements of GGML type `kind`, or a negative value: -1 unknown kind,
+ * -2 n not a positive multiple of the block.  frontier_core.rs:146-151 row_bytes(), with
+ * the same table (F32, BF16, Q8_0, Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS) plus Q4_K and Q3_K. */
+int64_t ugb_row_bytes(uint32_t kind, int64_t n);
+
+/* Q8_1 activation buffer ("xq"): `batch` vectors of k elements (k a multiple of 32), laid
+ * out as int8 quants [batch][k] at offset 0, f32 block scales [batch][nbp] at
+ * ugb_q8act_scale_offset, int32 block sums [batch][nbp] at ugb_q8act_sum_offset, where
+ * nbp = k/32 rounded up to a multiple of 4.  The reference's activation block is
+ * {f32 d; i8 q[32]} (gpu_dp4a.cu:23-31); this is the same data split into 16-byte aligned
+ * arrays plus the block sum that Q4_K's min term needs. */
+size_t ugb_q8act_bytes(int64_t k, int64_t batch);
+size_t ugb_q8act_scale_offset(int64_t k, int64_t batch);
+size_t ugb_q8act_sum_offset(int64_t k, int64_t batch);
+
+/* ---- kernels ----------------------------------------------------------------------------- */
+
+/* Quantise `batch` fp32 vectors x_dev [batch][k] into the Q8_1 buffer xq_dev.
+ * Per 32-block: a = max|x|, d = a/127, q = clamp(rint(x*(127/a)), -127, 127), s = sum q.
+ * Replaces quant_act (gpu_dp4a.cu:23-31, host hook graph_quant gpu_graph.rs:70-73) and
+ * prefill_quant's arithmetic (gpu_prefill.cu:111-123).  Non-finite inputs quantise to 0 and
+ * set UGB_STATUS_NONFINITE_IN. */
+ugb_status ugb_quant_q8_1(ugb_ctx *ctx, ugb_stream stream, const float *x_dev, void *xq_dev,
+                          int64_t k, int64_t batch);
+
+/* y_dev[v][r] = sum over 32-blocks b of row r of the scaled int32 block dot with activation
+ * vector v, for r < m, v < batch (<= UGB_MAX_BATCH).  w_dev holds m rows of `row_bytes`
+ * bytes in the unchanged GGUF block layout of `kind` (Q8_0, Q4_K or Q3_K), 16-byte aligned.
+ * Per block: Q8_0 isum*(d_w*d_x); Q4_K d_x*((d*sc)*isum - (dmin*m)*s); Q3_K isum*(d*d_x).
+ * Replaces linear_dp4a (gpu_dp4a.cu:40-52; hook graph_linear gpu_graph.rs:74-80) and
+ * frontier_matvec (frontier_quant.cu:58-66) with Q8_1 activations.  Weights are streamed
+ * once with bulk copies into shared memory; y rows are written once. */
+ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                      int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k, int64_t m,
+                      int64_t batch);
+
+/* Debug / parity view of the same kernel: out_dev[r][b] = the int32 block dot of row r and
+ * 32-block b with activation vector 0, no scaling (the integer the reference's CPU check
+ * forms, gpu_prefill.rs:111-115).  Used to prove the integer parts bit-exact. */
+ugb_status ugb_block_dots(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                          int64_t row_bytes, const void *xq_dev, int32_t *out_dev, int64_t k,
+                          int64_t m);
+
+/* Fill a weight matrix of m rows x k elements of `kind` with seeded synthetic blocks
+ * (quants uniform over the whole code range, fp16 scales |N(0,1)|*0.002 from a fixed
+ * 256-entry quantile table).  Stand-in for GGUF weights when benchmarking. */
+ugb_status ugb_fill_synthetic(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, void *w_dev,
+                              int64_t k, int64_t m, uint64_t seed);
+
+/* ---- host-buffer entry points (synchronous) --------------------------------------------- */
+
+/* y_host[m] = W x_host[k], synchronously: copy x to the device, quantise, matvec, copy y
+ * back, then check the status word.  Returns UGB_ENONFINITE for a non-finite x or y, as the
+ * reference's Gpu::matvec (llm.rs:246-273) and Weights::linear (frontier_backend.rs:243-275)
+ * fail on non-finite data.  Uses a per-context device workspace grown on demand. */
+ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                      int64_t row_bytes, const float *x_host, float *y_host, int64_t k,
+                      int64_t m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* UGB_H */

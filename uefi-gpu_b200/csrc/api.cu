@@ -1,0 +1,277 @@
+// api.cu -- the extern "C" boundary of libugb (include/ugb.h): validation, context, status.
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <new>
+
+#include "common.cuh"
+#include "internal.hpp"
+
+namespace ugb {
+
+ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_t k, int64_t m) {
+  if (kind != UGB_Q8_0 && kind != UGB_Q4_K && kind != UGB_Q3_K) return UGB_EQUANT;
+  if (k <= 0 || k > UGB_MAX_K || m <= 0 || m > (int64_t{1} << 31) - 64) return UGB_ESHAPE;
+  const int64_t rb = ugb_row_bytes(kind, k);
+  if (rb < 0 || rb != row_bytes) return UGB_ESHAPE;
+  if (!w || (reinterpret_cast<uintptr_t>(w) & 15) != 0) return UGB_EALIGN;
+  return UGB_OK;
+}
+
+namespace {
+
+ugb_status check_ctx(ugb_ctx *ctx) {
+  if (!ctx || !ctx->status) return UGB_ECONTEXT;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return UGB_EBACKEND;
+  return UGB_OK;
+}
+
+bool aligned16(const void *p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Grow the host-buffer workspace to at least `bytes` (device) and `pinned` (host).
+ugb_status reserve(ugb_ctx *ctx, size_t bytes, size_t pinned) {
+  if (bytes > ctx->work_bytes) {
+    if (ctx->work) {
+      cudaDeviceSynchronize();
+      cudaFree(ctx->work);
+      ctx->work = nullptr;
+      ctx->work_bytes = 0;
+    }
+    const size_t want = round_up(bytes, 1 << 20);
+    if (cudaMalloc(&ctx->work, want) != cudaSuccess) return UGB_EBACKEND;
+    ctx->work_bytes = want;
+  }
+  if (pinned > ctx->pinned_bytes) {
+    if (ctx->pinned) {
+      cudaDeviceSynchronize();
+      cudaFreeHost(ctx->pinned);
+      ctx->pinned = nullptr;
+      ctx->pinned_bytes = 0;
+    }
+    const size_t want = round_up(pinned, 1 << 16);
+    if (cudaMallocHost(reinterpret_cast<void **>(&ctx->pinned), want) != cudaSuccess) return UGB_EBACKEND;
+    ctx->pinned_bytes = want;
+  }
+  return UGB_OK;
+}
+
+ugb_status read_status_bits(ugb_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
+  if (cudaMemcpyAsync(ctx->status_host, ctx->status, 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  if (cudaMemsetAsync(ctx->status, 0, 4, stream) != cudaSuccess) return UGB_EBACKEND;
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
+  const uint32_t b = *ctx->status_host;
+  if (bits) *bits = b;
+  if (b & ST_TIMEOUT) return UGB_ETIMEOUT;
+  if (b & (ST_NONFINITE_IN | ST_NONFINITE_OUT)) return UGB_ENONFINITE;
+  if (b & ST_BADARG) return UGB_ESHAPE;
+  return UGB_OK;
+}
+
+}  // namespace
+}  // namespace ugb
+
+using namespace ugb;
+
+extern "C" {
+
+ugb_status ugb_init(int device, ugb_ctx **out) {
+  if (!out) return UGB_ECONTEXT;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return UGB_EBACKEND;
+  if (cudaSetDevice(device) != cudaSuccess) return UGB_EBACKEND;
+  ugb_ctx *ctx = new (std::nothrow) ugb_ctx();
+  if (!ctx) return UGB_EBACKEND;
+  ctx->device = device;
+  int v = 0;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device);
+  ctx->sm_count = v;
+  cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device);
+  ctx->smem_optin = static_cast<size_t>(v);
+  if (cudaMalloc(&ctx->status, 4) != cudaSuccess || cudaMemset(ctx->status, 0, 4) != cudaSuccess ||
+      cudaMallocHost(reinterpret_cast<void **>(&ctx->status_host), 4) != cudaSuccess) {
+    ugb_destroy(ctx);
+    return UGB_EBACKEND;
+  }
+  const ugb_status st = init_matvec_kernels(ctx);
+  if (st != UGB_OK) {
+    ugb_destroy(ctx);
+    return st;
+  }
+  *out = ctx;
+  return UGB_OK;
+}
+
+ugb_status ugb_destroy(ugb_ctx *ctx) {
+  if (!ctx) return UGB_ECONTEXT;
+  cudaSetDevice(ctx->device);
+  cudaDeviceSynchronize();
+  if (ctx->status) cudaFree(ctx->status);
+  if (ctx->status_host) cudaFreeHost(ctx->status_host);
+  if (ctx->work) cudaFree(ctx->work);
+  if (ctx->pinned) cudaFreeHost(ctx->pinned);
+  delete ctx;
+  return UGB_OK;
+}
+
+const char *ugb_status_string(ugb_status s) {
+  switch (s) {
+    case UGB_OK: return "ok";
+    case UGB_ESHAPE: return "shape";
+    case UGB_ENONFINITE: return "non-finite";
+    case UGB_ETIMEOUT: return "timeout";
+    case UGB_EBACKEND: return "backend";
+    case UGB_EALIGN: return "alignment";
+    case UGB_EQUANT: return "quant kind";
+    case UGB_ECONTEXT: return "context";
+  }
+  return "unknown";
+}
+
+ugb_status ugb_status_read(ugb_ctx *ctx, ugb_stream stream, uint32_t *bits) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  return read_status_bits(ctx, stream, bits);
+}
+
+int64_t ugb_row_bytes(uint32_t kind, int64_t n) {
+  // frontier_core.rs:146-151, plus ggml's Q4_K / Q3_K.
+  int64_t block, bytes;
+  switch (kind) {
+    case 0: block = 1; bytes = 4; break;      // F32
+    case 8: block = 32; bytes = 34; break;    // Q8_0
+    case 11: block = 256; bytes = 110; break; // Q3_K
+    case 12: block = 256; bytes = 144; break; // Q4_K
+    case 14: block = 256; bytes = 210; break; // Q6_K
+    case 18: block = 256; bytes = 98; break;  // IQ3_XXS
+    case 20: block = 32; bytes = 18; break;   // IQ4_NL
+    case 23: block = 256; bytes = 136; break; // IQ4_XS
+    case 30: block = 1; bytes = 2; break;     // BF16
+    default: return -1;
+  }
+  if (n <= 0 || n % block != 0) return -2;
+  return n / block * bytes;
+}
+
+size_t ugb_q8act_bytes(int64_t k, int64_t batch) {
+  if (k <= 0 || k % 32 || batch <= 0) return 0;
+  return q8act_layout(k, batch).bytes;
+}
+size_t ugb_q8act_scale_offset(int64_t k, int64_t batch) {
+  if (k <= 0 || k % 32 || batch <= 0) return 0;
+  return q8act_layout(k, batch).d_off;
+}
+size_t ugb_q8act_sum_offset(int64_t k, int64_t batch) {
+  if (k <= 0 || k % 32 || batch <= 0) return 0;
+  return q8act_layout(k, batch).s_off;
+}
+
+ugb_status ugb_quant_q8_1(ugb_ctx *ctx, ugb_stream stream, const float *x_dev, void *xq_dev,
+                          int64_t k, int64_t batch) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  if (k <= 0 || k % 32 || k > UGB_MAX_K || batch <= 0 || batch > 65536) return UGB_ESHAPE;
+  if (!x_dev || (reinterpret_cast<uintptr_t>(x_dev) & 3) || !aligned16(xq_dev)) return UGB_EALIGN;
+  return launch_quant_q8_1(ctx, stream, x_dev, static_cast<uint8_t *>(xq_dev), k, batch, false);
+}
+
+ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                      int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k, int64_t m,
+                      int64_t batch) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  st = check_weights(kind, w_dev, row_bytes, k, m);
+  if (st != UGB_OK) return st;
+  if (batch <= 0 || batch > UGB_MAX_BATCH) return UGB_ESHAPE;
+  if (!aligned16(xq_dev) || !y_dev || (reinterpret_cast<uintptr_t>(y_dev) & 3)) return UGB_EALIGN;
+  MatvecArgs a;
+  a.kind = kind;
+  a.w = static_cast<const uint8_t *>(w_dev);
+  a.row_bytes = row_bytes;
+  a.k = k;
+  a.m = m;
+  a.xq = static_cast<const uint8_t *>(xq_dev);
+  a.xl = q8act_layout(k, batch);
+  a.y = y_dev;
+  a.ldy = m;
+  a.batch = batch;
+  return launch_matvec(ctx, stream, a);
+}
+
+ugb_status ugb_block_dots(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                          int64_t row_bytes, const void *xq_dev, int32_t *out_dev, int64_t k,
+                          int64_t m) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  st = check_weights(kind, w_dev, row_bytes, k, m);
+  if (st != UGB_OK) return st;
+  if (!aligned16(xq_dev) || !out_dev || (reinterpret_cast<uintptr_t>(out_dev) & 3)) return UGB_EALIGN;
+  MatvecArgs a;
+  a.kind = kind;
+  a.w = static_cast<const uint8_t *>(w_dev);
+  a.row_bytes = row_bytes;
+  a.k = k;
+  a.m = m;
+  a.xq = static_cast<const uint8_t *>(xq_dev);
+  a.xl = q8act_layout(k, 1);
+  a.batch = 1;
+  a.dots = out_dev;
+  return launch_matvec(ctx, stream, a);
+}
+
+ugb_status ugb_fill_synthetic(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, void *w_dev,
+                              int64_t k, int64_t m, uint64_t seed) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  st = check_weights(kind, w_dev, ugb_row_bytes(kind, k), k, m);
+  if (st != UGB_OK) return st;
+  return launch_fill_synthetic(ctx, stream, kind, static_cast<uint8_t *>(w_dev), k, m, seed);
+}
+
+ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                      int64_t row_bytes, const float *x_host, float *y_host, int64_t k,
+                      int64_t m) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  st = check_weights(kind, w_dev, row_bytes, k, m);
+  if (st != UGB_OK) return st;
+  if (!x_host || !y_host) return UGB_EALIGN;
+  std::lock_guard<std::mutex> lock(ctx->mu);
+  const Q8Act xl = q8act_layout(k, 1);
+  const size_t x_off = 0, xq_off = round_up(k * 4, 256), y_off = xq_off + round_up(xl.bytes, 256);
+  st = reserve(ctx, y_off + round_up(m * 4, 256), static_cast<size_t>(k + m) * 4);
+  if (st != UGB_OK) return st;
+  uint8_t *base = static_cast<uint8_t *>(ctx->work);
+  float *x_dev = reinterpret_cast<float *>(base + x_off);
+  uint8_t *xq = base + xq_off;
+  float *y_dev = reinterpret_cast<float *>(base + y_off);
+  std::memcpy(ctx->pinned, x_host, static_cast<size_t>(k) * 4);
+  if (cudaMemcpyAsync(x_dev, ctx->pinned, k * 4, cudaMemcpyHostToDevice, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  st = launch_quant_q8_1(ctx, stream, x_dev, xq, k, 1, false);
+  if (st != UGB_OK) return st;
+  MatvecArgs a;
+  a.kind = kind;
+  a.w = static_cast<const uint8_t *>(w_dev);
+  a.row_bytes = row_bytes;
+  a.k = k;
+  a.m = m;
+  a.xq = xq;
+  a.xl = xl;
+  a.y = y_dev;
+  a.ldy = m;
+  a.batch = 1;
+  st = launch_matvec(ctx, stream, a);
+  if (st != UGB_OK) return st;
+  float *y_pin = ctx->pinned + k;
+  if (cudaMemcpyAsync(y_pin, y_dev, m * 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  st = read_status_bits(ctx, stream, nullptr);  // synchronises the stream
+  if (st != UGB_OK) return st;
+  std::memcpy(y_host, y_pin, static_cast<size_t>(m) * 4);
+  return UGB_OK;
+}
+
+}  // extern "C"

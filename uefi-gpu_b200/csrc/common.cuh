@@ -1,0 +1,176 @@
+// common.cuh -- sm_100a device helpers shared by every kernel of libugb.
+//
+// Bulk-copy (TMA) + mbarrier pipeline primitives written as inline PTX, bounded waits that
+// report through the device status word instead of hanging, and small integer helpers.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include "../../include/ugb.h"
+
+namespace ugb {
+
+// Bits of the device status word (ugb_ctx::status).  Any kernel may OR these in; the host
+// reads and clears the word with ugb_status_read().
+enum : uint32_t {
+  ST_NONFINITE_IN = 1u << 0,   // a non-finite activation reached a quantiser
+  ST_NONFINITE_OUT = 1u << 1,  // a kernel produced a non-finite output
+  ST_TIMEOUT = 1u << 2,        // a bounded wait gave up (copy or peer never arrived)
+  ST_BADARG = 1u << 3,         // a descriptor failed a device-side bounds check
+};
+
+__device__ __forceinline__ void status_or(uint32_t *status, uint32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+// ---- shared-memory addressing -----------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t lds32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v));
+}
+
+// ---- mbarrier -----------------------------------------------------------------------------
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Default limit of every device-side wait: far above any legitimate copy latency, short
+// enough that a lost copy surfaces as UGB_ETIMEOUT instead of a hung GPU.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Wait for phase `parity` of an mbarrier, giving up after kWaitLimitNs.  Returns false on
+// timeout (the caller records ST_TIMEOUT and leaves uniformly).
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - start > kWaitLimitNs) return false;
+  }
+}
+
+// ---- bulk copies (TMA, non-tensor) ---------------------------------------------------------
+
+// Global -> shared bulk copy completing on an mbarrier.  dst, src 16-byte aligned; bytes a
+// positive multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes,
+                                         uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---- programmatic dependent launch -----------------------------------------------------------
+
+// Block until the grids this launch depends on have completed and flushed (no-op when the
+// launch carried no programmatic dependency).
+__device__ __forceinline__ void grid_dep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Allow the next grid in the stream to begin launching.
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---- numerics ---------------------------------------------------------------------------------
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t h) {
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h & 0xffffu)));
+}
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// 32 little-endian bytes starting at a 2-byte aligned shared address, as 8 words, from 9
+// aligned loads: word i = bytes [4i, 4i+4) of the run.
+__device__ __forceinline__ void lds_words8_u2(uint32_t addr, uint32_t (&w)[8]) {
+  const uint32_t a4 = addr & ~3u;
+  const uint32_t sh = (addr & 3u) * 8u;
+  uint32_t r[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) r[i] = lds32(a4 + 4u * i);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) w[i] = __funnelshift_rc(r[i], r[i + 1], sh);
+}
+
+__device__ __forceinline__ uint32_t lds16_u2(uint32_t addr) {
+  const uint32_t w = lds32(addr & ~3u);
+  return (w >> ((addr & 3u) * 8u)) & 0xffffu;
+}
+
+__device__ __forceinline__ uint32_t lds8(uint32_t addr) {
+  const uint32_t w = lds32(addr & ~3u);
+  return (w >> ((addr & 3u) * 8u)) & 0xffu;
+}
+
+__host__ __device__ constexpr inline uint64_t round_up(uint64_t x, uint64_t m) {
+  return (x + m - 1) / m * m;
+}
+
+}  // namespace ugb

@@ -1,0 +1,60 @@
+// internal.hpp -- host-side declarations shared by the .cu files of libugb.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+#include <cuda_runtime.h>
+
+#include "../../include/ugb.h"
+
+struct ugb_ctx {
+  int device = 0;
+  int sm_count = 0;
+  size_t smem_optin = 0;        // max dynamic shared memory per block
+  uint32_t *status = nullptr;   // device status word
+  uint32_t *status_host = nullptr;  // pinned mirror for ugb_status_read
+  // Workspace of the host-buffer entry points (x staging, xq, y staging).
+  void *work = nullptr;
+  size_t work_bytes = 0;
+  float *pinned = nullptr;      // pinned host staging for ugb_linear
+  size_t pinned_bytes = 0;
+  std::mutex mu;
+};
+
+namespace ugb {
+
+inline ugb_status cuda_status(cudaError_t e) { return e == cudaSuccess ? UGB_OK : UGB_EBACKEND; }
+
+// Q8_1 activation layout (see ugb.h ugb_q8act_bytes).
+struct Q8Act {
+  int64_t k = 0, batch = 0, nbp = 0;
+  size_t d_off = 0, s_off = 0, bytes = 0;
+};
+Q8Act q8act_layout(int64_t k, int64_t batch);
+
+// Streaming matvec launch description.
+struct MatvecArgs {
+  uint32_t kind = 0;
+  const uint8_t *w = nullptr;
+  int64_t row_bytes = 0, k = 0, m = 0;
+  const uint8_t *xq = nullptr;   // Q8_1 buffer
+  Q8Act xl;                      // its layout
+  float *y = nullptr;            // [batch][ldy]
+  int64_t ldy = 0;
+  int64_t batch = 1;
+  int32_t *dots = nullptr;       // debug: block dots instead of y
+  bool pdl = false;              // launch with programmatic stream serialisation
+};
+
+ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a);
+ugb_status launch_quant_q8_1(ugb_ctx *ctx, cudaStream_t stream, const float *x, uint8_t *xq,
+                             int64_t k, int64_t batch, bool pdl);
+ugb_status launch_fill_synthetic(ugb_ctx *ctx, cudaStream_t stream, uint32_t kind, uint8_t *w,
+                                 int64_t k, int64_t m, uint64_t seed);
+ugb_status init_matvec_kernels(ugb_ctx *ctx);
+
+// Validation shared by entry points: kind supported by the matvec kernels, k a multiple of
+// its block, row_bytes consistent.
+ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_t k, int64_t m);
+
+}  // namespace ugb
