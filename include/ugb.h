@@ -136,6 +136,25 @@ ugb_status ugb_block_dots(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const 
 ugb_status ugb_fill_synthetic(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, void *w_dev,
                               int64_t k, int64_t m, uint64_t seed);
 
+/* ---- streams and graphs ------------------------------------------------------------------ */
+
+/* Launch this context's kernels with programmatic dependent launch (enable != 0): each
+ * kernel starts streaming its weights while the previous kernel in the stream drains, and
+ * waits for that kernel's results before reading its activation.  Only valid when the kernel
+ * immediately before a matvec does not write that matvec's weights (true for a decode graph,
+ * whose weights are static).  Off by default. */
+ugb_status ugb_set_pdl(ugb_ctx *ctx, int enable);
+
+/* CUDA-graph capture of a sequence of ugb_* calls on `stream`, replacing the reference's
+ * prebuilt per-token command list submitted as one GPFIFO entry (gpu_graph.rs:24-69,
+ * forward_gpu gpu_graph.rs:170-197).  begin/end bracket the calls (cudaStreamBeginCapture /
+ * cudaStreamEndCapture + instantiate); launch replays the graph on any stream. */
+typedef struct ugb_graph ugb_graph;
+ugb_status ugb_graph_begin(ugb_ctx *ctx, ugb_stream stream);
+ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out);
+ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream);
+ugb_status ugb_graph_destroy(ugb_graph *graph);
+
 /* ---- host-buffer entry points (synchronous) --------------------------------------------- */
 
 /* y_host[m] = W x_host[k], synchronously: copy x to the device, quantise, matvec, copy y

@@ -44,6 +44,11 @@ SIGNATURES = {
     "ugb_block_dots": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_fill_synthetic": (_int, [_vp, _vp, _u32, _vp, _i64, _i64, _u64]),
     "ugb_linear": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
+    "ugb_set_pdl": (_int, [_vp, _int]),
+    "ugb_graph_begin": (_int, [_vp, _vp]),
+    "ugb_graph_end": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
+    "ugb_graph_launch": (_int, [_vp, _vp]),
+    "ugb_graph_destroy": (_int, [_vp]),
 }
 
 
@@ -146,6 +151,23 @@ class Context:
         check("ugb_fill_synthetic", lib().ugb_fill_synthetic(self.handle, _stream(stream), kind,
                                                                _ptr(w), k, m, seed))
 
+    def set_pdl(self, enable: bool) -> None:
+        check("ugb_set_pdl", lib().ugb_set_pdl(self.handle, 1 if enable else 0))
+
+    def capture(self, fn, stream) -> "Graph":
+        """Capture the ugb_* calls fn() makes on `stream` (a non-default torch stream) into a
+        replayable CUDA graph."""
+        import torch
+        with torch.cuda.stream(stream):
+            check("ugb_graph_begin", lib().ugb_graph_begin(self.handle, stream.cuda_stream))
+            try:
+                fn()
+            finally:
+                h = _vp()
+                code = lib().ugb_graph_end(self.handle, stream.cuda_stream, ctypes.byref(h))
+        check("ugb_graph_end", code)
+        return Graph(h)
+
     # ---- host-buffer entry points -----------------------------------------------------------
     def linear(self, kind: int, w, rb: int, x_host, k: int, m: int, stream=None):
         """Gpu::matvec / Weights::linear equivalent: numpy x in, numpy y out (synchronous)."""
@@ -156,6 +178,27 @@ class Context:
                                 x.ctypes.data, y.ctypes.data, k, m)
         check("ugb_linear", code)
         return y
+
+
+class Graph:
+    """An instantiated CUDA graph of ugb_* calls (ugb_graph_end / launch / destroy)."""
+
+    def __init__(self, handle):
+        self.handle = handle
+
+    def launch(self, stream=None) -> None:
+        check("ugb_graph_launch", lib().ugb_graph_launch(self.handle, _stream(stream)))
+
+    def close(self) -> None:
+        if self.handle:
+            lib().ugb_graph_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def alloc_q8act(k: int, batch: int = 1, device: str = "cuda"):

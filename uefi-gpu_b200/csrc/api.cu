@@ -174,7 +174,7 @@ ugb_status ugb_quant_q8_1(ugb_ctx *ctx, ugb_stream stream, const float *x_dev, v
   if (st != UGB_OK) return st;
   if (k <= 0 || k % 32 || k > UGB_MAX_K || batch <= 0 || batch > 65536) return UGB_ESHAPE;
   if (!x_dev || (reinterpret_cast<uintptr_t>(x_dev) & 3) || !aligned16(xq_dev)) return UGB_EALIGN;
-  return launch_quant_q8_1(ctx, stream, x_dev, static_cast<uint8_t *>(xq_dev), k, batch, false);
+  return launch_quant_q8_1(ctx, stream, x_dev, static_cast<uint8_t *>(xq_dev), k, batch, ctx->pdl);
 }
 
 ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
@@ -197,6 +197,7 @@ ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
   a.y = y_dev;
   a.ldy = m;
   a.batch = batch;
+  a.pdl = ctx->pdl;
   return launch_matvec(ctx, stream, a);
 }
 
@@ -230,6 +231,57 @@ ugb_status ugb_fill_synthetic(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, vo
   return launch_fill_synthetic(ctx, stream, kind, static_cast<uint8_t *>(w_dev), k, m, seed);
 }
 
+ugb_status ugb_set_pdl(ugb_ctx *ctx, int enable) {
+  if (!ctx) return UGB_ECONTEXT;
+  ctx->pdl = enable != 0;
+  return UGB_OK;
+}
+
+struct ugb_graph {
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+ugb_status ugb_graph_begin(ugb_ctx *ctx, ugb_stream stream) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  if (!stream) return UGB_ECONTEXT;  // the legacy default stream cannot be captured
+  return cuda_status(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+}
+
+ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  if (!out) return UGB_ECONTEXT;
+  *out = nullptr;
+  ugb_graph *g = new (std::nothrow) ugb_graph();
+  if (!g) return UGB_EBACKEND;
+  if (cudaStreamEndCapture(stream, &g->graph) != cudaSuccess) {
+    delete g;
+    return UGB_EBACKEND;
+  }
+  if (cudaGraphInstantiate(&g->exec, g->graph, 0) != cudaSuccess) {
+    cudaGraphDestroy(g->graph);
+    delete g;
+    return UGB_EBACKEND;
+  }
+  *out = g;
+  return UGB_OK;
+}
+
+ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream) {
+  if (!graph || !graph->exec) return UGB_ECONTEXT;
+  return cuda_status(cudaGraphLaunch(graph->exec, stream));
+}
+
+ugb_status ugb_graph_destroy(ugb_graph *graph) {
+  if (!graph) return UGB_ECONTEXT;
+  if (graph->exec) cudaGraphExecDestroy(graph->exec);
+  if (graph->graph) cudaGraphDestroy(graph->graph);
+  delete graph;
+  return UGB_OK;
+}
+
 ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
                       int64_t row_bytes, const float *x_host, float *y_host, int64_t k,
                       int64_t m) {
@@ -239,6 +291,7 @@ ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
   if (st != UGB_OK) return st;
   if (!x_host || !y_host) return UGB_EALIGN;
   std::lock_guard<std::mutex> lock(ctx->mu);
+  // x -> device, quant_act, matvec, y -> host (the reference's Gpu::matvec round trip).
   const Q8Act xl = q8act_layout(k, 1);
   const size_t x_off = 0, xq_off = round_up(k * 4, 256), y_off = xq_off + round_up(xl.bytes, 256);
   st = reserve(ctx, y_off + round_up(m * 4, 256), static_cast<size_t>(k + m) * 4);

@@ -48,6 +48,10 @@ __device__ __forceinline__ void sts8(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.b8 [%0], %1;" ::"r"(addr), "r"(v));
 }
 
+__device__ __forceinline__ void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.b32 [%0], %1;" ::"r"(addr), "r"(v));
+}
+
 // ---- mbarrier -----------------------------------------------------------------------------
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -68,14 +72,25 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// Arrive without release ordering.  Used to hand a ring stage back to the producer: the
+// consumer's shared-memory reads of the stage have completed (their values were consumed by
+// the arithmetic that precedes this instruction), and a release arrive would also wait for
+// the thread's earlier global stores to become visible -- a full L2 round trip per stage.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+// Test a phase; if it has not completed, the thread is suspended in hardware until it
+// completes or about kSuspendNs pass, so waiting warps do not spin on issue slots.
+constexpr uint32_t kSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -95,9 +110,9 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
-  for (uint32_t it = 0;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - start > kWaitLimitNs) return false;
+    if (globaltimer_ns() - start > kWaitLimitNs) return false;
   }
 }
 
@@ -147,16 +162,38 @@ __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
-// 32 little-endian bytes starting at a 2-byte aligned shared address, as 8 words, from 9
-// aligned loads: word i = bytes [4i, 4i+4) of the run.
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
+// The 40 bytes at addr & ~7 as 10 words (five 64-bit loads), shifted down by one word when
+// addr & 7 >= 4, so that s[0] holds byte (addr & ~3) onward.  64-bit loads of runs spaced 34
+// or 110 bytes apart (GGUF Q8_0 / Q3_K blocks) hit 16 distinct bank pairs per half-warp, so
+// they are conflict-free where 32-bit loads of the same runs are 2-way conflicted.
+__device__ __forceinline__ void lds_window9(uint32_t addr, uint32_t (&s)[9]) {
+  const uint32_t a8 = addr & ~7u;
+  uint32_t r[10];
+#pragma unroll
+  for (int i = 0; i < 5; ++i) {
+    const uint2 v = lds64(a8 + 8u * i);
+    r[2 * i] = v.x;
+    r[2 * i + 1] = v.y;
+  }
+  const bool hi = (addr & 4u) != 0;
+#pragma unroll
+  for (int i = 0; i < 9; ++i) s[i] = hi ? r[i + 1] : r[i];
+}
+
+// 32 little-endian bytes starting at a 2-byte aligned shared address, as 8 words:
+// word i = bytes [4i, 4i+4) of the run.
 __device__ __forceinline__ void lds_words8_u2(uint32_t addr, uint32_t (&w)[8]) {
-  const uint32_t a4 = addr & ~3u;
+  uint32_t s[9];
+  lds_window9(addr, s);
   const uint32_t sh = (addr & 3u) * 8u;
-  uint32_t r[9];
 #pragma unroll
-  for (int i = 0; i < 9; ++i) r[i] = lds32(a4 + 4u * i);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) w[i] = __funnelshift_rc(r[i], r[i + 1], sh);
+  for (int i = 0; i < 8; ++i) w[i] = __funnelshift_rc(s[i], s[i + 1], sh);
 }
 
 __device__ __forceinline__ uint32_t lds16_u2(uint32_t addr) {

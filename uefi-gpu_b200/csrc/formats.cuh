@@ -56,12 +56,14 @@ struct WUnit {
 };
 
 // Q8_0 block at a 2-byte aligned shared address: fp16 d then 32 int8 (frontier_core.rs:172).
+// One 40-byte window (five 64-bit loads) holds the whole 34-byte block at any even offset.
 __device__ __forceinline__ void load_wunit_q8_0(uint32_t blk, WUnit &w) {
-  uint32_t q[8];
-  lds_words8_u2(blk + 2, q);
+  uint32_t s[9];
+  lds_window9(blk, s);
+  const uint32_t sh = (blk & 3u) * 8u;  // 0 or 16: where d starts inside s[0]
 #pragma unroll
-  for (int i = 0; i < 8; ++i) w.q[i] = static_cast<int>(q[i]);
-  w.d = half_bits_to_float(lds16_u2(blk));
+  for (int i = 0; i < 8; ++i) w.q[i] = static_cast<int>(__funnelshift_rc(s[i], s[i + 1], sh + 16));
+  w.d = half_bits_to_float(s[0] >> sh);
   w.dm = 0.f;
   w.sc_lo = w.sc_hi = 0;
 }

@@ -18,6 +18,7 @@ struct ugb_ctx {
   size_t work_bytes = 0;
   float *pinned = nullptr;      // pinned host staging for ugb_linear
   size_t pinned_bytes = 0;
+  bool pdl = false;             // programmatic dependent launch for every kernel
   std::mutex mu;
 };
 

@@ -2,16 +2,26 @@
 //
 // Replaces linear_dp4a / qkv_dp4a / gateup_dp4a (gpu_dp4a.cu:32-64) and frontier_matvec
 // (frontier_quant.cu:58-66).  Design for sm_100a:
-//  * Persistent CTAs (grid = min(row groups, SMs x resident CTAs)), 8 warps each.
-//  * Work item = (group of R consecutive rows) x (K chunk).  One elected thread streams the
-//    item's R row segments (GGUF bytes, unchanged) and the activation chunk into a stage of
-//    a multi-stage shared-memory ring with cp.async.bulk, completing on one mbarrier per
-//    stage; weights carry an L2 evict-first hint since each byte is read exactly once.
-//  * Warp w owns rows w*RW..w*RW+RW-1 of the group; lane l takes 32-element units l, l+32, ..
-//    of the chunk, forms the exact int32 block dot with dp4a and accumulates the scaled term
-//    in fp32 registers across chunks.  The row total is a fixed xor-shuffle tree, so results
+//  * Persistent CTAs, 8 consumer warps + 1 producer warp, coupled only through per-stage
+//    full / empty mbarriers (no CTA-wide barrier per item; every wait is bounded and a lost
+//    copy sets UGB_STATUS_TIMEOUT instead of hanging).
+//  * The producer streams work items -- groups of consecutive rows, in the unchanged GGUF
+//    byte layout -- into a multi-stage shared-memory ring with cp.async.bulk (one copy per
+//    item when whole rows fit a stage, one per row chunk otherwise), weights carrying an L2
+//    evict-first hint since each byte is read once.  The first stages are requested before
+//    the programmatic launch dependency resolves, overlapping the previous kernel's tail.
+//  * The Q8_1 activation is bulk-copied into shared memory once per CTA.
+//  * Two consumers:
+//    - mv_rows_kernel (batch 1, whole rows): each warp owns RW rows; lane l covers slots
+//      l, l+32, ... of the warp's flattened (row, 32-element unit) space, keeps the matching
+//      activation units in registers for the whole kernel (every item spans the whole row),
+//      and the RW row totals come out of one transposed shuffle tree.  This keeps the
+//      per-row instruction overhead small enough to stream at HBM speed.
+//    - mv_stream_kernel (batches, long rows split into K chunks, int-dot dumps): one warp per
+//      row, activation units read from shared memory, row sums kept in registers across the
+//      row's chunks.
+//  * Integer block dots are exact (dp4a); the fp32 accumulation order is fixed, so results
 //    are deterministic run to run.
-//  * Every mbarrier wait is bounded; a lost copy sets UGB_STATUS_TIMEOUT and the CTA leaves.
 #include <algorithm>
 #include <cmath>
 
@@ -21,28 +31,33 @@
 namespace ugb {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr uint32_t kBarBytes = 128;  // mbarrier area at the start of dynamic shared memory
+constexpr int kWarps = 8;                    // consumer warps per CTA
+constexpr int kThreads = kWarps * 32 + 32;   // + one producer warp
+constexpr uint32_t kBarBytes = 256;          // mbarriers at the start of dynamic shared memory
+constexpr int kMaxStages = 8;
+constexpr size_t kXBudget = 100 * 1024;      // activation bytes staged per CTA
+constexpr uint32_t kItemTarget = 32 * 1024;  // weight bytes per pipeline stage
+constexpr size_t kSmPerKernel = 112 * 1024;  // shared memory one kernel takes per SM
+constexpr int kSlots = 4;                    // activation units a lane keeps in registers
 
 struct MvParams {
   const uint8_t *w;
-  const uint8_t *w_end;       // w + m * row_bytes
-  const uint8_t *w_end16;     // w_end rounded down to 16 bytes
+  const uint8_t *w_end16;     // (w + m * row_bytes) rounded down to 16 bytes
   uint64_t row_bytes;
-  int k, m, batch;
-  int kc, nch, ngroups;
+  int k, m;
+  int rows;                   // rows per item (8 * rows-per-warp)
+  int kc, nch, ngroups;       // K chunk (elements), chunks per row, row groups (items / nch)
   uint32_t seg_stride, stage_bytes;
-  uint32_t xq_off, xd_off, xs_off, kcb4;
   int stages;
-  const uint8_t *xq;
+  uint32_t x_q, x_d, x_s;     // shared offsets of the staged activation arrays
+  uint32_t ring;              // shared offset of the weight ring
+  const uint8_t *xq;          // Q8_1 buffer: quants [nb][k], scales / sums [nb][nbp]
   const float *xd;
   const int *xs;
-  int64_t xq_stride, xds_stride;
+  int nbp;
   float *y;
   int64_t ldy;
   int32_t *dots;
-  int64_t dots_ld;
   uint32_t *status;
 };
 
@@ -51,60 +66,64 @@ __host__ __device__ constexpr uint64_t bytes_of(uint64_t elems) {
   return elems / Fmt<KIND>::kElems * Fmt<KIND>::kBytes;
 }
 
-// Issue (or size) the copies of local item t into the stage at `stage`.  Called by one
-// thread.  Tail bytes that fall in the last partial 16 bytes of the weight buffer are copied
-// with plain loads first (bulk copies need 16-byte aligned ranges and must not read past the
-// buffer), then the barrier is armed with the bulk byte count, then the bulk copies go out.
-template <int KIND, int NB, int RW>
-__device__ void issue_item(const MvParams &p, int t, uint32_t stage, uint32_t bar,
-                           uint64_t pol_w, bool weights, bool acts, bool arm) {
-  const int j = t / p.nch, c = t - j * p.nch;
-  const int g = blockIdx.x + j * gridDim.x;
-  constexpr int R = kWarps * RW;
-  const int r0 = g * R;
-  const int nrows = min(R, p.m - r0);
-  const int k0 = c * p.kc;
-  const int klen = min(p.kc, p.k - k0);
-  const uint64_t seg_off = bytes_of<KIND>(k0), seg_len = bytes_of<KIND>(klen);
-  const uint32_t xlen = static_cast<uint32_t>(klen);
-  const uint32_t dlen = static_cast<uint32_t>(round_up(klen / 32, 4) * 4);
+__device__ __forceinline__ const uint8_t *floor16(const uint8_t *p) {
+  return reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15));
+}
+__device__ __forceinline__ const uint8_t *ceil16(const uint8_t *p) {
+  return reinterpret_cast<const uint8_t *>((reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15));
+}
 
-  if (arm) {
-    uint32_t tx = 0;
-    for (int r = 0; r < nrows; ++r) {
-      const uint8_t *src = p.w + static_cast<uint64_t>(r0 + r) * p.row_bytes + seg_off;
-      const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15));
-      const uint8_t *e = src + seg_len;
-      const uint8_t *a1 = reinterpret_cast<const uint8_t *>((reinterpret_cast<uintptr_t>(e) + 15) & ~uintptr_t(15));
-      if (e > p.w_end16) {  // only the final segment of the buffer can get here
-        const uint8_t *tb = a0 > p.w_end16 ? a0 : p.w_end16;
-        for (const uint8_t *b = tb; b < e; ++b)
-          sts8(stage + r * p.seg_stride + static_cast<uint32_t>(b - a0), *b);
-        a1 = tb;
-      }
-      tx += static_cast<uint32_t>(a1 - a0);
-    }
-    tx += NB * (xlen + dlen * (Fmt<KIND>::kNeedsSum ? 2u : 1u));
-    mbar_arrive_expect_tx(bar, tx);
+// Geometry of item t of this CTA: rows [r0, r0+nrows), K chunk c.  A CTA owns whole row
+// groups (g = blockIdx.x, blockIdx.x + gridDim.x, ...) and walks each group's K chunks in
+// order, so a row's partial sums stay in the owning warp's registers across its chunks.
+struct Item {
+  int r0, nrows, c;
+};
+__device__ __forceinline__ Item item_of(const MvParams &p, int t) {
+  const int j = p.nch == 1 ? t : t / p.nch;
+  const int g = blockIdx.x + j * gridDim.x;
+  Item it;
+  it.c = t - j * p.nch;
+  it.r0 = g * p.rows;
+  it.nrows = min(p.rows, p.m - it.r0);
+  return it;
+}
+
+// Byte range [a0, a1) a bulk copy may fetch for the span [src, e): 16-byte aligned, and
+// never past the last 16-byte boundary of the weight buffer; the bytes beyond (only in the
+// final span) go through plain loads.
+__device__ __forceinline__ void span16(const MvParams &p, const uint8_t *src, const uint8_t *e,
+                                       const uint8_t *&a0, const uint8_t *&a1) {
+  a0 = floor16(src);
+  a1 = ceil16(e);
+  if (e > p.w_end16) a1 = a0 > p.w_end16 ? a0 : p.w_end16;
+}
+
+// Copies of item t into `stage` (one thread).  When a row chunk is the whole row (nch == 1)
+// the item's rows are one contiguous span and one bulk copy fetches all of them.
+template <int KIND>
+__device__ void issue_item(const MvParams &p, int t, uint32_t stage, uint32_t bar, uint64_t pol) {
+  const Item it = item_of(p, t);
+  const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(it.c) * p.kc);
+  const uint64_t seg_len = bytes_of<KIND>(min(p.kc, p.k - it.c * p.kc));
+  const int spans = p.nch == 1 ? 1 : it.nrows;
+  uint32_t tx = 0;
+  for (int r = 0; r < spans; ++r) {
+    const uint8_t *src = p.w + static_cast<uint64_t>(it.r0 + r) * p.row_bytes + seg_off;
+    const uint8_t *e = p.nch == 1 ? p.w + static_cast<uint64_t>(it.r0 + it.nrows) * p.row_bytes : src + seg_len;
+    const uint8_t *a0, *a1;
+    span16(p, src, e, a0, a1);
+    const uint32_t dst = stage + r * p.seg_stride;
+    for (const uint8_t *b = a1; b < e; ++b) sts8(dst + static_cast<uint32_t>(b - a0), *b);
+    tx += static_cast<uint32_t>(a1 - a0);
   }
-  if (weights) {
-    for (int r = 0; r < nrows; ++r) {
-      const uint8_t *src = p.w + static_cast<uint64_t>(r0 + r) * p.row_bytes + seg_off;
-      const uint8_t *a0 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15));
-      const uint8_t *e = src + seg_len;
-      const uint8_t *a1 = reinterpret_cast<const uint8_t *>((reinterpret_cast<uintptr_t>(e) + 15) & ~uintptr_t(15));
-      if (e > p.w_end16) a1 = a0 > p.w_end16 ? a0 : p.w_end16;
-      if (a1 > a0) bulk_g2s(stage + r * p.seg_stride, a0, static_cast<uint32_t>(a1 - a0), bar, pol_w);
-    }
-  }
-  if (acts) {
-    const uint64_t pol_x = policy_evict_last();
-    for (int v = 0; v < NB; ++v) {
-      bulk_g2s(stage + p.xq_off + v * p.kc, p.xq + v * p.xq_stride + k0, xlen, bar, pol_x);
-      bulk_g2s(stage + p.xd_off + v * p.kcb4 * 4, p.xd + v * p.xds_stride + k0 / 32, dlen, bar, pol_x);
-      if (Fmt<KIND>::kNeedsSum)
-        bulk_g2s(stage + p.xs_off + v * p.kcb4 * 4, p.xs + v * p.xds_stride + k0 / 32, dlen, bar, pol_x);
-    }
+  mbar_arrive_expect_tx(bar, tx);
+  for (int r = 0; r < spans; ++r) {
+    const uint8_t *src = p.w + static_cast<uint64_t>(it.r0 + r) * p.row_bytes + seg_off;
+    const uint8_t *e = p.nch == 1 ? p.w + static_cast<uint64_t>(it.r0 + it.nrows) * p.row_bytes : src + seg_len;
+    const uint8_t *a0, *a1;
+    span16(p, src, e, a0, a1);
+    if (a1 > a0) bulk_g2s(stage + r * p.seg_stride, a0, static_cast<uint32_t>(a1 - a0), bar, pol);
   }
 }
 
@@ -114,128 +133,252 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-template <int KIND, int NB, int RW, bool DOTS>
-__global__ void __launch_bounds__(kThreads) mv_stream_kernel(const MvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int R = kWarps * RW;
-  const uint32_t bars = smem_u32(smem);
-  const uint32_t data = bars + kBarBytes;
-  const int my_groups = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                        static_cast<int>(gridDim.x);
-  const int T = my_groups * p.nch;
-
-  if (tid == 0) {
-    for (int s = 0; s < p.stages; ++s) mbar_init(bars + 8 * s, 1);
-    fence_mbar_init();
-    const uint64_t pol_w = policy_evict_first();
-    const int pre = min(T, p.stages);
-    // Weights do not depend on earlier kernels: arm and start them before waiting on the
-    // programmatic dependency, then fetch the activations.
-    for (int t = 0; t < pre; ++t)
-      issue_item<KIND, NB, RW>(p, t, data + (t % p.stages) * p.stage_bytes, bars + 8 * (t % p.stages),
-                               pol_w, true, false, true);
-    grid_dep_wait();
-    for (int t = 0; t < pre; ++t)
-      issue_item<KIND, NB, RW>(p, t, data + (t % p.stages) * p.stage_bytes, bars + 8 * (t % p.stages),
-                               pol_w, false, true, false);
+// Totals of RW per-lane row partials v[0..RW) over the warp with one transposed shuffle tree
+// (RW=4: 6 shuffles instead of 20).  The total of row r ends in lane r * (32 / RW); the lane
+// returns the total of its row in *out and whether it owns one.
+template <int RW>
+__device__ __forceinline__ bool reduce_rows(const float (&v)[RW], int lane, float &out) {
+  float c;
+  if constexpr (RW == 1) {
+    c = v[0];
+  } else if constexpr (RW == 2) {
+    const bool hi = lane & 16;
+    const float r = __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[1], 16);
+    c = (hi ? v[1] : v[0]) + r;  // row (hi ? 1 : 0)
+  } else {
+    const bool hi = lane & 16;
+    const float r0 = __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[2], 16);
+    const float r1 = __shfl_xor_sync(0xffffffffu, hi ? v[1] : v[3], 16);
+    const float a = (hi ? v[2] : v[0]) + r0;  // row (hi ? 2 : 0)
+    const float b = (hi ? v[3] : v[1]) + r1;  // row (hi ? 3 : 1)
+    const bool h8 = lane & 8;
+    const float r = __shfl_xor_sync(0xffffffffu, h8 ? a : b, 8);
+    c = (h8 ? b : a) + r;  // row (hi ? 2 : 0) + (h8 ? 1 : 0)
   }
-  grid_dep_wait();
-  grid_dep_launch();
+#pragma unroll
+  for (int o = 32 / RW / 2; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+  out = c;
+  return (lane & (32 / RW - 1)) == 0;
+}
+
+// Shared prologue: barriers, programmatic-launch hand-off, the producer warp's whole life,
+// and the activation staging.  Returns false in the producer warp (which is done), true in
+// consumer warps once the activation is in shared memory (ok = false if that copy timed out).
+template <int KIND, int NB>
+__device__ __forceinline__ bool prologue(const MvParams &p, uint32_t base, int T, bool &ok) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t full = base, empty = base + 64, xbar = base + 128;
+  const uint32_t ring = base + p.ring;
+  constexpr bool kSum = Fmt<KIND>::kNeedsSum;
+  const uint32_t xq_bytes = static_cast<uint32_t>(p.k), xd_bytes = static_cast<uint32_t>(p.nbp) * 4;
+  if (tid == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(full + 8 * s, 1);
+      mbar_init(empty + 8 * s, kWarps);
+    }
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+  }
   __syncthreads();
+  grid_dep_launch();
+  if (warp == kWarps) {
+    if (lane == 0) {
+      // Weights do not depend on earlier kernels: request the first stages before the
+      // programmatic dependency resolves, then stage the activation once for the CTA.
+      const uint64_t pol_w = policy_evict_first();
+      const int pre = min(T, p.stages);
+      for (int t = 0; t < pre; ++t) issue_item<KIND>(p, t, ring + t * p.stage_bytes, full + 8 * t, pol_w);
+      grid_dep_wait();
+      mbar_arrive_expect_tx(xbar, NB * (xq_bytes + xd_bytes * (kSum ? 2u : 1u)));
+      const uint64_t pol_x = policy_evict_last();
+      for (int v = 0; v < NB; ++v) {
+        bulk_g2s(base + p.x_q + v * xq_bytes, p.xq + static_cast<int64_t>(v) * p.k, xq_bytes, xbar, pol_x);
+        bulk_g2s(base + p.x_d + v * xd_bytes, p.xd + static_cast<int64_t>(v) * p.nbp, xd_bytes, xbar, pol_x);
+        if (kSum) bulk_g2s(base + p.x_s + v * xd_bytes, p.xs + static_cast<int64_t>(v) * p.nbp, xd_bytes, xbar, pol_x);
+      }
+      for (int t = pre; t < T; ++t) {
+        const int s = t % p.stages;
+        if (!mbar_wait_bounded(empty + 8 * s, ((t / p.stages) - 1) & 1)) {
+          status_or(p.status, ST_TIMEOUT);
+          break;
+        }
+        issue_item<KIND>(p, t, ring + s * p.stage_bytes, full + 8 * s, pol_w);
+      }
+    }
+    return false;
+  }
+  grid_dep_wait();  // consumers read the activation and write y only after the dependency
+  ok = __all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0));
+  if (!ok && lane == 0) status_or(p.status, ST_TIMEOUT);
+  return true;
+}
 
-  float acc[RW][NB];
-#pragma unroll
-  for (int rr = 0; rr < RW; ++rr)
-#pragma unroll
-    for (int v = 0; v < NB; ++v) acc[rr][v] = 0.f;
+// Wait for stage s of item t; false (and the status bit) if it never arrives.
+__device__ __forceinline__ bool wait_stage(const MvParams &p, uint32_t full, int t, int lane) {
+  const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(full + 8 * (t % p.stages), (t / p.stages) & 1));
+  if (!ok && lane == 0) status_or(p.status, ST_TIMEOUT);
+  return ok;
+}
 
-  for (int t = 0; t < T; ++t) {
+// Hand stage s back to the producer.  Every read of it has completed (the values were
+// consumed by the arithmetic before this point); a relaxed arrive avoids waiting for this
+// thread's earlier global stores.
+__device__ __forceinline__ void release_stage(uint32_t empty, int s, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive_relaxed(empty + 8 * s);
+}
+
+// Batch-1, whole-row consumer (see the file comment).  RW rows per warp, 8 * RW per item.
+template <int KIND, int RW, int J>
+__global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) {
+  static_assert(J % 2 == 0 && J <= kSlots, "slots are processed in pairs");
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t full = base, empty = base + 64;
+  const uint32_t ring = base + p.ring;
+  const int T = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                static_cast<int>(gridDim.x);
+  bool ok = true;
+  if (!prologue<KIND, 1>(p, base, T, ok)) return;
+
+  // Slot j of this lane is flat index f = lane + 32 j of the warp's RW x U (row, unit) space.
+  // Its row offset inside an item, its unit and its activation unit are fixed for the kernel.
+  const int U = p.k / 32;
+  const int total = RW * U;
+  uint32_t srow_off[J];
+  int sunit[J], srow[J];
+  XUnit xr[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int f = lane + 32 * j;
+    const bool valid = f < total;
+    const int r = valid ? f / U : 0;
+    const int u = valid ? f - r * U : 0;
+    srow[j] = valid ? r : RW;  // RW matches no row: the slot adds nothing
+    sunit[j] = u;
+    srow_off[j] = static_cast<uint32_t>((warp * RW + r) * p.row_bytes);
+    load_xunit(base + p.x_q + 32 * u, base + p.x_d + 4 * u, base + p.x_s + 4 * u,
+               Fmt<KIND>::kNeedsSum, xr[j]);
+  }
+
+  for (int t = 0; ok && t < T; ++t) {
     const int s = t % p.stages;
-    const uint32_t stage = data + s * p.stage_bytes;
-    // Warp-uniform so the shuffles below always see a full warp.
-    const bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(bars + 8 * s, (t / p.stages) & 1));
-    const int j = t / p.nch, c = t - j * p.nch;
-    const int g = blockIdx.x + j * gridDim.x;
-    const int r0 = g * R;
-    const int nrows = min(R, p.m - r0);
-    if (ok) {
-      const int k0 = c * p.kc;
-      const int nunits = min(p.kc, p.k - k0) / 32;
-      const uint64_t seg_off = bytes_of<KIND>(k0);
-      uint32_t seg[RW];
+    ok = wait_stage(p, full, t, lane);
+    if (!ok) break;
+    const Item it = item_of(p, t);
+    // The item's rows are one span fetched from floor16(first row).
+    const uint32_t stage = ring + s * p.stage_bytes +
+        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.w + static_cast<uint64_t>(it.r0) * p.row_bytes) & 15);
+    float acc[J];
 #pragma unroll
-      for (int rr = 0; rr < RW; ++rr) {
-        const int r = warp * RW + rr;
-        const uintptr_t src = reinterpret_cast<uintptr_t>(p.w + static_cast<uint64_t>(r0 + r) * p.row_bytes + seg_off);
-        seg[rr] = stage + r * p.seg_stride + static_cast<uint32_t>(src & 15);
+    for (int j = 0; j < J; j += 2) {
+      acc[j] = acc[j + 1] = 0.f;
+      if (j * 32 < total) {  // warp-uniform
+        WUnit wa, wb;
+        load_wunit<KIND>(stage + srow_off[j], sunit[j], wa);
+        load_wunit<KIND>(stage + srow_off[j + 1], sunit[j + 1], wb);
+        const int ia = unit_isum<KIND>(wa, xr[j]);
+        const int ib = unit_isum<KIND>(wb, xr[j + 1]);
+        acc[j] = unit_term<KIND>(wa, xr[j], ia);
+        acc[j + 1] = unit_term<KIND>(wb, xr[j + 1], ib);
+      }
+    }
+    release_stage(empty, s, lane);
+    float rs[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+      rs[r] = 0.f;
+#pragma unroll
+      for (int j = 0; j < J; ++j) rs[r] += srow[j] == r ? acc[j] : 0.f;
+    }
+    float tot;
+    if (reduce_rows<RW>(rs, lane, tot)) {
+      const int rr = warp * RW + lane / (32 / RW);
+      if (rr < it.nrows) {
+        p.y[it.r0 + rr] = tot;
+        if (!isfinite(tot)) status_or(p.status, ST_NONFINITE_OUT);
+      }
+    }
+  }
+}
+
+// General consumer: NB activation vectors, rows of any length (K chunks), or int-dot dumps
+// (DOTS).  One warp per row, 8 rows per item; lane l takes 32-element units l, l+32, ... of
+// the chunk with the activation read from shared memory.
+template <int KIND, int NB, bool DOTS>
+__global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const MvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t full = base, empty = base + 64;
+  const uint32_t ring = base + p.ring;
+  const int T = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                static_cast<int>(gridDim.x) * p.nch;
+  bool ok = true;
+  if (!prologue<KIND, NB>(p, base, T, ok)) return;
+  constexpr bool kSum = Fmt<KIND>::kNeedsSum;
+  const uint32_t xq_bytes = static_cast<uint32_t>(p.k), xd_bytes = static_cast<uint32_t>(p.nbp) * 4;
+
+  float acc[NB];
+#pragma unroll
+  for (int v = 0; v < NB; ++v) acc[v] = 0.f;
+
+  for (int t = 0; ok && t < T; ++t) {
+    const int s = t % p.stages;
+    ok = wait_stage(p, full, t, lane);
+    if (!ok) break;
+    const uint32_t stage = ring + s * p.stage_bytes;
+    const Item it = item_of(p, t);
+    const int k0 = it.c * p.kc;
+    if (warp < it.nrows) {
+      const int nunits = min(p.kc, p.k - k0) / 32;
+      const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(k0));
+      const uint8_t *row = p.w + static_cast<uint64_t>(it.r0 + warp) * p.row_bytes + seg_off;
+      uint32_t seg;
+      if (p.nch == 1) {
+        const uint8_t *first = floor16(p.w + static_cast<uint64_t>(it.r0) * p.row_bytes);
+        seg = stage + static_cast<uint32_t>(row - first);
+      } else {
+        seg = stage + warp * p.seg_stride + static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row) & 15);
       }
       for (int u = lane; u < nunits; u += 32) {
+        const int ug = k0 / 32 + u;  // unit index within the whole row
         XUnit x[NB];
 #pragma unroll
         for (int v = 0; v < NB; ++v)
-          load_xunit(stage + p.xq_off + v * p.kc + 32 * u, stage + p.xd_off + (v * p.kcb4 + u) * 4,
-                     stage + p.xs_off + (v * p.kcb4 + u) * 4, Fmt<KIND>::kNeedsSum, x[v]);
+          load_xunit(base + p.x_q + v * xq_bytes + 32 * ug, base + p.x_d + v * xd_bytes + 4 * ug,
+                     base + p.x_s + v * xd_bytes + 4 * ug, kSum, x[v]);
+        WUnit wu;
+        load_wunit<KIND>(seg, u, wu);
 #pragma unroll
-        for (int rr = 0; rr < RW; ++rr) {
-          const int r = warp * RW + rr;
-          if (r < nrows) {
-            WUnit wu;
-            load_wunit<KIND>(seg[rr], u, wu);
-#pragma unroll
-            for (int v = 0; v < NB; ++v) {
-              const int isum = unit_isum<KIND>(wu, x[v]);
-              if constexpr (DOTS) {
-                p.dots[static_cast<int64_t>(r0 + r) * p.dots_ld + k0 / 32 + u] = isum;
-              } else {
-                acc[rr][v] += unit_term<KIND>(wu, x[v], isum);
-              }
-            }
-          }
-        }
-      }
-      if (!DOTS && c == p.nch - 1) {
-#pragma unroll
-        for (int rr = 0; rr < RW; ++rr) {
-          const int r = warp * RW + rr;
-#pragma unroll
-          for (int v = 0; v < NB; ++v) {
-            const float val = warp_sum(acc[rr][v]);
-            acc[rr][v] = 0.f;
-            if (lane == 0 && r < nrows) {
-              p.y[v * p.ldy + r0 + r] = val;
-              if (!isfinite(val)) status_or(p.status, ST_NONFINITE_OUT);
-            }
+        for (int v = 0; v < NB; ++v) {
+          const int isum = unit_isum<KIND>(wu, x[v]);
+          if constexpr (DOTS) {
+            p.dots[static_cast<int64_t>(it.r0 + warp) * (p.k / 32) + ug] = isum;
+          } else {
+            acc[v] += unit_term<KIND>(wu, x[v], isum);
           }
         }
       }
     }
-    if (__syncthreads_or(!ok)) {
-      if (tid == 0) {
-        status_or(p.status, ST_TIMEOUT);
-        // Give copies still in flight a bounded chance to land before shared memory is
-        // released.
-        for (int q = 0; q < p.stages && t + q < T; ++q)
-          mbar_wait_bounded(bars + 8 * ((t + q) % p.stages), ((t + q) / p.stages) & 1);
+    release_stage(empty, s, lane);
+    if (!DOTS && it.c == p.nch - 1) {
+#pragma unroll
+      for (int v = 0; v < NB; ++v) {
+        const float val = warp_sum(acc[v]);
+        acc[v] = 0.f;
+        if (lane == 0 && warp < it.nrows) {
+          p.y[v * p.ldy + it.r0 + warp] = val;
+          if (!isfinite(val)) status_or(p.status, ST_NONFINITE_OUT);
+        }
       }
-      return;
-    }
-    if (tid == 0 && t + p.stages < T) {
-      const int tn = t + p.stages;
-      issue_item<KIND, NB, RW>(p, tn, stage, bars + 8 * s, policy_evict_first(), true, true, true);
     }
   }
 }
 
 // ---- host side ------------------------------------------------------------------------------
 
-struct Plan {
-  int kc = 0, nch = 0, ngroups = 0, stages = 0;
-  uint32_t seg_stride = 0, stage_bytes = 0, xq_off = 0, xd_off = 0, xs_off = 0, kcb4 = 0;
-  size_t smem = 0;
-};
-
-int gran_elems(uint32_t kind) { return kind == UGB_Q8_0 ? 128 : 256; }
 uint64_t elems_to_bytes(uint32_t kind, uint64_t e) {
   switch (kind) {
     case UGB_Q8_0: return bytes_of<UGB_Q8_0>(e);
@@ -244,126 +387,176 @@ uint64_t elems_to_bytes(uint32_t kind, uint64_t e) {
   }
 }
 
-Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, int rw) {
+size_t x_bytes(uint32_t kind, int64_t k, int nb) {
+  const size_t nbp = round_up(static_cast<uint64_t>(k / 32), 4);
+  return static_cast<size_t>(nb) * (static_cast<size_t>(k) + nbp * 4 * (kind == UGB_Q4_K ? 2 : 1));
+}
+
+struct Plan {
+  bool rows_kernel = false;   // mv_rows_kernel (else mv_stream_kernel)
+  int rw = 1, slots = 2;      // rows per warp and register slots per lane (rows kernel)
+  int rows = kWarps, kc = 0, nch = 1, ngroups = 0, stages = 2, ctas_per_sm = 1;
+  uint32_t seg_stride = 0, stage_bytes = 0, x_q = 0, x_d = 0, x_s = 0, ring = 0;
+  size_t smem = 0;
+};
+
+Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t smem_optin) {
   Plan pl;
-  const int gran = gran_elems(kind);
-  int nch = static_cast<int>((k + 1023) / 1024);
-  int kc = static_cast<int>(round_up((k + nch - 1) / nch, gran));
-  if (kc > k) kc = static_cast<int>(k);
-  nch = static_cast<int>((k + kc - 1) / kc);
-  pl.kc = kc;
-  pl.nch = nch;
-  const int R = kWarps * rw;
-  pl.ngroups = static_cast<int>((m + R - 1) / R);
-  pl.seg_stride = static_cast<uint32_t>(round_up(elems_to_bytes(kind, kc) + 32, 16));
-  pl.kcb4 = static_cast<uint32_t>(round_up(kc / 32, 4));
-  const bool need_sum = kind == UGB_Q4_K;
-  uint32_t off = R * pl.seg_stride;
-  pl.xq_off = off;
-  off += nb * kc;
-  pl.xd_off = off;
-  off += nb * pl.kcb4 * 4;
-  pl.xs_off = off;
-  if (need_sum) off += nb * pl.kcb4 * 4;
-  pl.stage_bytes = static_cast<uint32_t>(round_up(off, 128));
-  int stages = static_cast<int>((48 * 1024 + pl.stage_bytes - 1) / pl.stage_bytes);
-  stages = std::max(2, std::min(8, stages));
+  const uint64_t rb = elems_to_bytes(kind, static_cast<uint64_t>(k));
+  const int64_t units = k / 32;
+  // Batch 1, whole rows: the rows kernel with the largest rows-per-warp whose item fits a
+  // stage and whose slots fit the register budget.
+  if (nb == 1 && !dots) {
+    for (int rw : {4, 2, 1}) {
+      const int64_t slots = (rw * units + 31) / 32;
+      if (rb * kWarps * rw <= kItemTarget && slots <= kSlots) {
+        pl.rows_kernel = true;
+        pl.rw = rw;
+        pl.slots = slots <= 2 ? 2 : 4;
+        break;
+      }
+    }
+  }
+  pl.rows = kWarps * pl.rw;
+  if (rb * pl.rows <= kItemTarget) {
+    pl.kc = static_cast<int>(k);
+    pl.nch = 1;
+    pl.stage_bytes = static_cast<uint32_t>(round_up(rb * pl.rows + 32, 128));
+  } else {
+    // K chunks sized so the item's 8 row chunks fill about one stage.
+    const int gran = kind == UGB_Q8_0 ? 128 : 256;  // chunk starts keep x arrays 16B aligned
+    const int nch = static_cast<int>((rb * pl.rows + kItemTarget - 1) / kItemTarget);
+    pl.kc = static_cast<int>(round_up((k + nch - 1) / nch, gran));
+    pl.nch = static_cast<int>((k + pl.kc - 1) / pl.kc);
+    pl.seg_stride = static_cast<uint32_t>(round_up(elems_to_bytes(kind, pl.kc) + 32, 16));
+    pl.stage_bytes = static_cast<uint32_t>(round_up(static_cast<uint64_t>(pl.rows) * pl.seg_stride, 128));
+  }
+  pl.ngroups = static_cast<int>((m + pl.rows - 1) / pl.rows);
+  const size_t nbp = round_up(static_cast<uint64_t>(k / 32), 4);
+  uint32_t off = kBarBytes;
+  pl.x_q = off;
+  off += static_cast<uint32_t>(round_up(static_cast<uint64_t>(nb) * k, 16));
+  pl.x_d = off;
+  off += static_cast<uint32_t>(nb * nbp * 4);
+  pl.x_s = off;
+  if (kind == UGB_Q4_K) off += static_cast<uint32_t>(nb * nbp * 4);
+  pl.ring = static_cast<uint32_t>(round_up(off, 128));
+  // One kernel takes at most about half an SM's shared memory (kSmPerKernel over its resident
+  // CTAs), so the next kernel in the stream can become resident beside it and prefetch its
+  // weights under programmatic dependent launch.
+  pl.ctas_per_sm = pl.ring + 2 * static_cast<size_t>(pl.stage_bytes) <= kSmPerKernel / 2 ? 2 : 1;
+  const size_t budget = std::max<size_t>(kSmPerKernel / pl.ctas_per_sm, pl.ring + 2 * pl.stage_bytes);
+  int stages = static_cast<int>((budget - pl.ring) / pl.stage_bytes);
+  stages = std::max(2, std::min(kMaxStages, stages));
+  while (stages > 2 && pl.ring + static_cast<size_t>(stages) * pl.stage_bytes > smem_optin) --stages;
   pl.stages = stages;
-  pl.smem = kBarBytes + static_cast<size_t>(stages) * pl.stage_bytes;
+  pl.smem = pl.ring + static_cast<size_t>(stages) * pl.stage_bytes;
   return pl;
 }
 
-template <int KIND, int NB, int RW, bool DOTS>
-const void *kernel_ptr() {
-  return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, NB, RW, DOTS>);
+template <int KIND>
+const void *rows_kernel_ptr(int rw, int slots) {
+#define UGB_RK(RW, J) if (rw == RW && slots == J) return reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J>);
+  UGB_RK(1, 2) UGB_RK(1, 4)
+  UGB_RK(2, 2) UGB_RK(2, 4)
+  UGB_RK(4, 2) UGB_RK(4, 4)
+#undef UGB_RK
+  return nullptr;
 }
 
-const void *select_kernel(uint32_t kind, int nb, bool dots) {
-#define UGB_MV_CASE(K)                                                 \
-  if (kind == K) {                                                     \
-    if (dots) return kernel_ptr<K, 1, 1, true>();                      \
-    switch (nb) {                                                      \
-      case 1: return kernel_ptr<K, 1, 1, false>();                     \
-      case 2: return kernel_ptr<K, 2, 1, false>();                     \
-      case 4: return kernel_ptr<K, 4, 1, false>();                     \
-      case 8: return kernel_ptr<K, 8, 1, false>();                     \
-      default: return nullptr;                                         \
-    }                                                                  \
+template <int KIND>
+const void *stream_kernel_ptr(int nb, bool dots) {
+  if (dots) return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, true>);
+  switch (nb) {
+    case 1: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, false>);
+    case 2: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 2, false>);
+    case 4: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 4, false>);
+    case 8: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 8, false>);
+    default: return nullptr;
   }
-  UGB_MV_CASE(UGB_Q8_0)
-  UGB_MV_CASE(UGB_Q4_K)
-  UGB_MV_CASE(UGB_Q3_K)
-#undef UGB_MV_CASE
-  return nullptr;
+}
+
+const void *select_kernel(uint32_t kind, const Plan &pl, int nb, bool dots) {
+  switch (kind) {
+    case UGB_Q8_0: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q8_0>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q8_0>(nb, dots);
+    case UGB_Q4_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q4_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q4_K>(nb, dots);
+    case UGB_Q3_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q3_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q3_K>(nb, dots);
+    default: return nullptr;
+  }
+}
+
+ugb_status allow_smem(const void *f, size_t bytes) {
+  return cuda_status(cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
 }
 
 }  // namespace
 
 ugb_status init_matvec_kernels(ugb_ctx *ctx) {
   for (uint32_t kind : {UGB_Q8_0, UGB_Q4_K, UGB_Q3_K}) {
-    for (int nb : {1, 2, 4, 8}) {
-      const void *f = select_kernel(kind, nb, false);
-      if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(ctx->smem_optin)) != cudaSuccess)
-        return UGB_EBACKEND;
-    }
-    const void *f = select_kernel(kind, 1, true);
-    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(ctx->smem_optin)) != cudaSuccess)
-      return UGB_EBACKEND;
+    Plan pl;
+    for (int rw : {1, 2, 4})
+      for (int j : {2, 4}) {
+        pl.rows_kernel = true;
+        pl.rw = rw;
+        pl.slots = j;
+        if (allow_smem(select_kernel(kind, pl, 1, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+      }
+    pl.rows_kernel = false;
+    for (int nb : {1, 2, 4, 8})
+      if (allow_smem(select_kernel(kind, pl, nb, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+    if (allow_smem(select_kernel(kind, pl, 1, true), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
   }
   return UGB_OK;
 }
 
 ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a) {
   const bool dots = a.dots != nullptr;
-  // A batch that is not 1, 2, 4 or 8 runs as several launches of those sizes (largest
-  // first), each streaming the weights once.
+  // A batch runs as launches of 8, 4, 2 or 1 vectors (largest first) whose staged
+  // activations fit kXBudget; each launch streams the weights once.
   int64_t done = 0;
   while (done < a.batch) {
     const int64_t rest = a.batch - done;
-    const int nb = dots ? 1 : (rest >= 8 ? 8 : rest >= 4 ? 4 : rest >= 2 ? 2 : 1);
-    const Plan pl = make_plan(a.kind, a.k, a.m, nb, 1);
+    int nb = dots ? 1 : (rest >= 8 ? 8 : rest >= 4 ? 4 : rest >= 2 ? 2 : 1);
+    while (nb > 1 && x_bytes(a.kind, a.k, nb) > kXBudget) nb /= 2;
+    const Plan pl = make_plan(a.kind, a.k, a.m, nb, dots, ctx->smem_optin);
     if (pl.smem > ctx->smem_optin) return UGB_ESHAPE;
-    const void *f = select_kernel(a.kind, nb, dots);
+    const void *f = select_kernel(a.kind, pl, nb, dots);
     if (!f) return UGB_EQUANT;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, kThreads, pl.smem) != cudaSuccess ||
         per_sm < 1)
       return UGB_EBACKEND;
+    per_sm = std::min(per_sm, pl.ctas_per_sm);
     MvParams p{};
     p.w = a.w;
-    p.w_end = a.w + a.m * a.row_bytes;
-    p.w_end16 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(p.w_end) & ~uintptr_t(15));
+    p.w_end16 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(a.w + a.m * a.row_bytes) & ~uintptr_t(15));
     p.row_bytes = static_cast<uint64_t>(a.row_bytes);
     p.k = static_cast<int>(a.k);
     p.m = static_cast<int>(a.m);
-    p.batch = nb;
+    p.rows = pl.rows;
     p.kc = pl.kc;
     p.nch = pl.nch;
     p.ngroups = pl.ngroups;
     p.seg_stride = pl.seg_stride;
     p.stage_bytes = pl.stage_bytes;
-    p.xq_off = pl.xq_off;
-    p.xd_off = pl.xd_off;
-    p.xs_off = pl.xs_off;
-    p.kcb4 = pl.kcb4;
     p.stages = pl.stages;
+    p.x_q = pl.x_q;
+    p.x_d = pl.x_d;
+    p.x_s = pl.x_s;
+    p.ring = pl.ring;
     p.xq = a.xq + done * a.xl.k;
     p.xd = reinterpret_cast<const float *>(a.xq + a.xl.d_off) + done * a.xl.nbp;
     p.xs = reinterpret_cast<const int *>(a.xq + a.xl.s_off) + done * a.xl.nbp;
-    p.xq_stride = a.xl.k;
-    p.xds_stride = a.xl.nbp;
+    p.nbp = static_cast<int>(a.xl.nbp);
     p.y = a.y ? a.y + done * a.ldy : nullptr;
     p.ldy = a.ldy;
     p.dots = a.dots;
-    p.dots_ld = a.k / 32;
     p.status = ctx->status;
     const int grid = static_cast<int>(std::min<int64_t>(pl.ngroups, static_cast<int64_t>(ctx->sm_count) * per_sm));
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(kThreads);  // 8 consumer warps + 1 producer warp
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];

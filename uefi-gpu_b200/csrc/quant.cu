@@ -16,8 +16,10 @@ __global__ void __launch_bounds__(256) quant_q8_1_kernel(const float *__restrict
                                                           uint8_t *__restrict__ xq, int64_t k,
                                                           int64_t batch, int nbp, size_t d_off,
                                                           size_t s_off, uint32_t *status) {
-  grid_dep_wait();
+  // Let the consumer launch (and prefetch its weights) now; it waits for this grid to finish
+  // before it reads the quantised activation.
   grid_dep_launch();
+  grid_dep_wait();
   const int lane = threadIdx.x & 31;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
   if (gw >= batch * nbp) return;
