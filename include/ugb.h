@@ -123,6 +123,17 @@ ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
                       int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k, int64_t m,
                       int64_t batch);
 
+/* Several matrices of the same kind and row length that share one activation, in one
+ * launch: y_dev[v] = [W_0 x_v ; W_1 x_v ; ...] (rows concatenated in order), count <= 4.
+ * w_devs (host array) holds the count device pointers, rows the count row counts.
+ * Replaces qkv_dp4a / gateup_dp4a (gpu_dp4a.cu:53-64, the fused Q/K/V and gate/up launches
+ * over separate GGUF tensors) and Gpu::batch (llm.rs:226-245, up to 3 tensors sharing one
+ * input).  Results are bit-identical to one ugb_matvec per matrix. */
+ugb_status ugb_matvec_multi(ugb_ctx *ctx, ugb_stream stream, uint32_t kind,
+                            const void *const *w_devs, const int64_t *rows, int count,
+                            int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k,
+                            int64_t batch);
+
 /* Debug / parity view of the same kernel: out_dev[r][b] = the int32 block dot of row r and
  * 32-block b with activation vector 0, no scaling (the integer the reference's CPU check
  * forms, gpu_prefill.rs:111-115).  Used to prove the integer parts bit-exact. */
@@ -154,6 +165,78 @@ ugb_status ugb_graph_begin(ugb_ctx *ctx, ugb_stream stream);
 ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out);
 ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream);
 ugb_status ugb_graph_destroy(ugb_graph *graph);
+
+/* ---- decoder (the per-token graph around the matvecs) ------------------------------------ */
+
+/* Shape of a Qwen2-style decoder (configs 2 and 4).  The reference hard-codes the 1.5B shape
+ * (llm.rs:314-321: DIM 1536, HIDDEN 8960, KV 256, HEAD 128, LAYERS 28). */
+typedef struct ugb_decoder_config {
+  int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, n_ctx;
+  float rope_theta, norm_eps;
+  uint32_t kind;      /* quant kind of the layer matrices: UGB_Q8_0, UGB_Q4_K or UGB_Q3_K */
+  uint32_t head_kind; /* quant kind of the output head */
+} ugb_decoder_config;
+
+/* Device pointers of one layer's GGUF tensors (blk.N.*): matrices in their GGUF block layout
+ * with row length n_embd (w_down: n_ff; wo: n_head*head_dim), norms f32, biases f32 or NULL. */
+typedef struct ugb_layer_weights {
+  const void *attn_norm, *wq, *wk, *wv, *bq, *bk, *bv, *wo;
+  const void *ffn_norm, *w_gate, *w_up, *w_down;
+} ugb_layer_weights;
+
+typedef struct ugb_model_weights {
+  const void *tok_embd;            /* Q8_0 [n_vocab][n_embd] (token_embd.weight) */
+  const void *output_norm;         /* f32 [n_embd] */
+  const void *output;              /* head_kind [n_vocab][n_embd]; tok_embd when tied */
+  const ugb_layer_weights *layers; /* host array of n_layer entries */
+} ugb_model_weights;
+
+typedef struct ugb_decoder ugb_decoder;
+
+/* Allocate the decoder's device state: fp32 KV cache (n_layer x n_head_kv x n_ctx x
+ * head_dim, for K and V; the reference keeps its cache in fp32 too, gpu_attention.cu:1),
+ * activations, RoPE table (f32 angle pos * powf(theta, -2i/head_dim), gpu_graph.rs:132),
+ * attention partials and the token state.  Replaces the reference's VRAM arenas and graph
+ * build (gpu_graph.rs:81-169).  head_dim must be 128; n_head a multiple of n_head_kv with
+ * at most 8 query heads per KV head. */
+ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config *cfg, ugb_decoder **out);
+ugb_status ugb_decoder_destroy(ugb_decoder *dec);
+
+/* Use the given weights (device memory, caller-owned, must outlive the decoder). */
+ugb_status ugb_decoder_bind(ugb_decoder *dec, const ugb_model_weights *w);
+
+/* Allocate and bind seeded synthetic weights owned by the decoder (see ugb_fill_synthetic;
+ * norms 1 +- 0.1, biases N(0, 0.02^2) approximately; tied head). */
+ugb_status ugb_decoder_synthetic(ugb_decoder *dec, uint64_t seed);
+
+/* Enqueue one token step on `stream`: embedding of the current token, every layer, the
+ * head and greedy selection.  The token comes from the previous step's greedy choice when
+ * there is one (the position then advances), else from ugb_decoder_set_state, so replaying a
+ * captured step decodes autoregressively on the device. */
+ugb_status ugb_decoder_step(ugb_decoder *dec, ugb_stream stream);
+
+/* Set the token and position the next step starts from (asynchronous host-to-device copy). */
+ugb_status ugb_decoder_set_state(ugb_decoder *dec, ugb_stream stream, int32_t token, int32_t pos);
+
+/* Synchronous: the token, position and greedy choice of the last step. */
+ugb_status ugb_decoder_get_state(ugb_decoder *dec, ugb_stream stream, int32_t *token,
+                                 int32_t *pos, int32_t *next_token);
+
+/* Synchronous copy of the last step's logits (n_vocab floats) to host memory. */
+ugb_status ugb_decoder_logits(ugb_decoder *dec, ugb_stream stream, float *logits_host);
+
+/* Synchronous copy of `count` cached positions starting at `pos` of one layer's rotated keys
+ * and values to host memory, each laid out [n_head_kv][count][head_dim].  No counterpart in
+ * the reference, whose host reads its KV cache at fixed device addresses (llm.rs:319-320);
+ * here it serves inspection and checkpointing of a sequence. */
+ugb_status ugb_decoder_read_kv(ugb_decoder *dec, ugb_stream stream, int32_t layer, int32_t pos,
+                               int32_t count, float *k_host, float *v_host);
+
+/* One token end to end, as the reference's forward() (llm.rs:339-388 / forward_gpu
+ * gpu_graph.rs:170-197): host token and position in, greedy next token out.  Replays a CUDA
+ * graph of the step (captured on first use) and checks the status word. */
+ugb_status ugb_decoder_token(ugb_decoder *dec, ugb_stream stream, int32_t token, int32_t pos,
+                             int32_t *next_token);
 
 /* ---- host-buffer entry points (synchronous) --------------------------------------------- */
 

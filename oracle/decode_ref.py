@@ -1,0 +1,122 @@
+"""CPU restatement of one decode token step of a Qwen2-style model.
+
+TEST INFRASTRUCTURE ONLY: the checker for the decoder's GPU token step (tests/, the smoke check)
+and the timed CPU leg of bench.py.  The product path never imports it.
+
+It follows the reference's CPU forward (driver/src/llm.rs:339-388) with the numerics of the
+reference's GPU decode graph (driver/src/gpu_graph.rs:139-162):
+  * every linear layer takes a block-32 Q8_1 activation (quant_act, driver/kernels/gpu_dp4a.cu:23-31)
+    and multiplies it by the weight's integer block dots (the C oracle's orc_matvec);
+  * RMSNorm y = x * (1 / sqrt(sum(x^2)/n + eps)) * w (llm.rs:323-327);
+  * Q/K/V biases added before RoPE; RoPE over the pairs (i, i + HD/2) with the table built from
+    the f32 angle pos * powf(theta, -(2i)/HD) (gpu_graph.rs:132, llm.rs:328-337);
+  * fp32 KV cache, scores q.k / sqrt(HD), exact exp softmax (gpu_attention.cu:1-26);
+  * SiLU(gate) * up (llm.rs:374), residual adds, final norm, head, first-maximum greedy
+    (llm.rs:383-385).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import pyoracle as po
+
+Q8_0 = po.Q8_0
+
+
+def rope_table(n_ctx: int, head_dim: int, theta: float) -> np.ndarray:
+    """[n_ctx][head_dim/2][2] (cos, sin) as float32 (gpu_graph.rs:132)."""
+    i = np.arange(head_dim // 2)
+    e = (-(2 * i).astype(np.float32) / np.float32(head_dim)).astype(np.float32)
+    f = np.power(np.float64(np.float32(theta)), e.astype(np.float64)).astype(np.float32)
+    ang = (np.arange(n_ctx, dtype=np.float32)[:, None] * f[None, :]).astype(np.float32)
+    a64 = ang.astype(np.float64)
+    return np.stack([np.cos(a64), np.sin(a64)], axis=-1).astype(np.float32)
+
+
+class RefDecoder:
+    """One sequence of decode steps on the CPU.
+
+    cfg: dict with the fields of ugb_decoder_config.  weights: dict with tok_embd (Q8_0 bytes),
+    output_norm (f32), output (head_kind bytes) and layers, a list of dicts with attn_norm,
+    ffn_norm, bq, bk, bv (f32, biases may be None) and wq, wk, wv, wo, w_gate, w_up, w_down
+    (raw GGUF row bytes of cfg["kind"])."""
+
+    def __init__(self, cfg: dict, weights: dict, mt: bool = False):
+        self.c = dict(cfg)
+        self.w = weights
+        self.mt = mt
+        c = self.c
+        self.hd = c["head_dim"]
+        self.kcache = np.zeros((c["n_layer"], c["n_head_kv"], c["n_ctx"], self.hd), np.float32)
+        self.vcache = np.zeros_like(self.kcache)
+        self.rope = rope_table(c["n_ctx"], self.hd, c["rope_theta"])
+
+    # ---- pieces ---------------------------------------------------------------------------
+
+    def linear(self, kind: int, w: np.ndarray, x: np.ndarray, m: int) -> np.ndarray:
+        k = x.size
+        q, d, s, _ = po.quant_act(x.reshape(1, k))
+        return po.matvec(kind, w, po.row_bytes(kind, k), q, d, s, k, m, 1, mt=self.mt)[0]
+
+    def norm(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
+        n = x.size
+        ss = np.float32(np.sum(x * x, dtype=np.float32))
+        scale = np.float32(1.0) / np.sqrt(ss / np.float32(n) + np.float32(self.c["norm_eps"]))
+        return (x * scale * w).astype(np.float32)
+
+    def rotate(self, v: np.ndarray, pos: int) -> np.ndarray:
+        """v [heads, HD] -> rotated copy."""
+        h2 = self.hd // 2
+        cs, sn = self.rope[pos, :, 0], self.rope[pos, :, 1]
+        v0, v1 = v[:, :h2], v[:, h2:]
+        return np.concatenate([v0 * cs - v1 * sn, v0 * sn + v1 * cs], axis=1).astype(np.float32)
+
+    def embed(self, token: int) -> np.ndarray:
+        n = self.c["n_embd"]
+        rb = po.row_bytes(Q8_0, n)
+        return po.dequantize(Q8_0, self.w["tok_embd"][token * rb:(token + 1) * rb], n)
+
+    # ---- one token -----------------------------------------------------------------------
+
+    def step(self, token: int, pos: int):
+        """Returns (logits f32 [n_vocab], greedy next token)."""
+        c, hd = self.c, self.hd
+        kind = c["kind"]
+        nh, nkv = c["n_head"], c["n_head_kv"]
+        group = nh // nkv
+        qrows, kvrows = nh * hd, nkv * hd
+        x = self.embed(token)
+        inv_sqrt = np.float32(1.0) / np.sqrt(np.float32(hd))
+        for li, L in enumerate(self.w["layers"]):
+            xn = self.norm(x, L["attn_norm"])
+            q = self.linear(kind, L["wq"], xn, qrows)
+            k = self.linear(kind, L["wk"], xn, kvrows)
+            v = self.linear(kind, L["wv"], xn, kvrows)
+            if L.get("bq") is not None:
+                q = q + L["bq"]
+            if L.get("bk") is not None:
+                k = k + L["bk"]
+            if L.get("bv") is not None:
+                v = v + L["bv"]
+            q = self.rotate(q.reshape(nh, hd), pos)
+            k = self.rotate(k.reshape(nkv, hd), pos)
+            self.kcache[li, :, pos] = k
+            self.vcache[li, :, pos] = v.reshape(nkv, hd)
+            att = np.empty((nh, hd), np.float32)
+            for h in range(nh):
+                kvh = h // group
+                keys = self.kcache[li, kvh, :pos + 1]
+                vals = self.vcache[li, kvh, :pos + 1]
+                sc = (keys @ q[h]).astype(np.float32) * inv_sqrt
+                e = np.exp(sc - sc.max()).astype(np.float32)
+                att[h] = (e @ vals).astype(np.float32) / np.float32(e.sum(dtype=np.float32))
+            x = (x + self.linear(kind, L["wo"], att.reshape(-1), c["n_embd"])).astype(np.float32)
+            xn = self.norm(x, L["ffn_norm"])
+            g = self.linear(kind, L["w_gate"], xn, c["n_ff"])
+            u = self.linear(kind, L["w_up"], xn, c["n_ff"])
+            with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g gives -0, as expf
+                h_act = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+            x = (x + self.linear(kind, L["w_down"], h_act, c["n_embd"])).astype(np.float32)
+        xn = self.norm(x, self.w["output_norm"])
+        logits = self.linear(c["head_kind"], self.w["output"], xn, c["n_vocab"])
+        return logits, int(np.argmax(logits))

@@ -97,7 +97,8 @@ SHAPES = [
     (Q8_0, 32768, 21),     # rows longer than a pipeline stage: K split into 12 chunks
     (Q4_K, 24576, 9),      # K-chunked, ragged row group
     (Q3_K, 65536, 5),      # K-chunked Q3_K at UGB_MAX_K
-    (Q8_0, 3584, 100),     # 7B output-head row length: two K chunks
+    (Q8_0, 3584, 100),     # 7B output-head row length
+    (Q8_0, 8960, 37),      # rows spread over all lanes, two per item, ragged last item
 ]
 
 
@@ -208,3 +209,32 @@ def test_shape_and_alignment_errors(ctx, ugb):
     assert lib.ugb_matvec(ctx.handle, s, Q8_0, w.data_ptr() + 2, rb, xq.data_ptr(), y.data_ptr(), k, m, 1) == ugb.EALIGN
     assert lib.ugb_matvec(ctx.handle, s, Q8_0, w.data_ptr(), rb, xq.data_ptr(), y.data_ptr(), k, m, 9) == ugb.ESHAPE
     assert lib.ugb_matvec(ctx.handle, s, Q8_0, w.data_ptr(), rb, xq.data_ptr(), y.data_ptr(), 48, m, 1) == ugb.ESHAPE
+
+
+@pytest.mark.parametrize("kind,k,rows,batch", [
+    (Q8_0, 1536, (1536, 256, 256), 1),   # fused Q/K/V of the 1.5B model (qkv_dp4a)
+    (Q8_0, 1536, (8960, 8960), 1),       # fused gate/up (gateup_dp4a)
+    (Q8_0, 1536, (100, 37, 5), 3),       # matrices that do not hold whole items: split launches
+    (Q4_K, 3584, (3584, 512, 512), 2),   # 7B Q/K/V
+    (Q8_0, 8960, (64, 48), 1),           # long rows, two rows per item
+])
+def test_matvec_multi_equals_separate(ctx, ugb, kind, k, rows, batch):
+    """ugb_matvec_multi == one ugb_matvec per matrix, bit for bit (Gpu::batch semantics)."""
+    torch = _torch()
+    ws = []
+    for i, m in enumerate(rows):
+        w, rb = make_weights(ctx, ugb, kind, k, m, seed=100 + i)
+        ws.append(w)
+    x = np.random.default_rng(7).standard_normal((batch, k)).astype(np.float32)
+    xq = quantize(ctx, ugb, x)
+    total = sum(rows)
+    y = torch.full((batch, total), float("nan"), dtype=torch.float32, device="cuda")
+    ctx.matvec_multi(kind, ws, rows, rb, xq, y, k, batch)
+    parts = []
+    for w, m in zip(ws, rows):
+        yi = torch.empty((batch, m), dtype=torch.float32, device="cuda")
+        ctx.matvec(kind, w, rb, xq, yi, k, m, batch)
+        parts.append(yi)
+    want = torch.cat(parts, dim=1).cpu().numpy()
+    assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    assert ctx.status_read()[0] == ugb.OK

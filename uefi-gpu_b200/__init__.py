@@ -23,6 +23,8 @@ MAX_BATCH = 8
 STATUS = {0: "ok", 1: "shape", 2: "non-finite", 3: "timeout", 4: "backend", 5: "alignment",
           6: "quant kind", 7: "context"}
 OK, ESHAPE, ENONFINITE, ETIMEOUT, EBACKEND, EALIGN, EQUANT, ECONTEXT = range(8)
+# Device status bits (ugb_status_read).
+STATUS_NONFINITE_IN, STATUS_NONFINITE_OUT, STATUS_TIMEOUT, STATUS_BADARG = 1, 2, 4, 8
 
 # Every symbol include/ugb.h declares, with (restype, argtypes).
 _vp = ctypes.c_void_p
@@ -41,10 +43,24 @@ SIGNATURES = {
     "ugb_q8act_sum_offset": (ctypes.c_size_t, [_i64, _i64]),
     "ugb_quant_q8_1": (_int, [_vp, _vp, _vp, _vp, _i64, _i64]),
     "ugb_matvec": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64, _i64]),
+    "ugb_matvec_multi": (_int, [_vp, _vp, _u32, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _int,
+                                _i64, _vp, _vp, _i64, _i64]),
     "ugb_block_dots": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_fill_synthetic": (_int, [_vp, _vp, _u32, _vp, _i64, _i64, _u64]),
     "ugb_linear": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_set_pdl": (_int, [_vp, _int]),
+    "ugb_decoder_create": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
+    "ugb_decoder_destroy": (_int, [_vp]),
+    "ugb_decoder_bind": (_int, [_vp, _vp]),
+    "ugb_decoder_synthetic": (_int, [_vp, _u64]),
+    "ugb_decoder_step": (_int, [_vp, _vp]),
+    "ugb_decoder_set_state": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32]),
+    "ugb_decoder_get_state": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int32),
+                                     ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
+    "ugb_decoder_logits": (_int, [_vp, _vp, _vp]),
+    "ugb_decoder_read_kv": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp, _vp]),
+    "ugb_decoder_token": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32,
+                                 ctypes.POINTER(ctypes.c_int32)]),
     "ugb_graph_begin": (_int, [_vp, _vp]),
     "ugb_graph_end": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
     "ugb_graph_launch": (_int, [_vp, _vp]),
@@ -143,6 +159,14 @@ class Context:
         check("ugb_matvec", lib().ugb_matvec(self.handle, _stream(stream), kind, _ptr(w), rb,
                                                _ptr(xq), _ptr(y), k, m, batch))
 
+    def matvec_multi(self, kind: int, ws, rows, rb: int, xq, y, k: int, batch: int = 1,
+                     stream=None) -> None:
+        n = len(ws)
+        wp = (_vp * n)(*[_ptr(w) for w in ws])
+        rp = (_i64 * n)(*rows)
+        check("ugb_matvec_multi", lib().ugb_matvec_multi(self.handle, _stream(stream), kind, wp, rp,
+                                                           n, rb, _ptr(xq), _ptr(y), k, batch))
+
     def block_dots(self, kind: int, w, rb: int, xq, out, k: int, m: int, stream=None) -> None:
         check("ugb_block_dots", lib().ugb_block_dots(self.handle, _stream(stream), kind, _ptr(w),
                                                        rb, _ptr(xq), _ptr(out), k, m))
@@ -178,6 +202,105 @@ class Context:
                                 x.ctypes.data, y.ctypes.data, k, m)
         check("ugb_linear", code)
         return y
+
+
+class DecoderConfig(ctypes.Structure):
+    """ugb_decoder_config."""
+    _fields_ = [("n_layer", ctypes.c_int32), ("n_embd", ctypes.c_int32), ("n_ff", ctypes.c_int32),
+                ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32),
+                ("head_dim", ctypes.c_int32), ("n_vocab", ctypes.c_int32), ("n_ctx", ctypes.c_int32),
+                ("rope_theta", ctypes.c_float), ("norm_eps", ctypes.c_float),
+                ("kind", ctypes.c_uint32), ("head_kind", ctypes.c_uint32)]
+
+
+class LayerWeights(ctypes.Structure):
+    """ugb_layer_weights (device pointers)."""
+    _fields_ = [(n, _vp) for n in ("attn_norm", "wq", "wk", "wv", "bq", "bk", "bv", "wo",
+                                   "ffn_norm", "w_gate", "w_up", "w_down")]
+
+
+class ModelWeights(ctypes.Structure):
+    """ugb_model_weights."""
+    _fields_ = [("tok_embd", _vp), ("output_norm", _vp), ("output", _vp),
+                ("layers", ctypes.POINTER(LayerWeights))]
+
+
+QWEN25_15B = dict(n_layer=28, n_embd=1536, n_ff=8960, n_head=12, n_head_kv=2, head_dim=128,
+                  n_vocab=151936, n_ctx=512, rope_theta=1e6, norm_eps=1e-6, kind=8, head_kind=8)
+
+
+class Decoder:
+    """ugb_decoder: the per-token decode graph around the quantised matvecs."""
+
+    def __init__(self, ctx: "Context", **cfg):
+        self.ctx = ctx
+        self.cfg = DecoderConfig(**cfg)
+        h = _vp()
+        check("ugb_decoder_create", lib().ugb_decoder_create(ctx.handle, ctypes.byref(self.cfg),
+                                                               ctypes.byref(h)))
+        self.handle = h
+        self._keep = None
+
+    def close(self) -> None:
+        if self.handle:
+            lib().ugb_decoder_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def synthetic(self, seed: int) -> None:
+        check("ugb_decoder_synthetic", lib().ugb_decoder_synthetic(self.handle, seed))
+
+    def bind(self, tok_embd, output_norm, output, layers) -> None:
+        """layers: list of dicts of torch tensors keyed like LayerWeights (None = absent)."""
+        arr = (LayerWeights * len(layers))()
+        for i, L in enumerate(layers):
+            for name, _ in LayerWeights._fields_:
+                t = L.get(name)
+                setattr(arr[i], name, t.data_ptr() if t is not None else None)
+        w = ModelWeights(tok_embd.data_ptr(), output_norm.data_ptr(), output.data_ptr(), arr)
+        self._keep = (arr, w, tok_embd, output_norm, output, layers)
+        check("ugb_decoder_bind", lib().ugb_decoder_bind(self.handle, ctypes.byref(w)))
+
+    def step(self, stream=None) -> None:
+        check("ugb_decoder_step", lib().ugb_decoder_step(self.handle, _stream(stream)))
+
+    def set_state(self, token: int, pos: int, stream=None) -> None:
+        check("ugb_decoder_set_state", lib().ugb_decoder_set_state(self.handle, _stream(stream),
+                                                                     token, pos))
+
+    def get_state(self, stream=None):
+        t, p, n = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        check("ugb_decoder_get_state", lib().ugb_decoder_get_state(
+            self.handle, _stream(stream), ctypes.byref(t), ctypes.byref(p), ctypes.byref(n)))
+        return t.value, p.value, n.value
+
+    def logits(self, stream=None):
+        import numpy as np
+        out = np.empty(self.cfg.n_vocab, dtype=np.float32)
+        check("ugb_decoder_logits", lib().ugb_decoder_logits(self.handle, _stream(stream),
+                                                               out.ctypes.data))
+        return out
+
+    def read_kv(self, layer: int, pos: int, count: int = 1, stream=None):
+        """(keys, values), each float32 [n_head_kv, count, head_dim] (rotated keys)."""
+        import numpy as np
+        shape = (self.cfg.n_head_kv, count, self.cfg.head_dim)
+        k = np.empty(shape, dtype=np.float32)
+        v = np.empty(shape, dtype=np.float32)
+        check("ugb_decoder_read_kv", lib().ugb_decoder_read_kv(self.handle, _stream(stream), layer, pos,
+                                                                 count, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def token(self, token: int, pos: int, stream=None) -> int:
+        nxt = ctypes.c_int32()
+        check("ugb_decoder_token", lib().ugb_decoder_token(self.handle, _stream(stream), token, pos,
+                                                             ctypes.byref(nxt)))
+        return nxt.value
 
 
 class Graph:

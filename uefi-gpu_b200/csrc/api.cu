@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "internal.hpp"
+#include "decode.hpp"
 
 namespace ugb {
 
@@ -94,7 +95,8 @@ ugb_status ugb_init(int device, ugb_ctx **out) {
     ugb_destroy(ctx);
     return UGB_EBACKEND;
   }
-  const ugb_status st = init_matvec_kernels(ctx);
+  ugb_status st = init_matvec_kernels(ctx);
+  if (st == UGB_OK) st = init_decode_kernels(ctx);
   if (st != UGB_OK) {
     ugb_destroy(ctx);
     return st;
@@ -196,6 +198,40 @@ ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
   a.xl = q8act_layout(k, batch);
   a.y = y_dev;
   a.ldy = m;
+  a.batch = batch;
+  a.pdl = ctx->pdl;
+  return launch_matvec(ctx, stream, a);
+}
+
+ugb_status ugb_matvec_multi(ugb_ctx *ctx, ugb_stream stream, uint32_t kind,
+                            const void *const *w_devs, const int64_t *rows, int count,
+                            int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k,
+                            int64_t batch) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  if (!w_devs || !rows || count < 1 || count > 4) return UGB_ESHAPE;
+  if (batch <= 0 || batch > UGB_MAX_BATCH) return UGB_ESHAPE;
+  if (!aligned16(xq_dev) || !y_dev || (reinterpret_cast<uintptr_t>(y_dev) & 3)) return UGB_EALIGN;
+  MatvecArgs a;
+  int64_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    st = check_weights(kind, w_devs[i], row_bytes, k, rows[i]);
+    if (st != UGB_OK) return st;
+    a.ws[i] = static_cast<const uint8_t *>(w_devs[i]);
+    a.seg_rows[i] = rows[i];
+    total += rows[i];
+  }
+  if (total > (int64_t{1} << 31) - 64) return UGB_ESHAPE;
+  a.nseg = count;
+  a.kind = kind;
+  a.w = a.ws[0];
+  a.row_bytes = row_bytes;
+  a.k = k;
+  a.m = total;
+  a.xq = static_cast<const uint8_t *>(xq_dev);
+  a.xl = q8act_layout(k, batch);
+  a.y = y_dev;
+  a.ldy = total;
   a.batch = batch;
   a.pdl = ctx->pdl;
   return launch_matvec(ctx, stream, a);

@@ -1,0 +1,455 @@
+// decoder.cu -- the decoder object behind ugb_decoder_*: device state, weight binding and
+// the per-token launch sequence (captured once as a CUDA graph for ugb_decoder_token).
+//
+// One token step (reference: gpu_graph.rs:139-162, llm.rs:339-388):
+//   embed -> per layer { rmsnorm+quant -> Q/K/V matvec (one launch over the three tensors)
+//   -> attention (bias, RoPE, fp16 KV write, flash-decoding, combine + quant) -> O matvec ->
+//   residual+rmsnorm+quant -> gate/up matvec (one launch) -> SiLU*up+quant -> down matvec }
+//   -> residual+rmsnorm+quant -> head matvec -> greedy.
+// Every kernel after the first launches with programmatic dependent launch, so each matvec
+// streams its first weight stages while the preceding kernel finishes.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <new>
+#include <random>
+#include <vector>
+
+#include "common.cuh"
+#include "decode.hpp"
+
+struct ugb_decoder {
+  ugb_ctx *ctx = nullptr;
+  ugb_decoder_config cfg{};
+  // device state
+  float *x = nullptr, *dx = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
+  uint8_t *xq = nullptr, *attq = nullptr, *hq = nullptr;
+  float *kcache = nullptr, *vcache = nullptr;
+  float2 *rope = nullptr;
+  float *part_m = nullptr, *part_l = nullptr, *part_o = nullptr;
+  int32_t *state = nullptr;      // [0] token [1] pos [2..3] greedy key
+  int32_t *state_host = nullptr; // pinned mirror
+  int n_split = 0;
+  // weights
+  ugb_model_weights w{};
+  std::vector<ugb_layer_weights> layers;
+  float *bias = nullptr;         // per layer [q;k;v] fused biases (bound when any bias is given)
+  std::vector<void *> owned;     // synthetic weights owned by the decoder
+  // replay
+  cudaStream_t cap = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+};
+
+namespace ugb {
+namespace {
+
+template <typename T>
+ugb_status dalloc(T **p, size_t count) {
+  return cuda_status(cudaMalloc(reinterpret_cast<void **>(p), count * sizeof(T)));
+}
+
+ugb_status check_config(const ugb_ctx *ctx, const ugb_decoder_config &c) {
+  if (c.n_layer < 1 || c.n_embd < 32 || c.n_embd % 32 || c.n_ff < 32 || c.n_ff % 32 ||
+      c.n_head < 1 || c.n_head_kv < 1 || c.n_head % c.n_head_kv || c.n_head / c.n_head_kv > 8 ||
+      c.head_dim != kHeadDim || c.n_vocab < 1 || c.n_ctx < 1 || c.n_ctx > 32768 ||
+      !(c.norm_eps > 0.f) || !(c.rope_theta > 0.f))
+    return UGB_ESHAPE;
+  for (uint32_t k : {c.kind, c.head_kind})
+    if (k != UGB_Q8_0 && k != UGB_Q4_K && k != UGB_Q3_K) return UGB_EQUANT;
+  if (ugb_row_bytes(c.kind, c.n_embd) < 0 || ugb_row_bytes(c.kind, c.n_ff) < 0 ||
+      ugb_row_bytes(c.kind, static_cast<int64_t>(c.n_head) * c.head_dim) < 0 ||
+      ugb_row_bytes(c.head_kind, c.n_embd) < 0)
+    return UGB_ESHAPE;
+  if (attn_partial_smem(c.n_head / c.n_head_kv) > ctx->smem_optin) return UGB_ESHAPE;
+  return UGB_OK;
+}
+
+void free_all(ugb_decoder *d) {
+  void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->xq, d->attq, d->hq, d->kcache,
+                  d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->state, d->bias};
+  for (void *b : bufs)
+    if (b) cudaFree(b);
+  for (void *b : d->owned) cudaFree(b);
+  if (d->state_host) cudaFreeHost(d->state_host);
+  if (d->exec) cudaGraphExecDestroy(d->exec);
+  if (d->graph) cudaGraphDestroy(d->graph);
+  if (d->cap) cudaStreamDestroy(d->cap);
+}
+
+}  // namespace
+}  // namespace ugb
+
+using namespace ugb;
+
+extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config *cfg, ugb_decoder **out) {
+  if (!ctx || !cfg || !out) return UGB_ECONTEXT;
+  *out = nullptr;
+  ugb_status st = check_config(ctx, *cfg);
+  if (st != UGB_OK) return st;
+  if (cudaSetDevice(ctx->device) != cudaSuccess) return UGB_EBACKEND;
+  ugb_decoder *d = new (std::nothrow) ugb_decoder();
+  if (!d) return UGB_EBACKEND;
+  d->ctx = ctx;
+  d->cfg = *cfg;
+  const ugb_decoder_config &c = *cfg;
+  const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
+  const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
+  const int group = c.n_head / c.n_head_kv;
+  d->n_split = (c.n_ctx + kAttnChunk - 1) / kAttnChunk;
+  const size_t kv = static_cast<size_t>(c.n_layer) * kvrows * c.n_ctx;
+  const int64_t act = std::max<int64_t>(c.n_embd, qrows);
+  bool ok = dalloc(&d->x, c.n_embd) == UGB_OK && dalloc(&d->dx, c.n_embd) == UGB_OK &&
+            dalloc(&d->qkv, qrows + 2 * kvrows) == UGB_OK && dalloc(&d->gu, 2 * static_cast<size_t>(c.n_ff)) == UGB_OK &&
+            dalloc(&d->logits, c.n_vocab) == UGB_OK &&
+            dalloc(&d->xq, q8act_layout(act, 1).bytes) == UGB_OK &&
+            dalloc(&d->attq, q8act_layout(qrows, 1).bytes) == UGB_OK &&
+            dalloc(&d->hq, q8act_layout(c.n_ff, 1).bytes) == UGB_OK &&
+            dalloc(&d->kcache, kv) == UGB_OK && dalloc(&d->vcache, kv) == UGB_OK &&
+            dalloc(&d->rope, static_cast<size_t>(c.n_ctx) * (c.head_dim / 2)) == UGB_OK &&
+            dalloc(&d->part_m, static_cast<size_t>(c.n_head_kv) * d->n_split * group) == UGB_OK &&
+            dalloc(&d->part_l, static_cast<size_t>(c.n_head_kv) * d->n_split * group) == UGB_OK &&
+            dalloc(&d->part_o, static_cast<size_t>(c.n_head_kv) * d->n_split * group * c.head_dim) == UGB_OK &&
+            dalloc(&d->state, 4) == UGB_OK &&
+            cudaMallocHost(reinterpret_cast<void **>(&d->state_host), 4 * sizeof(int32_t)) == cudaSuccess &&
+            cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) == cudaSuccess;
+  if (ok) {
+    // RoPE table as the reference builds it (gpu_graph.rs:132, llm.rs:330): the angle is the
+    // f32 product pos * powf(theta, -(2i)/head_dim); cos and sin of that f32 angle are taken in
+    // double and rounded once.
+    std::vector<float2> tab(static_cast<size_t>(c.n_ctx) * (c.head_dim / 2));
+    for (int p = 0; p < c.n_ctx; ++p)
+      for (int i = 0; i < c.head_dim / 2; ++i) {
+        const float e = -static_cast<float>(2 * i) / static_cast<float>(c.head_dim);
+        const float ang = static_cast<float>(p) * powf(c.rope_theta, e);
+        tab[static_cast<size_t>(p) * (c.head_dim / 2) + i] =
+            make_float2(static_cast<float>(std::cos(static_cast<double>(ang))),
+                        static_cast<float>(std::sin(static_cast<double>(ang))));
+      }
+    ok = cudaMemcpy(d->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) == cudaSuccess &&
+         cudaMemset(d->state, 0, 4 * sizeof(int32_t)) == cudaSuccess &&
+         cudaMemset(d->kcache, 0, kv * sizeof(float)) == cudaSuccess &&
+         cudaMemset(d->vcache, 0, kv * sizeof(float)) == cudaSuccess &&
+         cudaMemset(d->dx, 0, c.n_embd * sizeof(float)) == cudaSuccess;
+  }
+  if (!ok) {
+    free_all(d);
+    delete d;
+    return UGB_EBACKEND;
+  }
+  *out = d;
+  return UGB_OK;
+}
+
+extern "C" ugb_status ugb_decoder_destroy(ugb_decoder *dec) {
+  if (!dec) return UGB_ECONTEXT;
+  cudaSetDevice(dec->ctx->device);
+  cudaDeviceSynchronize();
+  free_all(dec);
+  delete dec;
+  return UGB_OK;
+}
+
+namespace ugb {
+namespace {
+
+bool matrix_ok(uint32_t kind, const void *p) {
+  return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && kind != 0;
+}
+
+ugb_status copy_bias(float *dst, const void *src, int64_t n) {
+  if (!src) return UGB_OK;
+  return cuda_status(cudaMemcpy(dst, src, n * sizeof(float), cudaMemcpyDeviceToDevice));
+}
+
+// Host-generated f32 vector: 1 + amp * u (u uniform in [-1, 1)) or amp * u when center == 0.
+ugb_status upload_vec(float **dst, int64_t n, float center, float amp, std::mt19937_64 &rng,
+                      std::vector<void *> &owned) {
+  std::vector<float> h(static_cast<size_t>(n));
+  std::uniform_real_distribution<float> u(-1.f, 1.f);
+  for (auto &v : h) v = center + amp * u(rng);
+  if (cudaMalloc(reinterpret_cast<void **>(dst), n * sizeof(float)) != cudaSuccess) return UGB_EBACKEND;
+  owned.push_back(*dst);
+  return cuda_status(cudaMemcpy(*dst, h.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+}
+
+ugb_status synth_matrix(ugb_ctx *ctx, const void **dst, uint32_t kind, int64_t k, int64_t m,
+                        uint64_t seed, std::vector<void *> &owned) {
+  const int64_t rb = ugb_row_bytes(kind, k);
+  void *p = nullptr;
+  if (rb < 0 || cudaMalloc(&p, static_cast<size_t>(rb * m)) != cudaSuccess) return UGB_EBACKEND;
+  owned.push_back(p);
+  *dst = p;
+  return launch_fill_synthetic(ctx, nullptr, kind, static_cast<uint8_t *>(p), k, m, seed);
+}
+
+MatvecArgs mv_args(const ugb_decoder *d, uint32_t kind, int64_t k, int64_t m, const uint8_t *xq, float *y) {
+  MatvecArgs a;
+  a.kind = kind;
+  a.row_bytes = ugb_row_bytes(kind, k);
+  a.k = k;
+  a.m = m;
+  a.xq = xq;
+  a.xl = q8act_layout(k, 1);
+  a.y = y;
+  a.ldy = m;
+  a.batch = 1;
+  a.pdl = true;
+  (void)d;
+  return a;
+}
+
+}  // namespace
+}  // namespace ugb
+
+extern "C" ugb_status ugb_decoder_bind(ugb_decoder *d, const ugb_model_weights *w) {
+  if (!d || !w || !w->layers) return UGB_ECONTEXT;
+  const ugb_decoder_config &c = d->cfg;
+  if (!matrix_ok(UGB_Q8_0, w->tok_embd) || !matrix_ok(c.head_kind, w->output) || !w->output_norm)
+    return UGB_EALIGN;
+  const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
+  const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
+  const int64_t brow = qrows + 2 * kvrows;
+  bool any_bias = false;
+  for (int l = 0; l < c.n_layer; ++l) {
+    const ugb_layer_weights &L = w->layers[l];
+    for (const void *m : {L.wq, L.wk, L.wv, L.wo, L.w_gate, L.w_up, L.w_down})
+      if (!matrix_ok(c.kind, m)) return UGB_EALIGN;
+    if (!L.attn_norm || !L.ffn_norm) return UGB_EALIGN;
+    any_bias = any_bias || L.bq || L.bk || L.bv;
+  }
+  cudaSetDevice(d->ctx->device);
+  if (d->bias) {
+    cudaFree(d->bias);
+    d->bias = nullptr;
+  }
+  if (any_bias) {
+    if (dalloc(&d->bias, static_cast<size_t>(c.n_layer) * brow) != UGB_OK) return UGB_EBACKEND;
+    if (cudaMemset(d->bias, 0, static_cast<size_t>(c.n_layer) * brow * sizeof(float)) != cudaSuccess) return UGB_EBACKEND;
+    for (int l = 0; l < c.n_layer; ++l) {
+      const ugb_layer_weights &L = w->layers[l];
+      float *b = d->bias + static_cast<size_t>(l) * brow;
+      if (copy_bias(b, L.bq, qrows) != UGB_OK || copy_bias(b + qrows, L.bk, kvrows) != UGB_OK ||
+          copy_bias(b + qrows + kvrows, L.bv, kvrows) != UGB_OK)
+        return UGB_EBACKEND;
+    }
+  }
+  d->w = *w;
+  d->layers.assign(w->layers, w->layers + c.n_layer);
+  d->w.layers = d->layers.data();
+  if (d->exec) {  // the captured step refers to the old weights
+    cudaGraphExecDestroy(d->exec);
+    cudaGraphDestroy(d->graph);
+    d->exec = nullptr;
+    d->graph = nullptr;
+  }
+  return UGB_OK;
+}
+
+extern "C" ugb_status ugb_decoder_synthetic(ugb_decoder *d, uint64_t seed) {
+  if (!d) return UGB_ECONTEXT;
+  const ugb_decoder_config &c = d->cfg;
+  cudaSetDevice(d->ctx->device);
+  std::mt19937_64 rng(seed);
+  const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
+  const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
+  std::vector<ugb_layer_weights> layers(c.n_layer);
+  ugb_model_weights w{};
+  uint64_t s = seed * 1000003ull;
+  ugb_status st = synth_matrix(d->ctx, &w.tok_embd, UGB_Q8_0, c.n_embd, c.n_vocab, ++s, d->owned);
+  float *onorm = nullptr;
+  if (st == UGB_OK) st = upload_vec(&onorm, c.n_embd, 1.f, 0.1f, rng, d->owned);
+  w.output_norm = onorm;
+  if (st == UGB_OK) {
+    if (c.head_kind == UGB_Q8_0) w.output = w.tok_embd;  // tied embeddings
+    else st = synth_matrix(d->ctx, &w.output, c.head_kind, c.n_embd, c.n_vocab, ++s, d->owned);
+  }
+  for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
+    ugb_layer_weights &L = layers[l];
+    float *an = nullptr, *fn = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    st = upload_vec(&an, c.n_embd, 1.f, 0.1f, rng, d->owned);
+    if (st == UGB_OK) st = upload_vec(&fn, c.n_embd, 1.f, 0.1f, rng, d->owned);
+    if (st == UGB_OK) st = upload_vec(&bq, qrows, 0.f, 0.02f, rng, d->owned);
+    if (st == UGB_OK) st = upload_vec(&bk, kvrows, 0.f, 0.02f, rng, d->owned);
+    if (st == UGB_OK) st = upload_vec(&bv, kvrows, 0.f, 0.02f, rng, d->owned);
+    L.attn_norm = an;
+    L.ffn_norm = fn;
+    L.bq = bq;
+    L.bk = bk;
+    L.bv = bv;
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wq, c.kind, c.n_embd, qrows, ++s, d->owned);
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wk, c.kind, c.n_embd, kvrows, ++s, d->owned);
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wv, c.kind, c.n_embd, kvrows, ++s, d->owned);
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wo, c.kind, qrows, c.n_embd, ++s, d->owned);
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.w_gate, c.kind, c.n_embd, c.n_ff, ++s, d->owned);
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.w_up, c.kind, c.n_embd, c.n_ff, ++s, d->owned);
+    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.w_down, c.kind, c.n_ff, c.n_embd, ++s, d->owned);
+  }
+  if (st != UGB_OK) return st;
+  if (cudaDeviceSynchronize() != cudaSuccess) return UGB_EBACKEND;
+  w.layers = layers.data();
+  return ugb_decoder_bind(d, &w);
+}
+
+extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
+  if (!d || !d->w.layers) return UGB_ECONTEXT;
+  const ugb_decoder_config &c = d->cfg;
+  ugb_ctx *ctx = d->ctx;
+  uint32_t *status = ctx->status;
+  const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
+  const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
+  const int64_t brow = qrows + 2 * kvrows;
+  const size_t kv_layer = static_cast<size_t>(kvrows) * c.n_ctx;
+  ugb_status st = launch_embed(stream, false, static_cast<const uint8_t *>(d->w.tok_embd), c.n_embd,
+                               c.n_vocab, c.n_ctx, d->state, d->x, status);
+  for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
+    const ugb_layer_weights &L = d->layers[l];
+    st = launch_rmsnorm_quant(stream, true, d->x, l == 0 ? nullptr : d->dx,
+                              static_cast<const float *>(L.attn_norm), c.n_embd, c.norm_eps, d->xq, status);
+    if (st != UGB_OK) break;
+    MatvecArgs a = mv_args(d, c.kind, c.n_embd, brow, d->xq, d->qkv);
+    a.nseg = 3;
+    a.ws[0] = static_cast<const uint8_t *>(L.wq);
+    a.ws[1] = static_cast<const uint8_t *>(L.wk);
+    a.ws[2] = static_cast<const uint8_t *>(L.wv);
+    a.seg_rows[0] = qrows;
+    a.seg_rows[1] = a.seg_rows[2] = kvrows;
+    st = launch_matvec(ctx, stream, a);
+    if (st != UGB_OK) break;
+    AttnParams ap{};
+    ap.qkv = d->qkv;
+    ap.bias = d->bias ? d->bias + static_cast<size_t>(l) * brow : nullptr;
+    ap.rope = d->rope;
+    ap.kcache = d->kcache + kv_layer * l;
+    ap.vcache = d->vcache + kv_layer * l;
+    ap.part_m = d->part_m;
+    ap.part_l = d->part_l;
+    ap.part_o = d->part_o;
+    ap.state = d->state;
+    ap.n_head = c.n_head;
+    ap.n_kv = c.n_head_kv;
+    ap.n_ctx = c.n_ctx;
+    ap.n_split = d->n_split;
+    ap.status = status;
+    st = launch_attention(stream, true, ap, d->attq);
+    if (st != UGB_OK) break;
+    a = mv_args(d, c.kind, qrows, c.n_embd, d->attq, d->dx);
+    a.w = static_cast<const uint8_t *>(L.wo);
+    st = launch_matvec(ctx, stream, a);
+    if (st != UGB_OK) break;
+    st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(L.ffn_norm), c.n_embd,
+                              c.norm_eps, d->xq, status);
+    if (st != UGB_OK) break;
+    a = mv_args(d, c.kind, c.n_embd, 2 * static_cast<int64_t>(c.n_ff), d->xq, d->gu);
+    a.nseg = 2;
+    a.ws[0] = static_cast<const uint8_t *>(L.w_gate);
+    a.ws[1] = static_cast<const uint8_t *>(L.w_up);
+    a.seg_rows[0] = a.seg_rows[1] = c.n_ff;
+    st = launch_matvec(ctx, stream, a);
+    if (st != UGB_OK) break;
+    st = launch_silu_quant(stream, true, d->gu, c.n_ff, d->hq, status);
+    if (st != UGB_OK) break;
+    a = mv_args(d, c.kind, c.n_ff, c.n_embd, d->hq, d->dx);
+    a.w = static_cast<const uint8_t *>(L.w_down);
+    st = launch_matvec(ctx, stream, a);
+  }
+  if (st != UGB_OK) return st;
+  st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(d->w.output_norm), c.n_embd,
+                            c.norm_eps, d->xq, status);
+  if (st != UGB_OK) return st;
+  MatvecArgs a = mv_args(d, c.head_kind, c.n_embd, c.n_vocab, d->xq, d->logits);
+  a.w = static_cast<const uint8_t *>(d->w.output);
+  st = launch_matvec(ctx, stream, a);
+  if (st != UGB_OK) return st;
+  return launch_argmax(stream, true, d->logits, c.n_vocab, d->state, ctx->sm_count);
+}
+
+extern "C" ugb_status ugb_decoder_set_state(ugb_decoder *d, ugb_stream stream, int32_t token, int32_t pos) {
+  if (!d) return UGB_ECONTEXT;
+  if (token < 0 || token >= d->cfg.n_vocab || pos < 0 || pos >= d->cfg.n_ctx) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  // Wait for any earlier copy out of the pinned mirror before overwriting it.
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
+  d->state_host[0] = token;
+  d->state_host[1] = pos;
+  d->state_host[2] = d->state_host[3] = 0;
+  return cuda_status(cudaMemcpyAsync(d->state, d->state_host, 4 * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+}
+
+extern "C" ugb_status ugb_decoder_get_state(ugb_decoder *d, ugb_stream stream, int32_t *token, int32_t *pos,
+                                            int32_t *next_token) {
+  if (!d) return UGB_ECONTEXT;
+  cudaSetDevice(d->ctx->device);
+  if (cudaMemcpyAsync(d->state_host, d->state, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  uint64_t key;
+  std::memcpy(&key, d->state_host + 2, 8);
+  if (token) *token = d->state_host[0];
+  if (pos) *pos = d->state_host[1];
+  if (next_token) *next_token = key ? static_cast<int32_t>(~static_cast<uint32_t>(key)) : -1;
+  return UGB_OK;
+}
+
+extern "C" ugb_status ugb_decoder_logits(ugb_decoder *d, ugb_stream stream, float *logits_host) {
+  if (!d || !logits_host) return UGB_ECONTEXT;
+  cudaSetDevice(d->ctx->device);
+  if (cudaMemcpyAsync(logits_host, d->logits, static_cast<size_t>(d->cfg.n_vocab) * sizeof(float),
+                      cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  return cuda_status(cudaStreamSynchronize(stream));
+}
+
+extern "C" ugb_status ugb_decoder_read_kv(ugb_decoder *d, ugb_stream stream, int32_t layer, int32_t pos,
+                                          int32_t count, float *k_host, float *v_host) {
+  if (!d || !k_host || !v_host) return UGB_ECONTEXT;
+  const ugb_decoder_config &c = d->cfg;
+  if (layer < 0 || layer >= c.n_layer || pos < 0 || count < 1 || count > c.n_ctx - pos) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  const size_t hd = static_cast<size_t>(c.head_dim);
+  const size_t layer_off = static_cast<size_t>(layer) * c.n_head_kv * c.n_ctx * hd;
+  const size_t row = count * hd * sizeof(float);
+  for (int which = 0; which < 2; ++which) {
+    const float *src = (which ? d->vcache : d->kcache) + layer_off + static_cast<size_t>(pos) * hd;
+    float *dst = which ? v_host : k_host;
+    // one row per KV head: [n_kv][n_ctx][hd] (pitch n_ctx*hd) -> [n_kv][count][hd]
+    if (cudaMemcpy2DAsync(dst, row, src, c.n_ctx * hd * sizeof(float), row, c.n_head_kv,
+                          cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+      return UGB_EBACKEND;
+  }
+  return cuda_status(cudaStreamSynchronize(stream));
+}
+
+extern "C" ugb_status ugb_decoder_token(ugb_decoder *d, ugb_stream stream, int32_t token, int32_t pos,
+                                        int32_t *next_token) {
+  if (!d || !next_token) return UGB_ECONTEXT;
+  cudaSetDevice(d->ctx->device);
+  if (!d->exec) {
+    if (cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return UGB_EBACKEND;
+    const ugb_status st = ugb_decoder_step(d, d->cap);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(d->cap, &g);
+    if (st != UGB_OK || e != cudaSuccess) {
+      if (g) cudaGraphDestroy(g);
+      return st != UGB_OK ? st : UGB_EBACKEND;
+    }
+    if (cudaGraphInstantiate(&d->exec, g, 0) != cudaSuccess) {
+      cudaGraphDestroy(g);
+      return UGB_EBACKEND;
+    }
+    d->graph = g;
+  }
+  ugb_status st = ugb_decoder_set_state(d, stream, token, pos);
+  if (st != UGB_OK) return st;
+  if (cudaGraphLaunch(d->exec, stream) != cudaSuccess) return UGB_EBACKEND;
+  if (cudaMemcpyAsync(d->state_host, d->state, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  uint32_t bits = 0;
+  st = ugb_status_read(d->ctx, stream, &bits);  // synchronises the stream
+  if (st != UGB_OK) return st;
+  uint64_t key;
+  std::memcpy(&key, d->state_host + 2, 8);
+  if (!key) return UGB_ENONFINITE;  // every logit was non-finite
+  *next_token = static_cast<int32_t>(~static_cast<uint32_t>(key));
+  return UGB_OK;
+}

@@ -36,7 +36,10 @@ Q8Act q8act_layout(int64_t k, int64_t batch);
 // Streaming matvec launch description.
 struct MatvecArgs {
   uint32_t kind = 0;
-  const uint8_t *w = nullptr;
+  const uint8_t *w = nullptr;    // single matrix (nseg == 0), or:
+  const uint8_t *ws[4] = {};     // up to 4 matrices of seg_rows[i] rows, y rows concatenated
+  int64_t seg_rows[4] = {};
+  int nseg = 0;
   int64_t row_bytes = 0, k = 0, m = 0;
   const uint8_t *xq = nullptr;   // Q8_1 buffer
   Q8Act xl;                      // its layout

@@ -40,9 +40,16 @@ constexpr uint32_t kItemTarget = 32 * 1024;  // weight bytes per pipeline stage
 constexpr size_t kSmPerKernel = 112 * 1024;  // shared memory one kernel takes per SM
 constexpr int kSlots = 4;                    // activation units a lane keeps in registers
 
+constexpr int kMaxSegs = 4;  // weight matrices sharing one activation in one launch
+
 struct MvParams {
-  const uint8_t *w;
-  const uint8_t *w_end16;     // (w + m * row_bytes) rounded down to 16 bytes
+  // Rows [seg_row0[i], seg_row0[i+1]) live in matrix w[i] (the reference's fused QKV /
+  // gate-up launches over separate GGUF tensors, gpu_dp4a.cu:53-64).  An item never spans
+  // two matrices.  w_end16[i]: end of matrix i rounded down to 16 bytes.
+  const uint8_t *w[kMaxSegs];
+  const uint8_t *w_end16[kMaxSegs];
+  int seg_row0[kMaxSegs];
+  int nseg;
   uint64_t row_bytes;
   int k, m;
   int rows;                   // rows per item (8 * rows-per-warp)
@@ -51,6 +58,7 @@ struct MvParams {
   int stages;
   uint32_t x_q, x_d, x_s;     // shared offsets of the staged activation arrays
   uint32_t ring;              // shared offset of the weight ring
+  uint32_t red;               // shared offset of cross-warp row partials (split kernel)
   const uint8_t *xq;          // Q8_1 buffer: quants [nb][k], scales / sums [nb][nbp]
   const float *xd;
   const int *xs;
@@ -89,14 +97,27 @@ __device__ __forceinline__ Item item_of(const MvParams &p, int t) {
   return it;
 }
 
-// Byte range [a0, a1) a bulk copy may fetch for the span [src, e): 16-byte aligned, and
-// never past the last 16-byte boundary of the weight buffer; the bytes beyond (only in the
-// final span) go through plain loads.
-__device__ __forceinline__ void span16(const MvParams &p, const uint8_t *src, const uint8_t *e,
-                                       const uint8_t *&a0, const uint8_t *&a1) {
+__device__ __forceinline__ int seg_of(const MvParams &p, int row) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxSegs; ++i) s += (i < p.nseg && row >= p.seg_row0[i]) ? 1 : 0;
+  return s;
+}
+
+// Address of row `row` (global row index across the matrices).
+__device__ __forceinline__ const uint8_t *row_ptr(const MvParams &p, int row) {
+  const int s = seg_of(p, row);
+  return p.w[s] + static_cast<uint64_t>(row - p.seg_row0[s]) * p.row_bytes;
+}
+
+// Byte range [a0, a1) a bulk copy may fetch for the span [src, e) of matrix `seg`: 16-byte
+// aligned, and never past the last 16-byte boundary of that matrix; the bytes beyond (only in
+// a matrix's final span) go through plain loads.
+__device__ __forceinline__ void span16(const MvParams &p, int seg, const uint8_t *src,
+                                       const uint8_t *e, const uint8_t *&a0, const uint8_t *&a1) {
   a0 = floor16(src);
   a1 = ceil16(e);
-  if (e > p.w_end16) a1 = a0 > p.w_end16 ? a0 : p.w_end16;
+  if (e > p.w_end16[seg]) a1 = a0 > p.w_end16[seg] ? a0 : p.w_end16[seg];
 }
 
 // Copies of item t into `stage` (one thread).  When a row chunk is the whole row (nch == 1)
@@ -104,25 +125,27 @@ __device__ __forceinline__ void span16(const MvParams &p, const uint8_t *src, co
 template <int KIND>
 __device__ void issue_item(const MvParams &p, int t, uint32_t stage, uint32_t bar, uint64_t pol) {
   const Item it = item_of(p, t);
+  const int seg = seg_of(p, it.r0);
+  const uint8_t *first = row_ptr(p, it.r0);
   const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(it.c) * p.kc);
   const uint64_t seg_len = bytes_of<KIND>(min(p.kc, p.k - it.c * p.kc));
   const int spans = p.nch == 1 ? 1 : it.nrows;
   uint32_t tx = 0;
   for (int r = 0; r < spans; ++r) {
-    const uint8_t *src = p.w + static_cast<uint64_t>(it.r0 + r) * p.row_bytes + seg_off;
-    const uint8_t *e = p.nch == 1 ? p.w + static_cast<uint64_t>(it.r0 + it.nrows) * p.row_bytes : src + seg_len;
+    const uint8_t *src = first + static_cast<uint64_t>(r) * p.row_bytes + seg_off;
+    const uint8_t *e = p.nch == 1 ? first + static_cast<uint64_t>(it.nrows) * p.row_bytes : src + seg_len;
     const uint8_t *a0, *a1;
-    span16(p, src, e, a0, a1);
+    span16(p, seg, src, e, a0, a1);
     const uint32_t dst = stage + r * p.seg_stride;
     for (const uint8_t *b = a1; b < e; ++b) sts8(dst + static_cast<uint32_t>(b - a0), *b);
     tx += static_cast<uint32_t>(a1 - a0);
   }
   mbar_arrive_expect_tx(bar, tx);
   for (int r = 0; r < spans; ++r) {
-    const uint8_t *src = p.w + static_cast<uint64_t>(it.r0 + r) * p.row_bytes + seg_off;
-    const uint8_t *e = p.nch == 1 ? p.w + static_cast<uint64_t>(it.r0 + it.nrows) * p.row_bytes : src + seg_len;
+    const uint8_t *src = first + static_cast<uint64_t>(r) * p.row_bytes + seg_off;
+    const uint8_t *e = p.nch == 1 ? first + static_cast<uint64_t>(it.nrows) * p.row_bytes : src + seg_len;
     const uint8_t *a0, *a1;
-    span16(p, src, e, a0, a1);
+    span16(p, seg, src, e, a0, a1);
     if (a1 > a0) bulk_g2s(stage + r * p.seg_stride, a0, static_cast<uint32_t>(a1 - a0), bar, pol);
   }
 }
@@ -269,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) 
     const Item it = item_of(p, t);
     // The item's rows are one span fetched from floor16(first row).
     const uint32_t stage = ring + s * p.stage_bytes +
-        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p.w + static_cast<uint64_t>(it.r0) * p.row_bytes) & 15);
+        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, it.r0)) & 15);
     float acc[J];
 #pragma unroll
     for (int j = 0; j < J; j += 2) {
@@ -299,6 +322,96 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) 
         p.y[it.r0 + rr] = tot;
         if (!isfinite(tot)) status_or(p.status, ST_NONFINITE_OUT);
       }
+    }
+  }
+}
+
+// Batch-1 consumer for rows too long to give each warp whole rows: an item of R rows is
+// spread over all 256 consumer lanes (flat index f = warp * 32 + lane + 256 j of the item's
+// R x U (row, unit) space), activation units again held in registers.  Each warp reduces its
+// share of the R rows; the per-warp partials meet in shared memory (double-buffered by item
+// parity) and warp 0 adds them in warp order.  The one named barrier per item also ANDs the
+// warps' wait results, so a timed-out stage makes every consumer warp stop together.
+template <int KIND, int R, int J>
+__global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const MvParams p) {
+  static_assert(J % 2 == 0 && J <= kSlots, "slots are processed in pairs");
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = smem_u32(smem);
+  const uint32_t full = base, empty = base + 64;
+  const uint32_t ring = base + p.ring;
+  const int T = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                static_cast<int>(gridDim.x);
+  bool ok = true;
+  if (!prologue<KIND, 1>(p, base, T, ok)) return;
+
+  const int U = p.k / 32;
+  const int total = R * U;
+  uint32_t srow_off[J];
+  int sunit[J], srow[J];
+  XUnit xr[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int f = warp * 32 + lane + kWarps * 32 * j;
+    const bool valid = f < total;
+    const int r = valid ? f / U : 0;
+    const int u = valid ? f - r * U : 0;
+    srow[j] = valid ? r : R;  // R matches no row: the slot adds nothing
+    sunit[j] = u;
+    srow_off[j] = static_cast<uint32_t>(r * p.row_bytes);
+    load_xunit(base + p.x_q + 32 * u, base + p.x_d + 4 * u, base + p.x_s + 4 * u,
+               Fmt<KIND>::kNeedsSum, xr[j]);
+  }
+  float *red = reinterpret_cast<float *>(smem + p.red);
+
+  for (int t = 0; t < T; ++t) {
+    const int s = t % p.stages;
+    const bool mine = __all_sync(0xffffffffu, mbar_wait_bounded(full + 8 * s, (t / p.stages) & 1));
+    const Item it = item_of(p, t);
+    float rs[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) rs[r] = 0.f;
+    if (mine) {
+      const uint32_t stage = ring + s * p.stage_bytes +
+          static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, it.r0)) & 15);
+      float acc[J];
+#pragma unroll
+      for (int j = 0; j < J; j += 2) {
+        acc[j] = acc[j + 1] = 0.f;
+        if ((warp * 32 + kWarps * 32 * j) < total) {  // warp-uniform
+          WUnit wa, wb;
+          load_wunit<KIND>(stage + srow_off[j], sunit[j], wa);
+          load_wunit<KIND>(stage + srow_off[j + 1], sunit[j + 1], wb);
+          acc[j] = unit_term<KIND>(wa, xr[j], unit_isum<KIND>(wa, xr[j]));
+          acc[j + 1] = unit_term<KIND>(wb, xr[j + 1], unit_isum<KIND>(wb, xr[j + 1]));
+        }
+      }
+      release_stage(empty, s, lane);
+#pragma unroll
+      for (int r = 0; r < R; ++r)
+#pragma unroll
+        for (int j = 0; j < J; ++j) rs[r] += srow[j] == r ? acc[j] : 0.f;
+    }
+    float tot;
+    const bool owner = reduce_rows<R>(rs, lane, tot);
+    if (owner) red[((t & 1) * kWarps + warp) * 4 + lane / (32 / R)] = tot;
+    uint32_t all;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\tsetp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.and.pred po, 1, %2, pi;\n\tselp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(all)
+        : "r"(mine ? 1u : 0u), "r"(kWarps * 32)
+        : "memory");
+    if (!all) {
+      if (!mine && lane == 0) status_or(p.status, ST_TIMEOUT);
+      break;
+    }
+    if (warp == 0 && lane < R && lane < it.nrows) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) sum += red[((t & 1) * kWarps + w) * 4 + lane];
+      p.y[it.r0 + lane] = sum;
+      if (!isfinite(sum)) status_or(p.status, ST_NONFINITE_OUT);
     }
   }
 }
@@ -334,10 +447,11 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const MvParams p
     if (warp < it.nrows) {
       const int nunits = min(p.kc, p.k - k0) / 32;
       const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(k0));
-      const uint8_t *row = p.w + static_cast<uint64_t>(it.r0 + warp) * p.row_bytes + seg_off;
+      const uint8_t *row0 = row_ptr(p, it.r0);
+      const uint8_t *row = row0 + static_cast<uint64_t>(warp) * p.row_bytes + seg_off;
       uint32_t seg;
       if (p.nch == 1) {
-        const uint8_t *first = floor16(p.w + static_cast<uint64_t>(it.r0) * p.row_bytes);
+        const uint8_t *first = floor16(row0);
         seg = stage + static_cast<uint32_t>(row - first);
       } else {
         seg = stage + warp * p.seg_stride + static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row) & 15);
@@ -393,10 +507,12 @@ size_t x_bytes(uint32_t kind, int64_t k, int nb) {
 }
 
 struct Plan {
-  bool rows_kernel = false;   // mv_rows_kernel (else mv_stream_kernel)
-  int rw = 1, slots = 2;      // rows per warp and register slots per lane (rows kernel)
+  bool rows_kernel = false;   // mv_rows_kernel
+  bool split = false;         // mv_split_kernel (neither: mv_stream_kernel)
+  int rw = 1, slots = 2;      // rows per warp (rows kernel) or per item (split kernel), and
+                              // register slots per lane
   int rows = kWarps, kc = 0, nch = 1, ngroups = 0, stages = 2, ctas_per_sm = 1;
-  uint32_t seg_stride = 0, stage_bytes = 0, x_q = 0, x_d = 0, x_s = 0, ring = 0;
+  uint32_t seg_stride = 0, stage_bytes = 0, x_q = 0, x_d = 0, x_s = 0, red = 0, ring = 0;
   size_t smem = 0;
 };
 
@@ -416,8 +532,18 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
         break;
       }
     }
+    // Rows too long for that: spread an item of R rows over all consumer lanes.
+    for (int r : {4, 2, 1}) {
+      if (pl.rows_kernel) break;
+      const int64_t slots = (r * units + kWarps * 32 - 1) / (kWarps * 32);
+      if (rb * r <= kItemTarget && slots <= kSlots) {
+        pl.split = true;
+        pl.rw = r;
+        pl.slots = slots <= 2 ? 2 : 4;
+      }
+    }
   }
-  pl.rows = kWarps * pl.rw;
+  pl.rows = pl.split ? pl.rw : kWarps * pl.rw;
   if (rb * pl.rows <= kItemTarget) {
     pl.kc = static_cast<int>(k);
     pl.nch = 1;
@@ -440,6 +566,8 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
   off += static_cast<uint32_t>(nb * nbp * 4);
   pl.x_s = off;
   if (kind == UGB_Q4_K) off += static_cast<uint32_t>(nb * nbp * 4);
+  pl.red = static_cast<uint32_t>(round_up(off, 16));
+  off = pl.red + 2 * kWarps * 4 * 4;
   pl.ring = static_cast<uint32_t>(round_up(off, 128));
   // One kernel takes at most about half an SM's shared memory (kSmPerKernel over its resident
   // CTAs), so the next kernel in the stream can become resident beside it and prefetch its
@@ -465,6 +593,16 @@ const void *rows_kernel_ptr(int rw, int slots) {
 }
 
 template <int KIND>
+const void *split_kernel_ptr(int r, int slots) {
+#define UGB_SK(R, J) if (r == R && slots == J) return reinterpret_cast<const void *>(&mv_split_kernel<KIND, R, J>);
+  UGB_SK(1, 2) UGB_SK(1, 4)
+  UGB_SK(2, 2) UGB_SK(2, 4)
+  UGB_SK(4, 2) UGB_SK(4, 4)
+#undef UGB_SK
+  return nullptr;
+}
+
+template <int KIND>
 const void *stream_kernel_ptr(int nb, bool dots) {
   if (dots) return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, true>);
   switch (nb) {
@@ -478,9 +616,12 @@ const void *stream_kernel_ptr(int nb, bool dots) {
 
 const void *select_kernel(uint32_t kind, const Plan &pl, int nb, bool dots) {
   switch (kind) {
-    case UGB_Q8_0: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q8_0>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q8_0>(nb, dots);
-    case UGB_Q4_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q4_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q4_K>(nb, dots);
-    case UGB_Q3_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q3_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q3_K>(nb, dots);
+    case UGB_Q8_0: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q8_0>(pl.rw, pl.slots)
+                          : pl.split ? split_kernel_ptr<UGB_Q8_0>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q8_0>(nb, dots);
+    case UGB_Q4_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q4_K>(pl.rw, pl.slots)
+                          : pl.split ? split_kernel_ptr<UGB_Q4_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q4_K>(nb, dots);
+    case UGB_Q3_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q3_K>(pl.rw, pl.slots)
+                          : pl.split ? split_kernel_ptr<UGB_Q3_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q3_K>(nb, dots);
     default: return nullptr;
   }
 }
@@ -500,6 +641,10 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
         pl.rw = rw;
         pl.slots = j;
         if (allow_smem(select_kernel(kind, pl, 1, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+        pl.rows_kernel = false;
+        pl.split = true;
+        if (allow_smem(select_kernel(kind, pl, 1, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+        pl.split = false;
       }
     pl.rows_kernel = false;
     for (int nb : {1, 2, 4, 8})
@@ -509,7 +654,13 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
   return UGB_OK;
 }
 
-ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a) {
+ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_in) {
+  MatvecArgs a = a_in;
+  if (a.nseg == 0) {
+    a.nseg = 1;
+    a.ws[0] = a.w;
+    a.seg_rows[0] = a.m;
+  }
   const bool dots = a.dots != nullptr;
   // A batch runs as launches of 8, 4, 2 or 1 vectors (largest first) whose staged
   // activations fit kXBudget; each launch streams the weights once.
@@ -527,9 +678,38 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a)
         per_sm < 1)
       return UGB_EBACKEND;
     per_sm = std::min(per_sm, pl.ctas_per_sm);
+    // Items must not straddle two matrices: every matrix but the last must hold whole items,
+    // otherwise the matrices go out as separate launches.
+    bool whole = true;
+    for (int i = 0; i + 1 < a.nseg; ++i) whole = whole && a.seg_rows[i] % pl.rows == 0;
+    if (a.nseg > 1 && !whole) {
+      int64_t row0 = 0;
+      for (int i = 0; i < a.nseg; ++i) {
+        MatvecArgs one = a;
+        one.nseg = 1;
+        one.w = a.ws[i];
+        one.ws[0] = a.ws[i];
+        one.m = one.seg_rows[0] = a.seg_rows[i];
+        if (a.y) one.y = a.y + row0;
+        if (a.dots) one.dots = a.dots + row0 * (a.k / 32);
+        const ugb_status st = launch_matvec(ctx, stream, one);
+        if (st != UGB_OK) return st;
+        row0 += a.seg_rows[i];
+      }
+      return UGB_OK;
+    }
     MvParams p{};
-    p.w = a.w;
-    p.w_end16 = reinterpret_cast<const uint8_t *>(reinterpret_cast<uintptr_t>(a.w + a.m * a.row_bytes) & ~uintptr_t(15));
+    p.nseg = a.nseg;
+    {
+      int64_t row0 = 0;
+      for (int i = 0; i < a.nseg; ++i) {
+        p.w[i] = a.ws[i];
+        p.w_end16[i] = reinterpret_cast<const uint8_t *>(
+            reinterpret_cast<uintptr_t>(a.ws[i] + a.seg_rows[i] * a.row_bytes) & ~uintptr_t(15));
+        p.seg_row0[i] = static_cast<int>(row0);
+        row0 += a.seg_rows[i];
+      }
+    }
     p.row_bytes = static_cast<uint64_t>(a.row_bytes);
     p.k = static_cast<int>(a.k);
     p.m = static_cast<int>(a.m);
@@ -544,6 +724,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a)
     p.x_d = pl.x_d;
     p.x_s = pl.x_s;
     p.ring = pl.ring;
+    p.red = pl.red;
     p.xq = a.xq + done * a.xl.k;
     p.xd = reinterpret_cast<const float *>(a.xq + a.xl.d_off) + done * a.xl.nbp;
     p.xs = reinterpret_cast<const int *>(a.xq + a.xl.s_off) + done * a.xl.nbp;
