@@ -1,24 +1,29 @@
-"""Benchmark of the B200 quantized linear-layer hot path (libugb) -- one JSON line on rank 0.
+"""Benchmark of the B200 quantized decode hot path (libugb) -- one JSON line on rank 0.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload c2|c1]
 
 Workloads:
-  c1  Q8_0 matvec 8960x1536 with block-32 activation quantisation.  A step is
-      quant_act + linear on one fp32 vector; weights rotate over 24 copies (350 MB > L2) so
-      every step streams its matrix from HBM.
+  c2  (default; the headline) greedy batch-1 decode of a random-init Qwen2.5-1.5B-shaped
+      decoder with every linear weight in Q8_0 (28 layers, hidden 1536, FFN 8960, 12/2 heads
+      of 128, vocab 151936, tied embeddings, context 512).  A step is one token: embedding,
+      28 layers of norm+quant / QKV / attention / O / norm+quant / gate+up / SiLU+quant / down,
+      final norm, head and greedy selection, replayed from one captured CUDA graph with the
+      token state kept on the device.  The timed tokens are the last K positions of the
+      512-position context.  1.655 GB of weights stream from HBM per token (> L2).
+  c1  Q8_0 matvec 8960x1536 with block-32 activation quantisation; weights
+      rotate over 24 copies (350 MB > L2).
 
-Multi-GPU: one process per GPU (torchrun), each an independent replica of the workload
-("replicas only": a single matvec has no exchange step); value = all ranks' units / the
-slowest rank's time (max over ranks of CUDA-event time).
+Multi-GPU: one process per GPU (torchrun), each an independent replica ("replicas only":
+batch-1 decode of a dense model has no exchange step worth sharding); value = all ranks'
+tokens / the slowest rank's time (max over ranks of CUDA-event time).
 
 The reference arm (--impl reference) times the CPU restatement of the reference path
-(oracle/, the reference Rust cannot be built here) on the host cores with all threads, on
+(oracle/; the reference Rust cannot be built here) on the host cores with all threads, on
 the same workload, metric and unit.
 """
 from __future__ import annotations
 
 import argparse
-import ctypes
 import importlib
 import json
 import os
@@ -26,7 +31,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 import numpy as np
@@ -35,8 +39,6 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 Q8_0 = 8
-C1_K, C1_M = 1536, 8960
-C1_ROTATE = 24
 
 
 def load_peaks():
@@ -108,7 +110,243 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def barrier(world, torch):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def reduce_max(v: float, world: int, torch) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---- workload c2: Qwen2.5-1.5B-shaped Q8_0 decode ------------------------------------------
+
+C2 = dict(n_layer=28, n_embd=1536, n_ff=8960, n_head=12, n_head_kv=2, head_dim=128, n_vocab=151936,
+          n_ctx=512, rope_theta=1e6, norm_eps=1e-6, kind=Q8_0, head_kind=Q8_0)
+
+
+def c2_shapes(c=C2):
+    """(name, k, m) of every Q8_0 matrix of one layer (GGUF blk.N.* tensors)."""
+    q, kv = c["n_head"] * c["head_dim"], c["n_head_kv"] * c["head_dim"]
+    e, f = c["n_embd"], c["n_ff"]
+    return [("wq", e, q), ("wk", e, kv), ("wv", e, kv), ("wo", q, e),
+            ("w_gate", e, f), ("w_up", e, f), ("w_down", f, e)]
+
+
+def q8_bytes(k, m):
+    return m * (k // 32) * 34
+
+
+def c2_token_bytes(c=C2, pos=None):
+    """Algorithmic bytes of one token: every weight once (layers + tied head, the embedding row
+    is 1.6 KB), plus the KV cache read at context `pos` (fp32 K and V of every layer)."""
+    layers = c["n_layer"] * sum(q8_bytes(k, m) for _, k, m in c2_shapes(c))
+    head = q8_bytes(c["n_embd"], c["n_vocab"])
+    if pos is None:
+        pos = c["n_ctx"]
+    kv = c["n_layer"] * 2 * c["n_head_kv"] * c["head_dim"] * 4 * pos
+    return layers + head + kv
+
+
+def c2_launches_per_token(c=C2):
+    # embed; per layer: rmsnorm+quant, QKV, attention partial, attention combine+quant, O,
+    # rmsnorm+quant, gate/up, SiLU+quant, down; final rmsnorm+quant, head, greedy
+    return 1 + 9 * c["n_layer"] + 3
+
+
+def c2_device_weights(ctx, ugb, torch, seed, c=C2):
+    """Seeded synthetic weights in device memory (GGUF layouts), bound to a decoder."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    rng = np.random.default_rng(seed)
+    s = [seed * 100003]
+
+    def mat(k, m):
+        s[0] += 1
+        t = torch.empty(q8_bytes(k, m), dtype=torch.uint8, device=dev)
+        ctx.fill_synthetic(Q8_0, t, k, m, s[0])
+        return t
+
+    def vec(n, center, amp):
+        return torch.from_numpy((center + amp * rng.uniform(-1, 1, n)).astype(np.float32)).to(dev)
+
+    q, kv = c["n_head"] * c["head_dim"], c["n_head_kv"] * c["head_dim"]
+    w = {"tok_embd": mat(c["n_embd"], c["n_vocab"]), "output_norm": vec(c["n_embd"], 1.0, 0.1)}
+    w["output"] = w["tok_embd"]  # tied embeddings
+    w["layers"] = []
+    for _ in range(c["n_layer"]):
+        L = {"attn_norm": vec(c["n_embd"], 1.0, 0.1), "ffn_norm": vec(c["n_embd"], 1.0, 0.1),
+             "bq": vec(q, 0.0, 0.02), "bk": vec(kv, 0.0, 0.02), "bv": vec(kv, 0.0, 0.02)}
+        for name, k, m in c2_shapes(c):
+            L[name] = mat(k, m)
+        w["layers"].append(L)
+    torch.cuda.synchronize()
+    return w
+
+
+def c2_host_weights(seed, c=C2):
+    """The same shapes and value distributions in host memory, for the CPU legs (quants uniform
+    in [-127, 127], fp16 scales |N(0,1)| * 0.002)."""
+    rng = np.random.default_rng(seed)
+
+    def mat(k, m):
+        nb = k // 32
+        b = np.empty((m, nb, 34), dtype=np.uint8)
+        b[:, :, 2:] = rng.integers(-127, 128, size=(m, nb, 32), dtype=np.int8).view(np.uint8)
+        sc = (0.002 * np.abs(rng.standard_normal((m, nb)))).astype(np.float16)
+        b[:, :, :2] = sc.view(np.uint8).reshape(m, nb, 2)
+        return b.reshape(-1)
+
+    def vec(n, center, amp):
+        return (center + amp * rng.uniform(-1, 1, n)).astype(np.float32)
+
+    q, kv = c["n_head"] * c["head_dim"], c["n_head_kv"] * c["head_dim"]
+    w = {"tok_embd": mat(c["n_embd"], c["n_vocab"]), "output_norm": vec(c["n_embd"], 1.0, 0.1)}
+    w["output"] = w["tok_embd"]
+    w["layers"] = []
+    for _ in range(c["n_layer"]):
+        L = {"attn_norm": vec(c["n_embd"], 1.0, 0.1), "ffn_norm": vec(c["n_embd"], 1.0, 0.1),
+             "bq": vec(q, 0.0, 0.02), "bk": vec(kv, 0.0, 0.02), "bv": vec(kv, 0.0, 0.02)}
+        for name, k, m in c2_shapes(c):
+            L[name] = mat(k, m)
+        w["layers"].append(L)
+    return w
+
+
+def c2_cpu(budget_s: float, max_tokens: int, c=C2):
+    """The oracle's decode forward (oracle/decode_ref.py; matvecs on all host threads) over the
+    last positions of the context: (tok/s, tokens timed, threads)."""
+    from oracle import pyoracle as orc
+    from oracle.decode_ref import RefDecoder
+    ref = RefDecoder(c, c2_host_weights(7), mt=True)
+    n = c["n_ctx"]
+    max_tokens = max(1, min(max_tokens, n - 2))
+    tok = 1
+    tok = ref.step(tok, n - max_tokens - 1)[1]  # warm (page in the weights)
+    t0 = time.perf_counter()
+    done = 0
+    for p in range(n - max_tokens, n):
+        tok = ref.step(tok, p)[1]
+        done += 1
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, done, orc.lib(True).orc_threads()
+
+
+def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = c2_device_weights(ctx, ugb, torch, seed=1 + rank, c=c)
+    dec = ugb.Decoder(ctx, **c)
+    dec.bind(w["tok_embd"], w["output_norm"], w["output"], w["layers"])
+    n_ctx = c["n_ctx"]
+    stream = torch.cuda.Stream()
+    cap = torch.cuda.Stream()
+
+    # One token step captured once; each replay reads the previous step's greedy token and
+    # advances the position on the device (embedding kernel), so K replays decode K tokens.
+    dec.set_state(1, 0, stream)
+    graph = ctx.capture(lambda: dec.step(), cap)
+
+    def run(first_pos, count, tok=1):
+        """count replays starting at first_pos; re-seed the state when the context is full."""
+        pos = first_pos
+        dec.set_state(tok, pos, stream)
+        for _ in range(count):
+            if pos == n_ctx:
+                pos = 0
+                dec.set_state(tok, 0, stream)
+            graph.launch(stream)
+            pos += 1
+
+    K, W = args.steps, args.warmup
+    start = max(0, n_ctx - K)
+    warm_start = max(0, start - W)
+    run(warm_start, W)
+    stream.synchronize()
+    code, bits = ctx.status_read(stream)
+    assert code == ugb.OK, ("status after warm-up", code, bits)
+
+    # -- timed region: K tokens, device time by CUDA events on the launching stream --
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
+    barrier(world, torch)
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dec.set_state(1, start, stream)
+    e0.record(stream)
+    pos = start
+    for _ in range(K):
+        if pos == n_ctx:
+            pos = 0
+            dec.set_state(1, 0, stream)
+        graph.launch(stream)
+        pos += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world, torch)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    code, bits = ctx.status_read(stream)
+    assert code == ugb.OK, ("status after timing", code, bits)
+    ms_max = reduce_max(ms, world, torch)
+    timed_pos = [(start + i) % n_ctx for i in range(K)]
+    token_bytes = float(np.mean([c2_token_bytes(c, p + 1) for p in timed_pos]))
+
+    # -- dominant kernel: the fused gate/up matvec (17920 x 1536 Q8_0, the largest launch of a
+    # layer), all 28 layers' matrices back to back in one graph (each launch streams its own
+    # 29 MB from HBM), timed by CUDA events on the launching stream --
+    xq = ugb.alloc_q8act(c["n_embd"], 1, device=dev)
+    xv = torch.randn(c["n_embd"], device=dev)
+    ctx.quant_q8_1(xv, xq, c["n_embd"], 1)
+    gu = torch.empty(2 * c["n_ff"], dtype=torch.float32, device=dev)
+    rb = ugb.row_bytes(Q8_0, c["n_embd"])
+    ctx.set_pdl(True)
+    kgraph = ctx.capture(lambda: [ctx.matvec_multi(Q8_0, [L["w_gate"], L["w_up"]], [c["n_ff"], c["n_ff"]], rb,
+                                                   xq, gu, c["n_embd"], 1) for L in w["layers"]], cap)
+    ctx.set_pdl(False)
+    kgraph.launch(stream)
+    stream.synchronize()
+    reps = 8
+    e0.record(stream)
+    for _ in range(reps):
+        kgraph.launch(stream)
+    e1.record(stream)
+    stream.synchronize()
+    kern_ms = e0.elapsed_time(e1) / (reps * c["n_layer"])
+    kern_bytes = 2 * q8_bytes(c["n_embd"], c["n_ff"]) + xq.numel() + gu.numel() * 4
+
+    # -- end to end through the host-facing C-ABI call: ugb_decoder_token (host token and
+    # position in: H2D of the state; graph replay; D2H of the state and the status word) --
+    e2e_steps = min(max(K, 32), n_ctx)
+    tok = 1
+    for p in range(3):
+        tok = dec.token(tok, n_ctx - e2e_steps - 3 + p, stream)
+    t0 = time.perf_counter()
+    for p in range(n_ctx - e2e_steps, n_ctx):
+        tok = dec.token(tok, p, stream)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
+    dec.close()
+    graph.close()
+    kgraph.close()
+    return {
+        "value": world * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
+        "gpu_launches": c2_launches_per_token(c) * K,
+        "token_bytes": token_bytes,
+        "kernel_ms": kern_ms, "kernel_bytes": kern_bytes,
+        "e2e": {"value": world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": 16 + 4},
+    }
+
+
 # ---- workload c1 ----------------------------------------------------------------------------
+
+C1_K, C1_M = 1536, 8960
+C1_ROTATE = 24
 
 # Algorithmic bytes of one step (quant_act + linear): the Q8_0 weights once, the fp32
 # activation once and the fp32 output once (the 1.7 KB Q8_1 intermediate stays in L2).
@@ -222,20 +460,9 @@ def c1_cpu(samples: int, mt: bool = True):
     return C1_BYTES / dt / 1e9, lib.orc_threads() if mt else 1
 
 
-# ---- plumbing ---------------------------------------------------------------------------------
-
-def barrier(world, torch):
-    if world > 1:
-        torch.distributed.barrier()
 
 
-def reduce_max(v: float, world: int, torch) -> float:
-    if world == 1:
-        return v
-    t = torch.tensor([v], dtype=torch.float64, device="cuda")
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
-
+# ---- driver -----------------------------------------------------------------------------------
 
 def main():
     ap = argparse.ArgumentParser()
@@ -243,8 +470,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c1"], default="c1")
-    ap.add_argument("--cpu-samples", type=int, default=300)
+    ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -252,33 +479,46 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     hbm_peak, _, peak_kind = load_peaks()
-    config = {"workload": "c1: Q8_0 matvec 8960x1536 + block-32 activation quantisation",
-              "rows": C1_M, "k": C1_K, "weight_copies_rotated": C1_ROTATE,
-              "l2": "inputs larger than L2 (24 rotated weight copies, 351 MB)",
-              "parallelism": f"replicas x{world}"}
-    base = {"metric": "quant matvec HBM GB/s", "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32, fp32 scale",
-            "data": "synthetic (seeded; quants uniform, fp16 scales |N(0,1)|*0.002)",
-            "config": config}
+    if args.workload == "c2":
+        config = {"workload": "c2: greedy batch-1 decode, Qwen2.5-1.5B-shaped, all linear weights Q8_0",
+                  "layers": C2["n_layer"], "hidden": C2["n_embd"], "ffn": C2["n_ff"],
+                  "heads": f"{C2['n_head']}/{C2['n_head_kv']}x{C2['head_dim']}", "vocab": C2["n_vocab"],
+                  "context": C2["n_ctx"], "kv_cache": "fp32 (as the reference's, gpu_attention.cu:1)",
+                  "timed_positions": f"last {min(args.steps, C2['n_ctx'])} of {C2['n_ctx']}",
+                  "l2": "inputs larger than L2 (1.655 GB of weights per token)",
+                  "parallelism": f"replicas x{world}"}
+        base = {"metric": "decode tok/s", "unit": "tok/s", "dtype": "int8 x int8 -> int32 (Q8_0 x Q8_1), fp32 glue"}
+    else:
+        config = {"workload": "c1: Q8_0 matvec 8960x1536 + block-32 activation quantisation",
+                  "rows": C1_M, "k": C1_K, "weight_copies_rotated": C1_ROTATE,
+                  "l2": "inputs larger than L2 (24 rotated weight copies, 351 MB)",
+                  "parallelism": f"replicas x{world}"}
+        base = {"metric": "quant matvec HBM GB/s", "unit": "GB/s", "dtype": "int8 x int8 -> int32, fp32 scale"}
+    base.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                 "scaling": "weak", "vs_baseline": None,
+                 "data": "synthetic (seeded random-init weights; quants uniform, fp16 scales |N(0,1)|*0.002)",
+                 "config": config})
 
     if args.impl == "reference":
         if rank != 0:
             return
         t0 = time.perf_counter()
-        value, cores = c1_cpu(args.cpu_samples)
-        steps = args.steps
         line = dict(base)
-        line.update({"impl": "reference", "value": value, "n_gpus": world,
-                     "ms_per_step": C1_BYTES / value / 1e6,
-                     "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores,
-                                      "kind": "port",
-                                      "sample": f"{args.cpu_samples} steps of quant_act + Q8_0 matvec 8960x1536 "
-                                                f"(oracle/ugb_oracle.c, POSIX threads over rows)"},
-                     "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+        if args.workload == "c2":
+            value, done, cores = c2_cpu(max(30.0, args.cpu_seconds), args.steps)
+            sample = (f"{done} decode tokens at the last positions of the 512 context, oracle/decode_ref.py "
+                      f"(numpy glue, oracle/ugb_oracle.c matvecs on POSIX threads over rows)")
+            ms = 1e3 / value
+        else:
+            value, cores = c1_cpu(300)
+            sample = "300 steps of quant_act + Q8_0 matvec 8960x1536 (oracle/ugb_oracle.c, POSIX threads over rows)"
+            ms = C1_BYTES / value / 1e6
+        line.update({"impl": "reference", "value": value, "ms_per_step": ms,
+                     "cpu_baseline": {"value": value, "unit": base["unit"], "cores": cores, "kind": "port",
+                                      "sample": sample},
+                     "e2e": {"value": value, "unit": base["unit"], "h2d_bytes_per_step": 0,
                              "d2h_bytes_per_step": 0},
                      "wall_s": time.perf_counter() - t0})
-        line["steps"] = steps
         print(json.dumps(line))
         return
 
@@ -290,24 +530,39 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     ugb = importlib.import_module("uefi-gpu_b200")
     ctx = ugb.Context(torch.cuda.current_device())
-    res = c1_gpu(args, ugb, ctx, torch, rank, world)
+    if args.workload == "c2":
+        res = c2_gpu(args, ugb, ctx, torch, rank, world)
+        kernel = "mv_rows_kernel<Q8_0> (fused gate/up, 17920x1536)"
+        traffic = load_traffic("c2_gate_up")
+    else:
+        res = c1_gpu(args, ugb, ctx, torch, rank, world)
+        kernel = "mv_rows_kernel<Q8_0> (8960x1536)"
+        traffic = load_traffic("c1_matvec")
 
-    kern_bytes = res["kernel_bytes"]
-    achieved = kern_bytes / (res["kernel_ms"] / 1e3) / 1e9
+    achieved = res["kernel_bytes"] / (res["kernel_ms"] / 1e3) / 1e9
     line = dict(base)
     line.update({
         "value": res["value"], "ms_per_step": res["ms_per_step"],
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "peak_source": peak_kind,
-                     "kernel": "mv_rows_kernel<Q8_0>", "kernel_ms": res["kernel_ms"],
-                     "traffic": load_traffic("c1_matvec")},
+                     "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                     if peak_kind == "measured" else "fallback 6650 GB/s",
+                     "kernel": kernel, "kernel_ms": res["kernel_ms"], "bytes_per_launch": res["kernel_bytes"],
+                     "traffic": traffic},
         "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
     })
+    if "token_bytes" in res:
+        step_gbs = res["token_bytes"] / (res["ms_per_step"] / 1e3) / 1e9
+        line["roofline"]["step"] = {"bytes_per_token": res["token_bytes"], "achieved": step_gbs,
+                                    "frac": step_gbs / hbm_peak}
     if rank == 0 and world == 1:
-        v, cores = c1_cpu(max(20, args.cpu_samples // 3))
-        line["cpu_baseline"] = {"value": v, "unit": "GB/s", "cores": cores, "kind": "port",
-                                "sample": f"{max(20, args.cpu_samples // 3)} steps of quant_act + "
-                                          f"Q8_0 matvec 8960x1536 on the host cores"}
+        if args.workload == "c2":
+            v, done, cores = c2_cpu(args.cpu_seconds, 64)
+            sample = f"{done} decode tokens (oracle/decode_ref.py; matvecs on the host threads)"
+        else:
+            v, cores = c1_cpu(100)
+            sample = "100 steps of quant_act + Q8_0 matvec 8960x1536 on the host cores"
+        line["cpu_baseline"] = {"value": v, "unit": base["unit"], "cores": cores, "kind": "port",
+                                "sample": sample}
     if rank == 0:
         print(json.dumps(line))
     ctx.close()
