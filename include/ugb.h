@@ -248,6 +248,26 @@ ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
                       int64_t row_bytes, const float *x_host, float *y_host, int64_t k,
                       int64_t m);
 
+/* ugb_linear without any allocation: the same x -> quantise -> matvec -> y round trip, with
+ * its device scratch in a fixed 2,183,168-byte array compiled into the library.  No
+ * counterpart in the reference (whose firmware host owns fixed VRAM arenas); it is for
+ * callers that must not let a library allocate on their behalf -- hosts that plan device
+ * memory up front, or loops that cannot take the implicit synchronisation or late
+ * out-of-memory failure of a first-use cudaMalloc.
+ *   - k <= UGB_LINEAR_STATIC_MAX_K and m <= UGB_LINEAR_STATIC_MAX_M, else UGB_ESHAPE (the
+ *     reference's own Weights::linear caps, frontier_backend.rs:245-248).
+ *   - The first call on a device looks up the array's address (cudaGetSymbolAddress with that
+ *     device current); make that first call before any stream capture begins.
+ *   - Nothing needs to start at zero: every scratch byte a call reads it wrote first.
+ *   - One array per device, shared by all contexts and streams: calls on the same device
+ *     that overlap in time race on it.  The call is synchronous, so back-to-back calls from
+ *     one thread are safe. */
+#define UGB_LINEAR_STATIC_MAX_K 16384
+#define UGB_LINEAR_STATIC_MAX_M 524288
+ugb_status ugb_linear_static(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                             int64_t row_bytes, const float *x_host, float *y_host, int64_t k,
+                             int64_t m);
+
 #ifdef __cplusplus
 }
 #endif

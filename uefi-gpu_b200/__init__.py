@@ -19,6 +19,7 @@ LIB_PATH = os.path.join(HERE, "libugb.so")
 
 F32, Q8_0, Q3_K, Q4_K = 0, 8, 11, 12
 MAX_BATCH = 8
+LINEAR_STATIC_MAX_K, LINEAR_STATIC_MAX_M = 16384, 524288  # ugb_linear_static's fixed scratch
 
 STATUS = {0: "ok", 1: "shape", 2: "non-finite", 3: "timeout", 4: "backend", 5: "alignment",
           6: "quant kind", 7: "context"}
@@ -48,6 +49,7 @@ SIGNATURES = {
     "ugb_block_dots": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_fill_synthetic": (_int, [_vp, _vp, _u32, _vp, _i64, _i64, _u64]),
     "ugb_linear": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
+    "ugb_linear_static": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_set_pdl": (_int, [_vp, _int]),
     "ugb_decoder_create": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
     "ugb_decoder_destroy": (_int, [_vp]),
@@ -201,6 +203,16 @@ class Context:
         code = lib().ugb_linear(self.handle, _stream(stream), kind, _ptr(w), rb,
                                 x.ctypes.data, y.ctypes.data, k, m)
         check("ugb_linear", code)
+        return y
+
+    def linear_static(self, kind: int, w, rb: int, x_host, k: int, m: int, stream=None):
+        """ugb_linear with the library's fixed device scratch (no allocation)."""
+        import numpy as np
+        x = np.ascontiguousarray(x_host, dtype=np.float32)
+        y = np.empty(m, dtype=np.float32)
+        code = lib().ugb_linear_static(self.handle, _stream(stream), kind, _ptr(w), rb,
+                                       x.ctypes.data, y.ctypes.data, k, m)
+        check("ugb_linear_static", code)
         return y
 
 
