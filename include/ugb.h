@@ -166,6 +166,42 @@ ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out);
 ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream);
 ugb_status ugb_graph_destroy(ugb_graph *graph);
 
+/* ---- Q8 prefill (INT8 tensor-core GEMM) ------------------------------------------------- */
+
+/* Bytes of a packed prefill operand of `rows` rows (weight rows or tokens) of length k:
+ * ceil(rows/128) tiles x k/32 blocks x (4096 B of int8 quants in the tcgen05 canonical
+ * K-major layout + 512 B of f32 scales).  -1 if k is not a positive multiple of 32. */
+int64_t ugb_prefill_packed_bytes(int64_t rows, int64_t k);
+
+/* One-time lossless repack of an n x k Q8_0 matrix (GGUF rows) into the packed prefill
+ * layout: the same quants and exactly converted fp16 scales, re-laid out in 128-row tiles
+ * (prefill_repack / init_swizzle, gpu_prefill.cu:39-46, gpu_prefill.rs:58-94, which pack
+ * 16-row mma.sync fragments instead).  packed_dev: ugb_prefill_packed_bytes(n, k) bytes,
+ * 16-byte aligned. */
+ugb_status ugb_prefill_repack_q8_0(ugb_ctx *ctx, ugb_stream stream, const void *w_dev, int64_t n,
+                                   int64_t k, void *packed_dev);
+
+/* Token-batched block-32 activation quantisation of x_dev [m][k] (fp32, row-major) into the
+ * packed prefill layout (prefill_quant, gpu_prefill.cu:47-59; the arithmetic of quant_act).
+ * Non-finite inputs are quantised as 0 and reported in the status word. */
+ugb_status ugb_prefill_quant(ugb_ctx *ctx, ugb_stream stream, const float *x_dev, int64_t m,
+                             int64_t k, void *packed_dev);
+
+/* y_dev[t][r] (row stride ldy) = sum over 32-blocks b of (float)I_b * (dw[r][b] * dx[t][b]),
+ * I_b the exact int32 block dot, for t < m tokens and r < n weight rows
+ * (prefill_gemm, gpu_prefill.cu:10-36; p_gemm, gpu_prefill.rs:25-30).  tcgen05 INT8 MMA:
+ * each block's int32 tile lands in tensor memory and is rescaled into fp32 accumulators. */
+ugb_status ugb_prefill_gemm_q8_0(ugb_ctx *ctx, ugb_stream stream, const void *w_packed,
+                                 const void *x_packed, float *y_dev, int64_t m, int64_t n,
+                                 int64_t k, int64_t ldy);
+
+/* Test path of the same GEMM: also writes every int32 block dot, dots_dev[b][t][r]
+ * (k/32 x m x n int32), and y_dev with ldy = n.  Proves the tensor-core integer parts
+ * bit-exact. */
+ugb_status ugb_prefill_block_dots(ugb_ctx *ctx, ugb_stream stream, const void *w_packed,
+                                  const void *x_packed, int32_t *dots_dev, float *y_dev, int64_t m,
+                                  int64_t n, int64_t k);
+
 /* ---- decoder (the per-token graph around the matvecs) ------------------------------------ */
 
 /* Shape of a Qwen2-style decoder (configs 2 and 4).  The reference hard-codes the 1.5B shape

@@ -57,6 +57,9 @@ def _load(name: str) -> ctypes.CDLL:
     lib.orc_prefill_repack_q8_0.restype = ctypes.c_int
     lib.orc_prefill_repack_q8_0.argtypes = [_c_u8p, ctypes.c_long, ctypes.c_long, ctypes.c_long,
                                             _c_i8p, _c_f32p]
+    lib.orc_prefill_gemm_q8_0.restype = ctypes.c_int
+    lib.orc_prefill_gemm_q8_0.argtypes = [_c_u8p, ctypes.c_long, ctypes.c_long, _c_f32p, ctypes.c_long,
+                                          _c_f32p, ctypes.c_int]
     lib.orc_silu_mul.restype = ctypes.c_float
     lib.orc_silu_mul.argtypes = [ctypes.c_float, ctypes.c_float]
     return lib
@@ -183,3 +186,18 @@ def prefill_repack_q8_0(w: np.ndarray, n: int, k: int, n_pad: int):
 
 def silu_mul(g: float, u: float) -> float:
     return lib().orc_silu_mul(g, u)
+
+
+def prefill_gemm_q8_0(w: np.ndarray, n: int, k: int, x: np.ndarray, threads: int = 0) -> np.ndarray:
+    """y [m][n] of the Q8 prefill GEMM on GGUF Q8_0 rows w (n x k) and fp32 tokens x [m][k]."""
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    m = x.shape[0]
+    y = np.empty((m, n), dtype=np.float32)
+    mt = threads != 1
+    l = lib(mt)
+    nthr = threads if threads > 0 else (l.orc_threads() if mt else 1)
+    rc = l.orc_prefill_gemm_q8_0(_p(w, _c_u8p), n, k, _p(x, _c_f32p), m, _p(y, _c_f32p), nthr)
+    if rc < 0:
+        raise ValueError(f"orc_prefill_gemm_q8_0 rc={rc}")
+    return y

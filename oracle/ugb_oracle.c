@@ -420,3 +420,56 @@ int orc_prefill_repack_q8_0(const uint8_t *w, long n, long k, long n_pad, int8_t
 }
 
 float orc_silu_mul(float g, float u) { return (g / (1.0f + expf(-g))) * u; }
+
+/* ---- prefill GEMM -------------------------------------------------------------------------- */
+
+typedef struct {
+  const uint8_t *w;
+  const int8_t *q;
+  const float *d;
+  float *y;
+  long n, k, t0, t1;
+} pf_span;
+
+static void *pf_span_run(void *arg) {
+  const pf_span *s = (const pf_span *)arg;
+  long nb = s->k / 32;
+  for (long t = s->t0; t < s->t1; t++)
+    for (long r = 0; r < s->n; r++) {
+      float acc = 0.0f;
+      for (long b = 0; b < nb; b++) {
+        const uint8_t *p = s->w + (r * nb + b) * 34;
+        int32_t dot = 0;
+        for (int j = 0; j < 32; j++) dot += (int32_t)(int8_t)p[2 + j] * (int32_t)s->q[t * s->k + b * 32 + j];
+        /* gpu_prefill.cu:31-34: fmaf((float)c, d_w * d_x, acc) in block order */
+        acc = fmaf((float)dot, orc_half(rd16(p)) * s->d[t * nb + b], acc);
+      }
+      s->y[t * s->n + r] = acc;
+    }
+  return NULL;
+}
+
+int orc_prefill_gemm_q8_0(const uint8_t *w, long n, long k, const float *x, long m, float *y, int threads) {
+  if (n <= 0 || m <= 0 || k <= 0 || k % 32) return -1;
+  long nb = k / 32;
+  int8_t *q = (int8_t *)malloc((size_t)(m * k));
+  float *d = (float *)malloc((size_t)(m * nb) * sizeof(float));
+  int32_t *s = (int32_t *)malloc((size_t)(m * nb) * sizeof(int32_t));
+  if (!q || !d || !s) { free(q); free(d); free(s); return -2; }
+  int bad = 0;
+  for (long t = 0; t < m; t++) bad |= orc_quant_act(x + t * k, q + t * k, d + t * nb, s + t * nb, k);
+  if (threads < 1) threads = 1;
+  if (threads > 256) threads = 256;
+  if (threads > m) threads = (int)m;
+  pf_span spans[256];
+  pthread_t tids[256];
+  for (int i = 0; i < threads; i++) {
+    spans[i].w = w; spans[i].q = q; spans[i].d = d; spans[i].y = y; spans[i].n = n; spans[i].k = k;
+    spans[i].t0 = m * i / threads; spans[i].t1 = m * (i + 1) / threads;
+  }
+  for (int i = 1; i < threads; i++) pthread_create(&tids[i], NULL, pf_span_run, &spans[i]);
+  pf_span_run(&spans[0]);
+  for (int i = 1; i < threads; i++) pthread_join(tids[i], NULL);
+  free(q); free(d); free(s);
+  return bad;
+}

@@ -51,6 +51,11 @@ SIGNATURES = {
     "ugb_linear": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_linear_static": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_set_pdl": (_int, [_vp, _int]),
+    "ugb_prefill_packed_bytes": (_i64, [_i64, _i64]),
+    "ugb_prefill_repack_q8_0": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "ugb_prefill_quant": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
+    "ugb_prefill_gemm_q8_0": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64]),
+    "ugb_prefill_block_dots": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64]),
     "ugb_decoder_create": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
     "ugb_decoder_destroy": (_int, [_vp]),
     "ugb_decoder_bind": (_int, [_vp, _vp]),
@@ -194,6 +199,25 @@ class Context:
         check("ugb_graph_end", code)
         return Graph(h)
 
+    # ---- Q8 prefill ---------------------------------------------------------------------------
+    def prefill_repack_q8_0(self, w, n: int, k: int, packed, stream=None) -> None:
+        check("ugb_prefill_repack_q8_0", lib().ugb_prefill_repack_q8_0(self.handle, _stream(stream), _ptr(w),
+                                                                         n, k, _ptr(packed)))
+
+    def prefill_quant(self, x, m: int, k: int, packed, stream=None) -> None:
+        check("ugb_prefill_quant", lib().ugb_prefill_quant(self.handle, _stream(stream), _ptr(x), m, k,
+                                                             _ptr(packed)))
+
+    def prefill_gemm(self, w_packed, x_packed, y, m: int, n: int, k: int, ldy: int | None = None,
+                     stream=None) -> None:
+        check("ugb_prefill_gemm_q8_0", lib().ugb_prefill_gemm_q8_0(
+            self.handle, _stream(stream), _ptr(w_packed), _ptr(x_packed), _ptr(y), m, n, k,
+            n if ldy is None else ldy))
+
+    def prefill_block_dots(self, w_packed, x_packed, dots, y, m: int, n: int, k: int, stream=None) -> None:
+        check("ugb_prefill_block_dots", lib().ugb_prefill_block_dots(
+            self.handle, _stream(stream), _ptr(w_packed), _ptr(x_packed), _ptr(dots), _ptr(y), m, n, k))
+
     # ---- host-buffer entry points -----------------------------------------------------------
     def linear(self, kind: int, w, rb: int, x_host, k: int, m: int, stream=None):
         """Gpu::matvec / Weights::linear equivalent: numpy x in, numpy y out (synchronous)."""
@@ -214,6 +238,21 @@ class Context:
                                        x.ctypes.data, y.ctypes.data, k, m)
         check("ugb_linear_static", code)
         return y
+
+
+def prefill_packed_bytes(rows: int, k: int) -> int:
+    """Bytes of a packed prefill operand (ugb_prefill_packed_bytes)."""
+    v = lib().ugb_prefill_packed_bytes(rows, k)
+    if v < 0:
+        raise UgbError("ugb_prefill_packed_bytes", ESHAPE)
+    return v
+
+
+def alloc_prefill(rows: int, k: int, device=None):
+    """A 16-byte aligned device buffer for a packed prefill operand."""
+    import torch
+    n = prefill_packed_bytes(rows, k)
+    return torch.empty(n, dtype=torch.uint8, device=device or "cuda")
 
 
 class DecoderConfig(ctypes.Structure):

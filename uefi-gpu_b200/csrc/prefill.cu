@@ -1,0 +1,503 @@
+// prefill.cu -- Q8 prefill: the weight repack, the token-batched activation quantiser and the
+// INT8 tensor-core GEMM on tcgen05 (sm_100a).
+//
+// Reference: prefill_repack / prefill_quant / prefill_gemm (kernels/gpu_prefill.cu:10-59) and
+// their host emitters p_quant / p_gemm (gpu_prefill.rs:22-30).  The reference multiplies a
+// 16-row x 8-token x K32 mma.sync fragment per Q8_0 block and scales each block's int32 result
+// by dw * dx in fp32 (fmaf((float)dot, dw*dx, acc)).  The same arithmetic is kept here:
+//
+//   Y[t][n] = sum over blocks b of  fmaf((float)I_b[t][n], dw[n][b] * dx[t][b], acc)
+//   I_b[t][n] = sum_{i<32} qx[t][32b+i] * qw[n][32b+i]          (int32, exact)
+//
+// B200 form.  One CTA computes a 128-token x 128-row output tile:
+//   * warp 0 streams stages of 4 K-blocks (A: 128 x 128 B of activation quants, B: 128 x 128 B
+//     of weight quants, and both scale vectors) into a 4-deep shared-memory ring with 1-D bulk
+//     copies -- both operands were written by the repack / quant kernels directly in the UMMA
+//     canonical K-major layout, so no tensor map is needed;
+//   * warp 1 issues one tcgen05.mma.kind::i8 (M=128, N=128, K=32) per K-block into one of four
+//     TMEM accumulators (128 columns each, overwrite mode): every block's int32 dot lands alone;
+//   * warps 2..9 (two per TMEM lane quarter, 64 columns each) read each block's int32 tile with
+//     tcgen05.ld, scale it by dw*dx and accumulate in fp32 registers, then store the tile.
+// Per-block scales are why the accumulator cannot stay in TMEM across K: the fp32 rescale of
+// every 32-deep block is the bound of this kernel, not the tensor pipe.
+//
+// Operand layout in global memory (written by ugb_prefill_repack_q8_0 / ugb_prefill_quant):
+//   quants [tile][kblock][4096 B]: one 128-row x 32-byte K-block in the canonical no-swizzle
+//     K-major layout -- 16-byte core-matrix rows, offset(r, j) = (r/8)*256 + (j/16)*128 +
+//     (r%8)*16 + (j%16)  (LBO = 128 B between the two 16-byte K halves, SBO = 256 B between
+//     8-row groups);
+//   scales [tile][kblock][128] f32 (dw converted exactly from fp16; dx = amax/127).
+// Rows / tokens past the matrix are zero (quant 0, scale 0).
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.hpp"
+#include "prefill.hpp"
+
+namespace ugb {
+namespace {
+
+constexpr int kBM = kPrefillTile;         // tokens per tile (UMMA M, TMEM lanes)
+constexpr int kBN = kPrefillTile;         // weight rows per tile (UMMA N, TMEM columns)
+constexpr int kKB = 4;                    // K-blocks (of 32) per stage
+constexpr int kStages = 4;
+constexpr int kAcc = 4;                   // TMEM accumulators
+constexpr int kTmemCols = kAcc * kBN;     // 512: the whole TMEM of the SM
+constexpr int kTileBytes = kPrefillTileBytes;         // 4096: one 128 x 32 B operand block
+constexpr int kScaleBytes = kPrefillTile * 4;          // 512
+constexpr int kStageBytes = kKB * (2 * kTileBytes + 2 * kScaleBytes);  // 36,864
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 32 * (2 + kEpiWarps);    // 320
+constexpr int kGemmSmem = kStages * kStageBytes + 256; // ring + barriers / TMEM slot
+
+// ---- tcgen05 wrappers ------------------------------------------------------------------------
+
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (=|+=) A[smem desc] x B[smem desc]^T, int8 x int8 -> int32, one elected thread.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive once on the mbarrier when every tcgen05.mma this thread issued so far has completed.
+__device__ __forceinline__ void mma_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+               : "memory");
+}
+// 32 consecutive TMEM columns of this warp's 32 lanes, one 32-bit value per column.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of one 128 x 32-byte K-major operand block in the canonical
+// no-swizzle layout: start >> 4, LBO = 128 B (K halves), SBO = 256 B (8-row groups),
+// descriptor version 1 (sm_100), base offset 0, no swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
+         (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46);
+}
+// Instruction descriptor: D s32, A s8, B s8, both K-major, N = kBN, M = kBM.
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                            (static_cast<uint32_t>(kBM >> 4) << 24);
+
+// Byte offset of (row r, K byte j) inside one canonical 128 x 32-byte block.
+__host__ __device__ __forceinline__ uint32_t canon_off(int r, int j) {
+  return static_cast<uint32_t>((r >> 3) * 256 + (j >> 4) * 128 + (r & 7) * 16 + (j & 15));
+}
+
+// ---- repack: GGUF Q8_0 rows -> canonical K-major tiles -------------------------------------
+
+// One thread per (row, K-block, 16-byte half): 16 quant bytes to their canonical place, and
+// the block's fp16 scale converted exactly to f32 (prefill_repack, gpu_prefill.cu:39-46, is
+// the same lossless re-layout into its mma.sync fragment order).  Rows past n are zero.
+__global__ void __launch_bounds__(256) repack_q8_0_kernel(const uint8_t *__restrict__ w, int64_t n, int nb,
+                                                          int64_t n_tiles, uint8_t *__restrict__ q_out,
+                                                          float *__restrict__ s_out) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = n_tiles * kPrefillTile * nb * 2;
+  if (i >= total) return;
+  const int half = static_cast<int>(i & 1);
+  const int b = static_cast<int>((i >> 1) % nb);
+  const int64_t row = (i >> 1) / nb;
+  const int64_t tile = row / kPrefillTile;
+  const int r = static_cast<int>(row % kPrefillTile);
+  uint32_t v[4] = {0, 0, 0, 0};
+  float scale = 0.f;
+  if (row < n) {
+    const uint8_t *blk = w + (row * nb + b) * 34;
+    const uint8_t *p = blk + 2 + half * 16;  // 2-byte aligned: assemble words from bytes
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      v[k] = p[4 * k] | (static_cast<uint32_t>(p[4 * k + 1]) << 8) | (static_cast<uint32_t>(p[4 * k + 2]) << 16) |
+             (static_cast<uint32_t>(p[4 * k + 3]) << 24);
+    scale = half_bits_to_float(blk[0] | (static_cast<uint32_t>(blk[1]) << 8));
+  }
+  uint8_t *dst = q_out + (tile * nb + b) * kPrefillTileBytes + canon_off(r, half * 16);
+  *reinterpret_cast<uint4 *>(dst) = make_uint4(v[0], v[1], v[2], v[3]);
+  if (half == 0) s_out[(tile * nb + b) * kPrefillTile + r] = scale;
+}
+
+// ---- activation quant: fp32 tokens -> canonical K-major tiles ------------------------------
+
+// One warp per (token, K-block): the block-32 quantisation of quant_act (a = max|x|,
+// d = a/127, q = clamp(rint(x * 127/a), +-127)), written in the canonical tile layout with one
+// 32-bit store per four quants (prefill_quant, gpu_prefill.cu:47-59, writes the same values
+// into its 8-token records).  Tokens past m are zero.
+__global__ void __launch_bounds__(256) prefill_quant_kernel(const float *__restrict__ x, int64_t m, int64_t k,
+                                                            int64_t ldx, int64_t m_tiles,
+                                                            uint8_t *__restrict__ q_out, float *__restrict__ s_out,
+                                                            uint32_t *status) {
+  grid_dep_launch();
+  grid_dep_wait();
+  const int lane = threadIdx.x & 31;
+  const int nb = static_cast<int>(k / 32);
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (gw >= m_tiles * kPrefillTile * nb) return;
+  const int b = static_cast<int>(gw % nb);
+  const int64_t t = gw / nb;
+  const float val = t < m ? x[t * ldx + b * 32 + lane] : 0.f;
+  const bool fin = isfinite(val);
+  float a = fin ? fabsf(val) : 0.f;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+  const float inv = a > 0.f ? 127.0f / a : 0.0f;
+  int qi = fin ? __float2int_rn(val * inv) : 0;
+  qi = max(-127, min(127, qi));
+  // gather four consecutive quants into lane 4w's word
+  uint32_t word = static_cast<uint32_t>(qi) & 0xFFu;
+  word |= (__shfl_down_sync(0xffffffffu, static_cast<uint32_t>(qi) & 0xFFu, 1) << 8);
+  word |= (__shfl_down_sync(0xffffffffu, static_cast<uint32_t>(qi) & 0xFFu, 2) << 16);
+  word |= (__shfl_down_sync(0xffffffffu, static_cast<uint32_t>(qi) & 0xFFu, 3) << 24);
+  const int64_t tile = t / kPrefillTile;
+  const int r = static_cast<int>(t % kPrefillTile);
+  if ((lane & 3) == 0)
+    *reinterpret_cast<uint32_t *>(q_out + (tile * nb + b) * kPrefillTileBytes + canon_off(r, lane)) = word;
+  const bool bad = __any_sync(0xffffffffu, !fin);
+  if (lane == 0) {
+    s_out[(tile * nb + b) * kPrefillTile + r] = a / 127.0f;
+    if (bad) status_or(status, ST_NONFINITE_IN);
+  }
+}
+
+// ---- the GEMM ------------------------------------------------------------------------------
+
+struct GemmParams {
+  const uint8_t *aq;  // activation tiles  [m_tiles][nb][4096]
+  const float *as;    //                   [m_tiles][nb][128]
+  const uint8_t *bq;  // weight tiles      [n_tiles][nb][4096]
+  const float *bs;    //                   [n_tiles][nb][128]
+  float *y;           // [m][ldy]
+  int64_t ldy, m, n;
+  int nb;
+  int32_t *dots;      // optional [nb][m][n] int32 block dots (test path)
+  uint32_t *status;
+};
+
+// mbarrier wait that gives up after the wait limit or as soon as another role of the CTA has
+// given up (the shared abort flag), so a failure ends every role within one limit.
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int *abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - start > kWaitLimitNs) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *ctl = smem + kStages * kStageBytes;
+  uint64_t *full = reinterpret_cast<uint64_t *>(ctl);  // [kStages] bulk data landed
+  uint64_t *empty = full + kStages;                    // [kStages] MMAs done + scales read
+  uint64_t *tfull = empty + kStages;                   // [kAcc] block's int32 tile ready
+  uint64_t *tempty = tfull + kAcc;                     // [kAcc] tile read by the epilogue
+  uint64_t *drain = tempty + kAcc;                     // [1] final commit on abort
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t m_tile = blockIdx.x, n_tile = blockIdx.y;
+  const int nb = p.nb;
+  const int n_stages = (nb + kKB - 1) / kKB;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), kEpiWarps + 1);
+    }
+    for (int i = 0; i < kAcc; ++i) {
+      mbar_init(smem_u32(&tfull[i]), 1);
+      mbar_init(smem_u32(&tempty[i]), kEpiWarps);
+    }
+    mbar_init(smem_u32(drain), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  grid_dep_launch();
+
+  if (warp == 0) {
+    // ---- producer: one elected lane streams stages of kKB K-blocks ----
+    if (lane == 0) {
+      grid_dep_wait();  // the activation tiles come from the preceding quant kernel
+      const uint64_t pol = policy_evict_last();
+      const uint8_t *a_base = p.aq + m_tile * nb * kTileBytes;
+      const uint8_t *b_base = p.bq + n_tile * nb * kTileBytes;
+      const float *sa_base = p.as + m_tile * nb * kPrefillTile;
+      const float *sb_base = p.bs + n_tile * nb * kPrefillTile;
+      int issued = 0;
+      for (int s = 0; s < n_stages; ++s) {
+        const int slot = s % kStages;
+        if (s >= kStages && !wait_or_abort(smem_u32(&empty[slot]), ((s / kStages) - 1) & 1, abort_flag)) break;
+        const int b0 = s * kKB, nblk = min(kKB, nb - b0);
+        uint8_t *st = smem + slot * kStageBytes;
+        const uint32_t bar = smem_u32(&full[slot]);
+        mbar_arrive_expect_tx(bar, nblk * (2 * kTileBytes + 2 * kScaleBytes));
+        bulk_g2s(smem_u32(st), a_base + static_cast<int64_t>(b0) * kTileBytes, nblk * kTileBytes, bar, pol);
+        bulk_g2s(smem_u32(st + kKB * kTileBytes), b_base + static_cast<int64_t>(b0) * kTileBytes, nblk * kTileBytes,
+                 bar, pol);
+        bulk_g2s(smem_u32(st + 2 * kKB * kTileBytes), sa_base + static_cast<int64_t>(b0) * kPrefillTile,
+                 nblk * kScaleBytes, bar, pol);
+        bulk_g2s(smem_u32(st + 2 * kKB * kTileBytes + kKB * kScaleBytes),
+                 sb_base + static_cast<int64_t>(b0) * kPrefillTile, nblk * kScaleBytes, bar, pol);
+        issued = s + 1;
+      }
+      // Never leave with bulk copies in flight into this CTA's shared memory.
+      for (int s = max(0, issued - kStages); s < issued; ++s)
+        mbar_wait_bounded(smem_u32(&full[s % kStages]), (s / kStages) & 1);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer: one tcgen05.mma per K-block into accumulator b % kAcc ----
+    if (lane == 0) {
+      bool ok = true;
+      for (int b = 0; b < nb && ok; ++b) {
+        const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc;
+        if (kb == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
+        if (ok && b >= kAcc) ok = wait_or_abort(smem_u32(&tempty[j]), ((b / kAcc) - 1) & 1, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + slot * kStageBytes);
+        mma_i8(tmem_base + static_cast<uint32_t>(j * kBN), smem_desc(st + kb * kTileBytes),
+               smem_desc(st + kKB * kTileBytes + kb * kTileBytes), kIdesc, 0u);
+        mma_commit(smem_u32(&tfull[j]));
+        if (kb == kKB - 1 || b == nb - 1) mma_commit(smem_u32(&empty[slot]));
+      }
+      // The last stages' release phases (commit + epilogue arrivals) are waited here, so no
+      // commit arrival can land after the CTA has exited.
+      for (int s = max(0, n_stages - kStages); s < n_stages && ok; ++s)
+        ok = wait_or_abort(smem_u32(&empty[s % kStages]), (s / kStages) & 1, abort_flag);
+    }
+  } else {
+    // ---- epilogue: rescale every block's int32 tile into fp32 accumulators ----
+    const int q = warp & 3;                // TMEM lane quarter this warp may access
+    const int h = (warp - 2) >> 2;         // column half
+    const int t_local = q * 32 + lane;     // token row of the tile
+    const int c0 = h * (kBN / 2);          // first of this warp's 64 columns
+    const int64_t t = m_tile * kBM + t_local;
+    float acc[kBN / 2];
+#pragma unroll
+    for (int i = 0; i < kBN / 2; ++i) acc[i] = 0.f;
+    bool ok = true;
+    for (int b = 0; b < nb && ok; ++b) {
+      const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc;
+      if (kb == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
+      if (ok) ok = wait_or_abort(smem_u32(&tfull[j]), (b / kAcc) & 1, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const uint8_t *st = smem + slot * kStageBytes;
+      const float *sa = reinterpret_cast<const float *>(st + 2 * kKB * kTileBytes) + kb * kPrefillTile;
+      const float *sb = reinterpret_cast<const float *>(st + 2 * kKB * kTileBytes + kKB * kScaleBytes) +
+                        kb * kPrefillTile;
+      const float dx = sa[t_local];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * kBN + c0 + c * 32), r);
+        tmem_ld_wait();
+        if (p.dots) {
+          for (int i = 0; i < 32; ++i) {
+            const int64_t nn = n_tile * kBN + c0 + c * 32 + i;
+            if (t < p.m && nn < p.n) p.dots[(static_cast<int64_t>(b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float s_w = sb[c0 + c * 32 + i];  // same address across the warp: broadcast
+          acc[c * 32 + i] = fmaf(static_cast<float>(static_cast<int32_t>(r[i])), s_w * dx, acc[c * 32 + i]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&tempty[j]));
+        if (kb == kKB - 1 || b == nb - 1) mbar_arrive(smem_u32(&empty[slot]));
+      }
+    }
+    if (ok && t < p.m) {
+      float *yrow = p.y + t * p.ldy + n_tile * kBN + c0;
+      const int64_t n_left = p.n - (n_tile * kBN + c0);
+      if (n_left >= kBN / 2 && (reinterpret_cast<uintptr_t>(yrow) & 15) == 0) {
+#pragma unroll
+        for (int i = 0; i < kBN / 2; i += 4)
+          *reinterpret_cast<float4 *>(yrow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+      } else {
+        for (int i = 0; i < kBN / 2; ++i)
+          if (i < n_left) yrow[i] = acc[i];
+      }
+    }
+  }
+  // Every role has finished (or given up); no tcgen05 work of this CTA is in flight once the
+  // epilogue has consumed the last accumulator or the MMA thread has drained below.
+  __syncthreads();
+  if (warp == 1) {
+    if (*abort_flag && lane == 0) {
+      // drain: one more commit tracks every MMA issued so far; wait for it with the limit
+      mma_commit(smem_u32(drain));
+      mbar_wait_bounded(smem_u32(drain), 0);
+    }
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+  if (threadIdx.x == 0 && *abort_flag) status_or(p.status, ST_TIMEOUT);
+}
+
+}  // namespace
+
+// ---- host ------------------------------------------------------------------------------------
+
+ugb_status init_prefill_kernels(ugb_ctx *ctx) {
+  if (ctx->smem_optin < static_cast<size_t>(kGemmSmem)) return UGB_EBACKEND;
+  return cuda_status(cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+}
+
+namespace {
+
+struct Packed {
+  int64_t tiles = 0, nb = 0;
+  size_t q_bytes = 0, bytes = 0;
+};
+
+Packed packed_layout(int64_t rows, int64_t k) {
+  Packed p;
+  p.tiles = (rows + kPrefillTile - 1) / kPrefillTile;
+  p.nb = k / 32;
+  p.q_bytes = static_cast<size_t>(p.tiles * p.nb) * kPrefillTileBytes;
+  p.bytes = p.q_bytes + static_cast<size_t>(p.tiles * p.nb) * kPrefillTile * sizeof(float);
+  return p;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, const void *x_packed, float *y,
+                       int32_t *dots, int64_t m, int64_t n, int64_t k, int64_t ldy) {
+  if (!ctx || !ctx->status) return UGB_ECONTEXT;
+  if (m < 1 || n < 1 || k < 32 || k % 32 || ldy < n || k / 32 > (1 << 20)) return UGB_ESHAPE;
+  if (!w_packed || !x_packed || !y || !aligned16(w_packed) || !aligned16(x_packed)) return UGB_EALIGN;
+  const Packed pw = packed_layout(n, k), px = packed_layout(m, k);
+  if (pw.tiles > 65535) return UGB_ESHAPE;
+  GemmParams p;
+  p.aq = static_cast<const uint8_t *>(x_packed);
+  p.as = reinterpret_cast<const float *>(static_cast<const uint8_t *>(x_packed) + px.q_bytes);
+  p.bq = static_cast<const uint8_t *>(w_packed);
+  p.bs = reinterpret_cast<const float *>(static_cast<const uint8_t *>(w_packed) + pw.q_bytes);
+  p.y = y;
+  p.ldy = ldy;
+  p.m = m;
+  p.n = n;
+  p.nb = static_cast<int>(k / 32);
+  p.dots = dots;
+  p.status = ctx->status;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(px.tiles), static_cast<unsigned>(pw.tiles));
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = kGemmSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, prefill_gemm_kernel, p));
+}
+
+}  // namespace
+}  // namespace ugb
+
+using namespace ugb;
+
+extern "C" {
+
+int64_t ugb_prefill_packed_bytes(int64_t rows, int64_t k) {
+  if (rows < 1 || k < 32 || k % 32) return -1;
+  return static_cast<int64_t>(packed_layout(rows, k).bytes);
+}
+
+ugb_status ugb_prefill_repack_q8_0(ugb_ctx *ctx, ugb_stream stream, const void *w_dev, int64_t n, int64_t k,
+                                   void *packed_dev) {
+  if (!ctx || !ctx->status) return UGB_ECONTEXT;
+  if (n < 1 || k < 32 || k % 32) return UGB_ESHAPE;
+  if (!w_dev || !packed_dev || !aligned16(packed_dev)) return UGB_EALIGN;
+  const Packed pw = packed_layout(n, k);
+  uint8_t *q = static_cast<uint8_t *>(packed_dev);
+  const int64_t total = pw.tiles * kPrefillTile * pw.nb * 2;
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > 0x7fffffff) return UGB_ESHAPE;
+  repack_q8_0_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<const uint8_t *>(w_dev), n, static_cast<int>(pw.nb), pw.tiles, q,
+      reinterpret_cast<float *>(q + pw.q_bytes));
+  return cuda_status(cudaGetLastError());
+}
+
+ugb_status ugb_prefill_quant(ugb_ctx *ctx, ugb_stream stream, const float *x_dev, int64_t m, int64_t k,
+                             void *packed_dev) {
+  if (!ctx || !ctx->status) return UGB_ECONTEXT;
+  if (m < 1 || k < 32 || k % 32) return UGB_ESHAPE;
+  if (!x_dev || !packed_dev || !aligned16(packed_dev)) return UGB_EALIGN;
+  const Packed px = packed_layout(m, k);
+  uint8_t *q = static_cast<uint8_t *>(packed_dev);
+  const int64_t warps = px.tiles * kPrefillTile * px.nb;
+  const int64_t blocks = (warps + 7) / 8;
+  if (blocks > 0x7fffffff) return UGB_ESHAPE;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, prefill_quant_kernel, x_dev, m, k, k, px.tiles, q,
+                                        reinterpret_cast<float *>(q + px.q_bytes), ctx->status));
+}
+
+ugb_status ugb_prefill_gemm_q8_0(ugb_ctx *ctx, ugb_stream stream, const void *w_packed, const void *x_packed,
+                                 float *y_dev, int64_t m, int64_t n, int64_t k, int64_t ldy) {
+  return launch_gemm(ctx, stream, w_packed, x_packed, y_dev, nullptr, m, n, k, ldy);
+}
+
+ugb_status ugb_prefill_block_dots(ugb_ctx *ctx, ugb_stream stream, const void *w_packed, const void *x_packed,
+                                  int32_t *dots_dev, float *y_dev, int64_t m, int64_t n, int64_t k) {
+  if (!dots_dev) return UGB_EALIGN;
+  return launch_gemm(ctx, stream, w_packed, x_packed, y_dev, dots_dev, m, n, k, n);
+}
+
+}  // extern "C"
