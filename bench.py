@@ -12,6 +12,9 @@ Workloads:
       512-position context.  1.655 GB of weights stream from HBM per token (> L2).
   c1  Q8_0 matvec 8960x1536 with block-32 activation quantisation; weights
       rotate over 24 copies (350 MB > L2).
+  c3  the linear layers of a 512-token Q8 prefill of the same model (config 3): per layer the
+      fused Q/K/V, O, fused gate/up and down GEMMs, each a block-32 activation quant plus the
+      tcgen05 INT8 GEMM; weights repacked once outside timing (as the reference does).
 
 Multi-GPU: one process per GPU (torchrun), each an independent replica ("replicas only":
 batch-1 decode of a dense model has no exchange step worth sharding); value = all ranks'
@@ -462,6 +465,160 @@ def c1_cpu(samples: int, mt: bool = True):
 
 
 
+# ---- workload c3: Q8 prefill GEMMs of the 1.5B-shaped model -------------------------------
+
+C3_TOKENS = 512
+
+
+def c3_gemms(c=C2):
+    """(name, n rows, k) of the four prefill GEMMs of a layer: fused Q/K/V, O, fused gate/up,
+    down (the K and V rows are the 512 rows after the 1536 Q rows)."""
+    q, kv = c["n_head"] * c["head_dim"], c["n_head_kv"] * c["head_dim"]
+    return [("qkv", q + 2 * kv, c["n_embd"]), ("o", c["n_embd"], q),
+            ("gate_up", 2 * c["n_ff"], c["n_embd"]), ("down", c["n_embd"], c["n_ff"])]
+
+
+def c3_ops_per_step(c=C2, m=C3_TOKENS):
+    return c["n_layer"] * sum(2 * m * n * k for _, n, k in c3_gemms(c))
+
+
+def c3_gpu(args, ugb, ctx, torch, rank, world, c=C2, m=C3_TOKENS):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    gen = torch.Generator(device="cpu").manual_seed(11 + rank)
+    layers = []
+    for li in range(c["n_layer"]):
+        L = []
+        for gi, (name, n, k) in enumerate(c3_gemms(c)):
+            w = torch.empty(q8_bytes(k, n), dtype=torch.uint8, device=dev)
+            ctx.fill_synthetic(Q8_0, w, k, n, seed=7000 + 8 * li + gi)
+            wp = ugb.alloc_prefill(n, k, device=dev)
+            ctx.prefill_repack_q8_0(w, n, k, wp)  # one-time setup, outside timing (as the reference)
+            del w
+            x = torch.randn((m, k), generator=gen).to(dev)
+            L.append((name, n, k, wp, x, ugb.alloc_prefill(m, k, device=dev),
+                      torch.empty((m, n), dtype=torch.float32, device=dev)))
+        layers.append(L)
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    cap = torch.cuda.Stream()
+
+    def step():
+        for L in layers:
+            for _, n, k, wp, x, xp, y in L:
+                ctx.prefill_quant(x, m, k, xp)
+                ctx.prefill_gemm(wp, xp, y, m, n, k)
+
+    ctx.set_pdl(True)
+    graph = ctx.capture(step, cap)
+    ctx.set_pdl(False)
+    for _ in range(args.warmup):
+        graph.launch(stream)
+    stream.synchronize()
+    code, bits = ctx.status_read(stream)
+    assert code == ugb.OK, ("status after warm-up", code, bits)
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
+    barrier(world, torch)
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.launch(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world, torch)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    ms_max = reduce_max(ms, world, torch)
+
+    # dominant kernel: the fused gate/up GEMM (512 x 17920 x 1536), 28 layers back to back
+    gu = [L[2] for L in layers]
+    kgraph = ctx.capture(lambda: [ctx.prefill_gemm(wp, xp, y, m, n, k) for _, n, k, wp, x, xp, y in gu], cap)
+    kgraph.launch(stream)
+    stream.synchronize()
+    reps = 4
+    e0.record(stream)
+    for _ in range(reps):
+        kgraph.launch(stream)
+    e1.record(stream)
+    stream.synchronize()
+    kern_ms = e0.elapsed_time(e1) / (reps * len(gu))
+    _, n_gu, k_gu = c3_gemms(c)[2]
+    kern_ops = 2 * m * n_gu * k_gu
+
+    # measured INT8 tensor peak on this GPU: cuBLAS int8 GEMM 8192^3 (torch._int_mm), burst
+    a8 = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    b8 = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a8, b8)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(10):
+        torch._int_mm(a8, b8)
+    e1.record()
+    torch.cuda.synchronize()
+    int8_tops = 2 * 8192 ** 3 / (e0.elapsed_time(e1) / 10 / 1e3) / 1e12
+    del a8, b8
+
+    # end to end: the prompt's activations come from pinned host memory (the first GEMM input)
+    # and the last GEMM's output goes back, around one step
+    x0 = layers[0][0][4]
+    y_last = layers[-1][-1][6]
+    x_host = torch.empty(x0.shape, dtype=torch.float32).pin_memory()
+    x_host.copy_(x0.cpu())
+    y_host = torch.empty(y_last.shape, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, min(args.steps, 10))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            x0.copy_(x_host, non_blocking=True)
+        graph.launch(stream)
+        with torch.cuda.stream(stream):
+            y_host.copy_(y_last, non_blocking=True)
+        stream.synchronize()
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
+    code, bits = ctx.status_read(stream)
+    assert code == ugb.OK, ("status after timing", code, bits)
+    graph.close()
+    kgraph.close()
+    return {
+        "value": world * m * args.steps / (ms_max / 1e3), "ms_per_step": ms_max / args.steps, "clocks": clocks,
+        "gpu_launches": 2 * len(c3_gemms(c)) * c["n_layer"] * args.steps,
+        "kernel_ms": kern_ms, "kernel_ops": kern_ops, "int8_tops": int8_tops,
+        "e2e": {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": x0.numel() * 4,
+                "d2h_bytes_per_step": y_last.numel() * 4},
+    }
+
+
+def c3_cpu(budget_s: float, c=C2):
+    """The oracle's prefill GEMM (oracle/ugb_oracle.c, POSIX threads over tokens) on one layer's
+    four GEMMs for as many tokens as fit the budget; scaled to the 28 layers: (tok/s, tokens,
+    threads)."""
+    from oracle import pyoracle as orc
+    rng = np.random.default_rng(3)
+    mats = []
+    for _, n, k in c3_gemms(c):
+        nb = k // 32
+        b = np.empty((n, nb, 34), dtype=np.uint8)
+        b[:, :, 2:] = rng.integers(-127, 128, size=(n, nb, 32), dtype=np.int8).view(np.uint8)
+        b[:, :, :2] = (0.002 * np.abs(rng.standard_normal((n, nb)))).astype(np.float16).view(np.uint8).reshape(n, nb, 2)
+        mats.append((b.reshape(-1), n, k))
+    threads = orc.lib(True).orc_threads()
+    tokens = threads
+    while True:
+        xs = [rng.standard_normal((tokens, k)).astype(np.float32) for _, _, k in mats]
+        t0 = time.perf_counter()
+        for (w, n, k), x in zip(mats, xs):
+            orc.prefill_gemm_q8_0(w, n, k, x)
+        dt = time.perf_counter() - t0
+        if dt * 4 > budget_s or tokens >= C3_TOKENS:
+            break
+        tokens *= 2
+    return tokens / (dt * c["n_layer"]), tokens, threads
+
+
 # ---- driver -----------------------------------------------------------------------------------
 
 def main():
@@ -470,7 +627,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c1", "c3"], default="c2")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -488,6 +645,16 @@ def main():
                   "l2": "inputs larger than L2 (1.655 GB of weights per token)",
                   "parallelism": f"replicas x{world}"}
         base = {"metric": "decode tok/s", "unit": "tok/s", "dtype": "int8 x int8 -> int32 (Q8_0 x Q8_1), fp32 glue"}
+    elif args.workload == "c3":
+        config = {"workload": "c3: Q8 prefill GEMMs of the Qwen2.5-1.5B-shaped Q8_0 model, 512-token prompt",
+                  "tokens": C3_TOKENS, "layers": C2["n_layer"],
+                  "gemms_per_layer": "qkv 2048x1536, o 1536x1536, gate_up 17920x1536, down 1536x8960",
+                  "per_gemm": "block-32 activation quant + tcgen05 INT8 GEMM with per-block fp32 rescale",
+                  "excluded": "prefill attention, norms, SiLU and the head (outside the hot-path scope)",
+                  "l2": "inputs larger than L2 (1.4 GB of repacked weights per step)",
+                  "parallelism": f"replicas x{world}"}
+        base = {"metric": "prefill tok/s (linear layers)", "unit": "tok/s",
+                "dtype": "int8 x int8 -> int32 per 32-block (tcgen05 kind::i8), fp32 rescale"}
     else:
         config = {"workload": "c1: Q8_0 matvec 8960x1536 + block-32 activation quantisation",
                   "rows": C1_M, "k": C1_K, "weight_copies_rotated": C1_ROTATE,
@@ -509,6 +676,11 @@ def main():
             sample = (f"{done} decode tokens at the last positions of the 512 context, oracle/decode_ref.py "
                       f"(numpy glue, oracle/ugb_oracle.c matvecs on POSIX threads over rows)")
             ms = 1e3 / value
+        elif args.workload == "c3":
+            value, toks, cores = c3_cpu(max(30.0, args.cpu_seconds))
+            sample = (f"the four GEMMs of one layer for {toks} tokens (oracle/ugb_oracle.c prefill GEMM, POSIX "
+                      f"threads over tokens), scaled to 28 layers")
+            ms = C3_TOKENS / value * 1e3
         else:
             value, cores = c1_cpu(300)
             sample = "300 steps of quant_act + Q8_0 matvec 8960x1536 (oracle/ugb_oracle.c, POSIX threads over rows)"
@@ -534,20 +706,32 @@ def main():
         res = c2_gpu(args, ugb, ctx, torch, rank, world)
         kernel = "mv_rows_kernel<Q8_0> (fused gate/up, 17920x1536)"
         traffic = load_traffic("c2_gate_up")
+    elif args.workload == "c3":
+        res = c3_gpu(args, ugb, ctx, torch, rank, world)
+        kernel = "prefill_gemm_kernel<128> (fused gate/up, 512 x 17920 x 1536)"
+        traffic = load_traffic("c3_gate_up")
     else:
         res = c1_gpu(args, ugb, ctx, torch, rank, world)
         kernel = "mv_rows_kernel<Q8_0> (8960x1536)"
         traffic = load_traffic("c1_matvec")
 
-    achieved = res["kernel_bytes"] / (res["kernel_ms"] / 1e3) / 1e9
     line = dict(base)
+    if "kernel_ops" in res:
+        achieved = res["kernel_ops"] / (res["kernel_ms"] / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": achieved, "peak": res["int8_tops"], "unit": "TOPS (int8)",
+                "frac": achieved / res["int8_tops"],
+                "peak_source": "measured in this run: cuBLAS int8 GEMM 8192^3 (torch._int_mm), burst",
+                "kernel": kernel, "kernel_ms": res["kernel_ms"], "ops_per_launch": res["kernel_ops"],
+                "traffic": traffic}
+    else:
+        achieved = res["kernel_bytes"] / (res["kernel_ms"] / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
+                if peak_kind == "measured" else "fallback 6650 GB/s",
+                "kernel": kernel, "kernel_ms": res["kernel_ms"], "bytes_per_launch": res["kernel_bytes"],
+                "traffic": traffic}
     line.update({
-        "value": res["value"], "ms_per_step": res["ms_per_step"],
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                     if peak_kind == "measured" else "fallback 6650 GB/s",
-                     "kernel": kernel, "kernel_ms": res["kernel_ms"], "bytes_per_launch": res["kernel_bytes"],
-                     "traffic": traffic},
+        "value": res["value"], "ms_per_step": res["ms_per_step"], "roofline": roof,
         "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
     })
     if "token_bytes" in res:
@@ -558,6 +742,9 @@ def main():
         if args.workload == "c2":
             v, done, cores = c2_cpu(args.cpu_seconds, 64)
             sample = f"{done} decode tokens (oracle/decode_ref.py; matvecs on the host threads)"
+        elif args.workload == "c3":
+            v, toks, cores = c3_cpu(args.cpu_seconds)
+            sample = f"one layer's four GEMMs for {toks} tokens on the host threads, scaled to 28 layers"
         else:
             v, cores = c1_cpu(100)
             sample = "100 steps of quant_act + Q8_0 matvec 8960x1536 on the host cores"

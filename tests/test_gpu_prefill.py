@@ -8,7 +8,7 @@ the CPU oracle, through the C ABI.
 * y equals the oracle's fmaf((float)dot, dw*dx, acc) accumulation in block order bit for bit
   (same operations in the same order), and within 1e-3 per row in any case.
 Shapes: the config-3 matrices (K 1536 / 8960; N 2048 / 1536 / 17920) at reduced token counts,
-and ragged edges (tokens and rows not multiples of the 128-row tile, a single K-block, K
+both CTA widths (128-row tiles, and 64-row halves when 128-row tiling leaves SMs idle), and ragged edges (tokens and rows not multiples of the 128-row tile, a single K-block, K
 whose block count is not a multiple of the 4-block stage).
 """
 from __future__ import annotations
@@ -99,7 +99,7 @@ def test_prefill_quant_bit_exact(ctx, ugb, orc, m, k):
     assert not s[:, m:].any()
 
 
-@pytest.mark.parametrize("m,n,k", [(200, 300, 256), (128, 128, 32), (37, 256, 416)])
+@pytest.mark.parametrize("m,n,k", [(200, 300, 256), (128, 128, 32), (37, 256, 416), (256, 18944, 64)])
 def test_block_dots_bit_exact(ctx, ugb, orc, m, n, k):
     rng = np.random.default_rng(7 * m + n)
     x = rng.standard_normal((m, k)).astype(np.float32)

@@ -38,17 +38,28 @@ namespace ugb {
 namespace {
 
 constexpr int kBM = kPrefillTile;         // tokens per tile (UMMA M, TMEM lanes)
-constexpr int kBN = kPrefillTile;         // weight rows per tile (UMMA N, TMEM columns)
 constexpr int kKB = 4;                    // K-blocks (of 32) per stage
 constexpr int kStages = 4;
 constexpr int kAcc = 4;                   // TMEM accumulators
-constexpr int kTmemCols = kAcc * kBN;     // 512: the whole TMEM of the SM
 constexpr int kTileBytes = kPrefillTileBytes;         // 4096: one 128 x 32 B operand block
 constexpr int kScaleBytes = kPrefillTile * 4;          // 512
-constexpr int kStageBytes = kKB * (2 * kTileBytes + 2 * kScaleBytes);  // 36,864
 constexpr int kEpiWarps = 8;
 constexpr int kGemmThreads = 32 * (2 + kEpiWarps);    // 320
-constexpr int kGemmSmem = kStages * kStageBytes + 256; // ring + barriers / TMEM slot
+
+// Per output-tile width BN (weight rows per CTA, UMMA N): 128, or 64 for GEMMs whose 128-wide
+// tiling leaves SMs idle (a 64-row CTA reads one half of each packed 128-row weight block).
+template <int BN>
+struct Geo {
+  static constexpr int kBBytes = BN * 32;                                   // B operand per block
+  static constexpr int kStageBytes = kKB * (kTileBytes + kBBytes + kScaleBytes + BN * 4);
+  static constexpr int kSmem = kStages * kStageBytes + 256;                 // + barriers
+  static constexpr int kTmemCols = kAcc * BN;                               // 512 or 256
+  static constexpr int kCols = BN / 2;                                      // per epilogue warp
+  // Instruction descriptor: D s32, A s8, B s8, both K-major, N = BN, M = 128.
+  static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
+                                     (static_cast<uint32_t>(BN >> 3) << 17) |
+                                     (static_cast<uint32_t>(kBM >> 4) << 24);
+};
 
 // ---- tcgen05 wrappers ------------------------------------------------------------------------
 
@@ -102,9 +113,28 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
   return static_cast<uint64_t>((saddr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
          (static_cast<uint64_t>(256 >> 4) << 32) | (1ull << 46);
 }
-// Instruction descriptor: D s32, A s8, B s8, both K-major, N = kBN, M = kBM.
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
-                            (static_cast<uint32_t>(kBM >> 4) << 24);
+// Packed pairs of fp32 (sm_100 f32x2 arithmetic: two lanes of round-to-nearest fma / mul per
+// instruction, each lane rounding exactly as fmaf / fmul).
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 
 // Byte offset of (row r, K byte j) inside one canonical 128 x 32-byte block.
 __host__ __device__ __forceinline__ uint32_t canon_off(int r, int j) {
@@ -214,9 +244,11 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParams p) {
+  using G = Geo<BN>;
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t *ctl = smem + kStages * kStageBytes;
+  uint8_t *ctl = smem + kStages * G::kStageBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(ctl);  // [kStages] bulk data landed
   uint64_t *empty = full + kStages;                    // [kStages] MMAs done + scales read
   uint64_t *tfull = empty + kStages;                   // [kAcc] block's int32 tile ready
@@ -224,9 +256,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
   uint64_t *drain = tempty + kAcc;                     // [1] final commit on abort
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+  // stage layout: [A: kKB x 4096][B: kKB x BN*32][dx: kKB x 128 f32][dw: kKB x BN f32]
+  constexpr int kOffB = kKB * kTileBytes;
+  constexpr int kOffSA = kOffB + kKB * G::kBBytes;
+  constexpr int kOffSB = kOffSA + kKB * kScaleBytes;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t m_tile = blockIdx.x, n_tile = blockIdx.y;
+  const int64_t m_tile = blockIdx.x;
+  const int64_t n_col0 = static_cast<int64_t>(blockIdx.y) * BN;  // first output column
+  const int64_t w_tile = n_col0 / kPrefillTile;                  // packed 128-row weight tile
+  const int w_half = static_cast<int>((n_col0 % kPrefillTile) / BN);  // which BN rows of it
   const int nb = p.nb;
   const int n_stages = (nb + kKB - 1) / kKB;
 
@@ -244,7 +283,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_alloc(smem_u32(tmem_slot), G::kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -259,24 +298,31 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       grid_dep_wait();  // the activation tiles come from the preceding quant kernel
       const uint64_t pol = policy_evict_last();
       const uint8_t *a_base = p.aq + m_tile * nb * kTileBytes;
-      const uint8_t *b_base = p.bq + n_tile * nb * kTileBytes;
+      const uint8_t *b_base = p.bq + w_tile * nb * kTileBytes + w_half * G::kBBytes;
       const float *sa_base = p.as + m_tile * nb * kPrefillTile;
-      const float *sb_base = p.bs + n_tile * nb * kPrefillTile;
+      const float *sb_base = p.bs + w_tile * nb * kPrefillTile + w_half * BN;
       int issued = 0;
       for (int s = 0; s < n_stages; ++s) {
         const int slot = s % kStages;
         if (s >= kStages && !wait_or_abort(smem_u32(&empty[slot]), ((s / kStages) - 1) & 1, abort_flag)) break;
         const int b0 = s * kKB, nblk = min(kKB, nb - b0);
-        uint8_t *st = smem + slot * kStageBytes;
+        uint8_t *st = smem + slot * G::kStageBytes;
         const uint32_t bar = smem_u32(&full[slot]);
-        mbar_arrive_expect_tx(bar, nblk * (2 * kTileBytes + 2 * kScaleBytes));
+        mbar_arrive_expect_tx(bar, nblk * (kTileBytes + G::kBBytes + kScaleBytes + BN * 4));
         bulk_g2s(smem_u32(st), a_base + static_cast<int64_t>(b0) * kTileBytes, nblk * kTileBytes, bar, pol);
-        bulk_g2s(smem_u32(st + kKB * kTileBytes), b_base + static_cast<int64_t>(b0) * kTileBytes, nblk * kTileBytes,
-                 bar, pol);
-        bulk_g2s(smem_u32(st + 2 * kKB * kTileBytes), sa_base + static_cast<int64_t>(b0) * kPrefillTile,
-                 nblk * kScaleBytes, bar, pol);
-        bulk_g2s(smem_u32(st + 2 * kKB * kTileBytes + kKB * kScaleBytes),
-                 sb_base + static_cast<int64_t>(b0) * kPrefillTile, nblk * kScaleBytes, bar, pol);
+        bulk_g2s(smem_u32(st + kOffSA), sa_base + static_cast<int64_t>(b0) * kPrefillTile, nblk * kScaleBytes, bar,
+                 pol);
+        if (BN == kPrefillTile) {  // whole tiles: one copy per operand and stage
+          bulk_g2s(smem_u32(st + kOffB), b_base + static_cast<int64_t>(b0) * kTileBytes, nblk * kTileBytes, bar, pol);
+          bulk_g2s(smem_u32(st + kOffSB), sb_base + static_cast<int64_t>(b0) * kPrefillTile, nblk * BN * 4, bar, pol);
+        } else {                   // half tiles: rows [w_half*BN, +BN) of every block
+          for (int i = 0; i < nblk; ++i) {
+            bulk_g2s(smem_u32(st + kOffB + i * G::kBBytes), b_base + static_cast<int64_t>(b0 + i) * kTileBytes,
+                     G::kBBytes, bar, pol);
+            bulk_g2s(smem_u32(st + kOffSB + i * BN * 4), sb_base + static_cast<int64_t>(b0 + i) * kPrefillTile,
+                     BN * 4, bar, pol);
+          }
+        }
         issued = s + 1;
       }
       // Never leave with bulk copies in flight into this CTA's shared memory.
@@ -293,9 +339,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
         if (ok && b >= kAcc) ok = wait_or_abort(smem_u32(&tempty[j]), ((b / kAcc) - 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + slot * kStageBytes);
-        mma_i8(tmem_base + static_cast<uint32_t>(j * kBN), smem_desc(st + kb * kTileBytes),
-               smem_desc(st + kKB * kTileBytes + kb * kTileBytes), kIdesc, 0u);
+        const uint32_t st = smem_u32(smem + slot * G::kStageBytes);
+        mma_i8(tmem_base + static_cast<uint32_t>(j * BN), smem_desc(st + kb * kTileBytes),
+               smem_desc(st + kOffB + kb * G::kBBytes), G::kIdesc, 0u);
         mma_commit(smem_u32(&tfull[j]));
         if (kb == kKB - 1 || b == nb - 1) mma_commit(smem_u32(&empty[slot]));
       }
@@ -306,14 +352,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     }
   } else {
     // ---- epilogue: rescale every block's int32 tile into fp32 accumulators ----
+    constexpr int kC = G::kCols;           // columns of this warp (64 or 32)
     const int q = warp & 3;                // TMEM lane quarter this warp may access
     const int h = (warp - 2) >> 2;         // column half
     const int t_local = q * 32 + lane;     // token row of the tile
-    const int c0 = h * (kBN / 2);          // first of this warp's 64 columns
+    const int c0 = h * kC;                 // first column of this warp
     const int64_t t = m_tile * kBM + t_local;
-    float acc[kBN / 2];
+    uint64_t acc[kC / 2];                  // pairs of fp32 accumulators
 #pragma unroll
-    for (int i = 0; i < kBN / 2; ++i) acc[i] = 0.f;
+    for (int i = 0; i < kC / 2; ++i) acc[i] = 0ull;
     bool ok = true;
     for (int b = 0; b < nb && ok; ++b) {
       const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc;
@@ -321,26 +368,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       if (ok) ok = wait_or_abort(smem_u32(&tfull[j]), (b / kAcc) & 1, abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint8_t *st = smem + slot * kStageBytes;
-      const float *sa = reinterpret_cast<const float *>(st + 2 * kKB * kTileBytes) + kb * kPrefillTile;
-      const float *sb = reinterpret_cast<const float *>(st + 2 * kKB * kTileBytes + kKB * kScaleBytes) +
-                        kb * kPrefillTile;
-      const float dx = sa[t_local];
+      const uint8_t *st = smem + slot * G::kStageBytes;
+      const float dx = reinterpret_cast<const float *>(st + kOffSA)[kb * kPrefillTile + t_local];
+      const float4 *dw4 = reinterpret_cast<const float4 *>(st + kOffSB + (kb * BN + c0) * 4);
+      const uint64_t dx2 = pk2(dx, dx);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+      for (int c = 0; c < kC / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * kBN + c0 + c * 32), r);
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * BN + c0 + c * 32), r);
         tmem_ld_wait();
         if (p.dots) {
           for (int i = 0; i < 32; ++i) {
-            const int64_t nn = n_tile * kBN + c0 + c * 32 + i;
+            const int64_t nn = n_col0 + c0 + c * 32 + i;
             if (t < p.m && nn < p.n) p.dots[(static_cast<int64_t>(b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
           }
         }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float s_w = sb[c0 + c * 32 + i];  // same address across the warp: broadcast
-          acc[c * 32 + i] = fmaf(static_cast<float>(static_cast<int32_t>(r[i])), s_w * dx, acc[c * 32 + i]);
+        for (int i = 0; i < 32; i += 4) {
+          const float4 w = dw4[(c * 32 + i) / 4];  // same address across the warp: broadcast
+          // fmaf((float)I, dw * dx, acc) per lane, two columns per instruction
+          const uint64_t s01 = mul2(pk2(w.x, w.y), dx2), s23 = mul2(pk2(w.z, w.w), dx2);
+          const uint64_t f01 = pk2(static_cast<float>(static_cast<int32_t>(r[i])),
+                                   static_cast<float>(static_cast<int32_t>(r[i + 1])));
+          const uint64_t f23 = pk2(static_cast<float>(static_cast<int32_t>(r[i + 2])),
+                                   static_cast<float>(static_cast<int32_t>(r[i + 3])));
+          acc[(c * 32 + i) / 2] = fma2(f01, s01, acc[(c * 32 + i) / 2]);
+          acc[(c * 32 + i) / 2 + 1] = fma2(f23, s23, acc[(c * 32 + i) / 2 + 1]);
         }
       }
       tc_fence_before();
@@ -351,30 +404,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       }
     }
     if (ok && t < p.m) {
-      float *yrow = p.y + t * p.ldy + n_tile * kBN + c0;
-      const int64_t n_left = p.n - (n_tile * kBN + c0);
-      if (n_left >= kBN / 2 && (reinterpret_cast<uintptr_t>(yrow) & 15) == 0) {
+      float *yrow = p.y + t * p.ldy + n_col0 + c0;
+      const int64_t n_left = p.n - (n_col0 + c0);
+      if (n_left >= kC && (reinterpret_cast<uintptr_t>(yrow) & 15) == 0) {
 #pragma unroll
-        for (int i = 0; i < kBN / 2; i += 4)
-          *reinterpret_cast<float4 *>(yrow + i) = make_float4(acc[i], acc[i + 1], acc[i + 2], acc[i + 3]);
+        for (int i = 0; i < kC / 2; i += 2) {
+          const float2 a0 = upk2(acc[i]), a1 = upk2(acc[i + 1]);
+          *reinterpret_cast<float4 *>(yrow + 2 * i) = make_float4(a0.x, a0.y, a1.x, a1.y);
+        }
       } else {
-        for (int i = 0; i < kBN / 2; ++i)
-          if (i < n_left) yrow[i] = acc[i];
+#pragma unroll
+        for (int i = 0; i < kC / 2; ++i) {
+          const float2 a = upk2(acc[i]);
+          if (2 * i < n_left) yrow[2 * i] = a.x;
+          if (2 * i + 1 < n_left) yrow[2 * i + 1] = a.y;
+        }
       }
     }
   }
-  // Every role has finished (or given up); no tcgen05 work of this CTA is in flight once the
-  // epilogue has consumed the last accumulator or the MMA thread has drained below.
+  // Every role has finished (or given up).  In the normal path every MMA was consumed by the
+  // epilogue; after an abort the MMA thread drains the tensor pipe before TMEM is freed.
   __syncthreads();
   if (warp == 1) {
     if (*abort_flag && lane == 0) {
-      // drain: one more commit tracks every MMA issued so far; wait for it with the limit
       mma_commit(smem_u32(drain));
       mbar_wait_bounded(smem_u32(drain), 0);
     }
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, G::kTmemCols);
   }
   if (threadIdx.x == 0 && *abort_flag) status_or(p.status, ST_TIMEOUT);
 }
@@ -384,8 +442,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
 // ---- host ------------------------------------------------------------------------------------
 
 ugb_status init_prefill_kernels(ugb_ctx *ctx) {
-  if (ctx->smem_optin < static_cast<size_t>(kGemmSmem)) return UGB_EBACKEND;
-  return cuda_status(cudaFuncSetAttribute(prefill_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  if (ctx->smem_optin < static_cast<size_t>(Geo<128>::kSmem)) return UGB_EBACKEND;
+  ugb_status st = cuda_status(
+      cudaFuncSetAttribute(prefill_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<128>::kSmem));
+  if (st != UGB_OK) return st;
+  return cuda_status(
+      cudaFuncSetAttribute(prefill_gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<64>::kSmem));
 }
 
 namespace {
@@ -412,7 +474,7 @@ ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, 
   if (m < 1 || n < 1 || k < 32 || k % 32 || ldy < n || k / 32 > (1 << 20)) return UGB_ESHAPE;
   if (!w_packed || !x_packed || !y || !aligned16(w_packed) || !aligned16(x_packed)) return UGB_EALIGN;
   const Packed pw = packed_layout(n, k), px = packed_layout(m, k);
-  if (pw.tiles > 65535) return UGB_ESHAPE;
+  if (2 * pw.tiles > 65535) return UGB_ESHAPE;
   GemmParams p;
   p.aq = static_cast<const uint8_t *>(x_packed);
   p.as = reinterpret_cast<const float *>(static_cast<const uint8_t *>(x_packed) + px.q_bytes);
@@ -425,17 +487,20 @@ ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, 
   p.nb = static_cast<int>(k / 32);
   p.dots = dots;
   p.status = ctx->status;
+  // 64-row CTAs when 128-row tiles would leave SMs idle (twice the CTAs, same packed layout)
+  const bool narrow = px.tiles * pw.tiles < ctx->sm_count;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(px.tiles), static_cast<unsigned>(pw.tiles));
+  cfg.gridDim = dim3(static_cast<unsigned>(px.tiles), static_cast<unsigned>(narrow ? 2 * pw.tiles : pw.tiles));
   cfg.blockDim = dim3(kGemmThreads);
-  cfg.dynamicSmemBytes = kGemmSmem;
+  cfg.dynamicSmemBytes = narrow ? Geo<64>::kSmem : Geo<128>::kSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, prefill_gemm_kernel, p));
+  return cuda_status(narrow ? cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<64>, p)
+                            : cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<128>, p));
 }
 
 }  // namespace
