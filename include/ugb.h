@@ -166,6 +166,71 @@ ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out);
 ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream);
 ugb_status ugb_graph_destroy(ugb_graph *graph);
 
+/* ---- MoE expert path ----------------------------------------------------------------------- */
+
+/* One independent matvec job: the 48-byte little-endian layout of the reference's
+ * FrontierJob / Dispatch descriptor (frontier_quant.cu:71-78, frontier_dispatch.rs:9-31).
+ * Here `input` is a Q8_1 activation (ugb_q8act layout for k = n and the call's batch) instead
+ * of fp32, and `output` receives [batch][m] fp32.  first_row / padding are ignored: the
+ * library assigns CTAs to jobs itself. */
+typedef struct ugb_job {
+  uint64_t weights, input, output; /* device pointers */
+  uint32_t kind, n, m, row_bytes;
+  uint32_t first_row, padding;
+} ugb_job;
+#define UGB_MAX_JOBS 32
+
+/* Up to UGB_MAX_JOBS matvecs in as few launches as possible (one per (kind, n) group); each
+ * job streams its own matrix against its own activation (frontier_multi_matvec,
+ * frontier_quant.cu:79-93).  As the reference's packer, rejects empty or oversized jobs,
+ * inconsistent row_bytes and overlapping outputs (UGB_ESHAPE).  jobs is a host array. */
+ugb_status ugb_matvec_jobs(ugb_ctx *ctx, ugb_stream stream, const ugb_job *jobs, int count,
+                           int64_t batch);
+
+/* Router: per token, softmax over n_expert logits (frontier_forward.rs:47-51), the top_k
+ * experts by descending probability with ties to the lower id (:167), and weights
+ * p / (sum of the top_k p in rank order) (:168, :193).  logits [batch][n_expert] fp32 ->
+ * ids [batch][top_k] int32, weights [batch][top_k] fp32, all device memory.  A token with a
+ * non-finite logit gets ids -1 and sets the non-finite status bit.  n_expert <= 4096,
+ * top_k <= 32. */
+ugb_status ugb_moe_route(ugb_ctx *ctx, ugb_stream stream, const float *logits_dev, int64_t n_expert,
+                         int64_t top_k, int64_t batch, int32_t *ids_dev, float *weights_dev);
+
+/* out[t] (= or, with accumulate, +=) sum over ranks r of weights[t][r] * values[t][r] in rank
+ * order with a separate fp32 multiply and add (frontier_forward.rs:193-195,
+ * frontier_cpu_axpy.rs:13-21).  Ranks whose id is outside [expert0, expert0 + n_local) are
+ * left out (expert parallelism: another device adds them). */
+ugb_status ugb_moe_combine(ugb_ctx *ctx, ugb_stream stream, const float *values_dev,
+                           const float *weights_dev, const int32_t *ids_dev, int64_t top_k,
+                           int64_t d, int64_t batch, int64_t expert0, int64_t n_local,
+                           int accumulate, float *out_dev);
+
+/* The routed expert SwiGLU of one MoE layer, device-resident (Forward::ffn's expert part,
+ * frontier_forward.rs:169-195): for every (token, rank) slot whose expert this device holds,
+ * h = silu(gate_e x) * up_e x, value = down_e h, and out[t] (+)= sum of weight * value.
+ * gate / up / down are the stacked GGUF expert tensors ([n_expert][rows][row_bytes]: gate and
+ * up ffn rows of length hidden, down hidden rows of length ffn) of global experts
+ * [expert0, expert0 + n_expert).  xq: Q8_1 of the batch tokens (length hidden). */
+typedef struct ugb_moe_args {
+  uint32_t kind;                 /* expert quant kind (UGB_Q3_K in config 5) */
+  int32_t accumulate;            /* 0: out = sum; 1: out += sum */
+  int64_t hidden, ffn, top_k, batch;
+  int64_t n_expert, expert0, n_expert_total;
+  const void *gate, *up, *down;  /* device, 16-byte aligned */
+  const void *xq;                /* device Q8_1 [batch] */
+  const int32_t *ids;            /* device [batch][top_k] global expert ids (ugb_moe_route) */
+  const float *weights;          /* device [batch][top_k] */
+  float *out;                    /* device [batch][hidden] */
+  void *workspace;               /* device, 256-byte aligned, >= ugb_moe_workspace_bytes() */
+  size_t workspace_bytes;
+} ugb_moe_args;
+/* Workspace of ugb_moe_experts, slots = batch * top_k, regions in this order, each starting
+ * 256-byte aligned: gate/up outputs f32 [slots][2 * ffn]; the SiLU outputs as Q8_1 (ugb_q8act
+ * layout for k = ffn, batch = slots); the expert outputs f32 [slots][hidden].  Slots routed to
+ * another device's experts are left unwritten. */
+size_t ugb_moe_workspace_bytes(int64_t hidden, int64_t ffn, int64_t top_k, int64_t batch);
+ugb_status ugb_moe_experts(ugb_ctx *ctx, ugb_stream stream, const ugb_moe_args *args);
+
 /* ---- Q8 prefill (INT8 tensor-core GEMM) ------------------------------------------------- */
 
 /* Bytes of a packed prefill operand of `rows` rows (weight rows or tokens) of length k:

@@ -51,6 +51,11 @@ SIGNATURES = {
     "ugb_linear": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_linear_static": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
     "ugb_set_pdl": (_int, [_vp, _int]),
+    "ugb_matvec_jobs": (_int, [_vp, _vp, _vp, _int, _i64]),
+    "ugb_moe_route": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
+    "ugb_moe_combine": (_int, [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _int, _vp]),
+    "ugb_moe_workspace_bytes": (ctypes.c_size_t, [_i64, _i64, _i64, _i64]),
+    "ugb_moe_experts": (_int, [_vp, _vp, _vp]),
     "ugb_prefill_packed_bytes": (_i64, [_i64, _i64]),
     "ugb_prefill_repack_q8_0": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
     "ugb_prefill_quant": (_int, [_vp, _vp, _vp, _i64, _i64, _vp]),
@@ -199,6 +204,26 @@ class Context:
         check("ugb_graph_end", code)
         return Graph(h)
 
+    # ---- MoE ----------------------------------------------------------------------------------
+    def matvec_jobs(self, jobs, batch: int = 1, stream=None) -> None:
+        """jobs: list of Job (device pointers)."""
+        arr = (Job * len(jobs))(*jobs)
+        check("ugb_matvec_jobs", lib().ugb_matvec_jobs(self.handle, _stream(stream), ctypes.cast(arr, _vp),
+                                                         len(jobs), batch))
+
+    def moe_route(self, logits, n_expert: int, top_k: int, batch: int, ids, weights, stream=None) -> None:
+        check("ugb_moe_route", lib().ugb_moe_route(self.handle, _stream(stream), _ptr(logits), n_expert, top_k,
+                                                     batch, _ptr(ids), _ptr(weights)))
+
+    def moe_combine(self, values, weights, ids, top_k: int, d: int, batch: int, out, expert0: int = 0,
+                    n_local: int = 1 << 30, accumulate: bool = False, stream=None) -> None:
+        check("ugb_moe_combine", lib().ugb_moe_combine(self.handle, _stream(stream), _ptr(values), _ptr(weights),
+                                                         _ptr(ids), top_k, d, batch, expert0, n_local,
+                                                         int(accumulate), _ptr(out)))
+
+    def moe_experts(self, args: "MoeArgs", stream=None) -> None:
+        check("ugb_moe_experts", lib().ugb_moe_experts(self.handle, _stream(stream), ctypes.byref(args)))
+
     # ---- Q8 prefill ---------------------------------------------------------------------------
     def prefill_repack_q8_0(self, w, n: int, k: int, packed, stream=None) -> None:
         check("ugb_prefill_repack_q8_0", lib().ugb_prefill_repack_q8_0(self.handle, _stream(stream), _ptr(w),
@@ -238,6 +263,39 @@ class Context:
                                        x.ctypes.data, y.ctypes.data, k, m)
         check("ugb_linear_static", code)
         return y
+
+
+class Job(ctypes.Structure):
+    """ugb_job: the 48-byte FrontierJob descriptor layout."""
+    _fields_ = [("weights", ctypes.c_uint64), ("input", ctypes.c_uint64), ("output", ctypes.c_uint64),
+                ("kind", ctypes.c_uint32), ("n", ctypes.c_uint32), ("m", ctypes.c_uint32),
+                ("row_bytes", ctypes.c_uint32), ("first_row", ctypes.c_uint32), ("padding", ctypes.c_uint32)]
+
+
+assert ctypes.sizeof(Job) == 48
+
+
+class MoeArgs(ctypes.Structure):
+    """ugb_moe_args."""
+    _fields_ = [("kind", ctypes.c_uint32), ("accumulate", ctypes.c_int32),
+                ("hidden", ctypes.c_int64), ("ffn", ctypes.c_int64), ("top_k", ctypes.c_int64),
+                ("batch", ctypes.c_int64), ("n_expert", ctypes.c_int64), ("expert0", ctypes.c_int64),
+                ("n_expert_total", ctypes.c_int64), ("gate", _vp), ("up", _vp), ("down", _vp), ("xq", _vp),
+                ("ids", _vp), ("weights", _vp), ("out", _vp), ("workspace", _vp),
+                ("workspace_bytes", ctypes.c_size_t)]
+
+
+def moe_workspace_bytes(hidden: int, ffn: int, top_k: int, batch: int) -> int:
+    return lib().ugb_moe_workspace_bytes(hidden, ffn, top_k, batch)
+
+
+def moe_workspace_layout(hidden: int, ffn: int, top_k: int, batch: int) -> dict:
+    """Offsets of the ugb_moe_experts workspace regions (as include/ugb.h documents them)."""
+    slots = top_k * batch
+    rup = lambda v: (v + 255) // 256 * 256
+    hq = rup(slots * 2 * ffn * 4)
+    hq_bytes = q8act_bytes(ffn, slots)
+    return {"slots": slots, "gu": 0, "hq": hq, "values": hq + rup(hq_bytes)}
 
 
 def prefill_packed_bytes(rows: int, k: int) -> int:

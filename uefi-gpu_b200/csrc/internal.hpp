@@ -33,12 +33,14 @@ struct Q8Act {
 };
 Q8Act q8act_layout(int64_t k, int64_t batch);
 
+constexpr int kMaxMatvecSegs = 32;  // matrices (segments or jobs) of one matvec launch
+
 // Streaming matvec launch description.
 struct MatvecArgs {
   uint32_t kind = 0;
   const uint8_t *w = nullptr;    // single matrix (nseg == 0), or:
-  const uint8_t *ws[4] = {};     // up to 4 matrices of seg_rows[i] rows, y rows concatenated
-  int64_t seg_rows[4] = {};
+  const uint8_t *ws[kMaxMatvecSegs] = {};  // matrices of seg_rows[i] rows, y rows concatenated
+  int64_t seg_rows[kMaxMatvecSegs] = {};
   int nseg = 0;
   int64_t row_bytes = 0, k = 0, m = 0;
   const uint8_t *xq = nullptr;   // Q8_1 buffer
@@ -48,6 +50,21 @@ struct MatvecArgs {
   int64_t batch = 1;
   int32_t *dots = nullptr;       // debug: block dots instead of y
   bool pdl = false;              // launch with programmatic stream serialisation
+  // Job table (njobs > 0): job i = matrix ws[i] of seg_rows[i] rows with its own Q8_1
+  // activation jx[i] (layout xl, `batch` vectors) and output jy[i] ([batch][seg_rows[i]]).
+  int njobs = 0;
+  const uint8_t *jx[kMaxMatvecSegs] = {};
+  float *jy[kMaxMatvecSegs] = {};
+  // Routed experts (ids set; batch 1): slot s < n_slots, matrix i < per_slot uses expert
+  // ids[s] of the stacked tensor ebase[i] (n_expert experts of m rows, estride bytes apart,
+  // global ids from expert0; other ids < n_total are another device's and are skipped),
+  // activation vector s / x_div of xq (layout xl) and writes y + s * y_slot + i * m.
+  const int32_t *ids = nullptr;
+  int n_slots = 0, per_slot = 1, n_expert = 0, x_div = 1;
+  int expert0 = 0, n_total = 0;  // held experts are global ids [expert0, expert0 + n_expert)
+  const uint8_t *ebase[2] = {};
+  uint64_t estride = 0;
+  int64_t y_slot = 0;
 };
 
 ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a);

@@ -40,7 +40,17 @@ constexpr uint32_t kItemTarget = 32 * 1024;  // weight bytes per pipeline stage
 constexpr size_t kSmPerKernel = 112 * 1024;  // shared memory one kernel takes per SM
 constexpr int kSlots = 4;                    // activation units a lane keeps in registers
 
-constexpr int kMaxSegs = 4;  // weight matrices sharing one activation in one launch
+constexpr int kMaxSegs = kMaxMatvecSegs;  // matrices of one launch (segments or table jobs)
+
+// How a launch maps CTAs to matrices:
+//  kSegments -- up to kMaxSegs matrices share one activation; their rows are concatenated and
+//               every CTA walks row groups of the whole set (fused Q/K/V, gate/up);
+//  kTable    -- up to kMaxSegs independent jobs, each with its own activation and output
+//               (the reference's FrontierJob table, frontier_quant.cu:71-93); CTAs
+//               [cta0[j], cta0[j+1]) serve job j only;
+//  kRouted   -- expert jobs resolved on the device: slot s uses expert ids[s] of a stacked
+//               expert tensor (GGUF *_exps, experts contiguous), cpj CTAs per job.
+enum MvMode : int { kSegments = 0, kTable = 1, kRouted = 2 };
 
 struct MvParams {
   // Rows [seg_row0[i], seg_row0[i+1]) live in matrix w[i] (the reference's fused QKV /
@@ -67,7 +77,97 @@ struct MvParams {
   int64_t ldy;
   int32_t *dots;
   uint32_t *status;
+  int mode;                   // MvMode
+  // kTable: job j = matrix w[j] of jm[j] rows, activation (jxq, jxd, jxs)[j], output jy[j]
+  // ([batch][jm[j]]), CTAs [cta0[j], cta0[j+1]).
+  int njobs;
+  int jm[kMaxSegs];
+  int cta0[kMaxSegs + 1];
+  const uint8_t *jxq[kMaxSegs];
+  const float *jxd[kMaxSegs];
+  const int *jxs[kMaxSegs];
+  float *jy[kMaxSegs];
+  // kRouted: job j = (slot s = j / per_slot, matrix i = j % per_slot); expert e = ids[s]
+  // (0 <= e < n_total; a slot whose expert another device holds is skipped); weights
+  // ebase[i] + (e - expert0) * estride (m rows); activation vector s / x_div of the Q8_1
+  // buffer (xq, xd, xs); output y + s * y_slot + i * m.
+  const int32_t *ids;
+  int per_slot, n_expert, x_div, cpj;
+  int expert0, n_total;       // this device holds global experts [expert0, expert0 + n_expert)
+  const uint8_t *ebase[2];
+  uint64_t estride;
+  int64_t y_slot;
 };
+
+// What one CTA works on: its index among the CTAs of its matrix (set), that matrix's rows,
+// weights (job modes), activation and output.  Rows are global over the segments in
+// kSegments mode and local to the job otherwise; y is indexed by that row either way.
+struct View {
+  bool skip;                  // routed slot of an expert this device does not hold
+  int cta, ncta, m, ngroups;
+  const uint8_t *w, *w_end16;
+  const uint8_t *xq;
+  const float *xd;
+  const int *xs;
+  float *y;
+  int64_t ldy;
+};
+
+__device__ __forceinline__ const uint8_t *floor16(const uint8_t *p);
+
+// kRouted reads the expert ids the previous kernel wrote: call after grid_dep_wait().
+__device__ __forceinline__ View make_view(const MvParams &p) {
+  View v;
+  v.ldy = p.ldy;
+  v.skip = false;
+  if (p.mode == kSegments) {
+    v.cta = blockIdx.x;
+    v.ncta = gridDim.x;
+    v.m = p.m;
+    v.ngroups = p.ngroups;
+    v.w = v.w_end16 = nullptr;
+    v.xq = p.xq;
+    v.xd = p.xd;
+    v.xs = p.xs;
+    v.y = p.y;
+  } else if (p.mode == kTable) {
+    int j = 0;
+    for (int i = 1; i < p.njobs; ++i) j += static_cast<int>(blockIdx.x) >= p.cta0[i] ? 1 : 0;
+    v.cta = static_cast<int>(blockIdx.x) - p.cta0[j];
+    v.ncta = p.cta0[j + 1] - p.cta0[j];
+    v.m = p.jm[j];
+    v.ngroups = (v.m + p.rows - 1) / p.rows;
+    v.w = p.w[j];
+    v.w_end16 = p.w_end16[j];
+    v.xq = p.jxq[j];
+    v.xd = p.jxd[j];
+    v.xs = p.jxs[j];
+    v.y = p.jy[j];
+    v.ldy = v.m;
+  } else {
+    const int j = static_cast<int>(blockIdx.x) / p.cpj;
+    v.cta = static_cast<int>(blockIdx.x) - j * p.cpj;
+    v.ncta = p.cpj;
+    const int s = j / p.per_slot, i = j - s * p.per_slot;
+    const int e = p.ids[s];
+    if (e < 0 || e >= p.n_total) {  // never index outside the expert tensor
+      if (v.cta == 0 && threadIdx.x == 0) status_or(p.status, ST_BADARG);
+      v.skip = true;
+    }
+    const int el = e - p.expert0;
+    if (el < 0 || el >= p.n_expert) v.skip = true;
+    v.m = p.m;
+    v.ngroups = p.ngroups;
+    v.w = p.ebase[i] + static_cast<uint64_t>(v.skip ? 0 : el) * p.estride;
+    v.w_end16 = floor16(v.w + static_cast<uint64_t>(p.m) * p.row_bytes);
+    const int xv = s / p.x_div;
+    v.xq = p.xq + static_cast<int64_t>(xv) * p.k;
+    v.xd = p.xd + static_cast<int64_t>(xv) * p.nbp;
+    v.xs = p.xs + static_cast<int64_t>(xv) * p.nbp;
+    v.y = p.y + static_cast<int64_t>(s) * p.y_slot + static_cast<int64_t>(i) * p.m;
+  }
+  return v;
+}
 
 template <int KIND>
 __host__ __device__ constexpr uint64_t bytes_of(uint64_t elems) {
@@ -87,14 +187,19 @@ __device__ __forceinline__ const uint8_t *ceil16(const uint8_t *p) {
 struct Item {
   int r0, nrows, c;
 };
-__device__ __forceinline__ Item item_of(const MvParams &p, int t) {
+__device__ __forceinline__ Item item_of(const MvParams &p, const View &v, int t) {
   const int j = p.nch == 1 ? t : t / p.nch;
-  const int g = blockIdx.x + j * gridDim.x;
+  const int g = v.cta + j * v.ncta;
   Item it;
   it.c = t - j * p.nch;
   it.r0 = g * p.rows;
-  it.nrows = min(p.rows, p.m - it.r0);
+  it.nrows = min(p.rows, v.m - it.r0);
   return it;
+}
+
+// Items of this CTA: its row groups times the K chunks of each.
+__device__ __forceinline__ int items_of(const MvParams &p, const View &v) {
+  return (v.ngroups - v.cta + v.ncta - 1) / v.ncta * p.nch;
 }
 
 __device__ __forceinline__ int seg_of(const MvParams &p, int row) {
@@ -104,8 +209,9 @@ __device__ __forceinline__ int seg_of(const MvParams &p, int row) {
   return s;
 }
 
-// Address of row `row` (global row index across the matrices).
-__device__ __forceinline__ const uint8_t *row_ptr(const MvParams &p, int row) {
+// Address of row `row` (global across the segments, or of the CTA's job).
+__device__ __forceinline__ const uint8_t *row_ptr(const MvParams &p, const View &v, int row) {
+  if (p.mode != kSegments) return v.w + static_cast<uint64_t>(row) * p.row_bytes;
   const int s = seg_of(p, row);
   return p.w[s] + static_cast<uint64_t>(row - p.seg_row0[s]) * p.row_bytes;
 }
@@ -113,20 +219,21 @@ __device__ __forceinline__ const uint8_t *row_ptr(const MvParams &p, int row) {
 // Byte range [a0, a1) a bulk copy may fetch for the span [src, e) of matrix `seg`: 16-byte
 // aligned, and never past the last 16-byte boundary of that matrix; the bytes beyond (only in
 // a matrix's final span) go through plain loads.
-__device__ __forceinline__ void span16(const MvParams &p, int seg, const uint8_t *src,
+__device__ __forceinline__ void span16(const MvParams &p, const View &v, int seg, const uint8_t *src,
                                        const uint8_t *e, const uint8_t *&a0, const uint8_t *&a1) {
+  const uint8_t *end16 = p.mode == kSegments ? p.w_end16[seg] : v.w_end16;
   a0 = floor16(src);
   a1 = ceil16(e);
-  if (e > p.w_end16[seg]) a1 = a0 > p.w_end16[seg] ? a0 : p.w_end16[seg];
+  if (e > end16) a1 = a0 > end16 ? a0 : end16;
 }
 
 // Copies of item t into `stage` (one thread).  When a row chunk is the whole row (nch == 1)
 // the item's rows are one contiguous span and one bulk copy fetches all of them.
 template <int KIND>
-__device__ void issue_item(const MvParams &p, int t, uint32_t stage, uint32_t bar, uint64_t pol) {
-  const Item it = item_of(p, t);
-  const int seg = seg_of(p, it.r0);
-  const uint8_t *first = row_ptr(p, it.r0);
+__device__ void issue_item(const MvParams &p, const View &v, int t, uint32_t stage, uint32_t bar, uint64_t pol) {
+  const Item it = item_of(p, v, t);
+  const int seg = p.mode == kSegments ? seg_of(p, it.r0) : 0;
+  const uint8_t *first = row_ptr(p, v, it.r0);
   const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(it.c) * p.kc);
   const uint64_t seg_len = bytes_of<KIND>(min(p.kc, p.k - it.c * p.kc));
   const int spans = p.nch == 1 ? 1 : it.nrows;
@@ -135,7 +242,7 @@ __device__ void issue_item(const MvParams &p, int t, uint32_t stage, uint32_t ba
     const uint8_t *src = first + static_cast<uint64_t>(r) * p.row_bytes + seg_off;
     const uint8_t *e = p.nch == 1 ? first + static_cast<uint64_t>(it.nrows) * p.row_bytes : src + seg_len;
     const uint8_t *a0, *a1;
-    span16(p, seg, src, e, a0, a1);
+    span16(p, v, seg, src, e, a0, a1);
     const uint32_t dst = stage + r * p.seg_stride;
     for (const uint8_t *b = a1; b < e; ++b) sts8(dst + static_cast<uint32_t>(b - a0), *b);
     tx += static_cast<uint32_t>(a1 - a0);
@@ -145,7 +252,7 @@ __device__ void issue_item(const MvParams &p, int t, uint32_t stage, uint32_t ba
     const uint8_t *src = first + static_cast<uint64_t>(r) * p.row_bytes + seg_off;
     const uint8_t *e = p.nch == 1 ? first + static_cast<uint64_t>(it.nrows) * p.row_bytes : src + seg_len;
     const uint8_t *a0, *a1;
-    span16(p, seg, src, e, a0, a1);
+    span16(p, v, seg, src, e, a0, a1);
     if (a1 > a0) bulk_g2s(stage + r * p.seg_stride, a0, static_cast<uint32_t>(a1 - a0), bar, pol);
   }
 }
@@ -188,7 +295,7 @@ __device__ __forceinline__ bool reduce_rows(const float (&v)[RW], int lane, floa
 // and the activation staging.  Returns false in the producer warp (which is done), true in
 // consumer warps once the activation is in shared memory (ok = false if that copy timed out).
 template <int KIND, int NB>
-__device__ __forceinline__ bool prologue(const MvParams &p, uint32_t base, int T, bool &ok) {
+__device__ __forceinline__ bool prologue(const MvParams &p, const View &v, uint32_t base, int T, bool &ok) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t full = base, empty = base + 64, xbar = base + 128;
   const uint32_t ring = base + p.ring;
@@ -210,14 +317,14 @@ __device__ __forceinline__ bool prologue(const MvParams &p, uint32_t base, int T
       // programmatic dependency resolves, then stage the activation once for the CTA.
       const uint64_t pol_w = policy_evict_first();
       const int pre = min(T, p.stages);
-      for (int t = 0; t < pre; ++t) issue_item<KIND>(p, t, ring + t * p.stage_bytes, full + 8 * t, pol_w);
+      for (int t = 0; t < pre; ++t) issue_item<KIND>(p, v, t, ring + t * p.stage_bytes, full + 8 * t, pol_w);
       grid_dep_wait();
       mbar_arrive_expect_tx(xbar, NB * (xq_bytes + xd_bytes * (kSum ? 2u : 1u)));
       const uint64_t pol_x = policy_evict_last();
-      for (int v = 0; v < NB; ++v) {
-        bulk_g2s(base + p.x_q + v * xq_bytes, p.xq + static_cast<int64_t>(v) * p.k, xq_bytes, xbar, pol_x);
-        bulk_g2s(base + p.x_d + v * xd_bytes, p.xd + static_cast<int64_t>(v) * p.nbp, xd_bytes, xbar, pol_x);
-        if (kSum) bulk_g2s(base + p.x_s + v * xd_bytes, p.xs + static_cast<int64_t>(v) * p.nbp, xd_bytes, xbar, pol_x);
+      for (int b = 0; b < NB; ++b) {
+        bulk_g2s(base + p.x_q + b * xq_bytes, v.xq + static_cast<int64_t>(b) * p.k, xq_bytes, xbar, pol_x);
+        bulk_g2s(base + p.x_d + b * xd_bytes, v.xd + static_cast<int64_t>(b) * p.nbp, xd_bytes, xbar, pol_x);
+        if (kSum) bulk_g2s(base + p.x_s + b * xd_bytes, v.xs + static_cast<int64_t>(b) * p.nbp, xd_bytes, xbar, pol_x);
       }
       for (int t = pre; t < T; ++t) {
         const int s = t % p.stages;
@@ -225,7 +332,7 @@ __device__ __forceinline__ bool prologue(const MvParams &p, uint32_t base, int T
           status_or(p.status, ST_TIMEOUT);
           break;
         }
-        issue_item<KIND>(p, t, ring + s * p.stage_bytes, full + 8 * s, pol_w);
+        issue_item<KIND>(p, v, t, ring + s * p.stage_bytes, full + 8 * s, pol_w);
       }
     }
     return false;
@@ -260,10 +367,12 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) 
   const uint32_t base = smem_u32(smem);
   const uint32_t full = base, empty = base + 64;
   const uint32_t ring = base + p.ring;
-  const int T = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                static_cast<int>(gridDim.x);
+  if (p.mode == kRouted) grid_dep_wait();  // the expert ids come from the previous kernel
+  const View v = make_view(p);
+  if (v.skip) return;  // nothing staged or issued yet
+  const int T = items_of(p, v);
   bool ok = true;
-  if (!prologue<KIND, 1>(p, base, T, ok)) return;
+  if (!prologue<KIND, 1>(p, v, base, T, ok)) return;
 
   // Slot j of this lane is flat index f = lane + 32 j of the warp's RW x U (row, unit) space.
   // Its row offset inside an item, its unit and its activation unit are fixed for the kernel.
@@ -289,10 +398,10 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) 
     const int s = t % p.stages;
     ok = wait_stage(p, full, t, lane);
     if (!ok) break;
-    const Item it = item_of(p, t);
+    const Item it = item_of(p, v, t);
     // The item's rows are one span fetched from floor16(first row).
     const uint32_t stage = ring + s * p.stage_bytes +
-        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, it.r0)) & 15);
+        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, v, it.r0)) & 15);
     float acc[J];
 #pragma unroll
     for (int j = 0; j < J; j += 2) {
@@ -319,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) 
     if (reduce_rows<RW>(rs, lane, tot)) {
       const int rr = warp * RW + lane / (32 / RW);
       if (rr < it.nrows) {
-        p.y[it.r0 + rr] = tot;
+        v.y[it.r0 + rr] = tot;
         if (!isfinite(tot)) status_or(p.status, ST_NONFINITE_OUT);
       }
     }
@@ -340,10 +449,12 @@ __global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const MvParams p)
   const uint32_t base = smem_u32(smem);
   const uint32_t full = base, empty = base + 64;
   const uint32_t ring = base + p.ring;
-  const int T = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                static_cast<int>(gridDim.x);
+  if (p.mode == kRouted) grid_dep_wait();  // the expert ids come from the previous kernel
+  const View v = make_view(p);
+  if (v.skip) return;  // nothing staged or issued yet
+  const int T = items_of(p, v);
   bool ok = true;
-  if (!prologue<KIND, 1>(p, base, T, ok)) return;
+  if (!prologue<KIND, 1>(p, v, base, T, ok)) return;
 
   const int U = p.k / 32;
   const int total = R * U;
@@ -367,13 +478,13 @@ __global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const MvParams p)
   for (int t = 0; t < T; ++t) {
     const int s = t % p.stages;
     const bool mine = __all_sync(0xffffffffu, mbar_wait_bounded(full + 8 * s, (t / p.stages) & 1));
-    const Item it = item_of(p, t);
+    const Item it = item_of(p, v, t);
     float rs[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) rs[r] = 0.f;
     if (mine) {
       const uint32_t stage = ring + s * p.stage_bytes +
-          static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, it.r0)) & 15);
+          static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, v, it.r0)) & 15);
       float acc[J];
 #pragma unroll
       for (int j = 0; j < J; j += 2) {
@@ -410,7 +521,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const MvParams p)
       float sum = 0.f;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) sum += red[((t & 1) * kWarps + w) * 4 + lane];
-      p.y[it.r0 + lane] = sum;
+      v.y[it.r0 + lane] = sum;
       if (!isfinite(sum)) status_or(p.status, ST_NONFINITE_OUT);
     }
   }
@@ -426,28 +537,30 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const MvParams p
   const uint32_t base = smem_u32(smem);
   const uint32_t full = base, empty = base + 64;
   const uint32_t ring = base + p.ring;
-  const int T = (p.ngroups - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
-                static_cast<int>(gridDim.x) * p.nch;
+  if (p.mode == kRouted) grid_dep_wait();  // the expert ids come from the previous kernel
+  const View v = make_view(p);
+  if (v.skip) return;  // nothing staged or issued yet
+  const int T = items_of(p, v);
   bool ok = true;
-  if (!prologue<KIND, NB>(p, base, T, ok)) return;
+  if (!prologue<KIND, NB>(p, v, base, T, ok)) return;
   constexpr bool kSum = Fmt<KIND>::kNeedsSum;
   const uint32_t xq_bytes = static_cast<uint32_t>(p.k), xd_bytes = static_cast<uint32_t>(p.nbp) * 4;
 
   float acc[NB];
 #pragma unroll
-  for (int v = 0; v < NB; ++v) acc[v] = 0.f;
+  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
 
   for (int t = 0; ok && t < T; ++t) {
     const int s = t % p.stages;
     ok = wait_stage(p, full, t, lane);
     if (!ok) break;
     const uint32_t stage = ring + s * p.stage_bytes;
-    const Item it = item_of(p, t);
+    const Item it = item_of(p, v, t);
     const int k0 = it.c * p.kc;
     if (warp < it.nrows) {
       const int nunits = min(p.kc, p.k - k0) / 32;
       const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(k0));
-      const uint8_t *row0 = row_ptr(p, it.r0);
+      const uint8_t *row0 = row_ptr(p, v, it.r0);
       const uint8_t *row = row0 + static_cast<uint64_t>(warp) * p.row_bytes + seg_off;
       uint32_t seg;
       if (p.nch == 1) {
@@ -460,18 +573,18 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const MvParams p
         const int ug = k0 / 32 + u;  // unit index within the whole row
         XUnit x[NB];
 #pragma unroll
-        for (int v = 0; v < NB; ++v)
-          load_xunit(base + p.x_q + v * xq_bytes + 32 * ug, base + p.x_d + v * xd_bytes + 4 * ug,
-                     base + p.x_s + v * xd_bytes + 4 * ug, kSum, x[v]);
+        for (int b = 0; b < NB; ++b)
+          load_xunit(base + p.x_q + b * xq_bytes + 32 * ug, base + p.x_d + b * xd_bytes + 4 * ug,
+                     base + p.x_s + b * xd_bytes + 4 * ug, kSum, x[b]);
         WUnit wu;
         load_wunit<KIND>(seg, u, wu);
 #pragma unroll
-        for (int v = 0; v < NB; ++v) {
-          const int isum = unit_isum<KIND>(wu, x[v]);
+        for (int b = 0; b < NB; ++b) {
+          const int isum = unit_isum<KIND>(wu, x[b]);
           if constexpr (DOTS) {
             p.dots[static_cast<int64_t>(it.r0 + warp) * (p.k / 32) + ug] = isum;
           } else {
-            acc[v] += unit_term<KIND>(wu, x[v], isum);
+            acc[b] += unit_term<KIND>(wu, x[b], isum);
           }
         }
       }
@@ -479,11 +592,11 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const MvParams p
     release_stage(empty, s, lane);
     if (!DOTS && it.c == p.nch - 1) {
 #pragma unroll
-      for (int v = 0; v < NB; ++v) {
-        const float val = warp_sum(acc[v]);
-        acc[v] = 0.f;
+      for (int b = 0; b < NB; ++b) {
+        const float val = warp_sum(acc[b]);
+        acc[b] = 0.f;
         if (lane == 0 && warp < it.nrows) {
-          p.y[v * p.ldy + it.r0 + warp] = val;
+          v.y[b * v.ldy + it.r0 + warp] = val;
           if (!isfinite(val)) status_or(p.status, ST_NONFINITE_OUT);
         }
       }
@@ -656,12 +769,23 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
 
 ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_in) {
   MatvecArgs a = a_in;
-  if (a.nseg == 0) {
+  const int mode = a.ids ? kRouted : a.njobs > 0 ? kTable : kSegments;
+  if (mode == kTable) {
+    if (a.njobs > kMaxSegs) return UGB_ESHAPE;
+    a.nseg = a.njobs;
+    a.m = 0;
+    for (int i = 0; i < a.njobs; ++i) a.m = std::max(a.m, a.seg_rows[i]);
+  } else if (mode == kRouted) {
+    if (a.batch != 1 || a.per_slot < 1 || a.per_slot > 2 || a.n_slots < 1 || a.n_expert < 1 || a.x_div < 1)
+      return UGB_ESHAPE;
+    a.nseg = 1;
+  } else if (a.nseg == 0) {
     a.nseg = 1;
     a.ws[0] = a.w;
     a.seg_rows[0] = a.m;
   }
   const bool dots = a.dots != nullptr;
+  if (dots && mode != kSegments) return UGB_ESHAPE;
   // A batch runs as launches of 8, 4, 2 or 1 vectors (largest first) whose staged
   // activations fit kXBudget; each launch streams the weights once.
   int64_t done = 0;
@@ -682,7 +806,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     // otherwise the matrices go out as separate launches.
     bool whole = true;
     for (int i = 0; i + 1 < a.nseg; ++i) whole = whole && a.seg_rows[i] % pl.rows == 0;
-    if (a.nseg > 1 && !whole) {
+    if (mode == kSegments && a.nseg > 1 && !whole) {
       int64_t row0 = 0;
       for (int i = 0; i < a.nseg; ++i) {
         MatvecArgs one = a;
@@ -733,7 +857,42 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     p.ldy = a.ldy;
     p.dots = a.dots;
     p.status = ctx->status;
-    const int grid = static_cast<int>(std::min<int64_t>(pl.ngroups, static_cast<int64_t>(ctx->sm_count) * per_sm));
+    p.mode = mode;
+    const int64_t budget = static_cast<int64_t>(ctx->sm_count) * per_sm;
+    int grid = static_cast<int>(std::min<int64_t>(pl.ngroups, budget));
+    if (mode == kTable) {
+      // CTAs per job in proportion to its row groups (at least one, at most one per group).
+      int64_t groups = 0;
+      for (int i = 0; i < a.njobs; ++i) groups += (a.seg_rows[i] + pl.rows - 1) / pl.rows;
+      p.njobs = a.njobs;
+      int c = 0;
+      for (int i = 0; i < a.njobs; ++i) {
+        const int64_t g = (a.seg_rows[i] + pl.rows - 1) / pl.rows;
+        p.jm[i] = static_cast<int>(a.seg_rows[i]);
+        p.cta0[i] = c;
+        c += static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, budget * g / std::max<int64_t>(1, groups))));
+        p.jxq[i] = a.jx[i] + done * a.xl.k;
+        p.jxd[i] = reinterpret_cast<const float *>(a.jx[i] + a.xl.d_off) + done * a.xl.nbp;
+        p.jxs[i] = reinterpret_cast<const int *>(a.jx[i] + a.xl.s_off) + done * a.xl.nbp;
+        p.jy[i] = a.jy[i] + done * a.seg_rows[i];
+      }
+      p.cta0[a.njobs] = c;
+      grid = c;
+    } else if (mode == kRouted) {
+      const int jobs = a.n_slots * a.per_slot;
+      p.ids = a.ids;
+      p.per_slot = a.per_slot;
+      p.n_expert = a.n_expert;
+      p.expert0 = a.expert0;
+      p.n_total = a.n_total;
+      p.x_div = a.x_div;
+      p.ebase[0] = a.ebase[0];
+      p.ebase[1] = a.ebase[1];
+      p.estride = a.estride;
+      p.y_slot = a.y_slot;
+      p.cpj = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(pl.ngroups, budget / jobs)));
+      grid = p.cpj * jobs;
+    }
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
