@@ -267,39 +267,69 @@ ugb_status ugb_prefill_block_dots(ugb_ctx *ctx, ugb_stream stream, const void *w
                                   const void *x_packed, int32_t *dots_dev, float *y_dev, int64_t m,
                                   int64_t n, int64_t k);
 
+/* ---- collectives (NCCL over NVLink) for sharded decoding -------------------------------- */
+
+/* A communicator over the devices of one sharded decoder (one process or thread per GPU).
+ * NCCL is loaded at run time; without it these return UGB_EBACKEND.  Rank 0 makes the id
+ * with ugb_comm_unique_id and the caller hands it to every rank (e.g. over its own process
+ * group); ugb_comm_init is collective: every rank calls it at the same time. */
+typedef struct ugb_comm ugb_comm;
+#define UGB_COMM_ID_BYTES 128
+ugb_status ugb_comm_unique_id(uint8_t *id_out /* UGB_COMM_ID_BYTES */);
+ugb_status ugb_comm_init(ugb_ctx *ctx, int rank, int world, const uint8_t *id, ugb_comm **out);
+ugb_status ugb_comm_destroy(ugb_comm *comm);
+
 /* ---- decoder (the per-token graph around the matvecs) ------------------------------------ */
 
-/* Shape of a Qwen2-style decoder (configs 2 and 4).  The reference hard-codes the 1.5B shape
- * (llm.rs:314-321: DIM 1536, HIDDEN 8960, KV 256, HEAD 128, LAYERS 28). */
+/* Shape of a Qwen2/Qwen3-MoE-style decoder.  The reference hard-codes the 1.5B shape
+ * (llm.rs:314-321: DIM 1536, HIDDEN 8960, KV 256, HEAD 128, LAYERS 28) and decodes one
+ * sequence; here `batch` sequences (1..8) step together at a shared position, each with its
+ * own tokens and KV cache.
+ *  - n_expert = 0: dense SwiGLU FFN of n_ff (configs 2-4).  n_expert > 0: MoE FFN (config 5):
+ *    router matvec (kind) over n_expert experts, top_k routing, SwiGLU experts of
+ *    n_ff_expert in expert_kind (Forward::ffn, frontier_forward.rs:164-199).
+ *  - Expert parallelism: this device holds global experts [expert0, expert0 + n_expert_local)
+ *    (n_expert_local = 0: all).  With a communicator the layer outputs are summed over devices.
+ *  - Vocabulary split: this device holds head rows [vocab0, vocab0 + n_vocab_local)
+ *    (n_vocab_local = 0: all).  With a communicator the greedy keys are reduced over devices. */
 typedef struct ugb_decoder_config {
   int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, n_ctx;
   float rope_theta, norm_eps;
-  uint32_t kind;      /* quant kind of the layer matrices: UGB_Q8_0, UGB_Q4_K or UGB_Q3_K */
+  uint32_t kind;      /* quant kind of the attention (and dense FFN / router) matrices */
   uint32_t head_kind; /* quant kind of the output head */
+  int32_t batch;
+  int32_t n_expert, top_k, n_ff_expert;
+  uint32_t expert_kind;
+  int32_t expert0, n_expert_local;
+  int32_t vocab0, n_vocab_local;
 } ugb_decoder_config;
 
 /* Device pointers of one layer's GGUF tensors (blk.N.*): matrices in their GGUF block layout
- * with row length n_embd (w_down: n_ff; wo: n_head*head_dim), norms f32, biases f32 or NULL. */
+ * with row length n_embd (w_down: n_ff; wo: n_head*head_dim), norms f32, biases f32 or NULL.
+ * MoE layers use router (ffn_gate_inp, [n_expert][n_embd]) and the stacked expert tensors of
+ * the held experts (ffn_{gate,up,down}_exps: [n_expert_local][rows][row_bytes]) instead of
+ * w_gate / w_up / w_down. */
 typedef struct ugb_layer_weights {
   const void *attn_norm, *wq, *wk, *wv, *bq, *bk, *bv, *wo;
   const void *ffn_norm, *w_gate, *w_up, *w_down;
+  const void *router, *gate_exps, *up_exps, *down_exps;
 } ugb_layer_weights;
 
 typedef struct ugb_model_weights {
   const void *tok_embd;            /* Q8_0 [n_vocab][n_embd] (token_embd.weight) */
   const void *output_norm;         /* f32 [n_embd] */
-  const void *output;              /* head_kind [n_vocab][n_embd]; tok_embd when tied */
+  const void *output;              /* head_kind: the held rows [vocab0, +n_vocab_local) of the head */
   const ugb_layer_weights *layers; /* host array of n_layer entries */
 } ugb_model_weights;
 
 typedef struct ugb_decoder ugb_decoder;
 
-/* Allocate the decoder's device state: fp32 KV cache (n_layer x n_head_kv x n_ctx x
+/* Allocate the decoder's device state: fp32 KV cache (batch x n_layer x n_head_kv x n_ctx x
  * head_dim, for K and V; the reference keeps its cache in fp32 too, gpu_attention.cu:1),
  * activations, RoPE table (f32 angle pos * powf(theta, -2i/head_dim), gpu_graph.rs:132),
- * attention partials and the token state.  Replaces the reference's VRAM arenas and graph
- * build (gpu_graph.rs:81-169).  head_dim must be 128; n_head a multiple of n_head_kv with
- * at most 8 query heads per KV head. */
+ * attention partials, MoE workspace and the token state.  Replaces the reference's VRAM arenas
+ * and graph build (gpu_graph.rs:81-169).  head_dim must be 128; n_head a multiple of
+ * n_head_kv with at most 8 query heads per KV head. */
 ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config *cfg, ugb_decoder **out);
 ugb_status ugb_decoder_destroy(ugb_decoder *dec);
 
@@ -307,35 +337,50 @@ ugb_status ugb_decoder_destroy(ugb_decoder *dec);
 ugb_status ugb_decoder_bind(ugb_decoder *dec, const ugb_model_weights *w);
 
 /* Allocate and bind seeded synthetic weights owned by the decoder (see ugb_fill_synthetic;
- * norms 1 +- 0.1, biases N(0, 0.02^2) approximately; tied head). */
+ * norms 1 +- 0.1, biases N(0, 0.02^2) approximately for dense models; tied head when
+ * head_kind is Q8_0).  Expert e's tensors depend only on (seed, layer, e), so expert-parallel
+ * shards of one seed form one model. */
 ugb_status ugb_decoder_synthetic(ugb_decoder *dec, uint64_t seed);
 
-/* Enqueue one token step on `stream`: embedding of the current token, every layer, the
- * head and greedy selection.  The token comes from the previous step's greedy choice when
- * there is one (the position then advances), else from ugb_decoder_set_state, so replaying a
+/* Collectives for a sharded decoder (expert parallel and / or vocabulary split); NULL: none
+ * (a shard then computes its partial results only). */
+ugb_status ugb_decoder_set_comm(ugb_decoder *dec, ugb_comm *comm);
+
+/* Enqueue one token step on `stream`: embedding of the current tokens, every layer, the head
+ * and greedy selection.  A sequence's token comes from the previous step's greedy choice when
+ * there is one (the position then advances), else from ugb_decoder_set_tokens, so replaying a
  * captured step decodes autoregressively on the device. */
 ugb_status ugb_decoder_step(ugb_decoder *dec, ugb_stream stream);
 
-/* Set the token and position the next step starts from (asynchronous host-to-device copy). */
+/* Set the tokens ([batch]) and the shared position the next step starts from (asynchronous
+ * host-to-device copy).  ugb_decoder_set_state sets every sequence to `token`. */
+ugb_status ugb_decoder_set_tokens(ugb_decoder *dec, ugb_stream stream, const int32_t *tokens, int32_t pos);
 ugb_status ugb_decoder_set_state(ugb_decoder *dec, ugb_stream stream, int32_t token, int32_t pos);
 
-/* Synchronous: the token, position and greedy choice of the last step. */
+/* Synchronous: the tokens, position and greedy choices ([batch], -1 if none) of the last step.
+ * ugb_decoder_get_state reports sequence 0. */
+ugb_status ugb_decoder_get_tokens(ugb_decoder *dec, ugb_stream stream, int32_t *tokens, int32_t *pos,
+                                  int32_t *next_tokens);
 ugb_status ugb_decoder_get_state(ugb_decoder *dec, ugb_stream stream, int32_t *token,
                                  int32_t *pos, int32_t *next_token);
 
-/* Synchronous copy of the last step's logits (n_vocab floats) to host memory. */
+/* Synchronous copy of the last step's logits of the held head rows ([batch][n_vocab_local or
+ * n_vocab] floats) to host memory. */
 ugb_status ugb_decoder_logits(ugb_decoder *dec, ugb_stream stream, float *logits_host);
 
-/* Synchronous copy of `count` cached positions starting at `pos` of one layer's rotated keys
- * and values to host memory, each laid out [n_head_kv][count][head_dim].  No counterpart in
- * the reference, whose host reads its KV cache at fixed device addresses (llm.rs:319-320);
- * here it serves inspection and checkpointing of a sequence. */
-ugb_status ugb_decoder_read_kv(ugb_decoder *dec, ugb_stream stream, int32_t layer, int32_t pos,
+/* Synchronous copy of `count` cached positions starting at `pos` of sequence `seq`'s rotated
+ * keys and values in one layer to host memory, each laid out [n_head_kv][count][head_dim].
+ * No counterpart in the reference, whose host reads its KV cache at fixed device addresses
+ * (llm.rs:319-320); here it serves inspection and checkpointing of a sequence. */
+ugb_status ugb_decoder_read_kv(ugb_decoder *dec, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
                                int32_t count, float *k_host, float *v_host);
 
 /* One token end to end, as the reference's forward() (llm.rs:339-388 / forward_gpu
- * gpu_graph.rs:170-197): host token and position in, greedy next token out.  Replays a CUDA
- * graph of the step (captured on first use) and checks the status word. */
+ * gpu_graph.rs:170-197): host tokens and position in, greedy next tokens out.  Replays a CUDA
+ * graph of the step (captured on first use) and checks the status word.  ugb_decoder_token is
+ * the single-sequence form (every sequence gets `token`; returns sequence 0's choice). */
+ugb_status ugb_decoder_tokens(ugb_decoder *dec, ugb_stream stream, const int32_t *tokens, int32_t pos,
+                              int32_t *next_tokens);
 ugb_status ugb_decoder_token(ugb_decoder *dec, ugb_stream stream, int32_t token, int32_t pos,
                              int32_t *next_token);
 

@@ -12,7 +12,11 @@ reference's GPU decode graph (driver/src/gpu_graph.rs:139-162):
     the f32 angle pos * powf(theta, -(2i)/HD) (gpu_graph.rs:132, llm.rs:328-337);
   * fp32 KV cache, scores q.k / sqrt(HD), exact exp softmax (gpu_attention.cu:1-26);
   * SiLU(gate) * up (llm.rs:374), residual adds, final norm, head, first-maximum greedy
-    (llm.rs:383-385).
+    (llm.rs:383-385);
+  * an MoE FFN when cfg["n_expert"] > 0 (Forward::ffn, frontier_forward.rs:164-199): router
+    linear, softmax top-k with ties to the lower id and renormalised weights (the C oracle's
+    orc_moe_route), per selected expert gate / up linears, SiLU(gate) * up, down linear, and
+    out = sum of weight * value in rank order with a separate multiply and add.
 """
 from __future__ import annotations
 
@@ -76,6 +80,24 @@ class RefDecoder:
         rb = po.row_bytes(Q8_0, n)
         return po.dequantize(Q8_0, self.w["tok_embd"][token * rb:(token + 1) * rb], n)
 
+    def moe_ffn(self, L: dict, xn: np.ndarray) -> np.ndarray:
+        """Routed SwiGLU experts of one layer; L holds router and the stacked expert tensors
+        gate_exps / up_exps / down_exps (raw bytes, all n_expert experts)."""
+        c = self.c
+        ek, ne, ff, d = c["expert_kind"], c["n_expert"], c["n_ff_expert"], c["n_embd"]
+        scores = self.linear(c["kind"], L["router"], xn, ne)
+        ids, weights = po.moe_route(scores, c["top_k"])
+        rbi, rbf = po.row_bytes(ek, d), po.row_bytes(ek, ff)
+        out = np.zeros(d, np.float32)
+        for e, wgt in zip(ids, weights):
+            g = self.linear(ek, L["gate_exps"][e * ff * rbi:(e + 1) * ff * rbi], xn, ff)
+            u = self.linear(ek, L["up_exps"][e * ff * rbi:(e + 1) * ff * rbi], xn, ff)
+            with np.errstate(over="ignore"):
+                h = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+            v = self.linear(ek, L["down_exps"][e * d * rbf:(e + 1) * d * rbf], h, d)
+            out = (out + (np.float32(wgt) * v).astype(np.float32)).astype(np.float32)
+        return out
+
     # ---- one token -----------------------------------------------------------------------
 
     def step(self, token: int, pos: int):
@@ -112,6 +134,9 @@ class RefDecoder:
                 att[h] = (e @ vals).astype(np.float32) / np.float32(e.sum(dtype=np.float32))
             x = (x + self.linear(kind, L["wo"], att.reshape(-1), c["n_embd"])).astype(np.float32)
             xn = self.norm(x, L["ffn_norm"])
+            if c.get("n_expert", 0):
+                x = (x + self.moe_ffn(L, xn)).astype(np.float32)
+                continue
             g = self.linear(kind, L["w_gate"], xn, c["n_ff"])
             u = self.linear(kind, L["w_up"], xn, c["n_ff"])
             with np.errstate(over="ignore"):  # exp(-g) = inf for very negative g gives -0, as expf

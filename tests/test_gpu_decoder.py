@@ -55,14 +55,20 @@ def build_model(ctx, ugb, cfg, seed):
     dev["output"] = dev["tok_embd"] if cfg["head_kind"] == Q8_0 else mat(cfg["head_kind"], cfg["n_embd"],
                                                                          cfg["n_vocab"])
     layers = []
+    moe = cfg.get("n_expert", 0) > 0
     for _ in range(cfg["n_layer"]):
-        layers.append(dict(attn_norm=vec(cfg["n_embd"], 1.0, 0.1), ffn_norm=vec(cfg["n_embd"], 1.0, 0.1),
-                           bq=vec(qrows, 0.0, 0.02), bk=vec(kvrows, 0.0, 0.02), bv=vec(kvrows, 0.0, 0.02),
-                           wq=mat(kind, cfg["n_embd"], qrows), wk=mat(kind, cfg["n_embd"], kvrows),
-                           wv=mat(kind, cfg["n_embd"], kvrows), wo=mat(kind, qrows, cfg["n_embd"]),
-                           w_gate=mat(kind, cfg["n_embd"], cfg["n_ff"]),
-                           w_up=mat(kind, cfg["n_embd"], cfg["n_ff"]),
-                           w_down=mat(kind, cfg["n_ff"], cfg["n_embd"])))
+        L = dict(attn_norm=vec(cfg["n_embd"], 1.0, 0.1), ffn_norm=vec(cfg["n_embd"], 1.0, 0.1),
+                 wq=mat(kind, cfg["n_embd"], qrows), wk=mat(kind, cfg["n_embd"], kvrows),
+                 wv=mat(kind, cfg["n_embd"], kvrows), wo=mat(kind, qrows, cfg["n_embd"]))
+        if moe:  # Qwen3-MoE style: no Q/K/V biases, routed SwiGLU experts (stacked tensors)
+            ek, ne, ffe = cfg["expert_kind"], cfg["n_expert"], cfg["n_ff_expert"]
+            L.update(router=mat(kind, cfg["n_embd"], ne), gate_exps=mat(ek, cfg["n_embd"], ffe * ne),
+                     up_exps=mat(ek, cfg["n_embd"], ffe * ne), down_exps=mat(ek, ffe, cfg["n_embd"] * ne))
+        else:
+            L.update(bq=vec(qrows, 0.0, 0.02), bk=vec(kvrows, 0.0, 0.02), bv=vec(kvrows, 0.0, 0.02),
+                     w_gate=mat(kind, cfg["n_embd"], cfg["n_ff"]), w_up=mat(kind, cfg["n_embd"], cfg["n_ff"]),
+                     w_down=mat(kind, cfg["n_ff"], cfg["n_embd"]))
+        layers.append(L)
     dev["layers"] = layers
     torch.cuda.synchronize()
     host = {k: v.cpu().numpy() for k, v in dev.items() if k != "layers"}
@@ -199,3 +205,87 @@ def test_decoder_bad_arguments(ctx, ugb):
     with pytest.raises(ugb.UgbError):
         dec.token(SMALL["n_vocab"], 0)
     dec.close()
+
+
+MOE = dict(SMALL, n_expert=8, top_k=2, n_ff_expert=256, expert_kind=Q3_K, n_ff=0)
+
+
+def run_synced_batch(dec, refs, tokens):
+    """Batch form of run_synced: tokens [steps][batch]; one oracle per sequence."""
+    errs = []
+    for pos, toks in enumerate(tokens):
+        nxt = dec.tokens([int(t) for t in toks], pos)
+        logits = dec.logits()
+        if logits.ndim == 1:
+            logits = logits[None]
+        for b, ref in enumerate(refs):
+            ref_logits, ref_next = ref.step(int(toks[b]), pos)
+            for layer in range(ref.c["n_layer"]):
+                k, v = dec.read_kv(layer, pos, 1, b)
+                ref.kcache[layer, :, pos] = k[:, 0]
+                ref.vcache[layer, :, pos] = v[:, 0]
+            assert nxt[b] == int(np.argmax(logits[b]))
+            errs.append(rel_l2(logits[b], ref_logits))
+    return np.array(errs)
+
+
+def test_decoder_batch_matches_oracle(ctx, ugb):
+    """Three sequences stepped together: each agrees with its own oracle (state-synchronised)."""
+    from oracle.decode_ref import RefDecoder
+    cfg = dict(SMALL, batch=3)
+    dec, _, host = make_decoder(ctx, ugb, cfg, seed=31)
+    refs = [RefDecoder(SMALL, host) for _ in range(3)]
+    tokens = np.random.default_rng(8).integers(0, SMALL["n_vocab"], size=(40, 3))
+    errs = run_synced_batch(dec, refs, tokens)
+    assert errs.max() <= 5e-2
+    assert (errs <= 1e-4).mean() >= 0.8, errs
+    assert ctx.status_read()[1] == 0
+    dec.close()
+
+
+@pytest.mark.parametrize("batch", [1, 2])
+def test_moe_decoder_matches_oracle(ctx, ugb, batch):
+    """MoE FFN (router, top-2 of 8 Q3_K experts) in the token step, against the oracle."""
+    from oracle.decode_ref import RefDecoder
+    cfg = dict(MOE, batch=batch)
+    dec, _, host = make_decoder(ctx, ugb, cfg, seed=41)
+    refs = [RefDecoder(MOE, host) for _ in range(batch)]
+    tokens = np.random.default_rng(9).integers(0, SMALL["n_vocab"], size=(24, batch))
+    errs = run_synced_batch(dec, refs, tokens)
+    assert errs.max() <= 5e-2
+    assert (errs <= 1e-4).mean() >= 0.7, errs
+    assert ctx.status_read()[1] == 0
+    dec.close()
+
+
+def test_vocab_shard_logits(ctx, ugb):
+    """A decoder holding head rows [300, 700) computes exactly those logits (no communicator:
+    the greedy key covers the held rows only)."""
+    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=51)
+    rb = ugb.row_bytes(Q8_0, SMALL["n_embd"])
+    part = ugb.Decoder(ctx, **dict(SMALL, vocab0=300, n_vocab_local=400))
+    head = dev["tok_embd"][300 * rb:700 * rb]
+    part.bind(dev["tok_embd"], dev["output_norm"], head, dev["layers"])
+    for pos, tok in enumerate([4, 8, 15]):
+        dec.token(tok, pos)
+        full = dec.logits()
+        nxt = part.token(tok, pos)
+        np.testing.assert_array_equal(part.logits().view(np.uint32), full[300:700].view(np.uint32))
+        assert nxt == 300 + int(np.argmax(full[300:700]))
+    dec.close()
+    part.close()
+
+
+def test_moe_synthetic_deterministic(ctx, ugb):
+    """Two MoE decoders synthesised from one seed decode identically (the synthetic tensors
+    depend only on the seed, the layer and the expert)."""
+    cfg = dict(MOE, n_layer=1)
+    full = ugb.Decoder(ctx, **cfg)
+    full.synthetic(3)
+    other = ugb.Decoder(ctx, **cfg)
+    other.synthetic(3)
+    for pos, tok in enumerate([11, 12]):
+        assert full.token(tok, pos) == other.token(tok, pos)
+        np.testing.assert_array_equal(full.logits().view(np.uint32), other.logits().view(np.uint32))
+    full.close()
+    other.close()

@@ -67,10 +67,18 @@ SIGNATURES = {
     "ugb_decoder_synthetic": (_int, [_vp, _u64]),
     "ugb_decoder_step": (_int, [_vp, _vp]),
     "ugb_decoder_set_state": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32]),
+    "ugb_decoder_set_tokens": (_int, [_vp, _vp, _vp, ctypes.c_int32]),
+    "ugb_decoder_get_tokens": (_int, [_vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _vp]),
+    "ugb_decoder_tokens": (_int, [_vp, _vp, _vp, ctypes.c_int32, _vp]),
+    "ugb_decoder_set_comm": (_int, [_vp, _vp]),
+    "ugb_comm_unique_id": (_int, [_vp]),
+    "ugb_comm_init": (_int, [_vp, _int, _int, _vp, ctypes.POINTER(_vp)]),
+    "ugb_comm_destroy": (_int, [_vp]),
     "ugb_decoder_get_state": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int32),
                                      ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
     "ugb_decoder_logits": (_int, [_vp, _vp, _vp]),
-    "ugb_decoder_read_kv": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _vp, _vp]),
+    "ugb_decoder_read_kv": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                   _vp, _vp]),
     "ugb_decoder_token": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32,
                                  ctypes.POINTER(ctypes.c_int32)]),
     "ugb_graph_begin": (_int, [_vp, _vp]),
@@ -319,13 +327,17 @@ class DecoderConfig(ctypes.Structure):
                 ("n_head", ctypes.c_int32), ("n_head_kv", ctypes.c_int32),
                 ("head_dim", ctypes.c_int32), ("n_vocab", ctypes.c_int32), ("n_ctx", ctypes.c_int32),
                 ("rope_theta", ctypes.c_float), ("norm_eps", ctypes.c_float),
-                ("kind", ctypes.c_uint32), ("head_kind", ctypes.c_uint32)]
+                ("kind", ctypes.c_uint32), ("head_kind", ctypes.c_uint32), ("batch", ctypes.c_int32),
+                ("n_expert", ctypes.c_int32), ("top_k", ctypes.c_int32), ("n_ff_expert", ctypes.c_int32),
+                ("expert_kind", ctypes.c_uint32), ("expert0", ctypes.c_int32), ("n_expert_local", ctypes.c_int32),
+                ("vocab0", ctypes.c_int32), ("n_vocab_local", ctypes.c_int32)]
 
 
 class LayerWeights(ctypes.Structure):
     """ugb_layer_weights (device pointers)."""
     _fields_ = [(n, _vp) for n in ("attn_norm", "wq", "wk", "wv", "bq", "bk", "bv", "wo",
-                                   "ffn_norm", "w_gate", "w_up", "w_down")]
+                                   "ffn_norm", "w_gate", "w_up", "w_down",
+                                   "router", "gate_exps", "up_exps", "down_exps")]
 
 
 class ModelWeights(ctypes.Structure):
@@ -334,8 +346,33 @@ class ModelWeights(ctypes.Structure):
                 ("layers", ctypes.POINTER(LayerWeights))]
 
 
+COMM_ID_BYTES = 128
+
+
+class Comm:
+    """ugb_comm: an NCCL communicator for a sharded decoder.  Every rank constructs it at the
+    same time with the id rank 0 made (comm_unique_id)."""
+
+    def __init__(self, ctx: "Context", rank: int, world: int, uid: bytes):
+        buf = (ctypes.c_uint8 * COMM_ID_BYTES).from_buffer_copy(uid)
+        h = _vp()
+        check("ugb_comm_init", lib().ugb_comm_init(ctx.handle, rank, world, buf, ctypes.byref(h)))
+        self.handle = h
+
+    def close(self) -> None:
+        if self.handle:
+            lib().ugb_comm_destroy(self.handle)
+            self.handle = None
+
+
+def comm_unique_id() -> bytes:
+    buf = (ctypes.c_uint8 * COMM_ID_BYTES)()
+    check("ugb_comm_unique_id", lib().ugb_comm_unique_id(buf))
+    return bytes(buf)
+
+
 QWEN25_15B = dict(n_layer=28, n_embd=1536, n_ff=8960, n_head=12, n_head_kv=2, head_dim=128,
-                  n_vocab=151936, n_ctx=512, rope_theta=1e6, norm_eps=1e-6, kind=8, head_kind=8)
+                  n_vocab=151936, n_ctx=512, rope_theta=1e6, norm_eps=1e-6, kind=8, head_kind=8, batch=1)
 
 
 class Decoder:
@@ -343,6 +380,7 @@ class Decoder:
 
     def __init__(self, ctx: "Context", **cfg):
         self.ctx = ctx
+        cfg.setdefault("batch", 1)
         self.cfg = DecoderConfig(**cfg)
         h = _vp()
         check("ugb_decoder_create", lib().ugb_decoder_create(ctx.handle, ctypes.byref(self.cfg),
@@ -382,28 +420,50 @@ class Decoder:
         check("ugb_decoder_set_state", lib().ugb_decoder_set_state(self.handle, _stream(stream),
                                                                      token, pos))
 
+    def set_tokens(self, tokens, pos: int, stream=None) -> None:
+        arr = (ctypes.c_int32 * len(tokens))(*tokens)
+        check("ugb_decoder_set_tokens", lib().ugb_decoder_set_tokens(self.handle, _stream(stream), arr, pos))
+
+    def set_comm(self, comm: "Comm | None") -> None:
+        check("ugb_decoder_set_comm", lib().ugb_decoder_set_comm(self.handle, comm.handle if comm else None))
+
     def get_state(self, stream=None):
         t, p, n = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
         check("ugb_decoder_get_state", lib().ugb_decoder_get_state(
             self.handle, _stream(stream), ctypes.byref(t), ctypes.byref(p), ctypes.byref(n)))
         return t.value, p.value, n.value
 
+    def get_tokens(self, stream=None):
+        """(tokens[batch], pos, next_tokens[batch])."""
+        b = self.cfg.batch
+        t, n, p = (ctypes.c_int32 * b)(), (ctypes.c_int32 * b)(), ctypes.c_int32()
+        check("ugb_decoder_get_tokens", lib().ugb_decoder_get_tokens(self.handle, _stream(stream), t,
+                                                                       ctypes.byref(p), n))
+        return list(t), p.value, list(n)
+
     def logits(self, stream=None):
         import numpy as np
-        out = np.empty(self.cfg.n_vocab, dtype=np.float32)
-        check("ugb_decoder_logits", lib().ugb_decoder_logits(self.handle, _stream(stream),
-                                                               out.ctypes.data))
-        return out
+        n = self.cfg.n_vocab_local or self.cfg.n_vocab
+        out = np.empty((self.cfg.batch, n), dtype=np.float32)
+        check("ugb_decoder_logits", lib().ugb_decoder_logits(self.handle, _stream(stream), out.ctypes.data))
+        return out[0] if self.cfg.batch == 1 else out
 
-    def read_kv(self, layer: int, pos: int, count: int = 1, stream=None):
+    def read_kv(self, layer: int, pos: int, count: int = 1, seq: int = 0, stream=None):
         """(keys, values), each float32 [n_head_kv, count, head_dim] (rotated keys)."""
         import numpy as np
         shape = (self.cfg.n_head_kv, count, self.cfg.head_dim)
         k = np.empty(shape, dtype=np.float32)
         v = np.empty(shape, dtype=np.float32)
-        check("ugb_decoder_read_kv", lib().ugb_decoder_read_kv(self.handle, _stream(stream), layer, pos,
+        check("ugb_decoder_read_kv", lib().ugb_decoder_read_kv(self.handle, _stream(stream), seq, layer, pos,
                                                                  count, k.ctypes.data, v.ctypes.data))
         return k, v
+
+    def tokens(self, tokens, pos: int, stream=None):
+        b = self.cfg.batch
+        arr = (ctypes.c_int32 * b)(*tokens)
+        nxt = (ctypes.c_int32 * b)()
+        check("ugb_decoder_tokens", lib().ugb_decoder_tokens(self.handle, _stream(stream), arr, pos, nxt))
+        return list(nxt)
 
     def token(self, token: int, pos: int, stream=None) -> int:
         nxt = ctypes.c_int32()

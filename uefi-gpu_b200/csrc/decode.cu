@@ -1,17 +1,14 @@
-// decode.cu -- the per-token glue around the quantised matvecs of a Qwen2-style decoder.
+// decode.cu -- the per-token glue around the quantised matvecs of a Qwen2-style decoder, for a
+// batch of up to 8 sequences decoded together.
 //
 // The reference runs the same steps as separate kernels in its prebuilt decode command list
 // (gpu_graph.rs:139-162): fused_resnorm -> quant_act -> qkv_dp4a -> rope_bias ->
 // fused_attention -> quant_act -> linear(o) -> fused_resnorm -> quant_act -> gateup_dp4a ->
 // quant_act -> linear(down), then the output head and greedy_tiles/greedy_finish.  Here each
 // glue step also produces the Q8_1 activation its consumer needs, attention is split over the
-// context (flash-decoding) with the KV cache in fp16, and greedy selection is one atomicMax on
-// an order-preserving (value, id) key.  Every kernel takes part in programmatic dependent
-// launch: it lets the next kernel start, then waits for its own inputs.
-//
-// Decode state (int32 words in device memory): [0] token, [1] position, [2..3] the u64
-// greedy key of the last head (0 = none).  A token step reads the key left by the previous
-// step, so a replayed CUDA graph decodes autoregressively on the device.
+// context (flash-decoding), and greedy selection is one atomicMax on an order-preserving
+// (value, id) key.  Every kernel takes part in programmatic dependent launch: it lets the next
+// kernel start, then waits for its own inputs.  Sequence b of a batch is a grid dimension.
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
@@ -52,66 +49,88 @@ __device__ __forceinline__ uint64_t greedy_key(float v, uint32_t id) {
 
 __device__ __forceinline__ uint32_t key_id(uint64_t key) { return ~static_cast<uint32_t>(key); }
 
+// Vector b of a Q8_1 buffer of length-n vectors: (quants, scales, sums).
+struct Q8View {
+  int8_t *q;
+  float *d;
+  int32_t *s;
+};
+__device__ __forceinline__ Q8View q8_vec(uint8_t *buf, int n, size_t d_off, size_t s_off, int nbp, int b) {
+  Q8View v;
+  v.q = reinterpret_cast<int8_t *>(buf) + static_cast<int64_t>(b) * n;
+  v.d = reinterpret_cast<float *>(buf + d_off) + static_cast<int64_t>(b) * nbp;
+  v.s = reinterpret_cast<int32_t *>(buf + s_off) + static_cast<int64_t>(b) * nbp;
+  return v;
+}
+
 // ---- embedding --------------------------------------------------------------------------
 
-// Token of this step: the previous step's greedy choice when there is one (and the position
-// advances), else the host-provided token.  Then x = dequantised Q8_0 embedding row
-// (embedding_q8, gpu_embedding.cu:3-9; frontier_core.rs:172).  One CTA.  A position that
-// would run past the KV cache is pinned to its last slot and flagged, so no later kernel of
-// the step indexes outside the cache.
-__global__ void __launch_bounds__(512) embed_kernel(const uint8_t *__restrict__ tok_embd, int embd,
-                                                    int vocab, int n_ctx, int32_t *state,
-                                                    float *__restrict__ x, uint32_t *status) {
+// Sequence b = blockIdx.x: its token is the previous step's greedy choice when there is one,
+// else the host-provided token; x[b] = dequantised Q8_0 embedding row (embedding_q8,
+// gpu_embedding.cu:3-9; frontier_core.rs:172).  When the keys are set the shared position
+// advances (sequence 0's CTA moves it); a position that would run past the KV cache is pinned
+// to its last slot and flagged, so no later kernel of the step indexes outside the cache.
+// The keys are cleared by the next kernel, after every sequence has read its own.
+__global__ void __launch_bounds__(512) embed_kernel(const uint8_t *__restrict__ tok_embd, int embd, int vocab,
+                                                    int n_ctx, DecodeState *state, float *__restrict__ x,
+                                                    uint32_t *status) {
   grid_dep_launch();
   grid_dep_wait();
+  const int b = blockIdx.x;
   __shared__ int tok_s;
   if (threadIdx.x == 0) {
-    uint64_t *key = reinterpret_cast<uint64_t *>(state + 2);
-    int tok = state[0];
-    if (*key != 0) {
-      tok = static_cast<int>(key_id(*key));
-      state[1] += 1;
+    const unsigned long long key = state->key[b];
+    int tok = key != 0 ? static_cast<int>(key_id(key)) : state->token[b];
+    if (b == 0) {
+      int pos = state->pos + (key != 0 ? 1 : 0);
+      if (pos < 0 || pos >= n_ctx) {
+        status_or(status, ST_BADARG);
+        pos = pos < 0 ? 0 : n_ctx - 1;
+      }
+      state->pos = pos;
     }
     if (tok < 0 || tok >= vocab) {
       status_or(status, ST_BADARG);
       tok = 0;
     }
-    if (state[1] < 0 || state[1] >= n_ctx) {
-      status_or(status, ST_BADARG);
-      state[1] = state[1] < 0 ? 0 : n_ctx - 1;
-    }
-    state[0] = tok;
-    *key = 0;
+    state->token[b] = tok;
     tok_s = tok;
   }
   __syncthreads();
   const uint8_t *row = tok_embd + static_cast<uint64_t>(tok_s) * (embd / 32) * 34;
+  float *xb = x + static_cast<int64_t>(b) * embd;
   for (int i = threadIdx.x; i < embd; i += blockDim.x) {
     const uint8_t *blk = row + (i / 32) * 34;
     const uint32_t h = blk[0] | (static_cast<uint32_t>(blk[1]) << 8);
-    x[i] = half_bits_to_float(h) * static_cast<float>(static_cast<int8_t>(blk[2 + (i & 31)]));
+    xb[i] = half_bits_to_float(h) * static_cast<float>(static_cast<int8_t>(blk[2 + (i & 31)]));
   }
 }
 
 // ---- residual add + RMSNorm + quant -----------------------------------------------------
 
-// x += dx (when dx is given); y = x * (1/sqrt(mean(x^2) + eps)) * w; xq = Q8_1(y).
-// One CTA of 1024 threads; the sum of squares is a fixed-order tree (fused_resnorm,
-// gpu_fused.cu:28-35; llm.rs:323-327 on the CPU).
+// Sequence b = blockIdx.x: x += dx (when dx is given); y = x * (1/sqrt(mean(x^2) + eps)) * w;
+// xq[b] = Q8_1(y).  One CTA of 1024 threads per sequence; the sum of squares is a fixed-order
+// tree (fused_resnorm, gpu_fused.cu:28-35; llm.rs:323-327 on the CPU).  With clear_keys set
+// (the first norm of a step) the CTA also clears its sequence's greedy key, which the
+// embedding kernel has consumed by now.
 __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(float *__restrict__ x, const float *__restrict__ dx,
                                                              const float *__restrict__ w, int n, float eps,
                                                              uint8_t *__restrict__ xq, size_t d_off, size_t s_off,
-                                                             int nbp, uint32_t *status) {
+                                                             int nbp, DecodeState *clear_keys, uint32_t *status) {
   grid_dep_launch();
   grid_dep_wait();
   __shared__ float part[32];
+  const int b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (clear_keys && tid == 0) clear_keys->key[b] = 0;
+  float *xb = x + static_cast<int64_t>(b) * n;
+  const float *dxb = dx ? dx + static_cast<int64_t>(b) * n : nullptr;
   float ss = 0.f;
   for (int i = tid; i < n; i += blockDim.x) {
-    float v = x[i];
-    if (dx) {
-      v += dx[i];
-      x[i] = v;
+    float v = xb[i];
+    if (dxb) {
+      v += dxb[i];
+      xb[i] = v;
     }
     ss += v * v;
   }
@@ -127,18 +146,16 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(float *__restrict__
   }
   __syncthreads();
   const float scale = 1.0f / sqrtf(part[0] / static_cast<float>(n) + eps);
-  int8_t *q = reinterpret_cast<int8_t *>(xq);
-  float *d = reinterpret_cast<float *>(xq + d_off);
-  int32_t *s = reinterpret_cast<int32_t *>(xq + s_off);
+  const Q8View v = q8_vec(xq, n, d_off, s_off, nbp, b);
   bool bad = false;
   const int nb = n / 32;
-  for (int b = warp; b < nb; b += blockDim.x >> 5) {
-    const int i = b * 32 + lane;
-    bad |= quant_block(x[i] * scale * w[i], lane, q, d, s, b);
+  for (int blk = warp; blk < nb; blk += blockDim.x >> 5) {
+    const int i = blk * 32 + lane;
+    bad |= quant_block(xb[i] * scale * w[i], lane, v.q, v.d, v.s, blk);
   }
-  for (int b = nb + tid; b < nbp; b += blockDim.x) {
-    d[b] = 0.f;
-    s[b] = 0;
+  for (int blk = nb + tid; blk < nbp; blk += blockDim.x) {
+    v.d[blk] = 0.f;
+    v.s[blk] = 0;
   }
   if (bad && lane == 0) status_or(status, ST_NONFINITE_IN);
 }
@@ -146,40 +163,42 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(float *__restrict__
 // ---- SiLU(gate) * up + quant ------------------------------------------------------------
 
 // h = (g / (1 + exp(-g))) * u per element (gateup_dp4a epilogue, gpu_dp4a.cu:63), quantised
-// per 32-block; gu holds [gate rows ; up rows].  One warp per block.
+// per 32-block; gu[b] holds [gate rows ; up rows] of sequence b = blockIdx.y.  One warp per
+// block.
 __global__ void __launch_bounds__(256) silu_quant_kernel(const float *__restrict__ gu, int n_ff,
                                                          uint8_t *__restrict__ hq, size_t d_off, size_t s_off,
                                                          int nbp, uint32_t *status) {
   grid_dep_launch();
   grid_dep_wait();
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
-  float *d = reinterpret_cast<float *>(hq + d_off);
-  int32_t *s = reinterpret_cast<int32_t *>(hq + s_off);
+  const int blk = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int b = blockIdx.y;
+  const Q8View v = q8_vec(hq, n_ff, d_off, s_off, nbp, b);
   const int nb = n_ff / 32;
-  if (b >= nbp) return;
-  if (b >= nb) {
+  if (blk >= nbp) return;
+  if (blk >= nb) {
     if (lane == 0) {
-      d[b] = 0.f;
-      s[b] = 0;
+      v.d[blk] = 0.f;
+      v.s[blk] = 0;
     }
     return;
   }
-  const float g = gu[b * 32 + lane], u = gu[n_ff + b * 32 + lane];
-  const float h = (g / (1.0f + expf(-g))) * u;
-  if (quant_block(h, lane, reinterpret_cast<int8_t *>(hq), d, s, b) && lane == 0)
-    status_or(status, ST_NONFINITE_IN);
+  const float *g = gu + static_cast<int64_t>(b) * 2 * n_ff;
+  const float gv = g[blk * 32 + lane], uv = g[n_ff + blk * 32 + lane];
+  const float h = (gv / (1.0f + expf(-gv))) * uv;
+  if (quant_block(h, lane, v.q, v.d, v.s, blk) && lane == 0) status_or(status, ST_NONFINITE_IN);
 }
 
 // ---- attention ------------------------------------------------------------------------------
 
-// Flash-decoding over one KV head and one context chunk of kAttnChunk positions: the G query
-// heads of the group get their bias and RoPE (rope_bias, gpu_ops.cu:9-20: a = v0*c - v1*s,
-// b = v0*s + v1*c over pairs (i, i + HD/2)), the chunk holding `pos` also biases, rotates and
-// stores the new key and value (fp32 cache, as the reference keeps it: gpu_attention.cu:1), and
-// every chunk writes unnormalised partials (max, sum of exp, exp-weighted V) for the combine
-// step.  Scores are q.k / sqrt(HD) with an exact expf softmax (fused_attention,
-// gpu_attention.cu:2-26; llm.rs:358-368).
+// Flash-decoding over one KV head (blockIdx.x) and one context chunk of kAttnChunk positions
+// (blockIdx.y) of sequence b = blockIdx.z: the G query heads of the group get their bias and
+// RoPE (rope_bias, gpu_ops.cu:9-20: a = v0*c - v1*s, b = v0*s + v1*c over pairs
+// (i, i + HD/2)), the chunk holding `pos` also biases, rotates and stores the new key and
+// value (fp32 cache, as the reference keeps it: gpu_attention.cu:1), and every chunk writes
+// unnormalised partials (max, sum of exp, exp-weighted V) for the combine step.  Scores are
+// q.k / sqrt(HD) with an exact expf softmax (fused_attention, gpu_attention.cu:2-26;
+// llm.rs:358-368).
 template <int HD>
 __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
   extern __shared__ __align__(16) float sm[];
@@ -191,31 +210,33 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
   float *ps = vs + kAttnChunk * HD;         // [G][CH]
   float *kn = ps + G * kAttnChunk;          // [2][HD] new key / value (raw)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kvh = blockIdx.x, sp = blockIdx.y;
+  const int kvh = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
   grid_dep_launch();
   grid_dep_wait();
-  const int pos = a.state[1];
+  const int pos = a.state->pos;
   const int t0 = sp * kAttnChunk;
-  float *pm = a.part_m + (static_cast<size_t>(kvh) * a.n_split + sp) * G;
-  float *pl = a.part_l + (static_cast<size_t>(kvh) * a.n_split + sp) * G;
-  float *po = a.part_o + (static_cast<size_t>(kvh) * a.n_split + sp) * G * HD;
+  const size_t part = (static_cast<size_t>(b) * a.n_kv + kvh) * a.n_split + sp;
+  float *pm = a.part_m + part * G;
+  float *pl = a.part_l + part * G;
+  float *po = a.part_o + part * G * HD;
   if (pos < 0 || pos >= a.n_ctx) {  // the embedding step pins pos; this is a second guard
-    if (tid == 0 && sp == 0 && kvh == 0) status_or(a.status, ST_BADARG);
+    if (tid == 0 && sp == 0 && kvh == 0 && b == 0) status_or(a.status, ST_BADARG);
     return;
   }
   if (t0 > pos) return;  // the combine step only reads chunks <= pos / kAttnChunk
   const int nt = min(kAttnChunk, pos + 1 - t0);
   const int qrows = a.n_head * HD, kvrows = a.n_kv * HD;
+  const float *qkv = a.qkv + static_cast<int64_t>(b) * (qrows + 2 * kvrows);
   const float2 *rope = a.rope + static_cast<size_t>(pos) * (HD / 2);
   const bool has_new = pos < t0 + kAttnChunk;
   for (int i = tid; i < G * HD; i += blockDim.x) {
     const int row = (kvh * G) * HD + i;
-    r_s[i] = a.qkv[row] + (a.bias ? a.bias[row] : 0.f);
+    r_s[i] = qkv[row] + (a.bias ? a.bias[row] : 0.f);
   }
   if (has_new) {
     for (int i = tid; i < 2 * HD; i += blockDim.x) {
       const int row = qrows + (i < HD ? 0 : kvrows) + kvh * HD + (i % HD);
-      kn[i] = a.qkv[row] + (a.bias ? a.bias[row] : 0.f);
+      kn[i] = qkv[row] + (a.bias ? a.bias[row] : 0.f);
     }
   }
   __syncthreads();
@@ -225,6 +246,8 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
     const float v0 = r_s[base + j], v1 = r_s[base + j + HD / 2];
     q_s[i] = dd < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x;
   }
+  float *kcache = a.kcache + static_cast<int64_t>(b) * a.cache_seq;
+  float *vcache = a.vcache + static_cast<int64_t>(b) * a.cache_seq;
   const size_t cache_head = (static_cast<size_t>(kvh) * a.n_ctx) * HD;
   if (has_new && tid < HD) {
     const int j = tid % (HD / 2);
@@ -232,15 +255,15 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
     const float v0 = kn[j], v1 = kn[j + HD / 2];
     const float k = tid < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x;
     const float v = kn[HD + tid];
-    a.kcache[cache_head + static_cast<size_t>(pos) * HD + tid] = k;
-    a.vcache[cache_head + static_cast<size_t>(pos) * HD + tid] = v;
+    kcache[cache_head + static_cast<size_t>(pos) * HD + tid] = k;
+    vcache[cache_head + static_cast<size_t>(pos) * HD + tid] = v;
     ks[(pos - t0) * (HD + 1) + tid] = k;
     vs[(pos - t0) * HD + tid] = v;
   }
   const int n_old = has_new ? nt - 1 : nt;
   {
-    const float4 *kc = reinterpret_cast<const float4 *>(a.kcache + cache_head + static_cast<size_t>(t0) * HD);
-    const float4 *vc = reinterpret_cast<const float4 *>(a.vcache + cache_head + static_cast<size_t>(t0) * HD);
+    const float4 *kc = reinterpret_cast<const float4 *>(kcache + cache_head + static_cast<size_t>(t0) * HD);
+    const float4 *vc = reinterpret_cast<const float4 *>(vcache + cache_head + static_cast<size_t>(t0) * HD);
     for (int i = tid; i < n_old * (HD / 4); i += blockDim.x) {
       const int t = i / (HD / 4), dd = (i - t * (HD / 4)) * 4;
       const float4 kv = kc[i], vv = vc[i];
@@ -290,46 +313,50 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
   }
 }
 
-// Combine the chunk partials of one query head (log-sum-exp) and quantise the head's HD
-// outputs into the Q8_1 input of the output projection.  One CTA of HD threads per head.
+// Combine the chunk partials of query head blockIdx.x of sequence blockIdx.y (log-sum-exp)
+// and quantise the head's HD outputs into the Q8_1 input of the output projection.
 template <int HD>
 __global__ void __launch_bounds__(HD) attn_combine_quant_kernel(AttnParams a, uint8_t *__restrict__ xq,
-                                                                size_t d_off, size_t s_off) {
+                                                                size_t d_off, size_t s_off, int nbp) {
   grid_dep_launch();
   grid_dep_wait();
   const int G = a.n_head / a.n_kv;
-  const int h = blockIdx.x, kvh = h / G, g = h - kvh * G;
+  const int h = blockIdx.x, b = blockIdx.y, kvh = h / G, g = h - kvh * G;
   const int dd = threadIdx.x, lane = dd & 31;
-  const int pos = a.state[1];
+  const int pos = a.state->pos;
   const int ns = (pos >= 0 && pos < a.n_ctx) ? pos / kAttnChunk + 1 : 0;  // 0: flagged upstream
+  const size_t part0 = (static_cast<size_t>(b) * a.n_kv + kvh) * a.n_split;
   float mx = -FLT_MAX;
-  for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, a.part_m[(static_cast<size_t>(kvh) * a.n_split + sp) * G + g]);
+  for (int sp = 0; sp < ns; ++sp) mx = fmaxf(mx, a.part_m[(part0 + sp) * G + g]);
   float l = 0.f, o = 0.f;
   for (int sp = 0; sp < ns; ++sp) {
-    const size_t ps = static_cast<size_t>(kvh) * a.n_split + sp;
+    const size_t ps = part0 + sp;
     const float e = expf(a.part_m[ps * G + g] - mx);
     l += e * a.part_l[ps * G + g];
     o += e * a.part_o[(ps * G + g) * HD + dd];
   }
   const float v = ns ? o / l : 0.f;
-  const int b = (h * HD + dd) / 32;
-  if (quant_block(v, lane, reinterpret_cast<int8_t *>(xq), reinterpret_cast<float *>(xq + d_off),
-                  reinterpret_cast<int32_t *>(xq + s_off), b) && lane == 0)
-    status_or(a.status, ST_NONFINITE_IN);
+  const Q8View q = q8_vec(xq, a.n_head * HD, d_off, s_off, nbp, b);
+  const int blk = (h * HD + dd) / 32;
+  if (quant_block(v, lane, q.q, q.d, q.s, blk) && lane == 0) status_or(a.status, ST_NONFINITE_IN);
 }
 
 // ---- greedy ----------------------------------------------------------------------------------
 
-// The largest logit, lowest id on ties, into the state's greedy key (greedy_tiles /
+// The largest logit of sequence blockIdx.y (lowest id on ties; ids offset by id0 when this
+// device holds a slice of the vocabulary) into the state's greedy key (greedy_tiles /
 // greedy_finish, gpu_greedy.cu:13-27).  Non-finite logits are reported by the head matvec.
-__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ logits, int n, int32_t *state) {
+__global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ logits, int n, int id0,
+                                                     DecodeState *state) {
   grid_dep_launch();
   grid_dep_wait();
   __shared__ unsigned long long part[8];
+  const int b = blockIdx.y;
+  const float *lb = logits + static_cast<int64_t>(b) * n;
   uint64_t best = 0;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    const float v = logits[i];
-    if (isfinite(v)) best = max(best, greedy_key(v, static_cast<uint32_t>(i)));
+    const float v = lb[i];
+    if (isfinite(v)) best = max(best, greedy_key(v, static_cast<uint32_t>(id0 + i)));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) best = max(best, static_cast<uint64_t>(__shfl_xor_sync(0xffffffffu, best, o)));
@@ -337,7 +364,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const float *__restrict__ l
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < 8; ++w) best = max(best, static_cast<uint64_t>(part[w]));
-    atomicMax(reinterpret_cast<unsigned long long *>(state + 2), static_cast<unsigned long long>(best));
+    atomicMax(&state->key[b], static_cast<unsigned long long>(best));
   }
 }
 
@@ -376,41 +403,40 @@ ugb_status init_decode_kernels(ugb_ctx *ctx) {
                                           static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8)))));
 }
 
-ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab,
-                        int n_ctx, int32_t *state, float *x, uint32_t *status) {
-  return launch_ex(embed_kernel, dim3(1), dim3(512), 0, s, pdl, tok_embd, embd, vocab, n_ctx, state, x,
-                   status);
+ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,
+                        int batch, DecodeState *state, float *x, uint32_t *status) {
+  return launch_ex(embed_kernel, dim3(batch), dim3(512), 0, s, pdl, tok_embd, embd, vocab, n_ctx, state, x, status);
 }
 
-ugb_status launch_rmsnorm_quant(cudaStream_t s, bool pdl, float *x, const float *dx, const float *w,
-                                int n, float eps, uint8_t *xq, uint32_t *status) {
-  const Q8Act l = q8act_layout(n, 1);
-  return launch_ex(rmsnorm_quant_kernel, dim3(1), dim3(1024), 0, s, pdl, x, dx, w, n, eps, xq, l.d_off,
-                   l.s_off, static_cast<int>(l.nbp), status);
+ugb_status launch_rmsnorm_quant(cudaStream_t s, bool pdl, float *x, const float *dx, const float *w, int n,
+                                int batch, float eps, uint8_t *xq, DecodeState *clear_keys, uint32_t *status) {
+  const Q8Act l = q8act_layout(n, batch);
+  return launch_ex(rmsnorm_quant_kernel, dim3(batch), dim3(1024), 0, s, pdl, x, dx, w, n, eps, xq, l.d_off,
+                   l.s_off, static_cast<int>(l.nbp), clear_keys, status);
 }
 
-ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff, uint8_t *hq,
+ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff, int batch, uint8_t *hq,
                              uint32_t *status) {
-  const Q8Act l = q8act_layout(n_ff, 1);
+  const Q8Act l = q8act_layout(n_ff, batch);
   const int warps = static_cast<int>(l.nbp);
-  return launch_ex(silu_quant_kernel, dim3((warps + 7) / 8), dim3(256), 0, s, pdl, gu, n_ff, hq, l.d_off,
+  return launch_ex(silu_quant_kernel, dim3((warps + 7) / 8, batch), dim3(256), 0, s, pdl, gu, n_ff, hq, l.d_off,
                    l.s_off, warps, status);
 }
 
-ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, uint8_t *xq) {
+ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq) {
   const int group = a.n_head / a.n_kv;
-  ugb_status st = launch_ex(attn_partial_kernel<kHeadDim>, dim3(a.n_kv, a.n_split), dim3(256),
+  ugb_status st = launch_ex(attn_partial_kernel<kHeadDim>, dim3(a.n_kv, a.n_split, batch), dim3(256),
                             attn_partial_smem(group), s, pdl, a);
   if (st != UGB_OK) return st;
-  const Q8Act l = q8act_layout(static_cast<int64_t>(a.n_head) * kHeadDim, 1);
-  return launch_ex(attn_combine_quant_kernel<kHeadDim>, dim3(a.n_head), dim3(kHeadDim), 0, s, pdl, a, xq,
-                   l.d_off, l.s_off);
+  const Q8Act l = q8act_layout(static_cast<int64_t>(a.n_head) * kHeadDim, batch);
+  return launch_ex(attn_combine_quant_kernel<kHeadDim>, dim3(a.n_head, batch), dim3(kHeadDim), 0, s, pdl, a, xq,
+                   l.d_off, l.s_off, static_cast<int>(l.nbp));
 }
 
-ugb_status launch_argmax(cudaStream_t s, bool pdl, const float *logits, int n, int32_t *state,
-                         int sm_count) {
-  const int blocks = std::max(1, std::min(sm_count, (n + 255) / 256));
-  return launch_ex(argmax_kernel, dim3(blocks), dim3(256), 0, s, pdl, logits, n, state);
+ugb_status launch_argmax(cudaStream_t s, bool pdl, const float *logits, int n, int batch, int id0,
+                         DecodeState *state, int sm_count) {
+  const int blocks = std::max(1, std::min(sm_count / std::max(1, batch), (n + 255) / 256));
+  return launch_ex(argmax_kernel, dim3(blocks, batch), dim3(256), 0, s, pdl, logits, n, id0, state);
 }
 
 }  // namespace ugb

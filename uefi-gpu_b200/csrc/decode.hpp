@@ -1,5 +1,5 @@
-// decode.hpp -- shared declarations of the decode-step glue kernels (decode.cu) and the
-// decoder host object (decoder.cu).
+// decode.hpp -- shared declarations of the decode-step glue kernels (decode.cu), the MoE
+// launchers (moe.cu) and the decoder host object (decoder.cu).
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -12,31 +12,48 @@ namespace ugb {
 
 constexpr int kAttnChunk = 64;  // context positions per flash-decoding chunk
 constexpr int kHeadDim = 128;   // head dimension of every configuration served
+constexpr int kMaxSeq = 8;      // sequences one decoder steps together
+
+// Token state of a decoder in device memory.  A step reads key[b] left by the previous step
+// (0 = none): when set, sequence b's token becomes the key's id and the shared position
+// advances, so replaying a captured step decodes autoregressively without the host.
+struct DecodeState {
+  int32_t token[kMaxSeq];
+  int32_t pos;
+  int32_t pad;
+  unsigned long long key[kMaxSeq];  // greedy (value, complemented id) of the last head
+};
 
 struct AttnParams {
-  const float *qkv;       // [n_head*HD (q) ; n_kv*HD (k) ; n_kv*HD (v)] of this layer
-  const float *bias;      // same layout, or null
+  const float *qkv;       // [batch][n_head*HD (q) ; n_kv*HD (k) ; n_kv*HD (v)] of this layer
+  const float *bias;      // [q ; k ; v] rows of this layer, or null
   const float2 *rope;     // [n_ctx][HD/2] (cos, sin)
-  float *kcache;          // this layer: [n_kv][n_ctx][HD] (rotated keys)
+  float *kcache;          // sequence 0, this layer: [n_kv][n_ctx][HD] (rotated keys)
   float *vcache;
-  float *part_m, *part_l; // [n_kv][n_split][G]
-  float *part_o;          // [n_kv][n_split][G][HD]
-  const int32_t *state;   // [1] = position
+  int64_t cache_seq;      // elements between sequences' caches
+  float *part_m, *part_l; // [batch][n_kv][n_split][G]
+  float *part_o;          // [batch][n_kv][n_split][G][HD]
+  const DecodeState *state;
   int n_head, n_kv, n_ctx, n_split;
   uint32_t *status;
 };
 
 size_t attn_partial_smem(int group);
 
-ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab,
-                        int n_ctx, int32_t *state, float *x, uint32_t *status);
-ugb_status launch_rmsnorm_quant(cudaStream_t s, bool pdl, float *x, const float *dx, const float *w,
-                                int n, float eps, uint8_t *xq, uint32_t *status);
-ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff, uint8_t *hq,
+ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,
+                        int batch, DecodeState *state, float *x, uint32_t *status);
+ugb_status launch_rmsnorm_quant(cudaStream_t s, bool pdl, float *x, const float *dx, const float *w, int n,
+                                int batch, float eps, uint8_t *xq, DecodeState *clear_keys, uint32_t *status);
+ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff, int batch, uint8_t *hq,
                              uint32_t *status);
-ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, uint8_t *xq);
-ugb_status launch_argmax(cudaStream_t s, bool pdl, const float *logits, int n, int32_t *state,
-                         int sm_count);
+ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq);
+ugb_status launch_argmax(cudaStream_t s, bool pdl, const float *logits, int n, int batch, int id0,
+                         DecodeState *state, int sm_count);
 ugb_status init_decode_kernels(ugb_ctx *ctx);
+
+// The routed expert SwiGLU of one MoE layer (moe.cu), without the entry point's checks.
+ugb_status launch_moe_experts(ugb_ctx *ctx, cudaStream_t stream, const ugb_moe_args &m);
+ugb_status launch_moe_route(ugb_ctx *ctx, cudaStream_t stream, bool pdl, const float *logits, int n_expert,
+                            int top_k, int batch, int32_t *ids, float *weights);
 
 }  // namespace ugb

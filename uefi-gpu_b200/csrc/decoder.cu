@@ -1,11 +1,15 @@
 // decoder.cu -- the decoder object behind ugb_decoder_*: device state, weight binding and
-// the per-token launch sequence (captured once as a CUDA graph for ugb_decoder_token).
+// the per-token launch sequence (captured once as a CUDA graph for ugb_decoder_token[s]).
 //
-// One token step (reference: gpu_graph.rs:139-162, llm.rs:339-388):
+// One token step for `batch` sequences (reference: gpu_graph.rs:139-162, llm.rs:339-388;
+// MoE FFN: frontier_forward.rs:164-199):
 //   embed -> per layer { rmsnorm+quant -> Q/K/V matvec (one launch over the three tensors)
-//   -> attention (bias, RoPE, fp16 KV write, flash-decoding, combine + quant) -> O matvec ->
-//   residual+rmsnorm+quant -> gate/up matvec (one launch) -> SiLU*up+quant -> down matvec }
-//   -> residual+rmsnorm+quant -> head matvec -> greedy.
+//   -> attention (bias, RoPE, KV write, flash-decoding, combine + quant) -> O matvec ->
+//   residual+rmsnorm+quant -> FFN } -> residual+rmsnorm+quant -> head matvec -> greedy.
+//   Dense FFN: gate/up matvec (one launch) -> SiLU*up+quant -> down matvec.
+//   MoE FFN: router matvec -> top-k routing -> routed expert gate/up -> SiLU*up+quant ->
+//   routed down -> weighted combine [-> all-reduce over the expert-parallel devices].
+//   A vocabulary-split head ends with an all-reduce (max) of the greedy keys.
 // Every kernel after the first launches with programmatic dependent launch, so each matvec
 // streams its first weight stages while the preceding kernel finishes.
 #include <algorithm>
@@ -21,20 +25,30 @@
 struct ugb_decoder {
   ugb_ctx *ctx = nullptr;
   ugb_decoder_config cfg{};
+  int batch = 1;
+  int n_vocab_local = 0;   // head rows held
+  int n_expert_local = 0;  // experts held (MoE)
+  bool moe = false;
   // device state
   float *x = nullptr, *dx = nullptr, *qkv = nullptr, *gu = nullptr, *logits = nullptr;
+  float *rlogits = nullptr, *rweights = nullptr;
+  int32_t *rids = nullptr;
   uint8_t *xq = nullptr, *attq = nullptr, *hq = nullptr;
   float *kcache = nullptr, *vcache = nullptr;
+  int64_t cache_seq = 0;   // elements of one sequence's cache (all layers)
   float2 *rope = nullptr;
   float *part_m = nullptr, *part_l = nullptr, *part_o = nullptr;
-  int32_t *state = nullptr;      // [0] token [1] pos [2..3] greedy key
-  int32_t *state_host = nullptr; // pinned mirror
+  void *moe_ws = nullptr;
+  size_t moe_ws_bytes = 0;
+  ugb::DecodeState *state = nullptr;
+  ugb::DecodeState *state_host = nullptr;  // pinned mirror
   int n_split = 0;
   // weights
   ugb_model_weights w{};
   std::vector<ugb_layer_weights> layers;
-  float *bias = nullptr;         // per layer [q;k;v] fused biases (bound when any bias is given)
-  std::vector<void *> owned;     // synthetic weights owned by the decoder
+  float *bias = nullptr;   // per layer [q;k;v] fused biases (bound when any bias is given)
+  std::vector<void *> owned;
+  ugb_comm *comm = nullptr;
   // replay
   cudaStream_t cap = nullptr;
   cudaGraph_t graph = nullptr;
@@ -46,34 +60,53 @@ namespace {
 
 template <typename T>
 ugb_status dalloc(T **p, size_t count) {
-  return cuda_status(cudaMalloc(reinterpret_cast<void **>(p), count * sizeof(T)));
+  return cuda_status(cudaMalloc(reinterpret_cast<void **>(p), std::max<size_t>(count, 1) * sizeof(T)));
 }
 
+bool kind_ok(uint32_t k) { return k == UGB_Q8_0 || k == UGB_Q4_K || k == UGB_Q3_K; }
+
 ugb_status check_config(const ugb_ctx *ctx, const ugb_decoder_config &c) {
-  if (c.n_layer < 1 || c.n_embd < 32 || c.n_embd % 32 || c.n_ff < 32 || c.n_ff % 32 ||
-      c.n_head < 1 || c.n_head_kv < 1 || c.n_head % c.n_head_kv || c.n_head / c.n_head_kv > 8 ||
-      c.head_dim != kHeadDim || c.n_vocab < 1 || c.n_ctx < 1 || c.n_ctx > 32768 ||
-      !(c.norm_eps > 0.f) || !(c.rope_theta > 0.f))
+  if (c.n_layer < 1 || c.n_embd < 32 || c.n_embd % 32 || c.n_head < 1 || c.n_head_kv < 1 ||
+      c.n_head % c.n_head_kv || c.n_head / c.n_head_kv > 8 || c.head_dim != kHeadDim || c.n_vocab < 1 ||
+      c.n_ctx < 1 || c.n_ctx > 32768 || !(c.norm_eps > 0.f) || !(c.rope_theta > 0.f) || c.batch < 1 ||
+      c.batch > kMaxSeq)
     return UGB_ESHAPE;
-  for (uint32_t k : {c.kind, c.head_kind})
-    if (k != UGB_Q8_0 && k != UGB_Q4_K && k != UGB_Q3_K) return UGB_EQUANT;
-  if (ugb_row_bytes(c.kind, c.n_embd) < 0 || ugb_row_bytes(c.kind, c.n_ff) < 0 ||
-      ugb_row_bytes(c.kind, static_cast<int64_t>(c.n_head) * c.head_dim) < 0 ||
+  if (!kind_ok(c.kind) || !kind_ok(c.head_kind)) return UGB_EQUANT;
+  if (ugb_row_bytes(c.kind, c.n_embd) < 0 || ugb_row_bytes(c.kind, static_cast<int64_t>(c.n_head) * c.head_dim) < 0 ||
       ugb_row_bytes(c.head_kind, c.n_embd) < 0)
     return UGB_ESHAPE;
+  if (c.n_expert == 0) {
+    if (c.n_ff < 32 || c.n_ff % 32 || ugb_row_bytes(c.kind, c.n_ff) < 0) return UGB_ESHAPE;
+  } else {
+    if (!kind_ok(c.expert_kind)) return UGB_EQUANT;
+    const int local = c.n_expert_local ? c.n_expert_local : c.n_expert;
+    if (c.n_expert < 1 || c.n_expert > 4096 || c.top_k < 1 || c.top_k > 32 || c.top_k > c.n_expert ||
+        c.n_ff_expert < 32 || c.n_ff_expert % 32 || ugb_row_bytes(c.expert_kind, c.n_ff_expert) < 0 ||
+        ugb_row_bytes(c.expert_kind, c.n_embd) < 0 || c.expert0 < 0 || local < 1 || c.expert0 + local > c.n_expert)
+      return UGB_ESHAPE;
+  }
+  const int vl = c.n_vocab_local ? c.n_vocab_local : c.n_vocab;
+  if (c.vocab0 < 0 || vl < 1 || c.vocab0 + vl > c.n_vocab) return UGB_ESHAPE;
   if (attn_partial_smem(c.n_head / c.n_head_kv) > ctx->smem_optin) return UGB_ESHAPE;
   return UGB_OK;
 }
 
+void free_graph(ugb_decoder *d) {
+  if (d->exec) cudaGraphExecDestroy(d->exec);
+  if (d->graph) cudaGraphDestroy(d->graph);
+  d->exec = nullptr;
+  d->graph = nullptr;
+}
+
 void free_all(ugb_decoder *d) {
-  void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->xq, d->attq, d->hq, d->kcache,
-                  d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->state, d->bias};
+  void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->rlogits, d->rweights, d->rids, d->xq, d->attq,
+                  d->hq, d->kcache, d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->moe_ws, d->state,
+                  d->bias};
   for (void *b : bufs)
     if (b) cudaFree(b);
   for (void *b : d->owned) cudaFree(b);
   if (d->state_host) cudaFreeHost(d->state_host);
-  if (d->exec) cudaGraphExecDestroy(d->exec);
-  if (d->graph) cudaGraphDestroy(d->graph);
+  free_graph(d);
   if (d->cap) cudaStreamDestroy(d->cap);
 }
 
@@ -93,26 +126,40 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
   d->ctx = ctx;
   d->cfg = *cfg;
   const ugb_decoder_config &c = *cfg;
+  const int B = c.batch;
+  d->batch = B;
+  d->moe = c.n_expert > 0;
+  d->n_vocab_local = c.n_vocab_local ? c.n_vocab_local : c.n_vocab;
+  d->n_expert_local = d->moe ? (c.n_expert_local ? c.n_expert_local : c.n_expert) : 0;
   const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
   const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
   const int group = c.n_head / c.n_head_kv;
   d->n_split = (c.n_ctx + kAttnChunk - 1) / kAttnChunk;
-  const size_t kv = static_cast<size_t>(c.n_layer) * kvrows * c.n_ctx;
-  const int64_t act = std::max<int64_t>(c.n_embd, qrows);
-  bool ok = dalloc(&d->x, c.n_embd) == UGB_OK && dalloc(&d->dx, c.n_embd) == UGB_OK &&
-            dalloc(&d->qkv, qrows + 2 * kvrows) == UGB_OK && dalloc(&d->gu, 2 * static_cast<size_t>(c.n_ff)) == UGB_OK &&
-            dalloc(&d->logits, c.n_vocab) == UGB_OK &&
-            dalloc(&d->xq, q8act_layout(act, 1).bytes) == UGB_OK &&
-            dalloc(&d->attq, q8act_layout(qrows, 1).bytes) == UGB_OK &&
-            dalloc(&d->hq, q8act_layout(c.n_ff, 1).bytes) == UGB_OK &&
+  d->cache_seq = static_cast<int64_t>(c.n_layer) * kvrows * c.n_ctx;
+  const size_t kv = static_cast<size_t>(B) * d->cache_seq;
+  const size_t parts = static_cast<size_t>(B) * c.n_head_kv * d->n_split * group;
+  bool ok = dalloc(&d->x, static_cast<size_t>(B) * c.n_embd) == UGB_OK &&
+            dalloc(&d->dx, static_cast<size_t>(B) * c.n_embd) == UGB_OK &&
+            dalloc(&d->qkv, static_cast<size_t>(B) * (qrows + 2 * kvrows)) == UGB_OK &&
+            dalloc(&d->logits, static_cast<size_t>(B) * d->n_vocab_local) == UGB_OK &&
+            dalloc(&d->xq, q8act_layout(c.n_embd, B).bytes) == UGB_OK &&
+            dalloc(&d->attq, q8act_layout(qrows, B).bytes) == UGB_OK &&
             dalloc(&d->kcache, kv) == UGB_OK && dalloc(&d->vcache, kv) == UGB_OK &&
             dalloc(&d->rope, static_cast<size_t>(c.n_ctx) * (c.head_dim / 2)) == UGB_OK &&
-            dalloc(&d->part_m, static_cast<size_t>(c.n_head_kv) * d->n_split * group) == UGB_OK &&
-            dalloc(&d->part_l, static_cast<size_t>(c.n_head_kv) * d->n_split * group) == UGB_OK &&
-            dalloc(&d->part_o, static_cast<size_t>(c.n_head_kv) * d->n_split * group * c.head_dim) == UGB_OK &&
-            dalloc(&d->state, 4) == UGB_OK &&
-            cudaMallocHost(reinterpret_cast<void **>(&d->state_host), 4 * sizeof(int32_t)) == cudaSuccess &&
+            dalloc(&d->part_m, parts) == UGB_OK && dalloc(&d->part_l, parts) == UGB_OK &&
+            dalloc(&d->part_o, parts * c.head_dim) == UGB_OK && dalloc(&d->state, 1) == UGB_OK &&
+            cudaMallocHost(reinterpret_cast<void **>(&d->state_host), sizeof(DecodeState)) == cudaSuccess &&
             cudaStreamCreateWithFlags(&d->cap, cudaStreamNonBlocking) == cudaSuccess;
+  if (ok && d->moe) {
+    d->moe_ws_bytes = ugb_moe_workspace_bytes(c.n_embd, c.n_ff_expert, c.top_k, B);
+    ok = dalloc(&d->rlogits, static_cast<size_t>(B) * c.n_expert) == UGB_OK &&
+         dalloc(&d->rweights, static_cast<size_t>(B) * c.top_k) == UGB_OK &&
+         dalloc(&d->rids, static_cast<size_t>(B) * c.top_k) == UGB_OK &&
+         cudaMalloc(&d->moe_ws, d->moe_ws_bytes) == cudaSuccess;
+  } else if (ok) {
+    ok = dalloc(&d->gu, static_cast<size_t>(B) * 2 * c.n_ff) == UGB_OK &&
+         dalloc(&d->hq, q8act_layout(c.n_ff, B).bytes) == UGB_OK;
+  }
   if (ok) {
     // RoPE table as the reference builds it (gpu_graph.rs:132, llm.rs:330): the angle is the
     // f32 product pos * powf(theta, -(2i)/head_dim); cos and sin of that f32 angle are taken in
@@ -127,10 +174,10 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
                         static_cast<float>(std::sin(static_cast<double>(ang))));
       }
     ok = cudaMemcpy(d->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) == cudaSuccess &&
-         cudaMemset(d->state, 0, 4 * sizeof(int32_t)) == cudaSuccess &&
+         cudaMemset(d->state, 0, sizeof(DecodeState)) == cudaSuccess &&
          cudaMemset(d->kcache, 0, kv * sizeof(float)) == cudaSuccess &&
          cudaMemset(d->vcache, 0, kv * sizeof(float)) == cudaSuccess &&
-         cudaMemset(d->dx, 0, c.n_embd * sizeof(float)) == cudaSuccess;
+         cudaMemset(d->dx, 0, static_cast<size_t>(B) * c.n_embd * sizeof(float)) == cudaSuccess;
   }
   if (!ok) {
     free_all(d);
@@ -150,6 +197,13 @@ extern "C" ugb_status ugb_decoder_destroy(ugb_decoder *dec) {
   return UGB_OK;
 }
 
+extern "C" ugb_status ugb_decoder_set_comm(ugb_decoder *d, ugb_comm *comm) {
+  if (!d) return UGB_ECONTEXT;
+  d->comm = comm;
+  free_graph(d);  // the captured step may or may not contain the collectives
+  return UGB_OK;
+}
+
 namespace ugb {
 namespace {
 
@@ -162,7 +216,7 @@ ugb_status copy_bias(float *dst, const void *src, int64_t n) {
   return cuda_status(cudaMemcpy(dst, src, n * sizeof(float), cudaMemcpyDeviceToDevice));
 }
 
-// Host-generated f32 vector: 1 + amp * u (u uniform in [-1, 1)) or amp * u when center == 0.
+// Host-generated f32 vector: center + amp * u, u uniform in [-1, 1).
 ugb_status upload_vec(float **dst, int64_t n, float center, float amp, std::mt19937_64 &rng,
                       std::vector<void *> &owned) {
   std::vector<float> h(static_cast<size_t>(n));
@@ -173,30 +227,20 @@ ugb_status upload_vec(float **dst, int64_t n, float center, float amp, std::mt19
   return cuda_status(cudaMemcpy(*dst, h.data(), n * sizeof(float), cudaMemcpyHostToDevice));
 }
 
-ugb_status synth_matrix(ugb_ctx *ctx, const void **dst, uint32_t kind, int64_t k, int64_t m,
-                        uint64_t seed, std::vector<void *> &owned) {
+// `count` matrices of m x k stacked back to back; matrix i filled from seed0 + i.
+ugb_status synth_stack(ugb_ctx *ctx, const void **dst, uint32_t kind, int64_t k, int64_t m, int64_t count,
+                       uint64_t seed0, std::vector<void *> &owned) {
   const int64_t rb = ugb_row_bytes(kind, k);
   void *p = nullptr;
-  if (rb < 0 || cudaMalloc(&p, static_cast<size_t>(rb * m)) != cudaSuccess) return UGB_EBACKEND;
+  if (rb < 0 || cudaMalloc(&p, static_cast<size_t>(rb * m * count)) != cudaSuccess) return UGB_EBACKEND;
   owned.push_back(p);
   *dst = p;
-  return launch_fill_synthetic(ctx, nullptr, kind, static_cast<uint8_t *>(p), k, m, seed);
-}
-
-MatvecArgs mv_args(const ugb_decoder *d, uint32_t kind, int64_t k, int64_t m, const uint8_t *xq, float *y) {
-  MatvecArgs a;
-  a.kind = kind;
-  a.row_bytes = ugb_row_bytes(kind, k);
-  a.k = k;
-  a.m = m;
-  a.xq = xq;
-  a.xl = q8act_layout(k, 1);
-  a.y = y;
-  a.ldy = m;
-  a.batch = 1;
-  a.pdl = true;
-  (void)d;
-  return a;
+  for (int64_t i = 0; i < count; ++i) {
+    const ugb_status st = launch_fill_synthetic(ctx, nullptr, kind, static_cast<uint8_t *>(p) + i * rb * m, k, m,
+                                                seed0 + static_cast<uint64_t>(i));
+    if (st != UGB_OK) return st;
+  }
+  return UGB_OK;
 }
 
 }  // namespace
@@ -213,8 +257,16 @@ extern "C" ugb_status ugb_decoder_bind(ugb_decoder *d, const ugb_model_weights *
   bool any_bias = false;
   for (int l = 0; l < c.n_layer; ++l) {
     const ugb_layer_weights &L = w->layers[l];
-    for (const void *m : {L.wq, L.wk, L.wv, L.wo, L.w_gate, L.w_up, L.w_down})
+    for (const void *m : {L.wq, L.wk, L.wv, L.wo})
       if (!matrix_ok(c.kind, m)) return UGB_EALIGN;
+    if (d->moe) {
+      if (!matrix_ok(c.kind, L.router)) return UGB_EALIGN;
+      for (const void *m : {L.gate_exps, L.up_exps, L.down_exps})
+        if (!matrix_ok(c.expert_kind, m)) return UGB_EALIGN;
+    } else {
+      for (const void *m : {L.w_gate, L.w_up, L.w_down})
+        if (!matrix_ok(c.kind, m)) return UGB_EALIGN;
+    }
     if (!L.attn_norm || !L.ffn_norm) return UGB_EALIGN;
     any_bias = any_bias || L.bq || L.bk || L.bv;
   }
@@ -237,12 +289,7 @@ extern "C" ugb_status ugb_decoder_bind(ugb_decoder *d, const ugb_model_weights *
   d->w = *w;
   d->layers.assign(w->layers, w->layers + c.n_layer);
   d->w.layers = d->layers.data();
-  if (d->exec) {  // the captured step refers to the old weights
-    cudaGraphExecDestroy(d->exec);
-    cudaGraphDestroy(d->graph);
-    d->exec = nullptr;
-    d->graph = nullptr;
-  }
+  free_graph(d);  // the captured step refers to the old weights
   return UGB_OK;
 }
 
@@ -250,40 +297,65 @@ extern "C" ugb_status ugb_decoder_synthetic(ugb_decoder *d, uint64_t seed) {
   if (!d) return UGB_ECONTEXT;
   const ugb_decoder_config &c = d->cfg;
   cudaSetDevice(d->ctx->device);
-  std::mt19937_64 rng(seed);
   const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
   const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
   std::vector<ugb_layer_weights> layers(c.n_layer);
   ugb_model_weights w{};
-  uint64_t s = seed * 1000003ull;
-  ugb_status st = synth_matrix(d->ctx, &w.tok_embd, UGB_Q8_0, c.n_embd, c.n_vocab, ++s, d->owned);
+  // every tensor's seed depends on (seed, layer, tensor[, expert]) only, so the shards of an
+  // expert-parallel or vocabulary-split model agree on the tensors they share
+  const uint64_t base = seed * 1000003ull;
+  auto tseed = [&](int layer, int slot) { return base + 64ull * (layer + 1) + slot; };
+  ugb_status st = synth_stack(d->ctx, &w.tok_embd, UGB_Q8_0, c.n_embd, c.n_vocab, 1, base, d->owned);
+  std::mt19937_64 rng0(seed);
   float *onorm = nullptr;
-  if (st == UGB_OK) st = upload_vec(&onorm, c.n_embd, 1.f, 0.1f, rng, d->owned);
+  if (st == UGB_OK) st = upload_vec(&onorm, c.n_embd, 1.f, 0.1f, rng0, d->owned);
   w.output_norm = onorm;
   if (st == UGB_OK) {
-    if (c.head_kind == UGB_Q8_0) w.output = w.tok_embd;  // tied embeddings
-    else st = synth_matrix(d->ctx, &w.output, c.head_kind, c.n_embd, c.n_vocab, ++s, d->owned);
+    if (c.head_kind == UGB_Q8_0) {  // tied embeddings: the held rows of token_embd
+      w.output = static_cast<const uint8_t *>(w.tok_embd) + static_cast<int64_t>(c.vocab0) * ugb_row_bytes(UGB_Q8_0, c.n_embd);
+    } else {
+      st = synth_stack(d->ctx, &w.output, c.head_kind, c.n_embd, d->n_vocab_local, 1,
+                       base + 7 + static_cast<uint64_t>(c.vocab0), d->owned);
+    }
   }
   for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
     ugb_layer_weights &L = layers[l];
-    float *an = nullptr, *fn = nullptr, *bq = nullptr, *bk = nullptr, *bv = nullptr;
+    std::mt19937_64 rng(seed * 7919ull + l);
+    float *an = nullptr, *fn = nullptr;
     st = upload_vec(&an, c.n_embd, 1.f, 0.1f, rng, d->owned);
     if (st == UGB_OK) st = upload_vec(&fn, c.n_embd, 1.f, 0.1f, rng, d->owned);
-    if (st == UGB_OK) st = upload_vec(&bq, qrows, 0.f, 0.02f, rng, d->owned);
-    if (st == UGB_OK) st = upload_vec(&bk, kvrows, 0.f, 0.02f, rng, d->owned);
-    if (st == UGB_OK) st = upload_vec(&bv, kvrows, 0.f, 0.02f, rng, d->owned);
     L.attn_norm = an;
     L.ffn_norm = fn;
-    L.bq = bq;
-    L.bk = bk;
-    L.bv = bv;
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wq, c.kind, c.n_embd, qrows, ++s, d->owned);
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wk, c.kind, c.n_embd, kvrows, ++s, d->owned);
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wv, c.kind, c.n_embd, kvrows, ++s, d->owned);
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.wo, c.kind, qrows, c.n_embd, ++s, d->owned);
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.w_gate, c.kind, c.n_embd, c.n_ff, ++s, d->owned);
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.w_up, c.kind, c.n_embd, c.n_ff, ++s, d->owned);
-    if (st == UGB_OK) st = synth_matrix(d->ctx, &L.w_down, c.kind, c.n_ff, c.n_embd, ++s, d->owned);
+    if (!d->moe) {  // the dense (Qwen2) shapes carry Q/K/V biases
+      float *bq = nullptr, *bk = nullptr, *bv = nullptr;
+      if (st == UGB_OK) st = upload_vec(&bq, qrows, 0.f, 0.02f, rng, d->owned);
+      if (st == UGB_OK) st = upload_vec(&bk, kvrows, 0.f, 0.02f, rng, d->owned);
+      if (st == UGB_OK) st = upload_vec(&bv, kvrows, 0.f, 0.02f, rng, d->owned);
+      L.bq = bq;
+      L.bk = bk;
+      L.bv = bv;
+    }
+    if (st == UGB_OK) st = synth_stack(d->ctx, &L.wq, c.kind, c.n_embd, qrows, 1, tseed(l, 0), d->owned);
+    if (st == UGB_OK) st = synth_stack(d->ctx, &L.wk, c.kind, c.n_embd, kvrows, 1, tseed(l, 1), d->owned);
+    if (st == UGB_OK) st = synth_stack(d->ctx, &L.wv, c.kind, c.n_embd, kvrows, 1, tseed(l, 2), d->owned);
+    if (st == UGB_OK) st = synth_stack(d->ctx, &L.wo, c.kind, qrows, c.n_embd, 1, tseed(l, 3), d->owned);
+    if (d->moe) {
+      const uint64_t eb = base + (1ull << 32) + static_cast<uint64_t>(l) * 3 * c.n_expert;
+      if (st == UGB_OK) st = synth_stack(d->ctx, &L.router, c.kind, c.n_embd, c.n_expert, 1, tseed(l, 4), d->owned);
+      if (st == UGB_OK)
+        st = synth_stack(d->ctx, &L.gate_exps, c.expert_kind, c.n_embd, c.n_ff_expert, d->n_expert_local,
+                         eb + c.expert0, d->owned);
+      if (st == UGB_OK)
+        st = synth_stack(d->ctx, &L.up_exps, c.expert_kind, c.n_embd, c.n_ff_expert, d->n_expert_local,
+                         eb + c.n_expert + c.expert0, d->owned);
+      if (st == UGB_OK)
+        st = synth_stack(d->ctx, &L.down_exps, c.expert_kind, c.n_ff_expert, c.n_embd, d->n_expert_local,
+                         eb + 2 * c.n_expert + c.expert0, d->owned);
+    } else {
+      if (st == UGB_OK) st = synth_stack(d->ctx, &L.w_gate, c.kind, c.n_embd, c.n_ff, 1, tseed(l, 5), d->owned);
+      if (st == UGB_OK) st = synth_stack(d->ctx, &L.w_up, c.kind, c.n_embd, c.n_ff, 1, tseed(l, 6), d->owned);
+      if (st == UGB_OK) st = synth_stack(d->ctx, &L.w_down, c.kind, c.n_ff, c.n_embd, 1, tseed(l, 7), d->owned);
+    }
   }
   if (st != UGB_OK) return st;
   if (cudaDeviceSynchronize() != cudaSuccess) return UGB_EBACKEND;
@@ -291,23 +363,47 @@ extern "C" ugb_status ugb_decoder_synthetic(ugb_decoder *d, uint64_t seed) {
   return ugb_decoder_bind(d, &w);
 }
 
+namespace ugb {
+namespace {
+
+MatvecArgs mv_args(uint32_t kind, int64_t k, int64_t m, int batch, const uint8_t *xq, float *y) {
+  MatvecArgs a;
+  a.kind = kind;
+  a.row_bytes = ugb_row_bytes(kind, k);
+  a.k = k;
+  a.m = m;
+  a.xq = xq;
+  a.xl = q8act_layout(k, batch);
+  a.y = y;
+  a.ldy = m;
+  a.batch = batch;
+  a.pdl = true;
+  return a;
+}
+
+}  // namespace
+}  // namespace ugb
+
 extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
   if (!d || !d->w.layers) return UGB_ECONTEXT;
   const ugb_decoder_config &c = d->cfg;
   ugb_ctx *ctx = d->ctx;
   uint32_t *status = ctx->status;
+  const int B = d->batch;
   const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
   const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
   const int64_t brow = qrows + 2 * kvrows;
   const size_t kv_layer = static_cast<size_t>(kvrows) * c.n_ctx;
-  ugb_status st = launch_embed(stream, false, static_cast<const uint8_t *>(d->w.tok_embd), c.n_embd,
-                               c.n_vocab, c.n_ctx, d->state, d->x, status);
+  const bool ep_reduce = d->moe && d->comm && d->n_expert_local < c.n_expert;
+  const bool vocab_reduce = d->comm && d->n_vocab_local < c.n_vocab;
+  ugb_status st = launch_embed(stream, false, static_cast<const uint8_t *>(d->w.tok_embd), c.n_embd, c.n_vocab,
+                               c.n_ctx, B, d->state, d->x, status);
   for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
     const ugb_layer_weights &L = d->layers[l];
-    st = launch_rmsnorm_quant(stream, true, d->x, l == 0 ? nullptr : d->dx,
-                              static_cast<const float *>(L.attn_norm), c.n_embd, c.norm_eps, d->xq, status);
+    st = launch_rmsnorm_quant(stream, true, d->x, l == 0 ? nullptr : d->dx, static_cast<const float *>(L.attn_norm),
+                              c.n_embd, B, c.norm_eps, d->xq, l == 0 ? d->state : nullptr, status);
     if (st != UGB_OK) break;
-    MatvecArgs a = mv_args(d, c.kind, c.n_embd, brow, d->xq, d->qkv);
+    MatvecArgs a = mv_args(c.kind, c.n_embd, brow, B, d->xq, d->qkv);
     a.nseg = 3;
     a.ws[0] = static_cast<const uint8_t *>(L.wq);
     a.ws[1] = static_cast<const uint8_t *>(L.wk);
@@ -322,6 +418,7 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
     ap.rope = d->rope;
     ap.kcache = d->kcache + kv_layer * l;
     ap.vcache = d->vcache + kv_layer * l;
+    ap.cache_seq = d->cache_seq;
     ap.part_m = d->part_m;
     ap.part_l = d->part_l;
     ap.part_o = d->part_o;
@@ -331,98 +428,166 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
     ap.n_ctx = c.n_ctx;
     ap.n_split = d->n_split;
     ap.status = status;
-    st = launch_attention(stream, true, ap, d->attq);
+    st = launch_attention(stream, true, ap, B, d->attq);
     if (st != UGB_OK) break;
-    a = mv_args(d, c.kind, qrows, c.n_embd, d->attq, d->dx);
+    a = mv_args(c.kind, qrows, c.n_embd, B, d->attq, d->dx);
     a.w = static_cast<const uint8_t *>(L.wo);
     st = launch_matvec(ctx, stream, a);
     if (st != UGB_OK) break;
-    st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(L.ffn_norm), c.n_embd,
-                              c.norm_eps, d->xq, status);
+    st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(L.ffn_norm), c.n_embd, B,
+                              c.norm_eps, d->xq, nullptr, status);
     if (st != UGB_OK) break;
-    a = mv_args(d, c.kind, c.n_embd, 2 * static_cast<int64_t>(c.n_ff), d->xq, d->gu);
-    a.nseg = 2;
-    a.ws[0] = static_cast<const uint8_t *>(L.w_gate);
-    a.ws[1] = static_cast<const uint8_t *>(L.w_up);
-    a.seg_rows[0] = a.seg_rows[1] = c.n_ff;
-    st = launch_matvec(ctx, stream, a);
-    if (st != UGB_OK) break;
-    st = launch_silu_quant(stream, true, d->gu, c.n_ff, d->hq, status);
-    if (st != UGB_OK) break;
-    a = mv_args(d, c.kind, c.n_ff, c.n_embd, d->hq, d->dx);
-    a.w = static_cast<const uint8_t *>(L.w_down);
-    st = launch_matvec(ctx, stream, a);
+    if (d->moe) {
+      a = mv_args(c.kind, c.n_embd, c.n_expert, B, d->xq, d->rlogits);
+      a.w = static_cast<const uint8_t *>(L.router);
+      st = launch_matvec(ctx, stream, a);
+      if (st == UGB_OK)
+        st = launch_moe_route(ctx, stream, true, d->rlogits, c.n_expert, c.top_k, B, d->rids, d->rweights);
+      if (st != UGB_OK) break;
+      ugb_moe_args m{};
+      m.kind = c.expert_kind;
+      m.accumulate = 0;
+      m.hidden = c.n_embd;
+      m.ffn = c.n_ff_expert;
+      m.top_k = c.top_k;
+      m.batch = B;
+      m.n_expert = d->n_expert_local;
+      m.expert0 = c.expert0;
+      m.n_expert_total = c.n_expert;
+      m.gate = L.gate_exps;
+      m.up = L.up_exps;
+      m.down = L.down_exps;
+      m.xq = d->xq;
+      m.ids = d->rids;
+      m.weights = d->rweights;
+      m.out = d->dx;
+      m.workspace = d->moe_ws;
+      m.workspace_bytes = d->moe_ws_bytes;
+      st = launch_moe_experts(ctx, stream, m);
+      if (st == UGB_OK && ep_reduce)
+        st = comm_allreduce_sum_f32(d->comm, d->dx, static_cast<size_t>(B) * c.n_embd, stream);
+    } else {
+      a = mv_args(c.kind, c.n_embd, 2 * static_cast<int64_t>(c.n_ff), B, d->xq, d->gu);
+      a.nseg = 2;
+      a.ws[0] = static_cast<const uint8_t *>(L.w_gate);
+      a.ws[1] = static_cast<const uint8_t *>(L.w_up);
+      a.seg_rows[0] = a.seg_rows[1] = c.n_ff;
+      st = launch_matvec(ctx, stream, a);
+      if (st != UGB_OK) break;
+      st = launch_silu_quant(stream, true, d->gu, c.n_ff, B, d->hq, status);
+      if (st != UGB_OK) break;
+      a = mv_args(c.kind, c.n_ff, c.n_embd, B, d->hq, d->dx);
+      a.w = static_cast<const uint8_t *>(L.w_down);
+      st = launch_matvec(ctx, stream, a);
+    }
   }
   if (st != UGB_OK) return st;
-  st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(d->w.output_norm), c.n_embd,
-                            c.norm_eps, d->xq, status);
+  st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(d->w.output_norm), c.n_embd, B,
+                            c.norm_eps, d->xq, nullptr, status);
   if (st != UGB_OK) return st;
-  MatvecArgs a = mv_args(d, c.head_kind, c.n_embd, c.n_vocab, d->xq, d->logits);
+  MatvecArgs a = mv_args(c.head_kind, c.n_embd, d->n_vocab_local, B, d->xq, d->logits);
   a.w = static_cast<const uint8_t *>(d->w.output);
   st = launch_matvec(ctx, stream, a);
   if (st != UGB_OK) return st;
-  return launch_argmax(stream, true, d->logits, c.n_vocab, d->state, ctx->sm_count);
+  st = launch_argmax(stream, true, d->logits, d->n_vocab_local, B, c.vocab0, d->state, ctx->sm_count);
+  if (st == UGB_OK && vocab_reduce) st = comm_allreduce_max_u64(d->comm, d->state->key, B, stream);
+  return st;
+}
+
+extern "C" ugb_status ugb_decoder_set_tokens(ugb_decoder *d, ugb_stream stream, const int32_t *tokens, int32_t pos) {
+  if (!d || !tokens) return UGB_ECONTEXT;
+  if (pos < 0 || pos >= d->cfg.n_ctx) return UGB_ESHAPE;
+  for (int b = 0; b < d->batch; ++b)
+    if (tokens[b] < 0 || tokens[b] >= d->cfg.n_vocab) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  // Wait for any earlier copy out of the pinned mirror before overwriting it.
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
+  std::memset(d->state_host, 0, sizeof(DecodeState));
+  for (int b = 0; b < d->batch; ++b) d->state_host->token[b] = tokens[b];
+  d->state_host->pos = pos;
+  return cuda_status(cudaMemcpyAsync(d->state, d->state_host, sizeof(DecodeState), cudaMemcpyHostToDevice, stream));
 }
 
 extern "C" ugb_status ugb_decoder_set_state(ugb_decoder *d, ugb_stream stream, int32_t token, int32_t pos) {
   if (!d) return UGB_ECONTEXT;
-  if (token < 0 || token >= d->cfg.n_vocab || pos < 0 || pos >= d->cfg.n_ctx) return UGB_ESHAPE;
+  int32_t t[kMaxSeq];
+  for (int b = 0; b < kMaxSeq; ++b) t[b] = token;
+  return ugb_decoder_set_tokens(d, stream, t, pos);
+}
+
+namespace {
+
+ugb_status fetch_state(ugb_decoder *d, cudaStream_t stream) {
   cudaSetDevice(d->ctx->device);
-  // Wait for any earlier copy out of the pinned mirror before overwriting it.
-  if (cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
-  d->state_host[0] = token;
-  d->state_host[1] = pos;
-  d->state_host[2] = d->state_host[3] = 0;
-  return cuda_status(cudaMemcpyAsync(d->state, d->state_host, 4 * sizeof(int32_t), cudaMemcpyHostToDevice, stream));
+  if (cudaMemcpyAsync(d->state_host, d->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  return UGB_OK;
+}
+
+int32_t next_of(const DecodeState *s, int b) {
+  return s->key[b] ? static_cast<int32_t>(~static_cast<uint32_t>(s->key[b])) : -1;
+}
+
+}  // namespace
+
+extern "C" ugb_status ugb_decoder_get_tokens(ugb_decoder *d, ugb_stream stream, int32_t *tokens, int32_t *pos,
+                                             int32_t *next_tokens) {
+  if (!d) return UGB_ECONTEXT;
+  const ugb_status st = fetch_state(d, stream);
+  if (st != UGB_OK) return st;
+  for (int b = 0; b < d->batch; ++b) {
+    if (tokens) tokens[b] = d->state_host->token[b];
+    if (next_tokens) next_tokens[b] = next_of(d->state_host, b);
+  }
+  if (pos) *pos = d->state_host->pos;
+  return UGB_OK;
 }
 
 extern "C" ugb_status ugb_decoder_get_state(ugb_decoder *d, ugb_stream stream, int32_t *token, int32_t *pos,
                                             int32_t *next_token) {
   if (!d) return UGB_ECONTEXT;
-  cudaSetDevice(d->ctx->device);
-  if (cudaMemcpyAsync(d->state_host, d->state, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-      cudaStreamSynchronize(stream) != cudaSuccess)
-    return UGB_EBACKEND;
-  uint64_t key;
-  std::memcpy(&key, d->state_host + 2, 8);
-  if (token) *token = d->state_host[0];
-  if (pos) *pos = d->state_host[1];
-  if (next_token) *next_token = key ? static_cast<int32_t>(~static_cast<uint32_t>(key)) : -1;
+  const ugb_status st = fetch_state(d, stream);
+  if (st != UGB_OK) return st;
+  if (token) *token = d->state_host->token[0];
+  if (pos) *pos = d->state_host->pos;
+  if (next_token) *next_token = next_of(d->state_host, 0);
   return UGB_OK;
 }
 
 extern "C" ugb_status ugb_decoder_logits(ugb_decoder *d, ugb_stream stream, float *logits_host) {
   if (!d || !logits_host) return UGB_ECONTEXT;
   cudaSetDevice(d->ctx->device);
-  if (cudaMemcpyAsync(logits_host, d->logits, static_cast<size_t>(d->cfg.n_vocab) * sizeof(float),
+  if (cudaMemcpyAsync(logits_host, d->logits, static_cast<size_t>(d->batch) * d->n_vocab_local * sizeof(float),
                       cudaMemcpyDeviceToHost, stream) != cudaSuccess)
     return UGB_EBACKEND;
   return cuda_status(cudaStreamSynchronize(stream));
 }
 
-extern "C" ugb_status ugb_decoder_read_kv(ugb_decoder *d, ugb_stream stream, int32_t layer, int32_t pos,
+extern "C" ugb_status ugb_decoder_read_kv(ugb_decoder *d, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
                                           int32_t count, float *k_host, float *v_host) {
   if (!d || !k_host || !v_host) return UGB_ECONTEXT;
   const ugb_decoder_config &c = d->cfg;
-  if (layer < 0 || layer >= c.n_layer || pos < 0 || count < 1 || count > c.n_ctx - pos) return UGB_ESHAPE;
+  if (seq < 0 || seq >= d->batch || layer < 0 || layer >= c.n_layer || pos < 0 || count < 1 || count > c.n_ctx - pos)
+    return UGB_ESHAPE;
   cudaSetDevice(d->ctx->device);
   const size_t hd = static_cast<size_t>(c.head_dim);
-  const size_t layer_off = static_cast<size_t>(layer) * c.n_head_kv * c.n_ctx * hd;
+  const size_t off = static_cast<size_t>(seq) * d->cache_seq + static_cast<size_t>(layer) * c.n_head_kv * c.n_ctx * hd;
   const size_t row = count * hd * sizeof(float);
   for (int which = 0; which < 2; ++which) {
-    const float *src = (which ? d->vcache : d->kcache) + layer_off + static_cast<size_t>(pos) * hd;
+    const float *src = (which ? d->vcache : d->kcache) + off + static_cast<size_t>(pos) * hd;
     float *dst = which ? v_host : k_host;
     // one row per KV head: [n_kv][n_ctx][hd] (pitch n_ctx*hd) -> [n_kv][count][hd]
-    if (cudaMemcpy2DAsync(dst, row, src, c.n_ctx * hd * sizeof(float), row, c.n_head_kv,
-                          cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    if (cudaMemcpy2DAsync(dst, row, src, c.n_ctx * hd * sizeof(float), row, c.n_head_kv, cudaMemcpyDeviceToHost,
+                          stream) != cudaSuccess)
       return UGB_EBACKEND;
   }
   return cuda_status(cudaStreamSynchronize(stream));
 }
 
-extern "C" ugb_status ugb_decoder_token(ugb_decoder *d, ugb_stream stream, int32_t token, int32_t pos,
-                                        int32_t *next_token) {
-  if (!d || !next_token) return UGB_ECONTEXT;
+extern "C" ugb_status ugb_decoder_tokens(ugb_decoder *d, ugb_stream stream, const int32_t *tokens, int32_t pos,
+                                         int32_t *next_tokens) {
+  if (!d || !tokens || !next_tokens) return UGB_ECONTEXT;
   cudaSetDevice(d->ctx->device);
   if (!d->exec) {
     if (cudaStreamBeginCapture(d->cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) return UGB_EBACKEND;
@@ -439,17 +604,27 @@ extern "C" ugb_status ugb_decoder_token(ugb_decoder *d, ugb_stream stream, int32
     }
     d->graph = g;
   }
-  ugb_status st = ugb_decoder_set_state(d, stream, token, pos);
+  ugb_status st = ugb_decoder_set_tokens(d, stream, tokens, pos);
   if (st != UGB_OK) return st;
   if (cudaGraphLaunch(d->exec, stream) != cudaSuccess) return UGB_EBACKEND;
-  if (cudaMemcpyAsync(d->state_host, d->state, 4 * sizeof(int32_t), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+  if (cudaMemcpyAsync(d->state_host, d->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
     return UGB_EBACKEND;
   uint32_t bits = 0;
   st = ugb_status_read(d->ctx, stream, &bits);  // synchronises the stream
   if (st != UGB_OK) return st;
-  uint64_t key;
-  std::memcpy(&key, d->state_host + 2, 8);
-  if (!key) return UGB_ENONFINITE;  // every logit was non-finite
-  *next_token = static_cast<int32_t>(~static_cast<uint32_t>(key));
+  for (int b = 0; b < d->batch; ++b) {
+    next_tokens[b] = next_of(d->state_host, b);
+    if (next_tokens[b] < 0) return UGB_ENONFINITE;  // every logit of a sequence was non-finite
+  }
   return UGB_OK;
+}
+
+extern "C" ugb_status ugb_decoder_token(ugb_decoder *d, ugb_stream stream, int32_t token, int32_t pos,
+                                        int32_t *next_token) {
+  if (!d || !next_token) return UGB_ECONTEXT;
+  int32_t t[kMaxSeq], n[kMaxSeq];
+  for (int b = 0; b < kMaxSeq; ++b) t[b] = token;
+  const ugb_status st = ugb_decoder_tokens(d, stream, t, pos, n);
+  *next_token = n[0];
+  return st;
 }

@@ -74,6 +74,11 @@ ugb_status launch_fill_synthetic(ugb_ctx *ctx, cudaStream_t stream, uint32_t kin
                                  int64_t k, int64_t m, uint64_t seed);
 ugb_status init_matvec_kernels(ugb_ctx *ctx);
 
+// Collectives of a sharded decode step (comm.cu).
+ugb_status comm_allreduce_sum_f32(ugb_comm *c, float *buf, size_t n, cudaStream_t stream);
+ugb_status comm_allreduce_max_u64(ugb_comm *c, unsigned long long *buf, size_t n, cudaStream_t stream);
+int comm_world(const ugb_comm *c);
+
 // Validation shared by entry points: kind supported by the matvec kernels, k a multiple of
 // its block, row_bytes consistent.
 ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_t k, int64_t m);

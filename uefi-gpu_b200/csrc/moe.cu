@@ -17,6 +17,7 @@
 #include <cmath>
 
 #include "common.cuh"
+#include "decode.hpp"
 #include "internal.hpp"
 
 namespace ugb {
@@ -209,6 +210,73 @@ MoeLayout moe_layout(int64_t hidden, int64_t ffn, int64_t top_k, int64_t batch) 
 
 }  // namespace
 
+namespace ugb {
+
+ugb_status launch_moe_route(ugb_ctx *ctx, cudaStream_t stream, bool pdl, const float *logits, int n_expert,
+                            int top_k, int batch, int32_t *ids, float *weights) {
+  return launch_pdl(moe_route_kernel, dim3(static_cast<unsigned>(batch)), dim3(32), stream, pdl, logits, n_expert,
+                    top_k, ids, weights, ctx->status);
+}
+
+// gate/up of every held slot (two routed matrices per slot sharing the token's activation) ->
+// SiLU*up quant -> down (one routed matrix per slot on its own activation) -> combine.
+ugb_status launch_moe_experts(ugb_ctx *ctx, cudaStream_t stream, const ugb_moe_args &m) {
+  const int64_t rb_in = ugb_row_bytes(m.kind, m.hidden), rb_ff = ugb_row_bytes(m.kind, m.ffn);
+  const MoeLayout l = moe_layout(m.hidden, m.ffn, m.top_k, m.batch);
+  uint8_t *ws = static_cast<uint8_t *>(m.workspace);
+  float *gu = reinterpret_cast<float *>(ws + l.gu);
+  uint8_t *hq = ws + l.hq;
+  float *values = reinterpret_cast<float *>(ws + l.values);
+  const int slots = static_cast<int>(l.slots);
+  MatvecArgs a;
+  a.kind = m.kind;
+  a.k = m.hidden;
+  a.m = m.ffn;
+  a.row_bytes = rb_in;
+  a.xq = static_cast<const uint8_t *>(m.xq);
+  a.xl = q8act_layout(m.hidden, m.batch);
+  a.y = gu;
+  a.pdl = true;
+  a.ids = m.ids;
+  a.n_slots = slots;
+  a.per_slot = 2;
+  a.n_expert = static_cast<int>(m.n_expert);
+  a.expert0 = static_cast<int>(m.expert0);
+  a.n_total = static_cast<int>(m.n_expert_total);
+  a.x_div = static_cast<int>(m.top_k);
+  a.ebase[0] = static_cast<const uint8_t *>(m.gate);
+  a.ebase[1] = static_cast<const uint8_t *>(m.up);
+  a.estride = static_cast<uint64_t>(rb_in) * m.ffn;
+  a.y_slot = 2 * m.ffn;
+  ugb_status st = launch_matvec(ctx, stream, a);
+  if (st != UGB_OK) return st;
+  st = launch_pdl(moe_silu_quant_kernel, dim3(static_cast<unsigned>((l.hl.nbp + 7) / 8), static_cast<unsigned>(slots)),
+                  dim3(256), stream, true, gu, static_cast<int>(m.ffn), m.ids, static_cast<int>(m.expert0),
+                  static_cast<int>(m.n_expert), hq, l.hl.d_off, l.hl.s_off, static_cast<int>(l.hl.nbp), ctx->status);
+  if (st != UGB_OK) return st;
+  MatvecArgs b = a;
+  b.k = m.ffn;
+  b.m = m.hidden;
+  b.row_bytes = rb_ff;
+  b.xq = hq;
+  b.xl = l.hl;
+  b.y = values;
+  b.per_slot = 1;
+  b.x_div = 1;
+  b.ebase[0] = static_cast<const uint8_t *>(m.down);
+  b.ebase[1] = nullptr;
+  b.estride = static_cast<uint64_t>(rb_ff) * m.hidden;
+  b.y_slot = m.hidden;
+  st = launch_matvec(ctx, stream, b);
+  if (st != UGB_OK) return st;
+  return launch_pdl(moe_combine_kernel, dim3(static_cast<unsigned>((m.hidden + 255) / 256), static_cast<unsigned>(m.batch)),
+                    dim3(256), stream, true, static_cast<const float *>(values), m.weights, m.ids,
+                    static_cast<int>(m.top_k), static_cast<int>(m.hidden), static_cast<int>(m.expert0),
+                    static_cast<int>(m.n_expert), m.accumulate, m.out, ctx->status);
+}
+
+}  // namespace ugb
+
 extern "C" {
 
 ugb_status ugb_matvec_jobs(ugb_ctx *ctx, ugb_stream stream, const ugb_job *jobs, int count, int64_t batch) {
@@ -265,8 +333,8 @@ ugb_status ugb_moe_route(ugb_ctx *ctx, ugb_stream stream, const float *logits_de
       batch > 65535)
     return UGB_ESHAPE;
   if (!logits_dev || !ids_dev || !weights_dev) return UGB_EALIGN;
-  return launch_pdl(moe_route_kernel, dim3(static_cast<unsigned>(batch)), dim3(32), stream, ctx->pdl, logits_dev,
-                    static_cast<int>(n_expert), static_cast<int>(top_k), ids_dev, weights_dev, ctx->status);
+  return launch_moe_route(ctx, stream, ctx->pdl, logits_dev, static_cast<int>(n_expert), static_cast<int>(top_k),
+                          static_cast<int>(batch), ids_dev, weights_dev);
 }
 
 size_t ugb_moe_workspace_bytes(int64_t hidden, int64_t ffn, int64_t top_k, int64_t batch) {
@@ -297,67 +365,15 @@ ugb_status ugb_moe_experts(ugb_ctx *ctx, ugb_stream stream, const ugb_moe_args *
   const int64_t rb_in = ugb_row_bytes(m->kind, m->hidden), rb_ff = ugb_row_bytes(m->kind, m->ffn);
   if (rb_in == -1 || rb_ff == -1) return UGB_EQUANT;
   if (rb_in < 0 || rb_ff < 0) return UGB_ESHAPE;
-  const MoeLayout l = moe_layout(m->hidden, m->ffn, m->top_k, m->batch);
   if (!m->gate || !m->up || !m->down || !m->xq || !m->ids || !m->weights || !m->out || !m->workspace)
     return UGB_EALIGN;
-  if (m->workspace_bytes < l.bytes || (reinterpret_cast<uintptr_t>(m->workspace) & 255)) return UGB_ESHAPE;
-  ugb_status st;
+  if (m->workspace_bytes < moe_layout(m->hidden, m->ffn, m->top_k, m->batch).bytes ||
+      (reinterpret_cast<uintptr_t>(m->workspace) & 255))
+    return UGB_ESHAPE;
   for (const void *w : {m->gate, m->up, m->down})
     if ((reinterpret_cast<uintptr_t>(w) & 15) != 0) return UGB_EALIGN;
   std::lock_guard<std::mutex> lock(ctx->mu);
-  uint8_t *ws = static_cast<uint8_t *>(m->workspace);
-  float *gu = reinterpret_cast<float *>(ws + l.gu);
-  uint8_t *hq = ws + l.hq;
-  float *values = reinterpret_cast<float *>(ws + l.values);
-  const int slots = static_cast<int>(l.slots);
-  // gate and up of every slot: two routed matrices per slot sharing the token's activation
-  MatvecArgs a;
-  a.kind = m->kind;
-  a.k = m->hidden;
-  a.m = m->ffn;
-  a.row_bytes = rb_in;
-  a.xq = static_cast<const uint8_t *>(m->xq);
-  a.xl = q8act_layout(m->hidden, m->batch);
-  a.y = gu;
-  a.pdl = true;
-  a.ids = m->ids;
-  a.n_slots = slots;
-  a.per_slot = 2;
-  a.n_expert = static_cast<int>(m->n_expert);
-  a.expert0 = static_cast<int>(m->expert0);
-  a.n_total = static_cast<int>(m->n_expert_total);
-  a.x_div = static_cast<int>(m->top_k);
-  a.ebase[0] = static_cast<const uint8_t *>(m->gate);
-  a.ebase[1] = static_cast<const uint8_t *>(m->up);
-  a.estride = static_cast<uint64_t>(rb_in) * m->ffn;
-  a.y_slot = 2 * m->ffn;
-  st = launch_matvec(ctx, stream, a);
-  if (st != UGB_OK) return st;
-  st = launch_pdl(moe_silu_quant_kernel, dim3(static_cast<unsigned>((l.hl.nbp + 7) / 8), static_cast<unsigned>(slots)),
-                  dim3(256), stream, true, gu, static_cast<int>(m->ffn), m->ids, static_cast<int>(m->expert0),
-                  static_cast<int>(m->n_expert), hq, l.hl.d_off, l.hl.s_off, static_cast<int>(l.hl.nbp),
-                  ctx->status);
-  if (st != UGB_OK) return st;
-  // down of every slot: one routed matrix per slot on the slot's own activation
-  MatvecArgs b = a;
-  b.k = m->ffn;
-  b.m = m->hidden;
-  b.row_bytes = rb_ff;
-  b.xq = hq;
-  b.xl = l.hl;
-  b.y = values;
-  b.per_slot = 1;
-  b.x_div = 1;
-  b.ebase[0] = static_cast<const uint8_t *>(m->down);
-  b.ebase[1] = nullptr;
-  b.estride = static_cast<uint64_t>(rb_ff) * m->hidden;
-  b.y_slot = m->hidden;
-  st = launch_matvec(ctx, stream, b);
-  if (st != UGB_OK) return st;
-  return launch_pdl(moe_combine_kernel, dim3(static_cast<unsigned>((m->hidden + 255) / 256), static_cast<unsigned>(m->batch)),
-                    dim3(256), stream, true, static_cast<const float *>(values), m->weights, m->ids,
-                    static_cast<int>(m->top_k), static_cast<int>(m->hidden), static_cast<int>(m->expert0),
-                    static_cast<int>(m->n_expert), m->accumulate, m->out, ctx->status);
+  return launch_moe_experts(ctx, stream, *m);
 }
 
 }  // extern "C"
