@@ -12,6 +12,10 @@ Workloads:
       512-position context.  1.655 GB of weights stream from HBM per token (> L2).
   c1  Q8_0 matvec 8960x1536 with block-32 activation quantisation; weights
       rotate over 24 copies (350 MB > L2).
+  c4  greedy decode of a Qwen2.5-7B-shaped model, Q4_K weights, batch 1 / 4 / 8 (--batch),
+      context 1024; under torchrun the head rows are split over the GPUs (config 4).
+  c5  greedy decode of a 48-layer MoE (192 Q3_K experts, top-8), batch 1 / 8, context 2048;
+      under torchrun the experts are split over the GPUs (config 5).
   c3  the linear layers of a 512-token Q8 prefill of the same model (config 3): per layer the
       fused Q/K/V, O, fused gate/up and down GEMMs, each a block-32 activation quant plus the
       tcgen05 INT8 GEMM; weights repacked once outside timing (as the reference does).
@@ -253,6 +257,7 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     # advances the position on the device (embedding kernel), so K replays decode K tokens.
     dec.set_state(1, 0, stream)
     graph = ctx.capture(lambda: dec.step(), cap)
+    kernels_per_token = graph.kernels()
 
     def run(first_pos, count, tok=1):
         """count replays starting at first_pos; re-seed the state when the context is full."""
@@ -338,7 +343,7 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     kgraph.close()
     return {
         "value": world * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
-        "gpu_launches": c2_launches_per_token(c) * K,
+        "gpu_launches": kernels_per_token * K,
         "token_bytes": token_bytes,
         "kernel_ms": kern_ms, "kernel_bytes": kern_bytes,
         "e2e": {"value": world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
@@ -619,6 +624,194 @@ def c3_cpu(budget_s: float, c=C2):
     return tokens / (dt * c["n_layer"]), tokens, threads
 
 
+# ---- workloads c4 / c5: batched and sharded decode of the larger configs ---------------------
+
+Q3_K, Q4_K = 11, 12
+KIND_BLOCK = {Q8_0: (32, 34), Q4_K: (256, 144), Q3_K: (256, 110)}
+
+# Qwen2.5-7B-shaped, Q4_K linear weights, Q8_0 head (tied here: the
+# same bytes stream per token), batch 1 / 4 / 8 at context 1024, head row-split over the GPUs.
+C4 = dict(n_layer=28, n_embd=3584, n_ff=18944, n_head=28, n_head_kv=4, head_dim=128, n_vocab=152064,
+          n_ctx=1024, rope_theta=1e6, norm_eps=1e-6, kind=Q4_K, head_kind=Q8_0)
+# 48 layers, hidden 4096, 192 Q3_K experts of 1536 (top-8 softmax),
+# 32 / 4 heads of 128, Q8_0 attention and router, vocab 151936, batch 1 / 8 at context 2048,
+# expert-parallel over the GPUs.
+C5 = dict(n_layer=48, n_embd=4096, n_ff=0, n_head=32, n_head_kv=4, head_dim=128, n_vocab=151936,
+          n_ctx=2048, rope_theta=1e6, norm_eps=1e-6, kind=Q8_0, head_kind=Q8_0, n_expert=192, top_k=8,
+          n_ff_expert=1536, expert_kind=Q3_K)
+
+
+def kbytes(kind, k, m):
+    e, b = KIND_BLOCK[kind]
+    return m * (k // e) * b
+
+
+def big_step_bytes(c, batch, pos, world=1, rank=0):
+    """Algorithmic bytes one device streams per step: its weights once (dense layers; the
+    routed experts actually selected by the batch -- top_k per token, at most every held
+    expert -- at their expected distinct count under uniform routing), its head rows, and the
+    batch's fp32 KV cache read at context `pos`."""
+    q, kv = c["n_head"] * c["head_dim"], c["n_head_kv"] * c["head_dim"]
+    e = c["n_embd"]
+    attn = kbytes(c["kind"], e, q + 2 * kv) + kbytes(c["kind"], q, e)
+    if c.get("n_expert", 0):
+        ne, k_, ff = c["n_expert"], c["top_k"], c["n_ff_expert"]
+        per_expert = 2 * kbytes(c["expert_kind"], e, ff) + kbytes(c["expert_kind"], ff, e)
+        distinct = ne * (1 - (1 - k_ / ne) ** batch)           # expected distinct experts touched
+        ffn = kbytes(c["kind"], e, ne) + distinct / world * per_expert
+    else:
+        ffn = kbytes(c["kind"], e, 2 * c["n_ff"]) + kbytes(c["kind"], c["n_ff"], e)
+    layers = c["n_layer"] * (attn + ffn)
+    vn = c.get("n_vocab_local") or c["n_vocab"]
+    head = kbytes(c["head_kind"], e, vn)
+    kvb = c["n_layer"] * 2 * kv * 4 * pos * batch
+    return layers + head + kvb
+
+
+def shard_config(c, workload, rank, world):
+    c = dict(c)
+    if workload == "c4" and world > 1:
+        per = -(-c["n_vocab"] // world)
+        c["vocab0"] = rank * per
+        c["n_vocab_local"] = min(per, c["n_vocab"] - c["vocab0"])
+    if workload == "c5" and world > 1:
+        per = c["n_expert"] // world
+        c["expert0"] = rank * per
+        c["n_expert_local"] = per if rank < world - 1 else c["n_expert"] - rank * per
+    return c
+
+
+def big_gpu(args, ugb, ctx, torch, rank, world, workload):
+    base = C4 if workload == "c4" else C5
+    batch = args.batch or (8 if workload == "c4" else 1)
+    c = shard_config(dict(base, batch=batch), workload, rank, world)
+    dec = ugb.Decoder(ctx, **c)
+    dec.synthetic(11)
+    comm = None
+    if world > 1:
+        uid = [ugb.comm_unique_id() if rank == 0 else None]
+        torch.distributed.broadcast_object_list(uid, src=0)
+        comm = ugb.Comm(ctx, rank, world, uid[0])
+        dec.set_comm(comm)
+    n_ctx = c["n_ctx"]
+    stream = torch.cuda.Stream()
+    cap = torch.cuda.Stream()
+    K, W = args.steps, args.warmup
+    if K + W > n_ctx - 1:
+        K = max(1, n_ctx - 1 - W)
+    start = n_ctx - K
+    toks = [1 + b for b in range(batch)]
+    dec.set_tokens(toks, 0, stream)
+    barrier(world, torch)
+    graph = ctx.capture(lambda: dec.step(), cap)
+    kernels = graph.kernels()  # includes NCCL's kernels when the step holds collectives
+    dec.set_tokens(toks, start - W, stream)
+    for _ in range(W):
+        graph.launch(stream)
+    stream.synchronize()
+    code, bits = ctx.status_read(stream)
+    assert code == ugb.OK, ("status after warm-up", code, bits)
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
+    barrier(world, torch)
+    torch.cuda.synchronize()
+    sampler.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        graph.launch(stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world, torch)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    code, bits = ctx.status_read(stream)
+    assert code == ugb.OK, ("status after timing", code, bits)
+    ms_max = reduce_max(ms, world, torch)
+    step_bytes = float(np.mean([big_step_bytes(c, batch, start + i + 1, world) for i in range(K)]))
+    # end to end: host tokens in, next tokens out, every step (ugb_decoder_tokens)
+    e2e_steps = max(3, min(K, 16))
+    barrier(world, torch)
+    nxt = toks
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        nxt = dec.tokens(nxt, n_ctx - e2e_steps + i, stream)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
+    barrier(world, torch)
+    graph.close()
+    dec.close()  # releases the decoder's own captured graph before the communicator goes
+    if comm:
+        comm.close()
+    return {
+        "value": batch * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
+        "gpu_launches": kernels * K, "step_bytes": step_bytes, "batch": batch,
+        "e2e": {"value": batch / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * 4 + 8,
+                "d2h_bytes_per_step": 112 + 4},
+        "config": c,
+    }
+
+
+def host_quant_matrix(rng, kind, k, m):
+    """Random GGUF blocks with sane fp16 scales (timing input for the CPU legs)."""
+    e, bsz = KIND_BLOCK[kind]
+    b = rng.integers(0, 256, size=(m, k // e, bsz), dtype=np.uint8)
+    half = np.frombuffer(np.float16(0.002).tobytes(), np.uint8)
+    if kind == Q8_0:
+        b[:, :, 0:2] = half
+    elif kind == Q4_K:
+        b[:, :, 0:2] = half
+        b[:, :, 2:4] = half
+    else:
+        b[:, :, 108:110] = half
+    return b.reshape(-1)
+
+
+def big_cpu(budget_s, workload, batch):
+    """The oracle decode forward on the host cores: a 1-layer and a 2-layer model of the
+    config's shapes, timed per token, extrapolated to the full depth (per-layer time = the
+    difference).  The oracle decodes one sequence at a time, so its tok/s is the same for any
+    batch."""
+    from oracle import pyoracle as orc
+    from oracle.decode_ref import RefDecoder
+    base = dict(C4 if workload == "c4" else C5)
+    rng = np.random.default_rng(5)
+    e, q, kv = base["n_embd"], base["n_head"] * base["head_dim"], base["n_head_kv"] * base["head_dim"]
+    kind = base["kind"]
+    tok = host_quant_matrix(rng, Q8_0, e, base["n_vocab"])
+
+    def layer():
+        L = {"attn_norm": np.ones(e, np.float32), "ffn_norm": np.ones(e, np.float32),
+             "wq": host_quant_matrix(rng, kind, e, q), "wk": host_quant_matrix(rng, kind, e, kv),
+             "wv": host_quant_matrix(rng, kind, e, kv), "wo": host_quant_matrix(rng, kind, q, e)}
+        if base.get("n_expert", 0):
+            ek, ne, ff = base["expert_kind"], base["n_expert"], base["n_ff_expert"]
+            L.update(router=host_quant_matrix(rng, kind, e, ne), gate_exps=host_quant_matrix(rng, ek, e, ff * ne),
+                     up_exps=host_quant_matrix(rng, ek, e, ff * ne), down_exps=host_quant_matrix(rng, ek, ff, e * ne))
+        else:
+            L.update(w_gate=host_quant_matrix(rng, kind, e, base["n_ff"]),
+                     w_up=host_quant_matrix(rng, kind, e, base["n_ff"]),
+                     w_down=host_quant_matrix(rng, kind, base["n_ff"], e))
+        return L
+
+    layers = [layer(), layer()]
+    times = []
+    for n in (1, 2):
+        cfg = dict(base, n_layer=n)
+        ref = RefDecoder(cfg, {"tok_embd": tok, "output": tok, "output_norm": np.ones(e, np.float32),
+                               "layers": layers[:n]}, mt=True)
+        t = 1
+        ref.step(t, 0)
+        t0 = time.perf_counter()
+        steps = 0
+        while steps < 2 or (time.perf_counter() - t0 < budget_s / 4 and steps < 8):
+            t = ref.step(t, steps + 1)[1]
+            steps += 1
+        times.append((time.perf_counter() - t0) / steps)
+    per_layer = max(times[1] - times[0], 0.0)
+    per_token = times[0] + (base["n_layer"] - 1) * per_layer
+    return 1.0 / per_token, per_token, orc.lib(True).orc_threads()
+
+
 # ---- driver -----------------------------------------------------------------------------------
 
 def main():
@@ -627,7 +820,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["c2", "c1", "c3"], default="c2")
+    ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5"], default="c2")
+    ap.add_argument("--batch", type=int, default=0, help="c4 / c5 sequences (default 8 / 1)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:
@@ -645,6 +839,21 @@ def main():
                   "l2": "inputs larger than L2 (1.655 GB of weights per token)",
                   "parallelism": f"replicas x{world}"}
         base = {"metric": "decode tok/s", "unit": "tok/s", "dtype": "int8 x int8 -> int32 (Q8_0 x Q8_1), fp32 glue"}
+    elif args.workload in ("c4", "c5"):
+        big = C4 if args.workload == "c4" else C5
+        bsz = args.batch or (8 if args.workload == "c4" else 1)
+        if args.workload == "c4":
+            name = "c4: greedy decode, Qwen2.5-7B-shaped, Q4_K linear weights, Q8_0 head"
+            split = f"head rows split over {world} GPU(s), greedy keys all-reduced (max) over NVLink"
+        else:
+            name = "c5: greedy decode, 48-layer MoE (192 Q3_K experts of 1536, top-8), Q8_0 attention / router"
+            split = f"experts split over {world} GPU(s) ({192 // world} each), layer outputs all-reduced over NVLink"
+        config = {"workload": name, "batch": bsz, "layers": big["n_layer"], "hidden": big["n_embd"],
+                  "heads": f"{big['n_head']}/{big['n_head_kv']}x{big['head_dim']}", "vocab": big["n_vocab"],
+                  "context": big["n_ctx"], "kv_cache": "fp32", "head": "tied to the Q8_0 token embedding",
+                  "l2": "inputs larger than L2", "parallelism": split if world > 1 else "1 GPU"}
+        base = {"metric": "decode tok/s", "unit": "tok/s",
+                "dtype": "int8 x int8 -> int32 (K-quant / Q8_0 x Q8_1), fp32 glue"}
     elif args.workload == "c3":
         config = {"workload": "c3: Q8 prefill GEMMs of the Qwen2.5-1.5B-shaped Q8_0 model, 512-token prompt",
                   "tokens": C3_TOKENS, "layers": C2["n_layer"],
@@ -662,7 +871,7 @@ def main():
                   "parallelism": f"replicas x{world}"}
         base = {"metric": "quant matvec HBM GB/s", "unit": "GB/s", "dtype": "int8 x int8 -> int32, fp32 scale"}
     base.update({"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-                 "scaling": "weak", "vs_baseline": None,
+                 "scaling": "strong" if args.workload in ("c4", "c5") else "weak", "vs_baseline": None,
                  "data": "synthetic (seeded random-init weights; quants uniform, fp16 scales |N(0,1)|*0.002)",
                  "config": config})
 
@@ -676,6 +885,11 @@ def main():
             sample = (f"{done} decode tokens at the last positions of the 512 context, oracle/decode_ref.py "
                       f"(numpy glue, oracle/ugb_oracle.c matvecs on POSIX threads over rows)")
             ms = 1e3 / value
+        elif args.workload in ("c4", "c5"):
+            value, per_token, cores = big_cpu(max(30.0, args.cpu_seconds), args.workload, 1)
+            sample = ("1- and 2-layer oracle models of the config's shapes (oracle/decode_ref.py, matvecs on POSIX "
+                      "threads), per-token time extrapolated to the full depth; one sequence at a time")
+            ms = per_token * 1e3
         elif args.workload == "c3":
             value, toks, cores = c3_cpu(max(30.0, args.cpu_seconds))
             sample = (f"the four GEMMs of one layer for {toks} tokens (oracle/ugb_oracle.c prefill GEMM, POSIX "
@@ -706,6 +920,10 @@ def main():
         res = c2_gpu(args, ugb, ctx, torch, rank, world)
         kernel = "mv_rows_kernel<Q8_0> (fused gate/up, 17920x1536)"
         traffic = load_traffic("c2_gate_up")
+    elif args.workload in ("c4", "c5"):
+        res = big_gpu(args, ugb, ctx, torch, rank, world, args.workload)
+        kernel = None
+        traffic = None
     elif args.workload == "c3":
         res = c3_gpu(args, ugb, ctx, torch, rank, world)
         kernel = "prefill_gemm_kernel<128> (fused gate/up, 512 x 17920 x 1536)"
@@ -716,7 +934,13 @@ def main():
         traffic = load_traffic("c1_matvec")
 
     line = dict(base)
-    if "kernel_ops" in res:
+    if "step_bytes" in res:
+        achieved = res["step_bytes"] / (res["ms_per_step"] / 1e3) / 1e9
+        roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "kernel": "whole decode step (one device)", "bytes_per_step": res["step_bytes"],
+                "traffic": None}
+    elif "kernel_ops" in res:
         achieved = res["kernel_ops"] / (res["kernel_ms"] / 1e3) / 1e12
         roof = {"bound": "tensor", "achieved": achieved, "peak": res["int8_tops"], "unit": "TOPS (int8)",
                 "frac": achieved / res["int8_tops"],
@@ -742,6 +966,9 @@ def main():
         if args.workload == "c2":
             v, done, cores = c2_cpu(args.cpu_seconds, 64)
             sample = f"{done} decode tokens (oracle/decode_ref.py; matvecs on the host threads)"
+        elif args.workload in ("c4", "c5"):
+            v, _, cores = big_cpu(args.cpu_seconds, args.workload, 1)
+            sample = "1- and 2-layer oracle models, per-token time extrapolated to the full depth"
         elif args.workload == "c3":
             v, toks, cores = c3_cpu(args.cpu_seconds)
             sample = f"one layer's four GEMMs for {toks} tokens on the host threads, scaled to 28 layers"

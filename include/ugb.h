@@ -165,6 +165,9 @@ ugb_status ugb_graph_begin(ugb_ctx *ctx, ugb_stream stream);
 ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out);
 ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream);
 ugb_status ugb_graph_destroy(ugb_graph *graph);
+/* Kernel launches one replay of the graph performs (its kernel nodes; collectives captured in
+ * it contribute their own kernels). */
+ugb_status ugb_graph_kernels(const ugb_graph *graph, int64_t *count);
 
 /* ---- MoE expert path ----------------------------------------------------------------------- */
 

@@ -85,6 +85,7 @@ SIGNATURES = {
     "ugb_graph_end": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
     "ugb_graph_launch": (_int, [_vp, _vp]),
     "ugb_graph_destroy": (_int, [_vp]),
+    "ugb_graph_kernels": (_int, [_vp, ctypes.POINTER(_i64)]),
 }
 
 
@@ -480,6 +481,12 @@ class Graph:
 
     def launch(self, stream=None) -> None:
         check("ugb_graph_launch", lib().ugb_graph_launch(self.handle, _stream(stream)))
+
+    def kernels(self) -> int:
+        """Kernel launches per replay (ugb_graph_kernels)."""
+        n = _i64(0)
+        check("ugb_graph_kernels", lib().ugb_graph_kernels(self.handle, ctypes.byref(n)))
+        return n.value
 
     def close(self) -> None:
         if self.handle:

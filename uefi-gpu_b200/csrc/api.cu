@@ -3,6 +3,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <new>
+#include <vector>
 
 #include "common.cuh"
 #include "internal.hpp"
@@ -310,6 +311,22 @@ ugb_status ugb_graph_end(ugb_ctx *ctx, ugb_stream stream, ugb_graph **out) {
 ugb_status ugb_graph_launch(ugb_graph *graph, ugb_stream stream) {
   if (!graph || !graph->exec) return UGB_ECONTEXT;
   return cuda_status(cudaGraphLaunch(graph->exec, stream));
+}
+
+ugb_status ugb_graph_kernels(const ugb_graph *g, int64_t *count) {
+  if (!g || !g->graph || !count) return UGB_ECONTEXT;
+  size_t n = 0;
+  if (cudaGraphGetNodes(g->graph, nullptr, &n) != cudaSuccess) return UGB_EBACKEND;
+  std::vector<cudaGraphNode_t> nodes(n);
+  if (n && cudaGraphGetNodes(g->graph, nodes.data(), &n) != cudaSuccess) return UGB_EBACKEND;
+  int64_t k = 0;
+  for (size_t i = 0; i < n; ++i) {
+    cudaGraphNodeType t;
+    if (cudaGraphNodeGetType(nodes[i], &t) != cudaSuccess) return UGB_EBACKEND;
+    k += t == cudaGraphNodeTypeKernel ? 1 : 0;
+  }
+  *count = k;
+  return UGB_OK;
 }
 
 ugb_status ugb_graph_destroy(ugb_graph *graph) {
