@@ -80,9 +80,11 @@ class RefDecoder:
         rb = po.row_bytes(Q8_0, n)
         return po.dequantize(Q8_0, self.w["tok_embd"][token * rb:(token + 1) * rb], n)
 
-    def moe_ffn(self, L: dict, xn: np.ndarray) -> np.ndarray:
+    def moe_ffn(self, L: dict, xn: np.ndarray, experts: range | None = None) -> np.ndarray:
         """Routed SwiGLU experts of one layer; L holds router and the stacked expert tensors
-        gate_exps / up_exps / down_exps (raw bytes, all n_expert experts)."""
+        gate_exps / up_exps / down_exps (raw bytes, all n_expert experts).  With `experts`,
+        only the selected experts in that range contribute (one expert-parallel shard's
+        partial sum)."""
         c = self.c
         ek, ne, ff, d = c["expert_kind"], c["n_expert"], c["n_ff_expert"], c["n_embd"]
         scores = self.linear(c["kind"], L["router"], xn, ne)
@@ -90,6 +92,8 @@ class RefDecoder:
         rbi, rbf = po.row_bytes(ek, d), po.row_bytes(ek, ff)
         out = np.zeros(d, np.float32)
         for e, wgt in zip(ids, weights):
+            if experts is not None and int(e) not in experts:
+                continue
             g = self.linear(ek, L["gate_exps"][e * ff * rbi:(e + 1) * ff * rbi], xn, ff)
             u = self.linear(ek, L["up_exps"][e * ff * rbi:(e + 1) * ff * rbi], xn, ff)
             with np.errstate(over="ignore"):
