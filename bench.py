@@ -682,7 +682,9 @@ def shard_config(c, workload, rank, world):
 
 
 def big_gpu(args, ugb, ctx, torch, rank, world, workload):
-    base = C4 if workload == "c4" else C5
+    base = dict(C4 if workload == "c4" else C5)
+    if args.layers:
+        base["n_layer"] = args.layers
     batch = args.batch or (8 if workload == "c4" else 1)
     c = shard_config(dict(base, batch=batch), workload, rank, world)
     dec = ugb.Decoder(ctx, **c)
@@ -822,6 +824,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=["c2", "c1", "c3", "c4", "c5"], default="c2")
     ap.add_argument("--batch", type=int, default=0, help="c4 / c5 sequences (default 8 / 1)")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="c4 / c5: decode this many layers instead of the config's (profiling captures only)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()
     if args.warmup < 3:

@@ -33,14 +33,15 @@ struct Q8Act {
 };
 Q8Act q8act_layout(int64_t k, int64_t batch);
 
-constexpr int kMaxMatvecSegs = 32;  // matrices (segments or jobs) of one matvec launch
+constexpr int kMaxMatvecSegs = 4;   // matrices sharing one activation in one matvec launch
+constexpr int kMaxMatvecJobs = 32;  // independent jobs of one job-table launch
 
 // Streaming matvec launch description.
 struct MatvecArgs {
   uint32_t kind = 0;
   const uint8_t *w = nullptr;    // single matrix (nseg == 0), or:
-  const uint8_t *ws[kMaxMatvecSegs] = {};  // matrices of seg_rows[i] rows, y rows concatenated
-  int64_t seg_rows[kMaxMatvecSegs] = {};
+  const uint8_t *ws[kMaxMatvecJobs] = {};  // matrices of seg_rows[i] rows, y rows concatenated
+  int64_t seg_rows[kMaxMatvecJobs] = {};    // (up to kMaxMatvecSegs segments, or the jobs)
   int nseg = 0;
   int64_t row_bytes = 0, k = 0, m = 0;
   const uint8_t *xq = nullptr;   // Q8_1 buffer
@@ -53,8 +54,8 @@ struct MatvecArgs {
   // Job table (njobs > 0): job i = matrix ws[i] of seg_rows[i] rows with its own Q8_1
   // activation jx[i] (layout xl, `batch` vectors) and output jy[i] ([batch][seg_rows[i]]).
   int njobs = 0;
-  const uint8_t *jx[kMaxMatvecSegs] = {};
-  float *jy[kMaxMatvecSegs] = {};
+  const uint8_t *jx[kMaxMatvecJobs] = {};
+  float *jy[kMaxMatvecJobs] = {};
   // Routed experts (ids set; batch 1): slot s < n_slots, matrix i < per_slot uses expert
   // ids[s] of the stacked tensor ebase[i] (n_expert experts of m rows, estride bytes apart,
   // global ids from expert0; other ids < n_total are another device's and are skipped),

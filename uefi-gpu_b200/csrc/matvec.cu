@@ -40,7 +40,8 @@ constexpr uint32_t kItemTarget = 32 * 1024;  // weight bytes per pipeline stage
 constexpr size_t kSmPerKernel = 112 * 1024;  // shared memory one kernel takes per SM
 constexpr int kSlots = 4;                    // activation units a lane keeps in registers
 
-constexpr int kMaxSegs = kMaxMatvecSegs;  // matrices of one launch (segments or table jobs)
+constexpr int kMaxSegs = kMaxMatvecSegs;  // matrices sharing one activation in one launch
+constexpr int kMaxJobs = kMaxMatvecJobs;  // jobs of one job-table launch
 
 // How a launch maps CTAs to matrices:
 //  kSegments -- up to kMaxSegs matrices share one activation; their rows are concatenated and
@@ -78,15 +79,6 @@ struct MvParams {
   int32_t *dots;
   uint32_t *status;
   int mode;                   // MvMode
-  // kTable: job j = matrix w[j] of jm[j] rows, activation (jxq, jxd, jxs)[j], output jy[j]
-  // ([batch][jm[j]]), CTAs [cta0[j], cta0[j+1]).
-  int njobs;
-  int jm[kMaxSegs];
-  int cta0[kMaxSegs + 1];
-  const uint8_t *jxq[kMaxSegs];
-  const float *jxd[kMaxSegs];
-  const int *jxs[kMaxSegs];
-  float *jy[kMaxSegs];
   // kRouted: job j = (slot s = j / per_slot, matrix i = j % per_slot); expert e = ids[s]
   // (0 <= e < n_total; a slot whose expert another device holds is skipped); weights
   // ebase[i] + (e - expert0) * estride (m rows); activation vector s / x_div of the Q8_1
@@ -97,6 +89,26 @@ struct MvParams {
   const uint8_t *ebase[2];
   uint64_t estride;
   int64_t y_slot;
+};
+
+// kTable launches carry the job table in a larger parameter block of their own, so the
+// frequent segment / routed launches keep a small one (a larger block costs launch latency
+// on every one of the hundreds of launches of a decode step).
+// Job j = matrix jw[j] of jm[j] rows, activation (jxq, jxd, jxs)[j], output jy[j]
+// ([batch][jm[j]]), CTAs [cta0[j], cta0[j+1]).
+struct MvTable {
+  int njobs;
+  int jm[kMaxJobs];
+  int cta0[kMaxJobs + 1];
+  const uint8_t *jw[kMaxJobs];
+  const uint8_t *jw_end16[kMaxJobs];
+  const uint8_t *jxq[kMaxJobs];
+  const float *jxd[kMaxJobs];
+  const int *jxs[kMaxJobs];
+  float *jy[kMaxJobs];
+};
+struct MvParamsT : MvParams {
+  MvTable t;
 };
 
 // What one CTA works on: its index among the CTAs of its matrix (set), that matrix's rows,
@@ -116,6 +128,29 @@ struct View {
 __device__ __forceinline__ const uint8_t *floor16(const uint8_t *p);
 
 // kRouted reads the expert ids the previous kernel wrote: call after grid_dep_wait().
+__device__ __forceinline__ View make_view(const MvParams &p);
+
+__device__ __forceinline__ View make_view(const MvParamsT &p) {
+  if (p.mode != kTable) return make_view(static_cast<const MvParams &>(p));
+  View v;
+  v.skip = false;
+  const MvTable &t = p.t;
+  int j = 0;
+  for (int i = 1; i < t.njobs; ++i) j += static_cast<int>(blockIdx.x) >= t.cta0[i] ? 1 : 0;
+  v.cta = static_cast<int>(blockIdx.x) - t.cta0[j];
+  v.ncta = t.cta0[j + 1] - t.cta0[j];
+  v.m = t.jm[j];
+  v.ngroups = (v.m + p.rows - 1) / p.rows;
+  v.w = t.jw[j];
+  v.w_end16 = t.jw_end16[j];
+  v.xq = t.jxq[j];
+  v.xd = t.jxd[j];
+  v.xs = t.jxs[j];
+  v.y = t.jy[j];
+  v.ldy = v.m;
+  return v;
+}
+
 __device__ __forceinline__ View make_view(const MvParams &p) {
   View v;
   v.ldy = p.ldy;
@@ -130,20 +165,6 @@ __device__ __forceinline__ View make_view(const MvParams &p) {
     v.xd = p.xd;
     v.xs = p.xs;
     v.y = p.y;
-  } else if (p.mode == kTable) {
-    int j = 0;
-    for (int i = 1; i < p.njobs; ++i) j += static_cast<int>(blockIdx.x) >= p.cta0[i] ? 1 : 0;
-    v.cta = static_cast<int>(blockIdx.x) - p.cta0[j];
-    v.ncta = p.cta0[j + 1] - p.cta0[j];
-    v.m = p.jm[j];
-    v.ngroups = (v.m + p.rows - 1) / p.rows;
-    v.w = p.w[j];
-    v.w_end16 = p.w_end16[j];
-    v.xq = p.jxq[j];
-    v.xd = p.jxd[j];
-    v.xs = p.jxs[j];
-    v.y = p.jy[j];
-    v.ldy = v.m;
   } else {
     const int j = static_cast<int>(blockIdx.x) / p.cpj;
     v.cta = static_cast<int>(blockIdx.x) - j * p.cpj;
@@ -359,8 +380,8 @@ __device__ __forceinline__ void release_stage(uint32_t empty, int s, int lane) {
 }
 
 // Batch-1, whole-row consumer (see the file comment).  RW rows per warp, 8 * RW per item.
-template <int KIND, int RW, int J>
-__global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) {
+template <int KIND, int RW, int J, class P>
+__global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const P p) {
   static_assert(J % 2 == 0 && J <= kSlots, "slots are processed in pairs");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -441,8 +462,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const MvParams p) 
 // share of the R rows; the per-warp partials meet in shared memory (double-buffered by item
 // parity) and warp 0 adds them in warp order.  The one named barrier per item also ANDs the
 // warps' wait results, so a timed-out stage makes every consumer warp stop together.
-template <int KIND, int R, int J>
-__global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const MvParams p) {
+template <int KIND, int R, int J, class P>
+__global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const P p) {
   static_assert(J % 2 == 0 && J <= kSlots, "slots are processed in pairs");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -530,8 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const MvParams p)
 // General consumer: NB activation vectors, rows of any length (K chunks), or int-dot dumps
 // (DOTS).  One warp per row, 8 rows per item; lane l takes 32-element units l, l+32, ... of
 // the chunk with the activation read from shared memory.
-template <int KIND, int NB, bool DOTS>
-__global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const MvParams p) {
+template <int KIND, int NB, bool DOTS, class P>
+__global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = smem_u32(smem);
@@ -645,9 +666,10 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
         break;
       }
     }
-    // Rows too long for that: spread an item of R rows over all consumer lanes.
+    // Rows too long for that: spread an item of R rows over all consumer lanes (the largest
+    // R whose item fits a stage and whose slots fit the registers).
     for (int r : {4, 2, 1}) {
-      if (pl.rows_kernel) break;
+      if (pl.rows_kernel || pl.split) break;
       const int64_t slots = (r * units + kWarps * 32 - 1) / (kWarps * 32);
       if (rb * r <= kItemTarget && slots <= kSlots) {
         pl.split = true;
@@ -695,9 +717,9 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
   return pl;
 }
 
-template <int KIND>
+template <int KIND, class P>
 const void *rows_kernel_ptr(int rw, int slots) {
-#define UGB_RK(RW, J) if (rw == RW && slots == J) return reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J>);
+#define UGB_RK(RW, J) if (rw == RW && slots == J) return reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J, P>);
   UGB_RK(1, 2) UGB_RK(1, 4)
   UGB_RK(2, 2) UGB_RK(2, 4)
   UGB_RK(4, 2) UGB_RK(4, 4)
@@ -705,9 +727,9 @@ const void *rows_kernel_ptr(int rw, int slots) {
   return nullptr;
 }
 
-template <int KIND>
+template <int KIND, class P>
 const void *split_kernel_ptr(int r, int slots) {
-#define UGB_SK(R, J) if (r == R && slots == J) return reinterpret_cast<const void *>(&mv_split_kernel<KIND, R, J>);
+#define UGB_SK(R, J) if (r == R && slots == J) return reinterpret_cast<const void *>(&mv_split_kernel<KIND, R, J, P>);
   UGB_SK(1, 2) UGB_SK(1, 4)
   UGB_SK(2, 2) UGB_SK(2, 4)
   UGB_SK(4, 2) UGB_SK(4, 4)
@@ -715,26 +737,32 @@ const void *split_kernel_ptr(int r, int slots) {
   return nullptr;
 }
 
-template <int KIND>
+template <int KIND, class P>
 const void *stream_kernel_ptr(int nb, bool dots) {
-  if (dots) return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, true>);
+  if (dots) return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, true, P>);
   switch (nb) {
-    case 1: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, false>);
-    case 2: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 2, false>);
-    case 4: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 4, false>);
-    case 8: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 8, false>);
+    case 1: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, false, P>);
+    case 2: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 2, false, P>);
+    case 4: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 4, false, P>);
+    case 8: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 8, false, P>);
     default: return nullptr;
   }
 }
 
-const void *select_kernel(uint32_t kind, const Plan &pl, int nb, bool dots) {
+template <int KIND, class P>
+const void *select_for(const Plan &pl, int nb, bool dots) {
+  return pl.rows_kernel ? rows_kernel_ptr<KIND, P>(pl.rw, pl.slots)
+         : pl.split     ? split_kernel_ptr<KIND, P>(pl.rw, pl.slots)
+                        : stream_kernel_ptr<KIND, P>(nb, dots);
+}
+
+// The kernel instance for a plan; `table` picks the instances that take the job table.
+const void *select_kernel(uint32_t kind, const Plan &pl, int nb, bool dots, bool table = false) {
+  if (table && dots) return nullptr;
   switch (kind) {
-    case UGB_Q8_0: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q8_0>(pl.rw, pl.slots)
-                          : pl.split ? split_kernel_ptr<UGB_Q8_0>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q8_0>(nb, dots);
-    case UGB_Q4_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q4_K>(pl.rw, pl.slots)
-                          : pl.split ? split_kernel_ptr<UGB_Q4_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q4_K>(nb, dots);
-    case UGB_Q3_K: return pl.rows_kernel ? rows_kernel_ptr<UGB_Q3_K>(pl.rw, pl.slots)
-                          : pl.split ? split_kernel_ptr<UGB_Q3_K>(pl.rw, pl.slots) : stream_kernel_ptr<UGB_Q3_K>(nb, dots);
+    case UGB_Q8_0: return table ? select_for<UGB_Q8_0, MvParamsT>(pl, nb, dots) : select_for<UGB_Q8_0, MvParams>(pl, nb, dots);
+    case UGB_Q4_K: return table ? select_for<UGB_Q4_K, MvParamsT>(pl, nb, dots) : select_for<UGB_Q4_K, MvParams>(pl, nb, dots);
+    case UGB_Q3_K: return table ? select_for<UGB_Q3_K, MvParamsT>(pl, nb, dots) : select_for<UGB_Q3_K, MvParams>(pl, nb, dots);
     default: return nullptr;
   }
 }
@@ -753,15 +781,20 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
         pl.rows_kernel = true;
         pl.rw = rw;
         pl.slots = j;
-        if (allow_smem(select_kernel(kind, pl, 1, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
-        pl.rows_kernel = false;
-        pl.split = true;
-        if (allow_smem(select_kernel(kind, pl, 1, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+        for (bool table : {false, true}) {
+          pl.rows_kernel = true;
+          pl.split = false;
+          if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+          pl.rows_kernel = false;
+          pl.split = true;
+          if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+        }
         pl.split = false;
       }
     pl.rows_kernel = false;
     for (int nb : {1, 2, 4, 8})
-      if (allow_smem(select_kernel(kind, pl, nb, false), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+      for (bool table : {false, true})
+        if (allow_smem(select_kernel(kind, pl, nb, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
     if (allow_smem(select_kernel(kind, pl, 1, true), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
   }
   return UGB_OK;
@@ -771,7 +804,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
   MatvecArgs a = a_in;
   const int mode = a.ids ? kRouted : a.njobs > 0 ? kTable : kSegments;
   if (mode == kTable) {
-    if (a.njobs > kMaxSegs) return UGB_ESHAPE;
+    if (a.njobs > kMaxJobs) return UGB_ESHAPE;
     a.nseg = a.njobs;
     a.m = 0;
     for (int i = 0; i < a.njobs; ++i) a.m = std::max(a.m, a.seg_rows[i]);
@@ -779,6 +812,8 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     if (a.batch != 1 || a.per_slot < 1 || a.per_slot > 2 || a.n_slots < 1 || a.n_expert < 1 || a.x_div < 1)
       return UGB_ESHAPE;
     a.nseg = 1;
+  } else if (a.nseg > kMaxSegs) {
+    return UGB_ESHAPE;
   } else if (a.nseg == 0) {
     a.nseg = 1;
     a.ws[0] = a.w;
@@ -795,7 +830,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     while (nb > 1 && x_bytes(a.kind, a.k, nb) > kXBudget) nb /= 2;
     const Plan pl = make_plan(a.kind, a.k, a.m, nb, dots, ctx->smem_optin);
     if (pl.smem > ctx->smem_optin) return UGB_ESHAPE;
-    const void *f = select_kernel(a.kind, pl, nb, dots);
+    const void *f = select_kernel(a.kind, pl, nb, dots, mode == kTable);
     if (!f) return UGB_EQUANT;
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, kThreads, pl.smem) != cudaSuccess ||
@@ -822,9 +857,10 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
       }
       return UGB_OK;
     }
-    MvParams p{};
-    p.nseg = a.nseg;
-    {
+    MvParamsT pt{};
+    MvParams &p = pt;
+    p.nseg = mode == kTable ? 1 : a.nseg;
+    if (mode != kTable) {
       int64_t row0 = 0;
       for (int i = 0; i < a.nseg; ++i) {
         p.w[i] = a.ws[i];
@@ -864,19 +900,23 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
       // CTAs per job in proportion to its row groups (at least one, at most one per group).
       int64_t groups = 0;
       for (int i = 0; i < a.njobs; ++i) groups += (a.seg_rows[i] + pl.rows - 1) / pl.rows;
-      p.njobs = a.njobs;
+      MvTable &t = pt.t;
+      t.njobs = a.njobs;
       int c = 0;
       for (int i = 0; i < a.njobs; ++i) {
         const int64_t g = (a.seg_rows[i] + pl.rows - 1) / pl.rows;
-        p.jm[i] = static_cast<int>(a.seg_rows[i]);
-        p.cta0[i] = c;
+        t.jm[i] = static_cast<int>(a.seg_rows[i]);
+        t.cta0[i] = c;
         c += static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, budget * g / std::max<int64_t>(1, groups))));
-        p.jxq[i] = a.jx[i] + done * a.xl.k;
-        p.jxd[i] = reinterpret_cast<const float *>(a.jx[i] + a.xl.d_off) + done * a.xl.nbp;
-        p.jxs[i] = reinterpret_cast<const int *>(a.jx[i] + a.xl.s_off) + done * a.xl.nbp;
-        p.jy[i] = a.jy[i] + done * a.seg_rows[i];
+        t.jw[i] = a.ws[i];
+        t.jw_end16[i] = reinterpret_cast<const uint8_t *>(
+            reinterpret_cast<uintptr_t>(a.ws[i] + a.seg_rows[i] * a.row_bytes) & ~uintptr_t(15));
+        t.jxq[i] = a.jx[i] + done * a.xl.k;
+        t.jxd[i] = reinterpret_cast<const float *>(a.jx[i] + a.xl.d_off) + done * a.xl.nbp;
+        t.jxs[i] = reinterpret_cast<const int *>(a.jx[i] + a.xl.s_off) + done * a.xl.nbp;
+        t.jy[i] = a.jy[i] + done * a.seg_rows[i];
       }
-      p.cta0[a.njobs] = c;
+      t.cta0[a.njobs] = c;
       grid = c;
     } else if (mode == kRouted) {
       const int jobs = a.n_slots * a.per_slot;
@@ -904,7 +944,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     attr[0].val.programmaticStreamSerializationAllowed = a.pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void *args[] = {&p};
+    void *args[] = {mode == kTable ? static_cast<void *>(&pt) : static_cast<void *>(&p)};
     if (cudaLaunchKernelExC(&cfg, f, args) != cudaSuccess) return UGB_EBACKEND;
     done += nb;
   }
