@@ -121,6 +121,21 @@ def test_decoder_matches_oracle(ctx, ugb, kind):
     dec.close()
 
 
+def test_decoder_wide_ffn_matches_oracle(ctx, ugb):
+    """A 4096-wide FFN (128 activation blocks) with 512-wide rows: the down rows take the
+    split-row kernel."""
+    from oracle.decode_ref import RefDecoder
+    cfg = dict(SMALL, n_ff=4096, n_embd=512, n_head=4, n_layer=2)
+    dec, _, host = make_decoder(ctx, ugb, cfg, seed=61)
+    ref = RefDecoder(cfg, host)
+    tokens = np.random.default_rng(4).integers(0, cfg["n_vocab"], size=24)
+    errs, agree = run_synced(dec, ref, tokens)
+    assert errs.max() <= 5e-2
+    assert (errs <= 1e-4).mean() >= 0.7, errs
+    assert ctx.status_read()[1] == 0
+    dec.close()
+
+
 def test_decoder_kv_cache_matches_oracle(ctx, ugb):
     """The cached rotated keys and values of the first layer equal the oracle's (they depend
     only on the embedding, the first norm and the QKV matvec)."""
