@@ -46,6 +46,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 Q8_0 = 8
+PATHS = {"auto": 0, "chain": 1, "token": 2}  # ugb_decoder_set_path values
 
 
 def load_peaks():
@@ -249,6 +250,7 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     w = c2_device_weights(ctx, ugb, torch, seed=1 + rank, c=c)
     dec = ugb.Decoder(ctx, **c)
     dec.bind(w["tok_embd"], w["output_norm"], w["output"], w["layers"])
+    active = dec.set_path(PATHS[args.path])
     n_ctx = c["n_ctx"]
     stream = torch.cuda.Stream()
     cap = torch.cuda.Stream()
@@ -304,9 +306,43 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     timed_pos = [(start + i) % n_ctx for i in range(K)]
     token_bytes = float(np.mean([c2_token_bytes(c, p + 1) for p in timed_pos]))
 
-    # -- dominant kernel: the fused gate/up matvec (17920 x 1536 Q8_0, the largest launch of a
-    # layer), all 28 layers' matrices back to back in one graph (each launch streams its own
-    # 29 MB from HBM), timed by CUDA events on the launching stream --
+    # -- dominant kernel.  Token path: the step is one launch of the persistent token kernel, so
+    # its CUDA-event time per launch is the step's and its algorithmic bytes are the token's.
+    # Launch chain: the fused gate/up matvec (17920 x 1536 Q8_0, the largest launch of a layer),
+    # all 28 layers' matrices back to back in one graph (each launch streams its own 29 MB from
+    # HBM), timed by CUDA events on the launching stream --
+    if active == ugb.PATH_TOKEN:
+        kern_ms, kern_bytes, kgraph = ms_max / K, token_bytes, None
+    else:
+        kern_ms, kern_bytes, kgraph = c2_gateup_kernel(ugb, ctx, torch, dev, w, c, cap, stream, e0, e1)
+
+    # -- end to end through the host-facing C-ABI call: ugb_decoder_token (host token and
+    # position in: H2D of the state; graph replay; D2H of the state and the status word) --
+    e2e_steps = min(max(K, 32), n_ctx)
+    tok = 1
+    for p in range(3):
+        tok = dec.token(tok, n_ctx - e2e_steps - 3 + p, stream)
+    t0 = time.perf_counter()
+    for p in range(n_ctx - e2e_steps, n_ctx):
+        tok = dec.token(tok, p, stream)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
+    dec.close()
+    graph.close()
+    if kgraph is not None:
+        kgraph.close()
+    return {
+        "value": world * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
+        "gpu_launches": kernels_per_token * K, "path": active,
+        "token_bytes": token_bytes,
+        "kernel_ms": kern_ms, "kernel_bytes": kern_bytes,
+        "e2e": {"value": world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
+                "d2h_bytes_per_step": 16 + 4},
+    }
+
+
+def c2_gateup_kernel(ugb, ctx, torch, dev, w, c, cap, stream, e0, e1):
+    """Per-launch time and algorithmic bytes of the launch chain's fused gate/up matvec."""
     xq = ugb.alloc_q8act(c["n_embd"], 1, device=dev)
     xv = torch.randn(c["n_embd"], device=dev)
     ctx.quant_q8_1(xv, xq, c["n_embd"], 1)
@@ -326,29 +362,7 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     stream.synchronize()
     kern_ms = e0.elapsed_time(e1) / (reps * c["n_layer"])
     kern_bytes = 2 * q8_bytes(c["n_embd"], c["n_ff"]) + xq.numel() + gu.numel() * 4
-
-    # -- end to end through the host-facing C-ABI call: ugb_decoder_token (host token and
-    # position in: H2D of the state; graph replay; D2H of the state and the status word) --
-    e2e_steps = min(max(K, 32), n_ctx)
-    tok = 1
-    for p in range(3):
-        tok = dec.token(tok, n_ctx - e2e_steps - 3 + p, stream)
-    t0 = time.perf_counter()
-    for p in range(n_ctx - e2e_steps, n_ctx):
-        tok = dec.token(tok, p, stream)
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
-    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
-    dec.close()
-    graph.close()
-    kgraph.close()
-    return {
-        "value": world * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
-        "gpu_launches": kernels_per_token * K,
-        "token_bytes": token_bytes,
-        "kernel_ms": kern_ms, "kernel_bytes": kern_bytes,
-        "e2e": {"value": world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
-                "d2h_bytes_per_step": 16 + 4},
-    }
+    return kern_ms, kern_bytes, kgraph
 
 
 # ---- workload c1 ----------------------------------------------------------------------------
@@ -695,6 +709,7 @@ def big_gpu(args, ugb, ctx, torch, rank, world, workload):
         torch.distributed.broadcast_object_list(uid, src=0)
         comm = ugb.Comm(ctx, rank, world, uid[0])
         dec.set_comm(comm)
+    active = dec.set_path(PATHS[args.path])
     n_ctx = c["n_ctx"]
     stream = torch.cuda.Stream()
     cap = torch.cuda.Stream()
@@ -746,7 +761,7 @@ def big_gpu(args, ugb, ctx, torch, rank, world, workload):
         comm.close()
     return {
         "value": batch * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
-        "gpu_launches": kernels * K, "step_bytes": step_bytes, "batch": batch,
+        "gpu_launches": kernels * K, "step_bytes": step_bytes, "batch": batch, "path": active,
         "e2e": {"value": batch / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * 4 + 8,
                 "d2h_bytes_per_step": 112 + 4},
         "config": c,
@@ -827,6 +842,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="c4 / c5: decode this many layers instead of the config's (profiling captures only)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--path", choices=sorted(PATHS), default="auto",
+                    help="c2 / c4 / c5 decoder path: persistent token kernel where it applies (auto), "
+                         "the per-kernel launch chain, or the token kernel only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -922,12 +940,20 @@ def main():
     ctx = ugb.Context(torch.cuda.current_device())
     if args.workload == "c2":
         res = c2_gpu(args, ugb, ctx, torch, rank, world)
-        kernel = "mv_rows_kernel<Q8_0> (fused gate/up, 17920x1536)"
-        traffic = load_traffic("c2_gate_up")
+        if res["path"] == ugb.PATH_TOKEN:
+            kernel = "token_kernel<Q8_0,Q8_0> (the whole decode step, one persistent launch per token)"
+            traffic = load_traffic("c2_token")
+            config["path"] = "token kernel: one persistent cooperative launch per token, 1 CTA per SM"
+        else:
+            kernel = "mv_rows_kernel<Q8_0> (fused gate/up, 17920x1536)"
+            traffic = load_traffic("c2_gate_up")
+            config["path"] = "launch chain: 256 kernels per token, captured as one CUDA graph"
     elif args.workload in ("c4", "c5"):
         res = big_gpu(args, ugb, ctx, torch, rank, world, args.workload)
         kernel = None
         traffic = None
+        config["path"] = ("token kernel: one persistent cooperative launch per token" if res["path"] == ugb.PATH_TOKEN
+                          else "launch chain captured as one CUDA graph")
     elif args.workload == "c3":
         res = c3_gpu(args, ugb, ctx, torch, rank, world)
         kernel = "prefill_gemm_kernel<128> (fused gate/up, 512 x 17920 x 1536)"

@@ -349,6 +349,23 @@ ugb_status ugb_decoder_synthetic(ugb_decoder *dec, uint64_t seed);
  * (a shard then computes its partial results only). */
 ugb_status ugb_decoder_set_comm(ugb_decoder *dec, ugb_comm *comm);
 
+/* How a step runs.
+ *   UGB_PATH_CHAIN -- the launch chain: about nine kernels per layer (matvecs, norms,
+ *     attention, SiLU), each waiting for the previous one, as the reference's per-token
+ *     command list (gpu_graph.rs:139-162).  Serves every configuration.
+ *   UGB_PATH_TOKEN -- one persistent cooperative kernel per token, one CTA per SM: weights
+ *     stream continuously through shared memory while device-wide counters order the phases.
+ *     Dense decoders at batch 1 on one device only, with Q8_0 or Q4_K layers, a Q8_0 head,
+ *     and 16-byte aligned tensors and rows.
+ *   UGB_PATH_AUTO (default) -- TOKEN where it applies, else CHAIN.
+ * Both paths compute the same step with the same arithmetic, except for fp32 summation order.
+ * `active` (may be NULL) receives the path the next steps take.  Asking for TOKEN where it does
+ * not apply returns UGB_ESHAPE and changes nothing.  No counterpart in the reference. */
+#define UGB_PATH_AUTO 0
+#define UGB_PATH_CHAIN 1
+#define UGB_PATH_TOKEN 2
+ugb_status ugb_decoder_set_path(ugb_decoder *dec, int32_t path, int32_t *active);
+
 /* Enqueue one token step on `stream`: embedding of the current tokens, every layer, the head
  * and greedy selection.  A sequence's token comes from the previous step's greedy choice when
  * there is one (the position then advances), else from ugb_decoder_set_tokens, so replaying a

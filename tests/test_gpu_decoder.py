@@ -11,6 +11,9 @@ at least 80% of steps within 1e-4 with the same greedy token (a flip-free step a
 ~1e-7).  Positions cross the 64-position attention chunk boundary.  The device-driven replay
 (each step's greedy token fed into the next on the device) must produce the same sequence as
 host-driven steps, and eager launches must equal the captured graph bitwise.
+
+Dense batch-1 decoders run either as the launch chain or as the persistent token kernel
+(ugb_decoder_set_path); the tests of that shape run on both paths.
 """
 from __future__ import annotations
 
@@ -76,10 +79,16 @@ def build_model(ctx, ugb, cfg, seed):
     return dev, host
 
 
-def make_decoder(ctx, ugb, cfg, seed):
+CHAIN, TOKEN = 1, 2
+PATHS = pytest.mark.parametrize("path", [CHAIN, TOKEN], ids=["chain", "token"])
+
+
+def make_decoder(ctx, ugb, cfg, seed, path=None):
     dev, host = build_model(ctx, ugb, cfg, seed)
     dec = ugb.Decoder(ctx, **cfg)
     dec.bind(dev["tok_embd"], dev["output_norm"], dev["output"], dev["layers"])
+    if path is not None:
+        assert dec.set_path(path) == path
     return dec, dev, host
 
 
@@ -105,11 +114,12 @@ def run_synced(dec, ref, tokens):
     return np.array(errs), np.array(agree)
 
 
-@pytest.mark.parametrize("kind", [Q8_0, Q4_K, Q3_K])
-def test_decoder_matches_oracle(ctx, ugb, kind):
+@pytest.mark.parametrize("kind,head_kind,path", [(Q8_0, Q8_0, CHAIN), (Q4_K, Q4_K, CHAIN), (Q3_K, Q3_K, CHAIN),
+                                                 (Q8_0, Q8_0, TOKEN), (Q4_K, Q8_0, TOKEN)])
+def test_decoder_matches_oracle(ctx, ugb, kind, head_kind, path):
     from oracle.decode_ref import RefDecoder
-    cfg = dict(SMALL, kind=kind, head_kind=Q8_0 if kind == Q8_0 else kind)
-    dec, _, host = make_decoder(ctx, ugb, cfg, seed=kind)
+    cfg = dict(SMALL, kind=kind, head_kind=head_kind)
+    dec, _, host = make_decoder(ctx, ugb, cfg, seed=kind, path=path)
     ref = RefDecoder(cfg, host)
     tokens = np.random.default_rng(5).integers(0, cfg["n_vocab"], size=70)
     errs, agree = run_synced(dec, ref, tokens)
@@ -121,12 +131,14 @@ def test_decoder_matches_oracle(ctx, ugb, kind):
     dec.close()
 
 
-def test_decoder_wide_ffn_matches_oracle(ctx, ugb):
-    """A 4096-wide FFN (128 activation blocks) with 512-wide rows: the down rows take the
-    split-row kernel."""
+@PATHS
+@pytest.mark.parametrize("n_ff", [4096, 8960])
+def test_decoder_wide_ffn_matches_oracle(ctx, ugb, path, n_ff):
+    """Wide FFNs with 512-wide rows: on the chain the down rows take the split-row kernel; in
+    the token kernel rows of more than 128 units read their activation from shared memory."""
     from oracle.decode_ref import RefDecoder
-    cfg = dict(SMALL, n_ff=4096, n_embd=512, n_head=4, n_layer=2)
-    dec, _, host = make_decoder(ctx, ugb, cfg, seed=61)
+    cfg = dict(SMALL, n_ff=n_ff, n_embd=512, n_head=4, n_layer=2)
+    dec, _, host = make_decoder(ctx, ugb, cfg, seed=61, path=path)
     ref = RefDecoder(cfg, host)
     tokens = np.random.default_rng(4).integers(0, cfg["n_vocab"], size=24)
     errs, agree = run_synced(dec, ref, tokens)
@@ -136,11 +148,12 @@ def test_decoder_wide_ffn_matches_oracle(ctx, ugb):
     dec.close()
 
 
-def test_decoder_kv_cache_matches_oracle(ctx, ugb):
+@PATHS
+def test_decoder_kv_cache_matches_oracle(ctx, ugb, path):
     """The cached rotated keys and values of the first layer equal the oracle's (they depend
     only on the embedding, the first norm and the QKV matvec)."""
     from oracle.decode_ref import RefDecoder
-    dec, _, host = make_decoder(ctx, ugb, SMALL, seed=21)
+    dec, _, host = make_decoder(ctx, ugb, SMALL, seed=21, path=path)
     ref = RefDecoder(SMALL, host)
     for pos, tok in enumerate([9, 400, 3, 77]):
         dec.token(tok, pos)
@@ -152,11 +165,13 @@ def test_decoder_kv_cache_matches_oracle(ctx, ugb):
     dec.close()
 
 
-def test_decoder_eager_step_equals_graph(ctx, ugb):
+@PATHS
+def test_decoder_eager_step_equals_graph(ctx, ugb, path):
     """ugb_decoder_step (eager launches) and ugb_decoder_token (captured graph) agree bitwise."""
-    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=11)
+    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=11, path=path)
     dec2 = ugb.Decoder(ctx, **SMALL)
     dec2.bind(dev["tok_embd"], dev["output_norm"], dev["output"], dev["layers"])
+    assert dec2.set_path(path) == path
     for pos, tok in enumerate([3, 17, 999, 0, 42]):
         a = dec.token(tok, pos)
         la = dec.logits()
@@ -171,15 +186,17 @@ def test_decoder_eager_step_equals_graph(ctx, ugb):
     dec2.close()
 
 
-def test_decoder_device_driven_replay(ctx, ugb):
+@PATHS
+def test_decoder_device_driven_replay(ctx, ugb, path):
     """Steps enqueued back to back feed each greedy token into the next step on the device;
     the sequence equals host-driven token steps."""
-    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=12)
+    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=12, path=path)
     seq = [7]
     for pos in range(12):
         seq.append(dec.token(seq[-1], pos))
     dec2 = ugb.Decoder(ctx, **SMALL)
     dec2.bind(dev["tok_embd"], dev["output_norm"], dev["output"], dev["layers"])
+    assert dec2.set_path(path) == path
     dec2.set_state(7, 0)
     got = []
     for _ in range(12):
@@ -192,10 +209,11 @@ def test_decoder_device_driven_replay(ctx, ugb):
     dec2.close()
 
 
-def test_decoder_context_end_is_flagged(ctx, ugb):
+@PATHS
+def test_decoder_context_end_is_flagged(ctx, ugb, path):
     ctx.status_read()  # clear
     cfg = dict(SMALL, n_ctx=8)
-    dec, _, _ = make_decoder(ctx, ugb, cfg, seed=13)
+    dec, _, _ = make_decoder(ctx, ugb, cfg, seed=13, path=path)
     dec.set_state(1, 7)
     dec.step()
     assert ctx.status_read()[1] == 0
@@ -276,7 +294,7 @@ def test_moe_decoder_matches_oracle(ctx, ugb, batch):
 def test_vocab_shard_logits(ctx, ugb):
     """A decoder holding head rows [300, 700) computes exactly those logits (no communicator:
     the greedy key covers the held rows only)."""
-    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=51)
+    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=51, path=CHAIN)  # a sharded head runs the chain
     rb = ugb.row_bytes(Q8_0, SMALL["n_embd"])
     part = ugb.Decoder(ctx, **dict(SMALL, vocab0=300, n_vocab_local=400))
     head = dev["tok_embd"][300 * rb:700 * rb]
@@ -304,3 +322,56 @@ def test_moe_synthetic_deterministic(ctx, ugb):
         np.testing.assert_array_equal(full.logits().view(np.uint32), other.logits().view(np.uint32))
     full.close()
     other.close()
+
+
+def test_decoder_path_selection(ctx, ugb):
+    """AUTO takes the token kernel for dense batch-1 decoders and the chain elsewhere; asking
+    for the token kernel where it does not apply fails and changes nothing."""
+    dec, dev, _ = make_decoder(ctx, ugb, SMALL, seed=71)
+    assert dec.set_path(ugb.PATH_AUTO) == TOKEN
+    assert dec.set_path(CHAIN) == CHAIN
+    assert dec.set_path(ugb.PATH_AUTO) == TOKEN
+    with pytest.raises(ugb.UgbError):
+        dec.set_path(7)
+    dec.close()
+    for cfg in (dict(SMALL, batch=2), dict(MOE), dict(SMALL, kind=Q3_K, head_kind=Q3_K),
+                dict(SMALL, vocab0=0, n_vocab_local=500)):
+        d = ugb.Decoder(ctx, **cfg)
+        d.synthetic(1)
+        assert d.set_path(ugb.PATH_AUTO) == CHAIN, cfg
+        with pytest.raises(ugb.UgbError):
+            d.set_path(TOKEN)
+        assert d.set_path(ugb.PATH_AUTO) == CHAIN
+        d.close()
+
+
+def test_token_kernel_matches_chain(ctx, ugb):
+    """The two paths decode the same greedy sequence over 150 device-driven steps (crossing two
+    attention chunk boundaries), with logits within 1e-3 at every step: they differ in fp32
+    summation order only (a Q8_1 rounding flip, at most ~1e-2, is rarer than that here)."""
+    cfg = dict(SMALL, n_ctx=200)
+    chain = ugb.Decoder(ctx, **cfg)
+    chain.synthetic(81)
+    assert chain.set_path(CHAIN) == CHAIN
+    tok = ugb.Decoder(ctx, **cfg)
+    tok.synthetic(81)
+    assert tok.set_path(TOKEN) == TOKEN
+    chain.set_state(5, 0)
+    tok.set_state(5, 0)
+    errs, same = [], 0
+    for _ in range(150):
+        chain.step()
+        tok.step()
+        a, b = chain.get_state(), tok.get_state()
+        la, lb = chain.logits(), tok.logits()
+        errs.append(rel_l2(lb, la))
+        same += a == b
+        if a != b:  # a (rare) greedy divergence: both continue from the chain's choice
+            chain.set_state(a[2], a[1] + 1)
+            tok.set_state(a[2], a[1] + 1)
+    errs = np.array(errs)
+    assert same >= 145, same
+    assert np.median(errs) <= 1e-5 and (errs <= 1e-3).mean() >= 0.95, errs
+    assert ctx.status_read()[1] == 0
+    chain.close()
+    tok.close()

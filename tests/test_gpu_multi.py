@@ -61,6 +61,7 @@ def _worker(rank, world, port, out):
     shard.set_comm(comm)
     full = ugb.Decoder(ctx, **SMALL)
     full.synthetic(5)
+    full.set_path(ugb.PATH_CHAIN)  # the sharded head runs the launch chain: compare like with like
     tok, same_tok, same_logits = 3, True, True
     for pos in range(10):
         dist.barrier()

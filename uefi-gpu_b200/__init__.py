@@ -71,6 +71,7 @@ SIGNATURES = {
     "ugb_decoder_get_tokens": (_int, [_vp, _vp, _vp, ctypes.POINTER(ctypes.c_int32), _vp]),
     "ugb_decoder_tokens": (_int, [_vp, _vp, _vp, ctypes.c_int32, _vp]),
     "ugb_decoder_set_comm": (_int, [_vp, _vp]),
+    "ugb_decoder_set_path": (_int, [_vp, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
     "ugb_comm_unique_id": (_int, [_vp]),
     "ugb_comm_init": (_int, [_vp, _int, _int, _vp, ctypes.POINTER(_vp)]),
     "ugb_comm_destroy": (_int, [_vp]),
@@ -348,6 +349,9 @@ class ModelWeights(ctypes.Structure):
 
 
 COMM_ID_BYTES = 128
+# How a decoder step runs (ugb_decoder_set_path): persistent token kernel where it applies, the
+# per-kernel launch chain, or the persistent token kernel only.
+PATH_AUTO, PATH_CHAIN, PATH_TOKEN = 0, 1, 2
 
 
 class Comm:
@@ -427,6 +431,12 @@ class Decoder:
 
     def set_comm(self, comm: "Comm | None") -> None:
         check("ugb_decoder_set_comm", lib().ugb_decoder_set_comm(self.handle, comm.handle if comm else None))
+
+    def set_path(self, path: int) -> int:
+        """PATH_AUTO / PATH_CHAIN / PATH_TOKEN; returns the path the next steps take."""
+        active = ctypes.c_int32()
+        check("ugb_decoder_set_path", lib().ugb_decoder_set_path(self.handle, path, ctypes.byref(active)))
+        return active.value
 
     def get_state(self, stream=None):
         t, p, n = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()

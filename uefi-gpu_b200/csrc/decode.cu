@@ -15,39 +15,10 @@
 
 #include "common.cuh"
 #include "decode.hpp"
+#include "glue.cuh"
 
 namespace ugb {
 namespace {
-
-// Q8_1 block-32 quantisation of one 32-element block held one value per lane (the
-// quant_act arithmetic, gpu_dp4a.cu:23-31).  Writes quants, scale and sum of block b.
-__device__ __forceinline__ bool quant_block(float v, int lane, int8_t *q, float *d, int32_t *s, int b) {
-  const bool fin = isfinite(v);
-  float a = fin ? fabsf(v) : 0.f;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-  const float inv = a > 0.f ? 127.0f / a : 0.0f;
-  int qi = fin ? __float2int_rn(v * inv) : 0;
-  qi = max(-127, min(127, qi));
-  q[b * 32 + lane] = static_cast<int8_t>(qi);
-  const int sum = __reduce_add_sync(0xffffffffu, qi);
-  if (lane == 0) {
-    d[b] = a / 127.0f;
-    s[b] = sum;
-  }
-  return __any_sync(0xffffffffu, !fin);
-}
-
-// Greedy key: value bits made order-preserving as an unsigned integer, then the complemented
-// id, so the larger key is the larger value and, for equal values, the lower id (the
-// reference keeps the first maximum, llm.rs:383-385).
-__device__ __forceinline__ uint64_t greedy_key(float v, uint32_t id) {
-  uint32_t b = __float_as_uint(v);
-  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return (static_cast<uint64_t>(b) << 32) | static_cast<uint64_t>(~id);
-}
-
-__device__ __forceinline__ uint32_t key_id(uint64_t key) { return ~static_cast<uint32_t>(key); }
 
 // Vector b of a Q8_1 buffer of length-n vectors: (quants, scales, sums).
 struct Q8View {

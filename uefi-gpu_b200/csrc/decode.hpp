@@ -56,4 +56,46 @@ ugb_status launch_moe_experts(ugb_ctx *ctx, cudaStream_t stream, const ugb_moe_a
 ugb_status launch_moe_route(ugb_ctx *ctx, cudaStream_t stream, bool pdl, const float *logits, int n_expert,
                             int top_k, int batch, int32_t *ids, float *weights);
 
+// ---- the persistent token kernel (token.cu) ----------------------------------------------------
+
+constexpr uint32_t kTokItemMax = 32 * 1024;  // bytes of one streamed item (whole rows)
+
+// One layer's tensors as the token kernel reads them (a device-side table, one entry per layer).
+struct TokLayer {
+  const uint8_t *wq, *wk, *wv, *wo, *wg, *wu, *wd;
+  const float *attn_norm, *ffn_norm;
+  const float *bias;  // [q; k; v] rows, or null
+};
+
+// Everything one launch of the token kernel needs (batch 1, dense FFN, one device).  The
+// o_* fields and ring_bytes are the shared-memory layout, filled in by launch_token.
+struct TokenStep {
+  const TokLayer *layers;
+  const uint8_t *tok_embd;    // Q8_0 [n_vocab][n_embd]
+  const uint8_t *head;        // head_kind [n_vocab][n_embd]
+  const float *out_norm;
+  float *qkv;                 // [q; k; v] of the current layer
+  float *dxo, *dxd;           // O and down projections (read by the next phase's residual add)
+  float *logits;              // [n_vocab]
+  uint8_t *hq;                // Q8_1 of SiLU(gate) * up: quants [n_ff] | scales | sums
+  float *kcache, *vcache;     // [n_layer][n_kv][n_ctx][HD]
+  const float2 *rope;         // [n_ctx][HD/2]
+  float *part_m, *part_l, *part_o;  // attention partials, [n_kv][n_split][G](.[HD])
+  DecodeState *state;
+  uint32_t *sync;             // token_sync_words() zeroed words: the step's counters
+  uint32_t *status;
+  int n_layer, n_embd, n_ff, n_head, n_kv, n_ctx, n_vocab, n_split;
+  float eps;
+  uint32_t rb_e, rb_q, rb_f, rb_h, rb_tok;  // row bytes at K = n_embd, n_head*HD, n_ff; head; embedding
+  int gu_blocks;              // FFN blocks a CTA holds at most
+  uint32_t o_xres, o_xq, o_xd, o_xs, o_scr, o_layers, o_gu, o_ring, ring_bytes;
+};
+
+constexpr size_t token_sync_words() { return 8 * 32; }
+
+// Whether the token kernel serves this decoder on this device (kinds, shapes, row alignment,
+// shared memory).
+bool token_supported(const ugb_ctx *ctx, uint32_t kind, uint32_t head_kind, TokenStep p);
+ugb_status launch_token(ugb_ctx *ctx, cudaStream_t stream, uint32_t kind, uint32_t head_kind, TokenStep p);
+
 }  // namespace ugb

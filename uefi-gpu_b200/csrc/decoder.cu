@@ -48,6 +48,12 @@ struct ugb_decoder {
   std::vector<ugb_layer_weights> layers;
   float *bias = nullptr;   // per layer [q;k;v] fused biases (bound when any bias is given)
   std::vector<void *> owned;
+  // persistent token kernel (dense, batch 1): its own buffers and the per-layer tensor table
+  float *dxd = nullptr;
+  uint8_t *tok_hq = nullptr;
+  uint32_t *tok_sync = nullptr;
+  ugb::TokLayer *tok_layers = nullptr;
+  int path = UGB_PATH_AUTO;
   ugb_comm *comm = nullptr;
   // replay
   cudaStream_t cap = nullptr;
@@ -101,7 +107,7 @@ void free_graph(ugb_decoder *d) {
 void free_all(ugb_decoder *d) {
   void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->rlogits, d->rweights, d->rids, d->xq, d->attq,
                   d->hq, d->kcache, d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->moe_ws, d->state,
-                  d->bias};
+                  d->bias, d->dxd, d->tok_hq, d->tok_sync, d->tok_layers};
   for (void *b : bufs)
     if (b) cudaFree(b);
   for (void *b : d->owned) cudaFree(b);
@@ -159,6 +165,11 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
   } else if (ok) {
     ok = dalloc(&d->gu, static_cast<size_t>(B) * 2 * c.n_ff) == UGB_OK &&
          dalloc(&d->hq, q8act_layout(c.n_ff, B).bytes) == UGB_OK;
+    if (ok && B == 1)
+      ok = dalloc(&d->dxd, c.n_embd) == UGB_OK && dalloc(&d->tok_hq, c.n_ff + 8 * (c.n_ff / 32)) == UGB_OK &&
+           dalloc(&d->tok_sync, token_sync_words()) == UGB_OK &&
+           dalloc(&d->tok_layers, c.n_layer) == UGB_OK &&
+           cudaMemset(d->tok_sync, 0, token_sync_words() * sizeof(uint32_t)) == cudaSuccess;
   }
   if (ok) {
     // RoPE table as the reference builds it (gpu_graph.rs:132, llm.rs:330): the angle is the
@@ -290,6 +301,20 @@ extern "C" ugb_status ugb_decoder_bind(ugb_decoder *d, const ugb_model_weights *
   d->layers.assign(w->layers, w->layers + c.n_layer);
   d->w.layers = d->layers.data();
   free_graph(d);  // the captured step refers to the old weights
+  if (d->tok_layers) {
+    std::vector<TokLayer> tab(c.n_layer);
+    for (int l = 0; l < c.n_layer; ++l) {
+      const ugb_layer_weights &L = d->layers[l];
+      tab[l] = TokLayer{static_cast<const uint8_t *>(L.wq),     static_cast<const uint8_t *>(L.wk),
+                        static_cast<const uint8_t *>(L.wv),     static_cast<const uint8_t *>(L.wo),
+                        static_cast<const uint8_t *>(L.w_gate), static_cast<const uint8_t *>(L.w_up),
+                        static_cast<const uint8_t *>(L.w_down), static_cast<const float *>(L.attn_norm),
+                        static_cast<const float *>(L.ffn_norm),
+                        d->bias ? d->bias + static_cast<size_t>(l) * brow : nullptr};
+    }
+    if (cudaMemcpy(d->tok_layers, tab.data(), tab.size() * sizeof(TokLayer), cudaMemcpyHostToDevice) != cudaSuccess)
+      return UGB_EBACKEND;
+  }
   return UGB_OK;
 }
 
@@ -384,8 +409,86 @@ MatvecArgs mv_args(uint32_t kind, int64_t k, int64_t m, int batch, const uint8_t
 }  // namespace
 }  // namespace ugb
 
+namespace ugb {
+namespace {
+
+// The token kernel's launch description for this decoder; false when the decoder is not one it
+// serves (MoE, batch > 1, a sharded head, kinds, shapes, alignment, shared memory).
+bool token_step_of(const ugb_decoder *d, TokenStep &p) {
+  const ugb_decoder_config &c = d->cfg;
+  if (d->moe || d->batch != 1 || !d->tok_layers || !d->w.layers || d->n_vocab_local != c.n_vocab) return false;
+  const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
+  p = TokenStep{};
+  p.layers = d->tok_layers;
+  p.tok_embd = static_cast<const uint8_t *>(d->w.tok_embd);
+  p.head = static_cast<const uint8_t *>(d->w.output);
+  p.out_norm = static_cast<const float *>(d->w.output_norm);
+  p.qkv = d->qkv;
+  p.dxo = d->dx;
+  p.dxd = d->dxd;
+  p.logits = d->logits;
+  p.hq = d->tok_hq;
+  p.kcache = d->kcache;
+  p.vcache = d->vcache;
+  p.rope = d->rope;
+  p.part_m = d->part_m;
+  p.part_l = d->part_l;
+  p.part_o = d->part_o;
+  p.state = d->state;
+  p.sync = d->tok_sync;
+  p.status = d->ctx->status;
+  p.n_layer = c.n_layer;
+  p.n_embd = c.n_embd;
+  p.n_ff = c.n_ff;
+  p.n_head = c.n_head;
+  p.n_kv = c.n_head_kv;
+  p.n_ctx = c.n_ctx;
+  p.n_vocab = c.n_vocab;
+  p.n_split = d->n_split;
+  p.eps = c.norm_eps;
+  p.rb_e = static_cast<uint32_t>(ugb_row_bytes(c.kind, c.n_embd));
+  p.rb_q = static_cast<uint32_t>(ugb_row_bytes(c.kind, qrows));
+  p.rb_f = static_cast<uint32_t>(ugb_row_bytes(c.kind, c.n_ff));
+  p.rb_h = static_cast<uint32_t>(ugb_row_bytes(c.head_kind, c.n_embd));
+  p.rb_tok = static_cast<uint32_t>(ugb_row_bytes(UGB_Q8_0, c.n_embd));
+  for (int l = 0; l < c.n_layer; ++l) {
+    const ugb_layer_weights &L = d->layers[l];
+    for (const void *m : {L.wq, L.wk, L.wv, L.wo, L.w_gate, L.w_up, L.w_down})
+      if (reinterpret_cast<uintptr_t>(m) & 15) return false;
+  }
+  if (reinterpret_cast<uintptr_t>(p.head) & 15) return false;
+  return token_supported(d->ctx, c.kind, c.head_kind, p);
+}
+
+bool use_token(const ugb_decoder *d, TokenStep &p) {
+  if (d->path == UGB_PATH_CHAIN || (d->comm && comm_world(d->comm) > 1)) return false;
+  return token_step_of(d, p);
+}
+
+}  // namespace
+}  // namespace ugb
+
+extern "C" ugb_status ugb_decoder_set_path(ugb_decoder *d, int32_t path, int32_t *active) {
+  if (!d) return UGB_ECONTEXT;
+  if (path != UGB_PATH_AUTO && path != UGB_PATH_CHAIN && path != UGB_PATH_TOKEN) return UGB_ESHAPE;
+  TokenStep p;
+  const bool can = token_step_of(d, p) && !(d->comm && comm_world(d->comm) > 1);
+  if (path == UGB_PATH_TOKEN && !can) return UGB_ESHAPE;
+  if (d->path != path) free_graph(d);
+  d->path = path;
+  if (active) *active = (path != UGB_PATH_CHAIN && can) ? UGB_PATH_TOKEN : UGB_PATH_CHAIN;
+  return UGB_OK;
+}
+
 extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
   if (!d || !d->w.layers) return UGB_ECONTEXT;
+  {
+    TokenStep tp;
+    if (use_token(d, tp)) {
+      cudaSetDevice(d->ctx->device);
+      return launch_token(d->ctx, stream, d->cfg.kind, d->cfg.head_kind, tp);
+    }
+  }
   const ugb_decoder_config &c = d->cfg;
   ugb_ctx *ctx = d->ctx;
   uint32_t *status = ctx->status;

@@ -26,6 +26,7 @@
 #include <cmath>
 
 #include "formats.cuh"
+#include "glue.cuh"
 #include "internal.hpp"
 
 namespace ugb {
@@ -276,40 +277,6 @@ __device__ void issue_item(const MvParams &p, const View &v, int t, uint32_t sta
     span16(p, v, seg, src, e, a0, a1);
     if (a1 > a0) bulk_g2s(stage + r * p.seg_stride, a0, static_cast<uint32_t>(a1 - a0), bar, pol);
   }
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-
-// Totals of RW per-lane row partials v[0..RW) over the warp with one transposed shuffle tree
-// (RW=4: 6 shuffles instead of 20).  The total of row r ends in lane r * (32 / RW); the lane
-// returns the total of its row in *out and whether it owns one.
-template <int RW>
-__device__ __forceinline__ bool reduce_rows(const float (&v)[RW], int lane, float &out) {
-  float c;
-  if constexpr (RW == 1) {
-    c = v[0];
-  } else if constexpr (RW == 2) {
-    const bool hi = lane & 16;
-    const float r = __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[1], 16);
-    c = (hi ? v[1] : v[0]) + r;  // row (hi ? 1 : 0)
-  } else {
-    const bool hi = lane & 16;
-    const float r0 = __shfl_xor_sync(0xffffffffu, hi ? v[0] : v[2], 16);
-    const float r1 = __shfl_xor_sync(0xffffffffu, hi ? v[1] : v[3], 16);
-    const float a = (hi ? v[2] : v[0]) + r0;  // row (hi ? 2 : 0)
-    const float b = (hi ? v[3] : v[1]) + r1;  // row (hi ? 3 : 1)
-    const bool h8 = lane & 8;
-    const float r = __shfl_xor_sync(0xffffffffu, h8 ? a : b, 8);
-    c = (h8 ? b : a) + r;  // row (hi ? 2 : 0) + (h8 ? 1 : 0)
-  }
-#pragma unroll
-  for (int o = 32 / RW / 2; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
-  out = c;
-  return (lane & (32 / RW - 1)) == 0;
 }
 
 // Shared prologue: barriers, programmatic-launch hand-off, the producer warp's whole life,
