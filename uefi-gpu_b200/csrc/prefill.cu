@@ -43,8 +43,8 @@ constexpr int kStages = 4;
 constexpr int kAcc = 4;                   // TMEM accumulators
 constexpr int kTileBytes = kPrefillTileBytes;         // 4096: one 128 x 32 B operand block
 constexpr int kScaleBytes = kPrefillTile * 4;          // 512
-constexpr int kEpiWarps = 8;
-constexpr int kGemmThreads = 32 * (2 + kEpiWarps);    // 320
+constexpr int kEpiWarps = 16;
+constexpr int kGemmThreads = 32 * (2 + kEpiWarps);    // 576
 
 // Per output-tile width BN (weight rows per CTA, UMMA N): 128, or 64 for GEMMs whose 128-wide
 // tiling leaves SMs idle (a 64-row CTA reads one half of each packed 128-row weight block).
@@ -54,7 +54,7 @@ struct Geo {
   static constexpr int kStageBytes = kKB * (kTileBytes + kBBytes + kScaleBytes + BN * 4);
   static constexpr int kSmem = kStages * kStageBytes + 256;                 // + barriers
   static constexpr int kTmemCols = kAcc * BN;                               // 512 or 256
-  static constexpr int kCols = BN / 2;                                      // per epilogue warp
+  static constexpr int kCols = BN / 4;                                      // per epilogue warp
   // Instruction descriptor: D s32, A s8, B s8, both K-major, N = BN, M = 128.
   static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) |
                                      (static_cast<uint32_t>(BN >> 3) << 17) |
@@ -104,6 +104,14 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
+// 16 consecutive TMEM columns of this warp's 32 lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor of one 128 x 32-byte K-major operand block in the canonical
@@ -134,6 +142,26 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// int32 -> fp32 of a block dot, two ways that give the same (exact) value: the conversion
+// instruction (a quarter-rate pipe on sm_100), and the bias trick on the integer and fp32 pipes
+// -- the bits of i + 0x4B400000 read as a float equal 2^23 + 2^22 + i exactly for
+// |i| < 2^22, so subtracting 12582912 leaves i.  A block dot is at most 32 * 127 * 127 in
+// magnitude.  The epilogue converts half of its values each way, so neither pipe alone bounds it.
+constexpr uint32_t kBiasBits = 0x4B400000u;
+constexpr float kBiasValue = 12582912.0f;
+static_assert(32 * 127 * 127 < (1 << 22), "block dots fit the bias trick");
+__device__ __forceinline__ uint64_t cvt2_i2f(uint32_t a, uint32_t b) {
+  return pk2(static_cast<float>(static_cast<int32_t>(a)), static_cast<float>(static_cast<int32_t>(b)));
+}
+__device__ __forceinline__ uint64_t cvt2_bias(uint32_t a, uint32_t b) {
+  return sub2(pk2(__uint_as_float(a + kBiasBits), __uint_as_float(b + kBiasBits)), pk2(kBiasValue, kBiasValue));
 }
 
 // Byte offset of (row r, K byte j) inside one canonical 128 x 32-byte block.
@@ -352,9 +380,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     }
   } else {
     // ---- epilogue: rescale every block's int32 tile into fp32 accumulators ----
-    constexpr int kC = G::kCols;           // columns of this warp (64 or 32)
+    constexpr int kC = G::kCols;           // columns of this warp (32 or 16)
     const int q = warp & 3;                // TMEM lane quarter this warp may access
-    const int h = (warp - 2) >> 2;         // column half
+    const int h = (warp - 2) >> 2;         // column quarter
     const int t_local = q * 32 + lane;     // token row of the tile
     const int c0 = h * kC;                 // first column of this warp
     const int64_t t = m_tile * kBM + t_local;
@@ -372,29 +400,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       const float dx = reinterpret_cast<const float *>(st + kOffSA)[kb * kPrefillTile + t_local];
       const float4 *dw4 = reinterpret_cast<const float4 *>(st + kOffSB + (kb * BN + c0) * 4);
       const uint64_t dx2 = pk2(dx, dx);
-#pragma unroll
-      for (int c = 0; c < kC / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * BN + c0 + c * 32), r);
-        tmem_ld_wait();
-        if (p.dots) {
-          for (int i = 0; i < 32; ++i) {
-            const int64_t nn = n_col0 + c0 + c * 32 + i;
-            if (t < p.m && nn < p.n) p.dots[(static_cast<int64_t>(b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
-          }
+      uint32_t r[kC];
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * BN + c0);
+      if constexpr (kC == 32) {
+        tmem_ld32(taddr, r);
+      } else {
+        tmem_ld16(taddr, r);
+      }
+      tmem_ld_wait();
+      if (p.dots) {
+        for (int i = 0; i < kC; ++i) {
+          const int64_t nn = n_col0 + c0 + i;
+          if (t < p.m && nn < p.n) p.dots[(static_cast<int64_t>(b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
         }
+      }
 #pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 w = dw4[(c * 32 + i) / 4];  // same address across the warp: broadcast
-          // fmaf((float)I, dw * dx, acc) per lane, two columns per instruction
-          const uint64_t s01 = mul2(pk2(w.x, w.y), dx2), s23 = mul2(pk2(w.z, w.w), dx2);
-          const uint64_t f01 = pk2(static_cast<float>(static_cast<int32_t>(r[i])),
-                                   static_cast<float>(static_cast<int32_t>(r[i + 1])));
-          const uint64_t f23 = pk2(static_cast<float>(static_cast<int32_t>(r[i + 2])),
-                                   static_cast<float>(static_cast<int32_t>(r[i + 3])));
-          acc[(c * 32 + i) / 2] = fma2(f01, s01, acc[(c * 32 + i) / 2]);
-          acc[(c * 32 + i) / 2 + 1] = fma2(f23, s23, acc[(c * 32 + i) / 2 + 1]);
-        }
+      for (int i = 0; i < kC; i += 4) {
+        const float4 w = dw4[i / 4];  // same address across the warp: broadcast
+        // fmaf((float)I, dw * dx, acc) per lane, two columns per instruction
+        const uint64_t s01 = mul2(pk2(w.x, w.y), dx2), s23 = mul2(pk2(w.z, w.w), dx2);
+        const uint64_t f01 = cvt2_i2f(r[i], r[i + 1]);
+        const uint64_t f23 = cvt2_bias(r[i + 2], r[i + 3]);
+        acc[i / 2] = fma2(f01, s01, acc[i / 2]);
+        acc[i / 2 + 1] = fma2(f23, s23, acc[i / 2 + 1]);
       }
       tc_fence_before();
       __syncwarp();

@@ -305,8 +305,9 @@ __device__ uint32_t produce(const TokenStep &p, uint32_t base, const TokPlan &pl
     mbar_arrive_expect_tx(full + 8 * (t % kNS), bytes);
     bulk_g2s(ring + off, src, bytes, full + 8 * (t % kNS), pol);
   };
-  for (int l = 0; l < p.n_layer && ok; ++l)
+  for (int l = 0; l < p.n_layer && ok; ++l) {
     for (int slot = kSlotQKV; slot <= kSlotDown && ok; ++slot) visit(p, pl, layers[l], slot, issue);
+  }
   if (ok) visit(p, pl, layers[0], kSlotHead, issue);
   return cur.t;
 }
