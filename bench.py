@@ -390,11 +390,12 @@ def c1_gpu(args, ugb, ctx, torch, rank, world):
     stream = torch.cuda.current_stream()
 
     def step(i):
-        # quant_act + linear (gpu_graph.rs:74-80); the matvec prefetches its weights while the
-        # quantiser runs (programmatic dependent launch)
+        # quant_act + linear (gpu_graph.rs:74-80) as one call: at this shape (batch 1, the matrix
+        # staged whole, one CTA per SM) the quantisation runs inside the matvec kernel, and each
+        # step's weight copies start while the previous step computes (programmatic dependent
+        # launch with two steps resident per SM)
         j = i % C1_ROTATE
-        ctx.quant_q8_1(xs[j], xq, C1_K, 1)
-        ctx.matvec(Q8_0, ws[j], rb, xq, y, C1_K, C1_M, 1)
+        ctx.matvec_f32(Q8_0, ws[j], rb, xs[j], xq, y, C1_K, C1_M, 1)
 
     # The K timed steps are one CUDA graph (the reference submits its per-token command list
     # as one GPFIFO entry); kernels launch with programmatic dependent launch so each matvec
@@ -421,7 +422,7 @@ def c1_gpu(args, ugb, ctx, torch, rank, world):
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     ms_max = reduce_max(ms, world, torch)
-    launches = 2 * args.steps  # quant_q8_1 + matvec per step
+    launches = args.steps  # one fused quant + matvec kernel per step
 
     # -- the dominant kernel (the matvec) back to back in a graph, for the roofline --
     reps = max(args.steps, 96)
@@ -960,7 +961,7 @@ def main():
         traffic = load_traffic("c3_gate_up")
     else:
         res = c1_gpu(args, ugb, ctx, torch, rank, world)
-        kernel = "mv_rows_kernel<Q8_0> (8960x1536)"
+        kernel = "mv_rows_kernel<Q8_0, burst> (8960x1536, ugb_matvec back to back under PDL)"
         traffic = load_traffic("c1_matvec")
 
     line = dict(base)

@@ -123,6 +123,17 @@ ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
                       int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k, int64_t m,
                       int64_t batch);
 
+/* ugb_quant_q8_1 then ugb_matvec as one call: y_dev = W x for fp32 activations x_dev
+ * [batch][k] (the quant_act + linear pair of graph_quant / graph_linear, gpu_graph.rs:70-80).
+ * The quants, scales and sums are ugb_quant_q8_1's bit for bit, so y_dev equals the two-call
+ * result exactly.  xq_scratch is a Q8_1 buffer of ugb_q8act_bytes(k, batch) bytes: a batch-1
+ * matrix small enough to be staged whole (one CTA per SM) is quantised inside the matvec
+ * itself and the scratch is not touched; other shapes quantise into it first.  Same
+ * arguments, limits and status bits as the two calls. */
+ugb_status ugb_matvec_f32(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                          int64_t row_bytes, const float *x_dev, void *xq_scratch, float *y_dev,
+                          int64_t k, int64_t m, int64_t batch);
+
 /* Several matrices of the same kind and row length that share one activation, in one
  * launch: y_dev[v] = [W_0 x_v ; W_1 x_v ; ...] (rows concatenated in order), count <= 4.
  * w_devs (host array) holds the count device pointers, rows the count row counts.

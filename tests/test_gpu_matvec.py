@@ -238,3 +238,57 @@ def test_matvec_multi_equals_separate(ctx, ugb, kind, k, rows, batch):
     want = torch.cat(parts, dim=1).cpu().numpy()
     assert np.array_equal(y.cpu().numpy().view(np.uint32), want.view(np.uint32))
     assert ctx.status_read()[0] == ugb.OK
+
+
+@pytest.mark.parametrize("kind,k,m", SHAPES)
+@pytest.mark.parametrize("batch", [1, 3])
+def test_matvec_f32_equals_two_calls(ctx, ugb, kind, k, m, batch):
+    """ugb_matvec_f32 (quantise inside the matvec when fused) gives exactly quant + matvec."""
+    torch = _torch()
+    w, rb = make_weights(ctx, ugb, kind, k, m, seed=3 * k + m)
+    rng = np.random.default_rng(k + 5 * m + batch)
+    x_np = (rng.standard_normal((batch, k)) * rng.uniform(0.1, 10)).astype(np.float32)
+    x = torch.from_numpy(x_np).cuda()
+    xq = ugb.alloc_q8act(k, batch)
+    ctx.quant_q8_1(x, xq, k, batch)
+    y2 = torch.full((batch, m), float("nan"), dtype=torch.float32, device="cuda")
+    ctx.matvec(kind, w, rb, xq, y2, k, m, batch)
+    scratch = ugb.alloc_q8act(k, batch)
+    y1 = torch.full((batch, m), float("nan"), dtype=torch.float32, device="cuda")
+    ctx.matvec_f32(kind, w, rb, x, scratch, y1, k, m, batch)
+    np.testing.assert_array_equal(y1.cpu().numpy().view(np.uint32), y2.cpu().numpy().view(np.uint32))
+    code, bits = ctx.status_read()
+    assert code == ugb.OK, bits
+
+
+def test_matvec_f32_fuses_c1(ctx, ugb, orc):
+    """At the C1 shape (batch 1) the quantisation runs inside the matvec: the scratch buffer is
+    never written, and the rows match the oracle on the scratch-free path."""
+    torch = _torch()
+    k, m = 1536, 8960
+    w, rb = make_weights(ctx, ugb, Q8_0, k, m, seed=11)
+    x_np = np.random.default_rng(12).standard_normal((1, k)).astype(np.float32)
+    x = torch.from_numpy(x_np).cuda()
+    scratch = ugb.alloc_q8act(k, 1)
+    scratch.fill_(0x5A)
+    y = torch.full((1, m), float("nan"), dtype=torch.float32, device="cuda")
+    ctx.matvec_f32(Q8_0, w, rb, x, scratch, y, k, m, 1)
+    torch.cuda.synchronize()
+    assert bool((scratch == 0x5A).all()), "the fused path must not use the scratch buffer"
+    qo, do, so, bad = orc.quant_act(x_np)
+    ref = orc.matvec(Q8_0, w.cpu().numpy(), rb, qo, do, so, k, m, 1)
+    assert_rows_close(y.cpu().numpy(), ref)
+    assert ctx.status_read()[0] == ugb.OK
+
+
+def test_matvec_f32_nonfinite_sets_status(ctx, ugb):
+    torch = _torch()
+    k, m = 1536, 64
+    w, rb = make_weights(ctx, ugb, Q8_0, k, m, seed=13)
+    x = torch.ones((1, k), dtype=torch.float32, device="cuda")
+    x[0, 77] = float("inf")
+    scratch = ugb.alloc_q8act(k, 1)
+    y = torch.empty((1, m), dtype=torch.float32, device="cuda")
+    ctx.matvec_f32(Q8_0, w, rb, x, scratch, y, k, m, 1)
+    code, bits = ctx.status_read()
+    assert code == ugb.ENONFINITE and bits & 1

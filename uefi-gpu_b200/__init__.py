@@ -44,6 +44,7 @@ SIGNATURES = {
     "ugb_q8act_sum_offset": (ctypes.c_size_t, [_i64, _i64]),
     "ugb_quant_q8_1": (_int, [_vp, _vp, _vp, _vp, _i64, _i64]),
     "ugb_matvec": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64, _i64]),
+    "ugb_matvec_f32": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _vp, _i64, _i64, _i64]),
     "ugb_matvec_multi": (_int, [_vp, _vp, _u32, ctypes.POINTER(_vp), ctypes.POINTER(_i64), _int,
                                 _i64, _vp, _vp, _i64, _i64]),
     "ugb_block_dots": (_int, [_vp, _vp, _u32, _vp, _i64, _vp, _vp, _i64, _i64]),
@@ -180,6 +181,12 @@ class Context:
                stream=None) -> None:
         check("ugb_matvec", lib().ugb_matvec(self.handle, _stream(stream), kind, _ptr(w), rb,
                                                _ptr(xq), _ptr(y), k, m, batch))
+
+    def matvec_f32(self, kind: int, w, rb: int, x, xq_scratch, y, k: int, m: int, batch: int = 1,
+                   stream=None) -> None:
+        """quant_q8_1 + matvec as one call (fused into the matvec for batch-1 staged shapes)."""
+        check("ugb_matvec_f32", lib().ugb_matvec_f32(self.handle, _stream(stream), kind, _ptr(w), rb,
+                                                       _ptr(x), _ptr(xq_scratch), _ptr(y), k, m, batch))
 
     def matvec_multi(self, kind: int, ws, rows, rb: int, xq, y, k: int, batch: int = 1,
                      stream=None) -> None:

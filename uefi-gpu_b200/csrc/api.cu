@@ -206,6 +206,33 @@ ugb_status ugb_matvec(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
   return launch_matvec(ctx, stream, a);
 }
 
+ugb_status ugb_matvec_f32(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
+                          int64_t row_bytes, const float *x_dev, void *xq_scratch, float *y_dev,
+                          int64_t k, int64_t m, int64_t batch) {
+  ugb_status st = check_ctx(ctx);
+  if (st != UGB_OK) return st;
+  st = check_weights(kind, w_dev, row_bytes, k, m);
+  if (st != UGB_OK) return st;
+  if (batch <= 0 || batch > UGB_MAX_BATCH) return UGB_ESHAPE;
+  if (!x_dev || (reinterpret_cast<uintptr_t>(x_dev) & 3) || !aligned16(xq_scratch) || !y_dev ||
+      (reinterpret_cast<uintptr_t>(y_dev) & 3))
+    return UGB_EALIGN;
+  MatvecArgs a;
+  a.kind = kind;
+  a.w = static_cast<const uint8_t *>(w_dev);
+  a.row_bytes = row_bytes;
+  a.k = k;
+  a.m = m;
+  a.xf = x_dev;
+  a.xq = static_cast<const uint8_t *>(xq_scratch);
+  a.xl = q8act_layout(k, batch);
+  a.y = y_dev;
+  a.ldy = m;
+  a.batch = batch;
+  a.pdl = ctx->pdl;
+  return launch_matvec(ctx, stream, a);
+}
+
 ugb_status ugb_matvec_multi(ugb_ctx *ctx, ugb_stream stream, uint32_t kind,
                             const void *const *w_devs, const int64_t *rows, int count,
                             int64_t row_bytes, const void *xq_dev, float *y_dev, int64_t k,
@@ -358,14 +385,13 @@ ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
   std::memcpy(ctx->pinned, x_host, static_cast<size_t>(k) * 4);
   if (cudaMemcpyAsync(x_dev, ctx->pinned, k * 4, cudaMemcpyHostToDevice, stream) != cudaSuccess)
     return UGB_EBACKEND;
-  st = launch_quant_q8_1(ctx, stream, x_dev, xq, k, 1, false);
-  if (st != UGB_OK) return st;
-  MatvecArgs a;
+  MatvecArgs a;  // quant_act fused into the matvec where it runs as a burst (else xq first)
   a.kind = kind;
   a.w = static_cast<const uint8_t *>(w_dev);
   a.row_bytes = row_bytes;
   a.k = k;
   a.m = m;
+  a.xf = x_dev;
   a.xq = xq;
   a.xl = xl;
   a.y = y_dev;

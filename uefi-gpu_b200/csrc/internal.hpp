@@ -46,6 +46,10 @@ struct MatvecArgs {
   int64_t row_bytes = 0, k = 0, m = 0;
   const uint8_t *xq = nullptr;   // Q8_1 buffer
   Q8Act xl;                      // its layout
+  // fp32 activation ([batch][k]) to quantise first, or null.  A batch-1 burst launch quantises
+  // it itself (every CTA, into shared memory); otherwise it is quantised into xq (then a
+  // scratch buffer of layout xl) by a launch of its own.
+  const float *xf = nullptr;
   float *y = nullptr;            // [batch][ldy]
   int64_t ldy = 0;
   int64_t batch = 1;

@@ -74,6 +74,7 @@ struct MvParams {
   const uint8_t *xq;          // Q8_1 buffer: quants [nb][k], scales / sums [nb][nbp]
   const float *xd;
   const int *xs;
+  const float *xf;            // burst launches only: fp32 activation quantised by every CTA
   int nbp;
   float *y;
   int64_t ldy;
@@ -289,6 +290,8 @@ __device__ __forceinline__ bool prologue(const MvParams &p, const View &v, uint3
   const uint32_t ring = base + p.ring;
   constexpr bool kSum = Fmt<KIND>::kNeedsSum;
   const uint32_t xq_bytes = static_cast<uint32_t>(p.k), xd_bytes = static_cast<uint32_t>(p.nbp) * 4;
+  const int pre = min(T, p.stages);
+  grid_dep_launch();  // the next kernel may become resident beside this one and start its own copies
   if (tid == 0) {
     for (int s = 0; s < p.stages; ++s) {
       mbar_init(full + 8 * s, 1);
@@ -296,16 +299,16 @@ __device__ __forceinline__ bool prologue(const MvParams &p, const View &v, uint3
     }
     mbar_init(xbar, 1);
     fence_mbar_init();
+    // Weights do not depend on earlier kernels: the first stages are requested before anything
+    // else, and before the programmatic dependency resolves.  The copy engine takes them one
+    // after another, so the sooner the first is issued, the sooner HBM is busy.
+    const uint64_t pol_w = policy_evict_first();
+    for (int t = 0; t < pre; ++t) issue_item<KIND>(p, v, t, ring + t * p.stage_bytes, full + 8 * t, pol_w);
   }
   __syncthreads();
-  grid_dep_launch();
   if (warp == kWarps) {
     if (lane == 0) {
-      // Weights do not depend on earlier kernels: request the first stages before the
-      // programmatic dependency resolves, then stage the activation once for the CTA.
-      const uint64_t pol_w = policy_evict_first();
-      const int pre = min(T, p.stages);
-      for (int t = 0; t < pre; ++t) issue_item<KIND>(p, v, t, ring + t * p.stage_bytes, full + 8 * t, pol_w);
+      // then the activation, once for the CTA, and the items that wait for a free stage
       grid_dep_wait();
       mbar_arrive_expect_tx(xbar, NB * (xq_bytes + xd_bytes * (kSum ? 2u : 1u)));
       const uint64_t pol_x = policy_evict_last();
@@ -314,6 +317,7 @@ __device__ __forceinline__ bool prologue(const MvParams &p, const View &v, uint3
         bulk_g2s(base + p.x_d + b * xd_bytes, v.xd + static_cast<int64_t>(b) * p.nbp, xd_bytes, xbar, pol_x);
         if (kSum) bulk_g2s(base + p.x_s + b * xd_bytes, v.xs + static_cast<int64_t>(b) * p.nbp, xd_bytes, xbar, pol_x);
       }
+      const uint64_t pol_w = policy_evict_first();
       for (int t = pre; t < T; ++t) {
         const int s = t % p.stages;
         if (!mbar_wait_bounded(empty + 8 * s, ((t / p.stages) - 1) & 1)) {
@@ -326,6 +330,66 @@ __device__ __forceinline__ bool prologue(const MvParams &p, const View &v, uint3
     return false;
   }
   grid_dep_wait();  // consumers read the activation and write y only after the dependency
+  ok = __all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0));
+  if (!ok && lane == 0) status_or(p.status, ST_TIMEOUT);
+  return true;
+}
+
+// Prologue of a burst launch (no producer warp): every item of the CTA has a stage of its own,
+// so all weight copies go out at once, first thing, and nothing is ever released.  Thread 0
+// requests the weights while thread 32 waits for the dependency and stages the activation.
+template <int KIND>
+__device__ __forceinline__ bool prologue_burst(const MvParams &p, const View &v, uint32_t base, int T, bool &ok) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  const uint32_t full = base, xbar = base + 128;
+  constexpr bool kSum = Fmt<KIND>::kNeedsSum;
+  grid_dep_launch();  // the next kernel may become resident beside this one and start its copies
+  if (tid == 0) {
+    for (int t = 0; t < T; ++t) mbar_init(full + 8 * t, 1);
+    mbar_init(xbar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const uint64_t pol_w = policy_evict_first();
+    for (int t = 0; t < T; ++t) issue_item<KIND>(p, v, t, base + p.ring + t * p.stage_bytes, full + 8 * t, pol_w);
+  } else if (tid == 32 && p.xf == nullptr) {
+    const uint32_t xq_bytes = static_cast<uint32_t>(p.k), xd_bytes = static_cast<uint32_t>(p.nbp) * 4;
+    grid_dep_wait();
+    mbar_arrive_expect_tx(xbar, xq_bytes + xd_bytes * (kSum ? 2u : 1u));
+    const uint64_t pol_x = policy_evict_last();
+    bulk_g2s(base + p.x_q, v.xq, xq_bytes, xbar, pol_x);
+    bulk_g2s(base + p.x_d, v.xd, xd_bytes, xbar, pol_x);
+    if (kSum) bulk_g2s(base + p.x_s, v.xs, xd_bytes, xbar, pol_x);
+  }
+  grid_dep_wait();  // the activation is read and y written only after the dependency
+  if (p.xf != nullptr) {
+    // The fp32 activation, quantised into shared memory by every CTA: quant_q8_1_kernel's
+    // arithmetic bit for bit (glue.cuh), four blocks per warp at a time, loads first.
+    constexpr int kQB = 4;
+    const int warp = tid >> 5, nb = p.k / 32;
+    uint8_t *smem = reinterpret_cast<uint8_t *>(__cvta_shared_to_generic(base));
+    int8_t *q = reinterpret_cast<int8_t *>(smem + p.x_q);
+    float *d = reinterpret_cast<float *>(smem + p.x_d);
+    int32_t *sm = reinterpret_cast<int32_t *>(smem + p.x_s);
+    bool bad = false;
+    for (int b0 = warp; b0 < nb; b0 += kWarps * kQB) {
+      float xv[kQB];
+      int bb[kQB];
+      bool live[kQB];
+#pragma unroll
+      for (int i = 0; i < kQB; ++i) {
+        bb[i] = b0 + i * kWarps;
+        live[i] = bb[i] < nb;
+        xv[i] = p.xf[static_cast<int64_t>(live[i] ? bb[i] : b0) * 32 + lane];
+      }
+      bad |= quant_blocks<kQB>(xv, bb, live, lane, q, d, sm);
+    }
+    if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
+    __syncthreads();
+    ok = true;
+    return true;
+  }
   ok = __all_sync(0xffffffffu, mbar_wait_bounded(xbar, 0));
   if (!ok && lane == 0) status_or(p.status, ST_TIMEOUT);
   return true;
@@ -347,8 +411,11 @@ __device__ __forceinline__ void release_stage(uint32_t empty, int s, int lane) {
 }
 
 // Batch-1, whole-row consumer (see the file comment).  RW rows per warp, 8 * RW per item.
-template <int KIND, int RW, int J, class P>
-__global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const P p) {
+// BURST: the launch gives every item of a CTA its own stage (one CTA per SM, about half its
+// shared memory and registers), so there is no producer warp and no stage reuse, and the next
+// kernel in the stream fits beside this one and streams its own weights meanwhile.
+template <int KIND, int RW, int J, class P, bool BURST>
+__global__ void __launch_bounds__(BURST ? kWarps * 32 : kThreads, BURST ? 2 : 1) mv_rows_kernel(const P p) {
   static_assert(J % 2 == 0 && J <= kSlots, "slots are processed in pairs");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -360,7 +427,11 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const P p) {
   if (v.skip) return;  // nothing staged or issued yet
   const int T = items_of(p, v);
   bool ok = true;
-  if (!prologue<KIND, 1>(p, v, base, T, ok)) return;
+  if constexpr (BURST) {
+    prologue_burst<KIND>(p, v, base, T, ok);
+  } else {
+    if (!prologue<KIND, 1>(p, v, base, T, ok)) return;
+  }
 
   // Slot j of this lane is flat index f = lane + 32 j of the warp's RW x U (row, unit) space.
   // Its row offset inside an item, its unit and its activation unit are fixed for the kernel.
@@ -382,15 +453,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const P p) {
                Fmt<KIND>::kNeedsSum, xr[j]);
   }
 
-  for (int t = 0; ok && t < T; ++t) {
-    const int s = t % p.stages;
-    ok = wait_stage(p, full, t, lane);
-    if (!ok) break;
-    const Item it = item_of(p, v, t);
-    // The item's rows are one span fetched from floor16(first row).
-    const uint32_t stage = ring + s * p.stage_bytes +
-        static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, v, it.r0)) & 15);
-    float acc[J];
+  // The slot dots of one item (staged at `stage`) and the row totals of an item's group.
+  auto item_acc = [&](uint32_t stage, float (&acc)[J]) {
 #pragma unroll
     for (int j = 0; j < J; j += 2) {
       acc[j] = acc[j + 1] = 0.f;
@@ -404,7 +468,8 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const P p) {
         acc[j + 1] = unit_term<KIND>(wb, xr[j + 1], ib);
       }
     }
-    release_stage(empty, s, lane);
+  };
+  auto item_out = [&](const Item &it, const float (&acc)[J], bool live) {
     float rs[RW];
 #pragma unroll
     for (int r = 0; r < RW; ++r) {
@@ -413,12 +478,45 @@ __global__ void __launch_bounds__(kThreads, 1) mv_rows_kernel(const P p) {
       for (int j = 0; j < J; ++j) rs[r] += srow[j] == r ? acc[j] : 0.f;
     }
     float tot;
-    if (reduce_rows<RW>(rs, lane, tot)) {
+    if (reduce_rows<RW>(rs, lane, tot) && live) {
       const int rr = warp * RW + lane / (32 / RW);
       if (rr < it.nrows) {
         v.y[it.r0 + rr] = tot;
         if (!isfinite(tot)) status_or(p.status, ST_NONFINITE_OUT);
       }
+    }
+  };
+  // The item's rows are one span fetched from floor16(first row).
+  auto stage_of = [&](int t, const Item &it) {
+    return ring + (t % p.stages) * p.stage_bytes +
+           static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row_ptr(p, v, it.r0)) & 15);
+  };
+
+  if constexpr (BURST) {
+    // Items two at a time: every item is already requested, and the two groups' dependency
+    // chains (shared-memory loads, dp4a, the shuffle tree) interleave.  With an odd count the
+    // last pair repeats its first item and drops the copy.
+    for (int t = 0; ok && t < T; t += 2) {
+      const bool two = t + 1 < T;
+      const int t1 = two ? t + 1 : t;
+      ok = wait_stage(p, full, t, lane) && wait_stage(p, full, t1, lane);
+      if (!ok) break;
+      const Item i0 = item_of(p, v, t), i1 = item_of(p, v, t1);
+      float a0[J], a1[J];
+      item_acc(stage_of(t, i0), a0);
+      item_acc(stage_of(t1, i1), a1);
+      item_out(i0, a0, true);
+      item_out(i1, a1, two);
+    }
+  } else {
+    for (int t = 0; ok && t < T; ++t) {
+      ok = wait_stage(p, full, t, lane);
+      if (!ok) break;
+      const Item it = item_of(p, v, t);
+      float acc[J];
+      item_acc(stage_of(t, it), acc);
+      release_stage(empty, t % p.stages, lane);
+      item_out(it, acc, true);
     }
   }
 }
@@ -609,6 +707,8 @@ size_t x_bytes(uint32_t kind, int64_t k, int nb) {
 
 struct Plan {
   bool rows_kernel = false;   // mv_rows_kernel
+  bool burst = false;         // its burst form (every item of a CTA staged at once)
+  int burst_stages = 0;       // items per CTA when the rows kernel can run as a burst (0: cannot)
   bool split = false;         // mv_split_kernel (neither: mv_stream_kernel)
   int rw = 1, slots = 2;      // rows per warp (rows kernel) or per item (split kernel), and
                               // register slots per lane
@@ -617,7 +717,7 @@ struct Plan {
   size_t smem = 0;
 };
 
-Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t smem_optin) {
+Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t smem_optin, int sm_count) {
   Plan pl;
   const uint64_t rb = elems_to_bytes(kind, static_cast<uint64_t>(k));
   const int64_t units = k / 32;
@@ -666,8 +766,8 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
   off += static_cast<uint32_t>(round_up(static_cast<uint64_t>(nb) * k, 16));
   pl.x_d = off;
   off += static_cast<uint32_t>(nb * nbp * 4);
-  pl.x_s = off;
-  if (kind == UGB_Q4_K) off += static_cast<uint32_t>(nb * nbp * 4);
+  pl.x_s = off;  // sums: read by Q4_K only, but always allocated (the fused quantiser writes them)
+  off += static_cast<uint32_t>(nb * nbp * 4);
   pl.red = static_cast<uint32_t>(round_up(off, 16));
   off = pl.red + 2 * kWarps * 4 * 4;
   pl.ring = static_cast<uint32_t>(round_up(off, 128));
@@ -681,12 +781,22 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
   while (stages > 2 && pl.ring + static_cast<size_t>(stages) * pl.stage_bytes > smem_optin) --stages;
   pl.stages = stages;
   pl.smem = pl.ring + static_cast<size_t>(stages) * pl.stage_bytes;
+  // The burst form: one CTA per SM holding all of its whole-row items at once, within
+  // kSmPerKernel so the next kernel fits beside it.
+  if (pl.rows_kernel && pl.nch == 1) {
+    const int64_t per_cta = (pl.ngroups + sm_count - 1) / sm_count;
+    if (per_cta <= kMaxStages && pl.ring + static_cast<size_t>(per_cta) * pl.stage_bytes <= kSmPerKernel)
+      pl.burst_stages = static_cast<int>(per_cta);
+  }
   return pl;
 }
 
 template <int KIND, class P>
-const void *rows_kernel_ptr(int rw, int slots) {
-#define UGB_RK(RW, J) if (rw == RW && slots == J) return reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J, P>);
+const void *rows_kernel_ptr(int rw, int slots, bool burst) {
+#define UGB_RK(RW, J)                                                                                 \
+  if (rw == RW && slots == J)                                                                         \
+    return burst ? reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J, P, true>)              \
+                 : reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J, P, false>);
   UGB_RK(1, 2) UGB_RK(1, 4)
   UGB_RK(2, 2) UGB_RK(2, 4)
   UGB_RK(4, 2) UGB_RK(4, 4)
@@ -718,7 +828,7 @@ const void *stream_kernel_ptr(int nb, bool dots) {
 
 template <int KIND, class P>
 const void *select_for(const Plan &pl, int nb, bool dots) {
-  return pl.rows_kernel ? rows_kernel_ptr<KIND, P>(pl.rw, pl.slots)
+  return pl.rows_kernel ? rows_kernel_ptr<KIND, P>(pl.rw, pl.slots, pl.burst)
          : pl.split     ? split_kernel_ptr<KIND, P>(pl.rw, pl.slots)
                         : stream_kernel_ptr<KIND, P>(nb, dots);
 }
@@ -751,6 +861,9 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
         for (bool table : {false, true}) {
           pl.rows_kernel = true;
           pl.split = false;
+          pl.burst = true;
+          if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+          pl.burst = false;
           if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
           pl.rows_kernel = false;
           pl.split = true;
@@ -788,6 +901,18 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
   }
   const bool dots = a.dots != nullptr;
   if (dots && mode != kSegments) return UGB_ESHAPE;
+  if (a.xf) {
+    // Quantise inside the matvec when it runs as one batch-1 burst, else as a launch of its own.
+    const Plan pl = make_plan(a.kind, a.k, a.m, 1, dots, ctx->smem_optin, ctx->sm_count);
+    const bool fused = mode == kSegments && a.nseg <= 1 && a.batch == 1 && !dots && pl.burst_stages > 0;
+    if (!fused) {
+      const ugb_status st = launch_quant_q8_1(ctx, stream, a.xf, const_cast<uint8_t *>(a.xq), a.k, a.batch, a.pdl);
+      if (st != UGB_OK) return st;
+      MatvecArgs b = a;
+      b.xf = nullptr;
+      return launch_matvec(ctx, stream, b);
+    }
+  }
   // A batch runs as launches of 8, 4, 2 or 1 vectors (largest first) whose staged
   // activations fit kXBudget; each launch streams the weights once.
   int64_t done = 0;
@@ -795,12 +920,20 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     const int64_t rest = a.batch - done;
     int nb = dots ? 1 : (rest >= 8 ? 8 : rest >= 4 ? 4 : rest >= 2 ? 2 : 1);
     while (nb > 1 && x_bytes(a.kind, a.k, nb) > kXBudget) nb /= 2;
-    const Plan pl = make_plan(a.kind, a.k, a.m, nb, dots, ctx->smem_optin);
+    Plan pl = make_plan(a.kind, a.k, a.m, nb, dots, ctx->smem_optin, ctx->sm_count);
+    if (mode == kSegments && pl.burst_stages > 0) {
+      // every CTA's items staged at once: grid = min(groups, SMs), at most burst_stages each
+      pl.burst = true;
+      pl.stages = pl.burst_stages;
+      pl.ctas_per_sm = 1;
+      pl.smem = pl.ring + static_cast<size_t>(pl.stages) * pl.stage_bytes;
+    }
     if (pl.smem > ctx->smem_optin) return UGB_ESHAPE;
     const void *f = select_kernel(a.kind, pl, nb, dots, mode == kTable);
     if (!f) return UGB_EQUANT;
+    const int threads = pl.burst ? kWarps * 32 : kThreads;
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, kThreads, pl.smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, f, threads, pl.smem) != cudaSuccess ||
         per_sm < 1)
       return UGB_EBACKEND;
     per_sm = std::min(per_sm, pl.ctas_per_sm);
@@ -855,6 +988,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
     p.xq = a.xq + done * a.xl.k;
     p.xd = reinterpret_cast<const float *>(a.xq + a.xl.d_off) + done * a.xl.nbp;
     p.xs = reinterpret_cast<const int *>(a.xq + a.xl.s_off) + done * a.xl.nbp;
+    p.xf = a.xf;  // only ever set for a batch-1 burst (checked above)
     p.nbp = static_cast<int>(a.xl.nbp);
     p.y = a.y ? a.y + done * a.ldy : nullptr;
     p.ldy = a.ldy;
@@ -903,7 +1037,7 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
 
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);  // 8 consumer warps + 1 producer warp
+    cfg.blockDim = dim3(threads);  // 8 consumer warps (+ 1 producer warp unless a burst)
     cfg.dynamicSmemBytes = pl.smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
