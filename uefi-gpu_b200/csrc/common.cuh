@@ -80,6 +80,11 @@ __device__ __forceinline__ void mbar_arrive_relaxed(uint32_t bar) {
   asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// n arrivals at once (n >= 1).
+__device__ __forceinline__ void mbar_arrive_relaxed_n(uint32_t bar, uint32_t n) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(n) : "memory");
+}
+
 // Test a phase; if it has not completed, the thread is suspended in hardware until it
 // completes or about kSuspendNs pass, so waiting warps do not spin on issue slots.
 constexpr uint32_t kSuspendNs = 1000000;

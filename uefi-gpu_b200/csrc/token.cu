@@ -206,41 +206,45 @@ __device__ void make_plan(const TokenStep &p, TokPlan &pl) {
   make_span(pl.sp[kSpanHead], r0, r1 - r0, p.rb_h, r0);
 }
 
-template <class F>
-__device__ __forceinline__ void visit_span(const Span &s, const uint8_t *w, uint32_t rb, F &f) {
-  int a = 0;
-  for (int i = 0; i < s.ni; ++i) {
-    const int nr = s.per + (i < s.rem ? 1 : 0);
-    f(w + static_cast<uint64_t>(s.first + a) * rb, static_cast<uint32_t>(nr) * rb, s.out0 + a, nr);
-    a += nr;
+// Spans [s0, s1] of matrix `slot`, and the matrix and row bytes of span `sp`.
+__device__ __forceinline__ void slot_spans(int slot, int &s0, int &s1) {
+  s0 = slot == kSlotQKV ? kSpanQ : slot + (kSpanO - kSlotO);
+  s1 = slot == kSlotQKV ? kSpanV : s0;
+}
+__device__ __forceinline__ const uint8_t *span_matrix(const TokenStep &p, const TokLayer &L, int sp) {
+  switch (sp) {
+    case kSpanQ: return L.wq;
+    case kSpanK: return L.wk;
+    case kSpanV: return L.wv;
+    case kSpanO: return L.wo;
+    case kSpanGate: return L.wg;
+    case kSpanUp: return L.wu;
+    case kSpanDown: return L.wd;
+    default: return p.head;
   }
+}
+__device__ __forceinline__ uint32_t span_rb(const TokenStep &p, int sp) {
+  return sp == kSpanO ? p.rb_q : sp == kSpanDown ? p.rb_f : sp == kSpanHead ? p.rb_h : p.rb_e;
 }
 
 // The items of matrix `slot` (of layer L) that this CTA streams, in stream order:
-// f(src, bytes, first output row, rows).
+// f(src, bytes, first output row, rows).  f has a single call site, so a caller's item body is
+// inlined once (the consumers' row-dot loops are the bulk of the kernel's code, and the code
+// a layer runs has to stay small enough for the instruction caches).
 template <class F>
 __device__ void visit(const TokenStep &p, const TokPlan &pl, const TokLayer &L, int slot, F &&f) {
-  switch (slot) {
-    case kSlotQKV:
-      visit_span(pl.sp[kSpanQ], L.wq, p.rb_e, f);
-      visit_span(pl.sp[kSpanK], L.wk, p.rb_e, f);
-      visit_span(pl.sp[kSpanV], L.wv, p.rb_e, f);
-      break;
-    case kSlotO:
-      visit_span(pl.sp[kSpanO], L.wo, p.rb_q, f);
-      break;
-    case kSlotGate:
-      visit_span(pl.sp[kSpanGate], L.wg, p.rb_e, f);
-      break;
-    case kSlotUp:
-      visit_span(pl.sp[kSpanUp], L.wu, p.rb_e, f);
-      break;
-    case kSlotDown:
-      visit_span(pl.sp[kSpanDown], L.wd, p.rb_f, f);
-      break;
-    default:
-      visit_span(pl.sp[kSpanHead], p.head, p.rb_h, f);
-      break;
+  int s0, s1;
+  slot_spans(slot, s0, s1);
+  for (int sp = s0; sp <= s1; ++sp) {
+    const Span &s = pl.sp[sp];
+    const uint8_t *w = span_matrix(p, L, sp);
+    const uint32_t rb = span_rb(p, sp);
+    int a = 0;
+    for (int i = 0; i < s.ni; ++i) {
+      const int nr = s.per + (i < s.rem ? 1 : 0);
+      f(w + static_cast<uint64_t>(s.first + a) * rb, static_cast<uint32_t>(nr) * rb, s.out0 + a, nr);
+      a += nr;
+    }
   }
 }
 
@@ -325,7 +329,7 @@ __device__ uint32_t produce(const TokenStep &p, uint32_t base, const TokPlan &pl
 // Either way an item's row groups are dealt round-robin over the warps, continuing from the
 // previous items of the matrix, so consecutive items are worked on by different warps at once.
 struct Slots {
-  int U, rw;
+  int U, rw, rwl;  // units per row, rows per group and its log2
   bool longrows;
   uint32_t off[kJ];  // byte offset of the slot's row inside a group
   int row[kJ];       // row of the slot inside a group (kNoRow: slot unused)
@@ -339,6 +343,7 @@ __device__ __forceinline__ void make_slots(const TokenStep &p, uint32_t base, in
   s.U = k / 32;
   s.longrows = s.U > 32 * kJ;
   s.rw = s.U <= 8 * kJ ? 4 : (s.U <= 16 * kJ ? 2 : 1);
+  s.rwl = s.rw == 4 ? 2 : s.rw == 2 ? 1 : 0;
   const int total = s.longrows ? 0 : s.rw * s.U;
 #pragma unroll
   for (int j = 0; j < kJ; ++j) {
@@ -423,27 +428,28 @@ __device__ bool consume(const TokenStep &p, uint32_t base, Cursor &cur, const To
     const uint32_t t = cur.t - 1;
     const uint32_t item = ring + off;
     const int group0 = groups;
-    const int ng = (nrows + s.rw - 1) / s.rw;
+    const int ng = (nrows + s.rw - 1) >> s.rwl;  // row groups of the item
     groups += ng;
-    const int first = (warp - group0 % kCW + kCW) % kCW;  // this warp's first group in the item
-    // Every warp waits for every item, even one it has no group of: a warp's arrival on the
-    // item's empty barrier must not overtake the previous use of that barrier slot (the
-    // producer reuses a slot only after seeing its previous item released).
+    const int first = (warp - group0) & (kCW - 1);  // this warp's first group in the item
+    // A warp with no group of the item neither waits for it nor releases it: the warp holding
+    // the item's group 0 releases it for them as well.  Every release follows a wait on the
+    // item, so none can overtake the previous use of the barrier slot (the producer reuses a
+    // slot only after seeing its previous item released).
+    if (first >= ng) return;
     ok = __all_sync(0xffffffffu, mbar_wait_step(p, full + 8 * (t % kNS), (t / kNS) & 1));
     if (!ok) return;
-    if (first < ng) {
-      if (s.longrows) {
-        warp_rows_long<KIND>(p, base, item, nrows, rb, s.U, row0, first, out);
-      } else if (s.rw == 4) {
-        warp_rows<KIND, 4>(item, nrows, rb, s, row0, first, out);
-      } else if (s.rw == 2) {
-        warp_rows<KIND, 2>(item, nrows, rb, s, row0, first, out);
-      } else {
-        warp_rows<KIND, 1>(item, nrows, rb, s, row0, first, out);
-      }
+    if (s.longrows) {
+      warp_rows_long<KIND>(p, base, item, nrows, rb, s.U, row0, first, out);
+    } else if (s.rw == 4) {
+      warp_rows<KIND, 4>(item, nrows, rb, s, row0, first, out);
+    } else if (s.rw == 2) {
+      warp_rows<KIND, 2>(item, nrows, rb, s, row0, first, out);
+    } else {
+      warp_rows<KIND, 1>(item, nrows, rb, s, row0, first, out);
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive_relaxed(empty + 8 * (t % kNS));
+    if (lane == 0)
+      mbar_arrive_relaxed_n(empty + 8 * (t % kNS), first == 0 ? static_cast<uint32_t>(kCW - min(ng, kCW) + 1) : 1u);
   });
   return ok;
 }
