@@ -416,7 +416,7 @@ __device__ __forceinline__ void release_stage(uint32_t empty, int s, int lane) {
 // kernel in the stream fits beside this one and streams its own weights meanwhile.
 template <int KIND, int RW, int J, class P, bool BURST>
 __global__ void __launch_bounds__(BURST ? kWarps * 32 : kThreads, BURST ? 2 : 1) mv_rows_kernel(const P p) {
-  static_assert(J % 2 == 0 && J <= kSlots, "slots are processed in pairs");
+  static_assert(J >= 2 && J <= kSlots, "2 to kSlots register slots");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = smem_u32(smem);
@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(BURST ? kWarps * 32 : kThreads, BURST ? 2 : 1)
   // The slot dots of one item (staged at `stage`) and the row totals of an item's group.
   auto item_acc = [&](uint32_t stage, float (&acc)[J]) {
 #pragma unroll
-    for (int j = 0; j < J; j += 2) {
+    for (int j = 0; j + 1 < J; j += 2) {
       acc[j] = acc[j + 1] = 0.f;
       if (j * 32 < total) {  // warp-uniform
         WUnit wa, wb;
@@ -466,6 +466,15 @@ __global__ void __launch_bounds__(BURST ? kWarps * 32 : kThreads, BURST ? 2 : 1)
         const int ib = unit_isum<KIND>(wb, xr[j + 1]);
         acc[j] = unit_term<KIND>(wa, xr[j], ia);
         acc[j + 1] = unit_term<KIND>(wb, xr[j + 1], ib);
+      }
+    }
+    if constexpr (J % 2 == 1) {  // odd slot count: the last slot alone
+      constexpr int j = J - 1;
+      acc[j] = 0.f;
+      if (j * 32 < total) {
+        WUnit wa;
+        load_wunit<KIND>(stage + srow_off[j], sunit[j], wa);
+        acc[j] = unit_term<KIND>(wa, xr[j], unit_isum<KIND>(wa, xr[j]));
       }
     }
   };
@@ -729,7 +738,7 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
       if (rb * kWarps * rw <= kItemTarget && slots <= kSlots) {
         pl.rows_kernel = true;
         pl.rw = rw;
-        pl.slots = slots <= 2 ? 2 : 4;
+        pl.slots = slots <= 2 ? 2 : static_cast<int>(slots);  // 2, 3 or 4
         break;
       }
     }
@@ -797,9 +806,9 @@ const void *rows_kernel_ptr(int rw, int slots, bool burst) {
   if (rw == RW && slots == J)                                                                         \
     return burst ? reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J, P, true>)              \
                  : reinterpret_cast<const void *>(&mv_rows_kernel<KIND, RW, J, P, false>);
-  UGB_RK(1, 2) UGB_RK(1, 4)
-  UGB_RK(2, 2) UGB_RK(2, 4)
-  UGB_RK(4, 2) UGB_RK(4, 4)
+  UGB_RK(1, 2) UGB_RK(1, 3) UGB_RK(1, 4)
+  UGB_RK(2, 2) UGB_RK(2, 3) UGB_RK(2, 4)
+  UGB_RK(4, 2) UGB_RK(4, 3) UGB_RK(4, 4)
 #undef UGB_RK
   return nullptr;
 }
@@ -854,7 +863,7 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
   for (uint32_t kind : {UGB_Q8_0, UGB_Q4_K, UGB_Q3_K}) {
     Plan pl;
     for (int rw : {1, 2, 4})
-      for (int j : {2, 4}) {
+      for (int j : {2, 3, 4}) {
         pl.rows_kernel = true;
         pl.rw = rw;
         pl.slots = j;
@@ -865,6 +874,7 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
           if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
           pl.burst = false;
           if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+          if (j == 3) continue;  // the split kernel takes 2 or 4 slots
           pl.rows_kernel = false;
           pl.split = true;
           if (allow_smem(select_kernel(kind, pl, 1, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
