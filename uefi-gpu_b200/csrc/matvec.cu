@@ -623,10 +623,13 @@ __global__ void __launch_bounds__(kThreads, 1) mv_split_kernel(const P p) {
 }
 
 // General consumer: NB activation vectors, rows of any length (K chunks), or int-dot dumps
-// (DOTS).  One warp per row, 8 rows per item; lane l takes 32-element units l, l+32, ... of
-// the chunk with the activation read from shared memory.
-template <int KIND, int NB, bool DOTS, class P>
+// (DOTS).  Warp w owns rows w * RW .. w * RW + RW - 1 of every item (8 * RW rows per item);
+// lane l takes 32-element units l, l+32, ... of the chunk.  The NB activation units of a unit
+// are read from shared memory once and serve all RW rows: with batches those reads, not the
+// weights, are what the shared-memory bandwidth goes to.
+template <int KIND, int NB, bool DOTS, class P, int RW>
 __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
+  static_assert(!DOTS || (NB == 1 && RW == 1), "block dots are dumped one row per warp");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t base = smem_u32(smem);
@@ -641,9 +644,11 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
   constexpr bool kSum = Fmt<KIND>::kNeedsSum;
   const uint32_t xq_bytes = static_cast<uint32_t>(p.k), xd_bytes = static_cast<uint32_t>(p.nbp) * 4;
 
-  float acc[NB];
+  float acc[RW][NB];
 #pragma unroll
-  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+  for (int r = 0; r < RW; ++r)
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[r][b] = 0.f;
 
   for (int t = 0; ok && t < T; ++t) {
     const int s = t % p.stages;
@@ -652,17 +657,20 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
     const uint32_t stage = ring + s * p.stage_bytes;
     const Item it = item_of(p, v, t);
     const int k0 = it.c * p.kc;
-    if (warp < it.nrows) {
+    if (warp * RW < it.nrows) {
       const int nunits = min(p.kc, p.k - k0) / 32;
       const uint64_t seg_off = bytes_of<KIND>(static_cast<uint64_t>(k0));
       const uint8_t *row0 = row_ptr(p, v, it.r0);
-      const uint8_t *row = row0 + static_cast<uint64_t>(warp) * p.row_bytes + seg_off;
-      uint32_t seg;
-      if (p.nch == 1) {
-        const uint8_t *first = floor16(row0);
-        seg = stage + static_cast<uint32_t>(row - first);
-      } else {
-        seg = stage + warp * p.seg_stride + static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row) & 15);
+      uint32_t seg[RW];
+#pragma unroll
+      for (int r = 0; r < RW; ++r) {
+        const int rr = warp * RW + r;
+        const uint8_t *row = row0 + static_cast<uint64_t>(rr) * p.row_bytes + seg_off;
+        if (p.nch == 1) {
+          seg[r] = stage + static_cast<uint32_t>(row - floor16(row0));
+        } else {
+          seg[r] = stage + rr * p.seg_stride + static_cast<uint32_t>(reinterpret_cast<uintptr_t>(row) & 15);
+        }
       }
       for (int u = lane; u < nunits; u += 32) {
         const int ug = k0 / 32 + u;  // unit index within the whole row
@@ -671,15 +679,20 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
         for (int b = 0; b < NB; ++b)
           load_xunit(base + p.x_q + b * xq_bytes + 32 * ug, base + p.x_d + b * xd_bytes + 4 * ug,
                      base + p.x_s + b * xd_bytes + 4 * ug, kSum, x[b]);
-        WUnit wu;
-        load_wunit<KIND>(seg, u, wu);
 #pragma unroll
-        for (int b = 0; b < NB; ++b) {
-          const int isum = unit_isum<KIND>(wu, x[b]);
-          if constexpr (DOTS) {
-            p.dots[static_cast<int64_t>(it.r0 + warp) * (p.k / 32) + ug] = isum;
-          } else {
-            acc[b] += unit_term<KIND>(wu, x[b], isum);
+        for (int r = 0; r < RW; ++r) {
+          if (warp * RW + r < it.nrows) {  // warp-uniform
+            WUnit wu;
+            load_wunit<KIND>(seg[r], u, wu);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+              const int isum = unit_isum<KIND>(wu, x[b]);
+              if constexpr (DOTS) {
+                p.dots[static_cast<int64_t>(it.r0 + warp) * (p.k / 32) + ug] = isum;
+              } else {
+                acc[r][b] += unit_term<KIND>(wu, x[b], isum);
+              }
+            }
           }
         }
       }
@@ -687,12 +700,16 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
     release_stage(empty, s, lane);
     if (!DOTS && it.c == p.nch - 1) {
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        const float val = warp_sum(acc[b]);
-        acc[b] = 0.f;
-        if (lane == 0 && warp < it.nrows) {
-          v.y[b * v.ldy + it.r0 + warp] = val;
-          if (!isfinite(val)) status_or(p.status, ST_NONFINITE_OUT);
+      for (int r = 0; r < RW; ++r) {
+        const int rr = warp * RW + r;
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          const float val = warp_sum(acc[r][b]);
+          acc[r][b] = 0.f;
+          if (lane == 0 && rr < it.nrows) {
+            v.y[b * v.ldy + it.r0 + rr] = val;
+            if (!isfinite(val)) status_or(p.status, ST_NONFINITE_OUT);
+          }
         }
       }
     }
@@ -753,6 +770,12 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
         pl.slots = slots <= 2 ? 2 : 4;
       }
     }
+  }
+  if (!pl.rows_kernel && !pl.split && !dots && nb > 1) {
+    // Batches: two rows per warp share each activation unit read from shared memory, when
+    // that still leaves a row group for every SM (four ran slower: 168 registers and spills
+    // at batch 8).
+    if ((m + 2 * kWarps - 1) / (2 * kWarps) >= sm_count) pl.rw = 2;
   }
   pl.rows = pl.split ? pl.rw : kWarps * pl.rw;
   if (rb * pl.rows <= kItemTarget) {
@@ -824,22 +847,24 @@ const void *split_kernel_ptr(int r, int slots) {
 }
 
 template <int KIND, class P>
-const void *stream_kernel_ptr(int nb, bool dots) {
-  if (dots) return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, true, P>);
+const void *stream_kernel_ptr(int nb, bool dots, int rw) {
+  if (dots) return rw == 1 ? reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, true, P, 1>) : nullptr;
+#define UGB_SK2(NB)                                                                             \
+  case NB:                                                                                      \
+    return rw == 2 ? reinterpret_cast<const void *>(&mv_stream_kernel<KIND, NB, false, P, 2>)   \
+                   : reinterpret_cast<const void *>(&mv_stream_kernel<KIND, NB, false, P, 1>);
   switch (nb) {
-    case 1: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 1, false, P>);
-    case 2: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 2, false, P>);
-    case 4: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 4, false, P>);
-    case 8: return reinterpret_cast<const void *>(&mv_stream_kernel<KIND, 8, false, P>);
+    UGB_SK2(1) UGB_SK2(2) UGB_SK2(4) UGB_SK2(8)
     default: return nullptr;
   }
+#undef UGB_SK2
 }
 
 template <int KIND, class P>
 const void *select_for(const Plan &pl, int nb, bool dots) {
   return pl.rows_kernel ? rows_kernel_ptr<KIND, P>(pl.rw, pl.slots, pl.burst)
          : pl.split     ? split_kernel_ptr<KIND, P>(pl.rw, pl.slots)
-                        : stream_kernel_ptr<KIND, P>(nb, dots);
+                        : stream_kernel_ptr<KIND, P>(nb, dots, pl.rw);
 }
 
 // The kernel instance for a plan; `table` picks the instances that take the job table.
@@ -882,9 +907,13 @@ ugb_status init_matvec_kernels(ugb_ctx *ctx) {
         pl.split = false;
       }
     pl.rows_kernel = false;
-    for (int nb : {1, 2, 4, 8})
-      for (bool table : {false, true})
-        if (allow_smem(select_kernel(kind, pl, nb, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+    for (int rw : {1, 2}) {
+      pl.rw = rw;
+      for (int nb : {1, 2, 4, 8})
+        for (bool table : {false, true})
+          if (allow_smem(select_kernel(kind, pl, nb, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+    }
+    pl.rw = 1;
     if (allow_smem(select_kernel(kind, pl, 1, true), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
   }
   return UGB_OK;
