@@ -778,19 +778,27 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
     if ((m + 2 * kWarps - 1) / (2 * kWarps) >= sm_count) pl.rw = 2;
   }
   pl.rows = pl.split ? pl.rw : kWarps * pl.rw;
-  if (rb * pl.rows <= kItemTarget) {
-    pl.kc = static_cast<int>(k);
-    pl.nch = 1;
-    pl.stage_bytes = static_cast<uint32_t>(round_up(rb * pl.rows + 32, 128));
-  } else {
-    // K chunks sized so the item's 8 row chunks fill about one stage.
-    const int gran = kind == UGB_Q8_0 ? 128 : 256;  // chunk starts keep x arrays 16B aligned
-    const int nch = static_cast<int>((rb * pl.rows + kItemTarget - 1) / kItemTarget);
-    pl.kc = static_cast<int>(round_up((k + nch - 1) / nch, gran));
-    pl.nch = static_cast<int>((k + pl.kc - 1) / pl.kc);
-    pl.seg_stride = static_cast<uint32_t>(round_up(elems_to_bytes(kind, pl.kc) + 32, 16));
-    pl.stage_bytes = static_cast<uint32_t>(round_up(static_cast<uint64_t>(pl.rows) * pl.seg_stride, 128));
-  }
+  auto size_items = [&](uint64_t target) {
+    if (rb * pl.rows <= target) {
+      pl.kc = static_cast<int>(k);
+      pl.nch = 1;
+      pl.seg_stride = 0;
+      pl.stage_bytes = static_cast<uint32_t>(round_up(rb * pl.rows + 32, 128));
+    } else {
+      // K chunks sized so the item's row chunks fill about one stage.
+      const int gran = kind == UGB_Q8_0 ? 128 : 256;  // chunk starts keep x arrays 16B aligned
+      const int nch = static_cast<int>((rb * pl.rows + target - 1) / target);
+      pl.kc = static_cast<int>(round_up((k + nch - 1) / nch, gran));
+      pl.nch = static_cast<int>((k + pl.kc - 1) / pl.kc);
+      pl.seg_stride = static_cast<uint32_t>(round_up(elems_to_bytes(kind, pl.kc) + 32, 16));
+      pl.stage_bytes = static_cast<uint32_t>(round_up(static_cast<uint64_t>(pl.rows) * pl.seg_stride, 128));
+    }
+  };
+  // Batches take stages twice as large where two still fit beside the activations: whole rows
+  // of the 3584-wide matrices in one copy, and row chunks twice as long otherwise (every chunk
+  // of every row is a copy of its own, and short copies do not keep HBM busy).
+  const bool batch_stream = !pl.rows_kernel && !pl.split && !dots && nb > 1;
+  size_items(batch_stream ? 2 * kItemTarget : kItemTarget);
   pl.ngroups = static_cast<int>((m + pl.rows - 1) / pl.rows);
   const size_t nbp = round_up(static_cast<uint64_t>(k / 32), 4);
   uint32_t off = kBarBytes;
@@ -803,6 +811,10 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
   pl.red = static_cast<uint32_t>(round_up(off, 16));
   off = pl.red + 2 * kWarps * 4 * 4;
   pl.ring = static_cast<uint32_t>(round_up(off, 128));
+  if (batch_stream && pl.ring + 2 * static_cast<size_t>(pl.stage_bytes) > smem_optin) {
+    size_items(kItemTarget);
+    pl.ngroups = static_cast<int>((m + pl.rows - 1) / pl.rows);
+  }
   // One kernel takes at most about half an SM's shared memory (kSmPerKernel over its resident
   // CTAs), so the next kernel in the stream can become resident beside it and prefetch its
   // weights under programmatic dependent launch.
