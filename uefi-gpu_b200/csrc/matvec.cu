@@ -683,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1) mv_stream_kernel(const P p) {
         for (int r = 0; r < RW; ++r) {
           if (warp * RW + r < it.nrows) {  // warp-uniform
             WUnit wu;
-            load_wunit<KIND>(seg[r], u, wu);
+            load_wunit<KIND, false>(seg[r], u, wu);
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
               const int isum = unit_isum<KIND>(wu, x[b]);
