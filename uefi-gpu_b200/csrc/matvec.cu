@@ -365,8 +365,8 @@ __device__ __forceinline__ bool prologue_burst(const MvParams &p, const View &v,
   grid_dep_wait();  // the activation is read and y written only after the dependency
   if (p.xf != nullptr) {
     // The fp32 activation, quantised into shared memory by every CTA: quant_q8_1_kernel's
-    // arithmetic bit for bit (glue.cuh), four blocks per warp at a time, loads first.
-    constexpr int kQB = 4;
+    // arithmetic bit for bit (glue.cuh), eight blocks per warp at a time, loads first.
+    constexpr int kQB = 8;
     const int warp = tid >> 5, nb = p.k / 32;
     uint8_t *smem = reinterpret_cast<uint8_t *>(__cvta_shared_to_generic(base));
     int8_t *q = reinterpret_cast<int8_t *>(smem + p.x_q);
