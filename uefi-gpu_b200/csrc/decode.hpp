@@ -58,7 +58,7 @@ ugb_status launch_moe_route(ugb_ctx *ctx, cudaStream_t stream, bool pdl, const f
 
 // ---- the persistent token kernel (token.cu) ----------------------------------------------------
 
-constexpr uint32_t kTokItemMax = 32 * 1024;  // bytes of one streamed item (whole rows)
+constexpr uint32_t kTokItemMax = 64 * 1024;  // bytes of one streamed item (whole rows)
 
 // One layer's tensors as the token kernel reads them (a device-side table, one entry per layer).
 struct TokLayer {
