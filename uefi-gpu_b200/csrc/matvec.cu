@@ -415,7 +415,7 @@ __device__ __forceinline__ void release_stage(uint32_t empty, int s, int lane) {
 // shared memory and registers), so there is no producer warp and no stage reuse, and the next
 // kernel in the stream fits beside this one and streams its own weights meanwhile.
 template <int KIND, int RW, int J, class P, bool BURST>
-__global__ void __launch_bounds__(BURST ? kWarps * 32 : kThreads, BURST ? 2 : 1) mv_rows_kernel(const P p) {
+__global__ void __launch_bounds__(BURST ? kWarps * 32 : kThreads, 2) mv_rows_kernel(const P p) {
   static_assert(J >= 2 && J <= kSlots, "2 to kSlots register slots");
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
