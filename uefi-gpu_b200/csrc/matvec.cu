@@ -11,15 +11,20 @@
 //    evict-first hint since each byte is read once.  The first stages are requested before
 //    the programmatic launch dependency resolves, overlapping the previous kernel's tail.
 //  * The Q8_1 activation is bulk-copied into shared memory once per CTA.
-//  * Two consumers:
+//  * Consumers:
 //    - mv_rows_kernel (batch 1, whole rows): each warp owns RW rows; lane l covers slots
 //      l, l+32, ... of the warp's flattened (row, 32-element unit) space, keeps the matching
 //      activation units in registers for the whole kernel (every item spans the whole row),
 //      and the RW row totals come out of one transposed shuffle tree.  This keeps the
-//      per-row instruction overhead small enough to stream at HBM speed.
-//    - mv_stream_kernel (batches, long rows split into K chunks, int-dot dumps): one warp per
-//      row, activation units read from shared memory, row sums kept in registers across the
-//      row's chunks.
+//      per-row instruction overhead small enough to stream at HBM speed.  Its burst form
+//      (matrices whose rows fit one CTA per SM) has no producer warp: every item gets its own
+//      stage and all copies go out first, at about half an SM, so the next launch becomes
+//      resident beside it; it can also quantise an fp32 activation itself (ugb_matvec_f32).
+//    - mv_split_kernel (batch 1, rows too long for whole rows per warp): an item's rows are
+//      spread over all consumer lanes, partials meet through a named-barrier reduction.
+//    - mv_stream_kernel (batches, long rows split into K chunks, int-dot dumps): RW rows per
+//      warp share each activation unit read from shared memory, row sums kept in registers
+//      across the row's chunks.
 //  * Integer block dots are exact (dp4a); the fp32 accumulation order is fixed, so results
 //    are deterministic run to run.
 #include <algorithm>
