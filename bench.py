@@ -47,6 +47,7 @@ sys.path.insert(0, ROOT)
 
 Q8_0 = 8
 PATHS = {"auto": 0, "chain": 1, "token": 2}  # ugb_decoder_set_path values
+KV_TYPES = {"f32": 0, "f16": 1}  # ugb_decoder_config.kv_type
 
 
 def load_peaks():
@@ -68,7 +69,8 @@ def load_traffic(key):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 20 ms from the start of the warm-up to
+    the end of the timed region (the GPU is busy with the benchmark throughout)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -83,7 +85,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=self.out, stderr=subprocess.DEVNULL)
         except (FileNotFoundError, OSError):
             self.proc = None
@@ -149,14 +151,18 @@ def q8_bytes(k, m):
     return m * (k // 32) * 34
 
 
+def kv_elem_bytes(c):
+    return 2 if c.get("kv_type", 0) == 1 else 4
+
+
 def c2_token_bytes(c=C2, pos=None):
     """Algorithmic bytes of one token: every weight once (layers + tied head, the embedding row
-    is 1.6 KB), plus the KV cache read at context `pos` (fp32 K and V of every layer)."""
+    is 1.6 KB), plus the KV cache read at context `pos` (K and V of every layer, fp16 or fp32)."""
     layers = c["n_layer"] * sum(q8_bytes(k, m) for _, k, m in c2_shapes(c))
     head = q8_bytes(c["n_embd"], c["n_vocab"])
     if pos is None:
         pos = c["n_ctx"]
-    kv = c["n_layer"] * 2 * c["n_head_kv"] * c["head_dim"] * 4 * pos
+    kv = c["n_layer"] * 2 * c["n_head_kv"] * c["head_dim"] * kv_elem_bytes(c) * pos
     return layers + head + kv
 
 
@@ -245,21 +251,18 @@ def c2_cpu(budget_s: float, max_tokens: int, c=C2):
     return done / dt, done, orc.lib(True).orc_threads()
 
 
-def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
-    dev = torch.device("cuda", torch.cuda.current_device())
-    w = c2_device_weights(ctx, ugb, torch, seed=1 + rank, c=c)
+def c2_timed_tokens(args, ugb, ctx, torch, world, w, c, stream, cap, sampler=None):
+    """A decoder of config c on weights w: K device-driven token replays of one captured step
+    at the last K positions of the context, after W warm-up replays.  Returns (decoder, graph,
+    path, kernels per token, max-over-ranks ms, timed positions, clocks)."""
     dec = ugb.Decoder(ctx, **c)
     dec.bind(w["tok_embd"], w["output_norm"], w["output"], w["layers"])
     active = dec.set_path(PATHS[args.path])
     n_ctx = c["n_ctx"]
-    stream = torch.cuda.Stream()
-    cap = torch.cuda.Stream()
-
     # One token step captured once; each replay reads the previous step's greedy token and
     # advances the position on the device (embedding kernel), so K replays decode K tokens.
     dec.set_state(1, 0, stream)
     graph = ctx.capture(lambda: dec.step(), cap)
-    kernels_per_token = graph.kernels()
 
     def run(first_pos, count, tok=1):
         """count replays starting at first_pos; re-seed the state when the context is full."""
@@ -274,17 +277,15 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
 
     K, W = args.steps, args.warmup
     start = max(0, n_ctx - K)
-    warm_start = max(0, start - W)
-    run(warm_start, W)
+    if sampler:
+        sampler.start()
+    run(max(0, start - W), W)
     stream.synchronize()
     code, bits = ctx.status_read(stream)
     assert code == ugb.OK, ("status after warm-up", code, bits)
-
     # -- timed region: K tokens, device time by CUDA events on the launching stream --
-    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
     barrier(world, torch)
     torch.cuda.synchronize()
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dec.set_state(1, start, stream)
     e0.record(stream)
@@ -298,12 +299,24 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     e1.record(stream)
     torch.cuda.synchronize()
     barrier(world, torch)
-    clocks = sampler.stop()
+    clocks = sampler.stop() if sampler else None
     ms = e0.elapsed_time(e1)
     code, bits = ctx.status_read(stream)
     assert code == ugb.OK, ("status after timing", code, bits)
-    ms_max = reduce_max(ms, world, torch)
-    timed_pos = [(start + i) % n_ctx for i in range(K)]
+    return dec, graph, active, graph.kernels(), reduce_max(ms, world, torch), [(start + i) % n_ctx for i in range(K)], clocks
+
+
+def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
+    dev = torch.device("cuda", torch.cuda.current_device())
+    w = c2_device_weights(ctx, ugb, torch, seed=1 + rank, c=c)
+    c = dict(c, kv_type=KV_TYPES[args.kv])
+    n_ctx = c["n_ctx"]
+    stream = torch.cuda.Stream()
+    cap = torch.cuda.Stream()
+    K = args.steps
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
+    dec, graph, active, kernels_per_token, ms_max, timed_pos, clocks = c2_timed_tokens(
+        args, ugb, ctx, torch, world, w, c, stream, cap, sampler)
     token_bytes = float(np.mean([c2_token_bytes(c, p + 1) for p in timed_pos]))
 
     # -- dominant kernel.  Token path: the step is one launch of the persistent token kernel, so
@@ -311,6 +324,7 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     # Launch chain: the fused gate/up matvec (17920 x 1536 Q8_0, the largest launch of a layer),
     # all 28 layers' matrices back to back in one graph (each launch streams its own 29 MB from
     # HBM), timed by CUDA events on the launching stream --
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if active == ugb.PATH_TOKEN:
         kern_ms, kern_bytes, kgraph = ms_max / K, token_bytes, None
     else:
@@ -331,10 +345,17 @@ def c2_gpu(args, ugb, ctx, torch, rank, world, c=C2):
     graph.close()
     if kgraph is not None:
         kgraph.close()
+    other = None
+    if c["kv_type"] == 1:  # the reference's own fp32 cache, same weights and positions
+        d2, g2, _, _, ms2, pos2, _ = c2_timed_tokens(args, ugb, ctx, torch, world, w, dict(c, kv_type=0), stream, cap)
+        d2.close()
+        g2.close()
+        other = {"kv_cache": "fp32", "value": world * K / (ms2 / 1e3), "ms_per_step": ms2 / K,
+                 "bytes_per_token": float(np.mean([c2_token_bytes(dict(c, kv_type=0), p + 1) for p in pos2]))}
     return {
         "value": world * K / (ms_max / 1e3), "ms_per_step": ms_max / K, "clocks": clocks,
         "gpu_launches": kernels_per_token * K, "path": active,
-        "token_bytes": token_bytes,
+        "token_bytes": token_bytes, "kv_other": other,
         "kernel_ms": kern_ms, "kernel_bytes": kern_bytes,
         "e2e": {"value": world / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 16,
                 "d2h_bytes_per_step": 16 + 4},
@@ -679,7 +700,7 @@ def big_step_bytes(c, batch, pos, world=1, rank=0):
     layers = c["n_layer"] * (attn + ffn)
     vn = c.get("n_vocab_local") or c["n_vocab"]
     head = kbytes(c["head_kind"], e, vn)
-    kvb = c["n_layer"] * 2 * kv * 4 * pos * batch
+    kvb = c["n_layer"] * 2 * kv * kv_elem_bytes(c) * pos * batch
     return layers + head + kvb
 
 
@@ -701,7 +722,7 @@ def big_gpu(args, ugb, ctx, torch, rank, world, workload):
     if args.layers:
         base["n_layer"] = args.layers
     batch = args.batch or (8 if workload == "c4" else 1)
-    c = shard_config(dict(base, batch=batch), workload, rank, world)
+    c = shard_config(dict(base, batch=batch, kv_type=KV_TYPES[args.kv]), workload, rank, world)
     dec = ugb.Decoder(ctx, **c)
     dec.synthetic(11)
     comm = None
@@ -723,16 +744,16 @@ def big_gpu(args, ugb, ctx, torch, rank, world, workload):
     barrier(world, torch)
     graph = ctx.capture(lambda: dec.step(), cap)
     kernels = graph.kernels()  # includes NCCL's kernels when the step holds collectives
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
+    sampler.start()
     dec.set_tokens(toks, start - W, stream)
     for _ in range(W):
         graph.launch(stream)
     stream.synchronize()
     code, bits = ctx.status_read(stream)
     assert code == ugb.OK, ("status after warm-up", code, bits)
-    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
     barrier(world, torch)
     torch.cuda.synchronize()
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(K):
@@ -843,6 +864,8 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="c4 / c5: decode this many layers instead of the config's (profiling captures only)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--kv", choices=sorted(KV_TYPES), default="f16",
+                    help="c2 / c4 / c5 KV cache element type (BASELINE config 2: fp16; the reference keeps fp32)")
     ap.add_argument("--path", choices=sorted(PATHS), default="auto",
                     help="c2 / c4 / c5 decoder path: persistent token kernel where it applies (auto), "
                          "the per-kernel launch chain, or the token kernel only")
@@ -857,7 +880,7 @@ def main():
         config = {"workload": "c2: greedy batch-1 decode, Qwen2.5-1.5B-shaped, all linear weights Q8_0",
                   "layers": C2["n_layer"], "hidden": C2["n_embd"], "ffn": C2["n_ff"],
                   "heads": f"{C2['n_head']}/{C2['n_head_kv']}x{C2['head_dim']}", "vocab": C2["n_vocab"],
-                  "context": C2["n_ctx"], "kv_cache": "fp32 (as the reference's, gpu_attention.cu:1)",
+                  "context": C2["n_ctx"], "kv_cache": "fp16" if args.kv == "f16" else "fp32",
                   "timed_positions": f"last {min(args.steps, C2['n_ctx'])} of {C2['n_ctx']}",
                   "l2": "inputs larger than L2 (1.655 GB of weights per token)",
                   "parallelism": f"replicas x{world}"}
@@ -873,7 +896,8 @@ def main():
             split = f"experts split over {world} GPU(s) ({192 // world} each), layer outputs all-reduced over NVLink"
         config = {"workload": name, "batch": bsz, "layers": big["n_layer"], "hidden": big["n_embd"],
                   "heads": f"{big['n_head']}/{big['n_head_kv']}x{big['head_dim']}", "vocab": big["n_vocab"],
-                  "context": big["n_ctx"], "kv_cache": "fp32", "head": "tied to the Q8_0 token embedding",
+                  "context": big["n_ctx"], "kv_cache": "fp16" if args.kv == "f16" else "fp32",
+                  "head": "tied to the Q8_0 token embedding",
                   "l2": "inputs larger than L2", "parallelism": split if world > 1 else "1 GPU"}
         base = {"metric": "decode tok/s", "unit": "tok/s",
                 "dtype": "int8 x int8 -> int32 (K-quant / Q8_0 x Q8_1), fp32 glue"}
@@ -904,7 +928,7 @@ def main():
         t0 = time.perf_counter()
         line = dict(base)
         if args.workload == "c2":
-            value, done, cores = c2_cpu(max(30.0, args.cpu_seconds), args.steps)
+            value, done, cores = c2_cpu(max(30.0, args.cpu_seconds), args.steps, dict(C2, kv_type=KV_TYPES[args.kv]))
             sample = (f"{done} decode tokens at the last positions of the 512 context, oracle/decode_ref.py "
                       f"(numpy glue, oracle/ugb_oracle.c matvecs on POSIX threads over rows)")
             ms = 1e3 / value
@@ -939,22 +963,23 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     ugb = importlib.import_module("uefi-gpu_b200")
     ctx = ugb.Context(torch.cuda.current_device())
+    decoder_path = None
     if args.workload == "c2":
         res = c2_gpu(args, ugb, ctx, torch, rank, world)
         if res["path"] == ugb.PATH_TOKEN:
             kernel = "token_kernel<Q8_0,Q8_0> (the whole decode step, one persistent launch per token)"
             traffic = load_traffic("c2_token")
-            config["path"] = "token kernel: one persistent cooperative launch per token, 1 CTA per SM"
+            decoder_path = "token kernel: one persistent cooperative launch per token, 1 CTA per SM"
         else:
             kernel = "mv_rows_kernel<Q8_0> (fused gate/up, 17920x1536)"
             traffic = load_traffic("c2_gate_up")
-            config["path"] = "launch chain: 256 kernels per token, captured as one CUDA graph"
+            decoder_path = "launch chain: 256 kernels per token, captured as one CUDA graph"
     elif args.workload in ("c4", "c5"):
         res = big_gpu(args, ugb, ctx, torch, rank, world, args.workload)
         kernel = None
         traffic = None
-        config["path"] = ("token kernel: one persistent cooperative launch per token" if res["path"] == ugb.PATH_TOKEN
-                          else "launch chain captured as one CUDA graph")
+        decoder_path = ("token kernel: one persistent cooperative launch per token" if res["path"] == ugb.PATH_TOKEN
+                        else "launch chain captured as one CUDA graph")
     elif args.workload == "c3":
         res = c3_gpu(args, ugb, ctx, torch, rank, world)
         kernel = "prefill_gemm_kernel<128> (fused gate/up, 512 x 17920 x 1536)"
@@ -989,13 +1014,17 @@ def main():
         "value": res["value"], "ms_per_step": res["ms_per_step"], "roofline": roof,
         "e2e": res["e2e"], "gpu_launches": res["gpu_launches"], "clocks": res["clocks"],
     })
+    if decoder_path:
+        line["decoder_path"] = decoder_path
+    if res.get("kv_other"):
+        line["kv_fp32"] = res["kv_other"]
     if "token_bytes" in res:
         step_gbs = res["token_bytes"] / (res["ms_per_step"] / 1e3) / 1e9
         line["roofline"]["step"] = {"bytes_per_token": res["token_bytes"], "achieved": step_gbs,
                                     "frac": step_gbs / hbm_peak}
     if rank == 0 and world == 1:
         if args.workload == "c2":
-            v, done, cores = c2_cpu(args.cpu_seconds, 64)
+            v, done, cores = c2_cpu(args.cpu_seconds, 64, dict(C2, kv_type=KV_TYPES[args.kv]))
             sample = f"{done} decode tokens (oracle/decode_ref.py; matvecs on the host threads)"
         elif args.workload in ("c4", "c5"):
             v, _, cores = big_cpu(args.cpu_seconds, args.workload, 1)

@@ -7,7 +7,8 @@
  * frontier_batch.rs:19-72) and exposes them to the model code as Gpu::matvec / Gpu::batch
  * (llm.rs:226-273) and trait Weights::{linear,batch} (frontier_forward.rs:14-22).  Each
  * entry point below names the reference interface it replaces.  A Rust host binds them with
- * `extern "C"`; the CUDA stream argument replaces the GPFIFO channel.
+ * `extern "C"` declarations of the same names and #[repr(C)] structs of the same field order;
+ * the CUDA stream argument replaces the GPFIFO channel.
  *
  * Conventions
  *  - Plain pointers and sizes only.  Pointers named `*_dev` or documented as device memory
@@ -52,6 +53,7 @@ typedef enum ugb_status {
 /* GGML type ids, the same numbers the reference uses for `kind` (frontier_core.rs:146-151). */
 enum {
   UGB_F32 = 0,
+  UGB_F16 = 1,
   UGB_Q8_0 = 8,
   UGB_Q3_K = 11,
   UGB_Q4_K = 12
@@ -305,7 +307,10 @@ ugb_status ugb_comm_destroy(ugb_comm *comm);
  *  - Expert parallelism: this device holds global experts [expert0, expert0 + n_expert_local)
  *    (n_expert_local = 0: all).  With a communicator the layer outputs are summed over devices.
  *  - Vocabulary split: this device holds head rows [vocab0, vocab0 + n_vocab_local)
- *    (n_vocab_local = 0: all).  With a communicator the greedy keys are reduced over devices. */
+ *    (n_vocab_local = 0: all).  With a communicator the greedy keys are reduced over devices.
+ *  - kv_type: element type of the KV cache, UGB_F32 (0, the reference's own cache,
+ *    gpu_attention.cu:1) or UGB_F16 (1: keys and values rounded to nearest even as they are
+ *    written; attention reads them back as fp16, the current position included). */
 typedef struct ugb_decoder_config {
   int32_t n_layer, n_embd, n_ff, n_head, n_head_kv, head_dim, n_vocab, n_ctx;
   float rope_theta, norm_eps;
@@ -316,6 +321,7 @@ typedef struct ugb_decoder_config {
   uint32_t expert_kind;
   int32_t expert0, n_expert_local;
   int32_t vocab0, n_vocab_local;
+  uint32_t kv_type;
 } ugb_decoder_config;
 
 /* Device pointers of one layer's GGUF tensors (blk.N.*): matrices in their GGUF block layout
@@ -338,8 +344,8 @@ typedef struct ugb_model_weights {
 
 typedef struct ugb_decoder ugb_decoder;
 
-/* Allocate the decoder's device state: fp32 KV cache (batch x n_layer x n_head_kv x n_ctx x
- * head_dim, for K and V; the reference keeps its cache in fp32 too, gpu_attention.cu:1),
+/* Allocate the decoder's device state: KV cache of kv_type (batch x n_layer x n_head_kv x n_ctx
+ * x head_dim, for K and V; the reference keeps its cache in fp32, gpu_attention.cu:1),
  * activations, RoPE table (f32 angle pos * powf(theta, -2i/head_dim), gpu_graph.rs:132),
  * attention partials, MoE workspace and the token state.  Replaces the reference's VRAM arenas
  * and graph build (gpu_graph.rs:81-169).  head_dim must be 128; n_head a multiple of
@@ -406,6 +412,60 @@ ugb_status ugb_decoder_logits(ugb_decoder *dec, ugb_stream stream, float *logits
 ugb_status ugb_decoder_read_kv(ugb_decoder *dec, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
                                int32_t count, float *k_host, float *v_host);
 
+/* The inverse of ugb_decoder_read_kv: host keys (already rotated) and values, each
+ * [n_head_kv][count][head_dim], into `count` cached positions from `pos` of sequence `seq` in
+ * one layer (an fp16 cache rounds them to nearest even).  Synchronous.  Restores a checkpointed
+ * sequence, or seeds a history to decode from.  No counterpart in the reference (its host
+ * writes the cache at fixed device addresses, llm.rs:319-320). */
+ugb_status ugb_decoder_write_kv(ugb_decoder *dec, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
+                                int32_t count, const float *k_host, const float *v_host);
+
+/* Step trace, for checking a step stage by stage against a CPU restatement: with tracing on,
+ * every step also records, per layer l < n_layer, the fields below for every sequence
+ * ([batch][len], fp32 unless Q8_1; a Q8_1 field is a ugb_q8act buffer of its length and the
+ * decoder's batch):
+ *   X         residual stream entering the layer (the embedding at l = 0)   [n_embd]
+ *   ATTN_NORM RMSNorm output before quantisation                             [n_embd]
+ *   ATTN_XQ   its Q8_1 quantisation, the Q/K/V matvec input                  Q8_1 n_embd
+ *   QKV       the Q/K/V matvec output (before biases)                        [q ; k ; v rows]
+ *   ATT       the attention output before quantisation                       [n_head * head_dim]
+ *   ATT_XQ    its Q8_1, the O matvec input                                   Q8_1 n_head*head_dim
+ *   O         the O matvec output                                            [n_embd]
+ *   FFN_NORM  the second RMSNorm output before quantisation                  [n_embd]
+ *   FFN_XQ    its Q8_1, the FFN input                                        Q8_1 n_embd
+ *   GATE_UP   gate rows then up rows (dense FFN)                             [2 n_ff]
+ *   H         SiLU(gate) * up before quantisation (dense FFN)                [n_ff]
+ *   H_XQ      its Q8_1, the down matvec input (dense FFN)                    Q8_1 n_ff
+ *   DOWN      the FFN output (down matvec, or the combined MoE experts)      [n_embd]
+ * and in record l = n_layer: X (the final residual), ATTN_NORM (the output norm) and ATTN_XQ
+ * (the head's input).  Tracing costs time and memory and is meant for tests; it is off by
+ * default.  ugb_decoder_trace_bytes gives a field's size (0: no such field);
+ * ugb_decoder_read_trace copies one field of the last step to host memory (synchronous).
+ * No counterpart in the reference. */
+/* Time limit of each wait of the persistent token kernel on other CTAs' progress (device-wide
+ * phase counters, ring hand-offs), in ns: 1e3 .. 6e10, default 2e9.  When a wait runs out the
+ * kernel records UGB_STATUS_TIMEOUT, every CTA leaves at its next wait, the counters are reset
+ * for the next launch and the step's results are not valid: ugb_decoder_token / tokens and
+ * ugb_status_read return UGB_ETIMEOUT, and the next step starts afresh.  The reference bounds its
+ * own waits the same way (frontier_gpu.rs:30-33, llm.rs:267-269). */
+ugb_status ugb_decoder_set_wait_limit(ugb_decoder *dec, uint64_t ns);
+
+/* Test hook for that path: with enable != 0 the first attention wait of every token-kernel step
+ * asks for one arrival more than there are CTAs, so it can end only by its time limit.  Lets a
+ * test see a bounded wait run out without any fault.  The launch chain has no such wait and is
+ * unaffected.  No counterpart in the reference. */
+ugb_status ugb_decoder_test_unreachable_wait(ugb_decoder *dec, int32_t enable);
+
+enum {
+  UGB_TRACE_X = 0, UGB_TRACE_ATTN_NORM, UGB_TRACE_ATTN_XQ, UGB_TRACE_QKV, UGB_TRACE_ATT, UGB_TRACE_ATT_XQ,
+  UGB_TRACE_O, UGB_TRACE_FFN_NORM, UGB_TRACE_FFN_XQ, UGB_TRACE_GATE_UP, UGB_TRACE_H, UGB_TRACE_H_XQ,
+  UGB_TRACE_DOWN, UGB_TRACE_FIELDS
+};
+ugb_status ugb_decoder_set_trace(ugb_decoder *dec, int32_t enable);
+size_t ugb_decoder_trace_bytes(const ugb_decoder *dec, int32_t field);
+ugb_status ugb_decoder_read_trace(ugb_decoder *dec, ugb_stream stream, int32_t layer, int32_t field, void *host,
+                                  size_t bytes);
+
 /* One token end to end, as the reference's forward() (llm.rs:339-388 / forward_gpu
  * gpu_graph.rs:170-197): host tokens and position in, greedy next tokens out.  Replays a CUDA
  * graph of the step (captured on first use) and checks the status word.  ugb_decoder_token is
@@ -433,8 +493,11 @@ ugb_status ugb_linear(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void
  * out-of-memory failure of a first-use cudaMalloc.
  *   - k <= UGB_LINEAR_STATIC_MAX_K and m <= UGB_LINEAR_STATIC_MAX_M, else UGB_ESHAPE (the
  *     reference's own Weights::linear caps, frontier_backend.rs:245-248).
- *   - The first call on a device looks up the array's address (cudaGetSymbolAddress with that
- *     device current); make that first call before any stream capture begins.
+ *   - Every call makes ctx's device current, as every entry point does.  The first call on a
+ *     device looks up the array's address (cudaGetSymbolAddress with that device current) and
+ *     caches it for the process; make that first call before any stream capture begins.  The
+ *     cache assumes the device's primary context lives as long as the process (not across a
+ *     cudaDeviceReset).
  *   - Nothing needs to start at zero: every scratch byte a call reads it wrote first.
  *   - One array per device, shared by all contexts and streams: calls on the same device
  *     that overlap in time race on it.  The call is synchronous, so back-to-back calls from

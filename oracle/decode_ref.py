@@ -10,7 +10,9 @@ reference's GPU decode graph (driver/src/gpu_graph.rs:139-162):
   * RMSNorm y = x * (1 / sqrt(sum(x^2)/n + eps)) * w (llm.rs:323-327);
   * Q/K/V biases added before RoPE; RoPE over the pairs (i, i + HD/2) with the table built from
     the f32 angle pos * powf(theta, -(2i)/HD) (gpu_graph.rs:132, llm.rs:328-337);
-  * fp32 KV cache, scores q.k / sqrt(HD), exact exp softmax (gpu_attention.cu:1-26);
+  * fp32 KV cache, scores q.k / sqrt(HD), exact exp softmax (gpu_attention.cu:1-26); with
+    cfg["kv_type"] == 1 the cache holds fp16 instead: keys and values are rounded to nearest
+    even as they are written, and attention reads them back (the current position included);
   * SiLU(gate) * up (llm.rs:374), residual adds, final norm, head, first-maximum greedy
     (llm.rs:383-385);
   * an MoE FFN when cfg["n_expert"] > 0 (Forward::ffn, frontier_forward.rs:164-199): router
@@ -54,13 +56,38 @@ class RefDecoder:
         self.kcache = np.zeros((c["n_layer"], c["n_head_kv"], c["n_ctx"], self.hd), np.float32)
         self.vcache = np.zeros_like(self.kcache)
         self.rope = rope_table(c["n_ctx"], self.hd, c["rope_theta"])
+        self.kv16 = c.get("kv_type", 0) == 1
 
     # ---- pieces ---------------------------------------------------------------------------
 
     def linear(self, kind: int, w: np.ndarray, x: np.ndarray, m: int) -> np.ndarray:
         k = x.size
         q, d, s, _ = po.quant_act(x.reshape(1, k))
-        return po.matvec(kind, w, po.row_bytes(kind, k), q, d, s, k, m, 1, mt=self.mt)[0]
+        return self.linear_q8(kind, w, q[0], d[0], s[0], m)
+
+    def linear_q8(self, kind: int, w: np.ndarray, q: np.ndarray, d: np.ndarray, s: np.ndarray, m: int) -> np.ndarray:
+        """The matvec of an already quantised Q8_1 activation (q int8 [k], d f32 [k/32], s int32 [k/32])."""
+        k = q.size
+        return po.matvec(kind, w, po.row_bytes(kind, k), q.reshape(1, k), d.reshape(1, -1), s.reshape(1, -1), k, m,
+                         1, mt=self.mt)[0]
+
+    def kv_round(self, v: np.ndarray) -> np.ndarray:
+        """The value the cache gives back for v (fp16 round to nearest even in an fp16 cache)."""
+        return v.astype(np.float16).astype(np.float32) if self.kv16 else v.astype(np.float32)
+
+    def attend(self, q: np.ndarray, keys: np.ndarray, vals: np.ndarray) -> np.ndarray:
+        """q [n_head, HD] (rotated), keys / vals [n_kv, t, HD] -> attention output [n_head, HD]:
+        scores q.k / sqrt(HD), exact exp softmax, probabilities times values (gpu_attention.cu:2-26)."""
+        nh, nkv = q.shape[0], keys.shape[0]
+        group = nh // nkv
+        inv_sqrt = np.float32(1.0) / np.sqrt(np.float32(self.hd))
+        att = np.empty((nh, self.hd), np.float32)
+        for h in range(nh):
+            kv = h // group
+            sc = (keys[kv] @ q[h]).astype(np.float32) * inv_sqrt
+            e = np.exp(sc - sc.max()).astype(np.float32)
+            att[h] = (e @ vals[kv]).astype(np.float32) / np.float32(e.sum(dtype=np.float32))
+        return att
 
     def norm(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
         n = x.size
@@ -109,10 +136,8 @@ class RefDecoder:
         c, hd = self.c, self.hd
         kind = c["kind"]
         nh, nkv = c["n_head"], c["n_head_kv"]
-        group = nh // nkv
         qrows, kvrows = nh * hd, nkv * hd
         x = self.embed(token)
-        inv_sqrt = np.float32(1.0) / np.sqrt(np.float32(hd))
         for li, L in enumerate(self.w["layers"]):
             xn = self.norm(x, L["attn_norm"])
             q = self.linear(kind, L["wq"], xn, qrows)
@@ -126,16 +151,9 @@ class RefDecoder:
                 v = v + L["bv"]
             q = self.rotate(q.reshape(nh, hd), pos)
             k = self.rotate(k.reshape(nkv, hd), pos)
-            self.kcache[li, :, pos] = k
-            self.vcache[li, :, pos] = v.reshape(nkv, hd)
-            att = np.empty((nh, hd), np.float32)
-            for h in range(nh):
-                kvh = h // group
-                keys = self.kcache[li, kvh, :pos + 1]
-                vals = self.vcache[li, kvh, :pos + 1]
-                sc = (keys @ q[h]).astype(np.float32) * inv_sqrt
-                e = np.exp(sc - sc.max()).astype(np.float32)
-                att[h] = (e @ vals).astype(np.float32) / np.float32(e.sum(dtype=np.float32))
+            self.kcache[li, :, pos] = self.kv_round(k)
+            self.vcache[li, :, pos] = self.kv_round(v.reshape(nkv, hd))
+            att = self.attend(q, self.kcache[li, :, :pos + 1], self.vcache[li, :, :pos + 1])
             x = (x + self.linear(kind, L["wo"], att.reshape(-1), c["n_embd"])).astype(np.float32)
             xn = self.norm(x, L["ffn_norm"])
             if c.get("n_expert", 0):

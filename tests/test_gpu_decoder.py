@@ -74,8 +74,16 @@ def build_model(ctx, ugb, cfg, seed):
         layers.append(L)
     dev["layers"] = layers
     torch.cuda.synchronize()
-    host = {k: v.cpu().numpy() for k, v in dev.items() if k != "layers"}
-    host["layers"] = [{k: v.cpu().numpy() for k, v in L.items()} for L in layers]
+    copies = {}  # a tensor bound twice (the tied head) is copied to the host once
+
+    def to_host(t):
+        key = (t.data_ptr(), t.numel())
+        if key not in copies:
+            copies[key] = t.cpu().numpy()
+        return copies[key]
+
+    host = {k: to_host(v) for k, v in dev.items() if k != "layers"}
+    host["layers"] = [{k: to_host(v) for k, v in L.items()} for L in layers]
     return dev, host
 
 
@@ -375,3 +383,35 @@ def test_token_kernel_matches_chain(ctx, ugb):
     assert ctx.status_read()[1] == 0
     chain.close()
     tok.close()
+
+
+def test_token_kernel_wait_runs_out(ctx, ugb):
+    """A device-wide wait of the token kernel that nothing can satisfy (test hook: one arrival
+    more than there are CTAs) ends by its 1 ms limit: the step returns UGB_ETIMEOUT promptly,
+    nothing faults or hangs, and the next steps on the same decoder decode exactly as a decoder
+    that never timed out (frontier_gpu.rs:30-33: a poll that gives up reports an error)."""
+    import time
+    dec = ugb.Decoder(ctx, **SMALL)
+    dec.synthetic(91)
+    assert dec.set_path(TOKEN) == TOKEN
+    good = ugb.Decoder(ctx, **SMALL)
+    good.synthetic(91)
+    assert good.set_path(TOKEN) == TOKEN
+    ctx.status_read()
+    dec.set_wait_limit(1_000_000)
+    dec.test_unreachable_wait(True)
+    for _ in range(2):  # twice: the counters were reset by the aborted launch
+        t0 = time.perf_counter()
+        with pytest.raises(ugb.UgbError) as e:
+            dec.token(5, 0)
+        assert e.value.code == ugb.ETIMEOUT
+        assert time.perf_counter() - t0 < 1.0
+    dec.test_unreachable_wait(False)
+    for pos, tok in enumerate([5, 9, 11, 400]):
+        assert dec.token(tok, pos) == good.token(tok, pos)
+        np.testing.assert_array_equal(dec.logits().view(np.uint32), good.logits().view(np.uint32))
+    assert ctx.status_read()[1] == 0
+    with pytest.raises(ugb.UgbError):
+        dec.set_wait_limit(10)  # below the 1 us floor
+    dec.close()
+    good.close()

@@ -17,7 +17,7 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libugb.so")
 
-F32, Q8_0, Q3_K, Q4_K = 0, 8, 11, 12
+F32, F16, Q8_0, Q3_K, Q4_K = 0, 1, 8, 11, 12
 MAX_BATCH = 8
 LINEAR_STATIC_MAX_K, LINEAR_STATIC_MAX_M = 16384, 524288  # ugb_linear_static's fixed scratch
 
@@ -83,6 +83,13 @@ SIGNATURES = {
                                    _vp, _vp]),
     "ugb_decoder_token": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32,
                                  ctypes.POINTER(ctypes.c_int32)]),
+    "ugb_decoder_write_kv": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                    _vp, _vp]),
+    "ugb_decoder_set_trace": (_int, [_vp, ctypes.c_int32]),
+    "ugb_decoder_set_wait_limit": (_int, [_vp, _u64]),
+    "ugb_decoder_test_unreachable_wait": (_int, [_vp, ctypes.c_int32]),
+    "ugb_decoder_trace_bytes": (ctypes.c_size_t, [_vp, ctypes.c_int32]),
+    "ugb_decoder_read_trace": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_size_t]),
     "ugb_graph_begin": (_int, [_vp, _vp]),
     "ugb_graph_end": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
     "ugb_graph_launch": (_int, [_vp, _vp]),
@@ -339,7 +346,7 @@ class DecoderConfig(ctypes.Structure):
                 ("kind", ctypes.c_uint32), ("head_kind", ctypes.c_uint32), ("batch", ctypes.c_int32),
                 ("n_expert", ctypes.c_int32), ("top_k", ctypes.c_int32), ("n_ff_expert", ctypes.c_int32),
                 ("expert_kind", ctypes.c_uint32), ("expert0", ctypes.c_int32), ("n_expert_local", ctypes.c_int32),
-                ("vocab0", ctypes.c_int32), ("n_vocab_local", ctypes.c_int32)]
+                ("vocab0", ctypes.c_int32), ("n_vocab_local", ctypes.c_int32), ("kv_type", ctypes.c_uint32)]
 
 
 class LayerWeights(ctypes.Structure):
@@ -354,6 +361,11 @@ class ModelWeights(ctypes.Structure):
     _fields_ = [("tok_embd", _vp), ("output_norm", _vp), ("output", _vp),
                 ("layers", ctypes.POINTER(LayerWeights))]
 
+
+# Fields of the step trace (ugb_decoder_set_trace), in the order of ugb.h's UGB_TRACE_* list.
+TRACE_FIELDS = ("X", "ATTN_NORM", "ATTN_XQ", "QKV", "ATT", "ATT_XQ", "O", "FFN_NORM", "FFN_XQ", "GATE_UP", "H",
+                "H_XQ", "DOWN")
+TRACE = {name: i for i, name in enumerate(TRACE_FIELDS)}
 
 COMM_ID_BYTES = 128
 # How a decoder step runs (ugb_decoder_set_path): persistent token kernel where it applies, the
@@ -475,6 +487,46 @@ class Decoder:
         check("ugb_decoder_read_kv", lib().ugb_decoder_read_kv(self.handle, _stream(stream), seq, layer, pos,
                                                                  count, k.ctypes.data, v.ctypes.data))
         return k, v
+
+    def write_kv(self, layer: int, pos: int, keys, values, seq: int = 0, stream=None) -> None:
+        """keys, values: float32 [n_head_kv, count, head_dim] (rotated keys) into the cache."""
+        import numpy as np
+        k = np.ascontiguousarray(keys, dtype=np.float32)
+        v = np.ascontiguousarray(values, dtype=np.float32)
+        assert k.shape == v.shape and k.shape[0] == self.cfg.n_head_kv and k.shape[2] == self.cfg.head_dim
+        check("ugb_decoder_write_kv", lib().ugb_decoder_write_kv(self.handle, _stream(stream), seq, layer, pos,
+                                                                   k.shape[1], k.ctypes.data, v.ctypes.data))
+
+    def set_wait_limit(self, ns: int) -> None:
+        check("ugb_decoder_set_wait_limit", lib().ugb_decoder_set_wait_limit(self.handle, ns))
+
+    def test_unreachable_wait(self, enable: bool) -> None:
+        check("ugb_decoder_test_unreachable_wait",
+              lib().ugb_decoder_test_unreachable_wait(self.handle, 1 if enable else 0))
+
+    def set_trace(self, enable: bool) -> None:
+        check("ugb_decoder_set_trace", lib().ugb_decoder_set_trace(self.handle, 1 if enable else 0))
+
+    def trace(self, layer: int, field: str, stream=None):
+        """One field of the last traced step: float32 [batch, len], or for a Q8_1 field
+        (name ending in _XQ) the tuple (q int8 [batch, n], d f32 [batch, n/32], s int32 [batch, n/32])."""
+        import numpy as np
+        f = TRACE[field]
+        n = lib().ugb_decoder_trace_bytes(self.handle, f)
+        raw = np.empty(n, dtype=np.uint8)
+        check("ugb_decoder_read_trace", lib().ugb_decoder_read_trace(self.handle, _stream(stream), layer, f,
+                                                                       raw.ctypes.data, n))
+        b = self.cfg.batch
+        if not field.endswith("_XQ"):
+            return raw.view(np.float32).reshape(b, -1)
+        k = {"ATTN_XQ": self.cfg.n_embd, "FFN_XQ": self.cfg.n_embd, "ATT_XQ": self.cfg.n_head * self.cfg.head_dim,
+             "H_XQ": self.cfg.n_ff}[field]
+        d_off, s_off = q8act_offsets(k, b)
+        nb, nbp = k // 32, (k // 32 + 3) // 4 * 4
+        q = raw[: b * k].view(np.int8).reshape(b, k)
+        d = raw[d_off: d_off + b * nbp * 4].view(np.float32).reshape(b, nbp)[:, :nb]
+        s = raw[s_off: s_off + b * nbp * 4].view(np.int32).reshape(b, nbp)[:, :nb]
+        return q, d, s
 
     def tokens(self, tokens, pos: int, stream=None):
         b = self.cfg.batch

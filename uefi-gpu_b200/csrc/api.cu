@@ -21,13 +21,26 @@ ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_
   return UGB_OK;
 }
 
-namespace {
-
 ugb_status check_ctx(ugb_ctx *ctx) {
   if (!ctx || !ctx->status) return UGB_ECONTEXT;
   if (cudaSetDevice(ctx->device) != cudaSuccess) return UGB_EBACKEND;
   return UGB_OK;
 }
+
+ugb_status read_status_bits(ugb_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
+  // The status word is cleared even when the read-back fails, so no bits leak into the next call.
+  const bool copied = cudaMemcpyAsync(ctx->status_host, ctx->status, 4, cudaMemcpyDeviceToHost, stream) == cudaSuccess;
+  const bool cleared = cudaMemsetAsync(ctx->status, 0, 4, stream) == cudaSuccess;
+  if (cudaStreamSynchronize(stream) != cudaSuccess || !copied || !cleared) return UGB_EBACKEND;
+  const uint32_t b = *ctx->status_host;
+  if (bits) *bits = b;
+  if (b & ST_TIMEOUT) return UGB_ETIMEOUT;
+  if (b & (ST_NONFINITE_IN | ST_NONFINITE_OUT)) return UGB_ENONFINITE;
+  if (b & ST_BADARG) return UGB_ESHAPE;
+  return UGB_OK;
+}
+
+namespace {
 
 bool aligned16(const void *p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -55,19 +68,6 @@ ugb_status reserve(ugb_ctx *ctx, size_t bytes, size_t pinned) {
     if (cudaMallocHost(reinterpret_cast<void **>(&ctx->pinned), want) != cudaSuccess) return UGB_EBACKEND;
     ctx->pinned_bytes = want;
   }
-  return UGB_OK;
-}
-
-ugb_status read_status_bits(ugb_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
-  if (cudaMemcpyAsync(ctx->status_host, ctx->status, 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
-    return UGB_EBACKEND;
-  if (cudaMemsetAsync(ctx->status, 0, 4, stream) != cudaSuccess) return UGB_EBACKEND;
-  if (cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
-  const uint32_t b = *ctx->status_host;
-  if (bits) *bits = b;
-  if (b & ST_TIMEOUT) return UGB_ETIMEOUT;
-  if (b & (ST_NONFINITE_IN | ST_NONFINITE_OUT)) return UGB_ENONFINITE;
-  if (b & ST_BADARG) return UGB_ESHAPE;
   return UGB_OK;
 }
 

@@ -87,7 +87,8 @@ __global__ void __launch_bounds__(512) embed_kernel(const uint8_t *__restrict__ 
 __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(float *__restrict__ x, const float *__restrict__ dx,
                                                              const float *__restrict__ w, int n, float eps,
                                                              uint8_t *__restrict__ xq, size_t d_off, size_t s_off,
-                                                             int nbp, DecodeState *clear_keys, uint32_t *status) {
+                                                             int nbp, DecodeState *clear_keys, uint32_t *status,
+                                                             float *__restrict__ pre) {
   grid_dep_launch();
   grid_dep_wait();
   __shared__ float part[32];
@@ -122,7 +123,9 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(float *__restrict__
   const int nb = n / 32;
   for (int blk = warp; blk < nb; blk += blockDim.x >> 5) {
     const int i = blk * 32 + lane;
-    bad |= quant_block(xb[i] * scale * w[i], lane, v.q, v.d, v.s, blk);
+    const float y = xb[i] * scale * w[i];
+    if (pre) pre[static_cast<int64_t>(b) * n + i] = y;
+    bad |= quant_block(y, lane, v.q, v.d, v.s, blk);
   }
   for (int blk = nb + tid; blk < nbp; blk += blockDim.x) {
     v.d[blk] = 0.f;
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_quant_kernel(float *__restrict__
 // block.
 __global__ void __launch_bounds__(256) silu_quant_kernel(const float *__restrict__ gu, int n_ff,
                                                          uint8_t *__restrict__ hq, size_t d_off, size_t s_off,
-                                                         int nbp, uint32_t *status) {
+                                                         int nbp, uint32_t *status, float *__restrict__ pre) {
   grid_dep_launch();
   grid_dep_wait();
   const int lane = threadIdx.x & 31;
@@ -157,6 +160,7 @@ __global__ void __launch_bounds__(256) silu_quant_kernel(const float *__restrict
   const float *g = gu + static_cast<int64_t>(b) * 2 * n_ff;
   const float gv = g[blk * 32 + lane], uv = g[n_ff + blk * 32 + lane];
   const float h = (gv / (1.0f + expf(-gv))) * uv;
+  if (pre) pre[static_cast<int64_t>(b) * n_ff + blk * 32 + lane] = h;
   if (quant_block(h, lane, v.q, v.d, v.s, blk) && lane == 0) status_or(status, ST_NONFINITE_IN);
 }
 
@@ -166,11 +170,11 @@ __global__ void __launch_bounds__(256) silu_quant_kernel(const float *__restrict
 // (blockIdx.y) of sequence b = blockIdx.z: the G query heads of the group get their bias and
 // RoPE (rope_bias, gpu_ops.cu:9-20: a = v0*c - v1*s, b = v0*s + v1*c over pairs
 // (i, i + HD/2)), the chunk holding `pos` also biases, rotates and stores the new key and
-// value (fp32 cache, as the reference keeps it: gpu_attention.cu:1), and every chunk writes
+// value (fp32 cache as the reference keeps it, gpu_attention.cu:1, or fp16), and every chunk writes
 // unnormalised partials (max, sum of exp, exp-weighted V) for the combine step.  Scores are
 // q.k / sqrt(HD) with an exact expf softmax (fused_attention, gpu_attention.cu:2-26;
 // llm.rs:358-368).
-template <int HD>
+template <int HD, typename KV>
 __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
   extern __shared__ __align__(16) float sm[];
   const int G = a.n_head / a.n_kv;
@@ -217,27 +221,28 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
     const float v0 = r_s[base + j], v1 = r_s[base + j + HD / 2];
     q_s[i] = dd < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x;
   }
-  float *kcache = a.kcache + static_cast<int64_t>(b) * a.cache_seq;
-  float *vcache = a.vcache + static_cast<int64_t>(b) * a.cache_seq;
+  KV *kcache = static_cast<KV *>(a.kcache) + static_cast<int64_t>(b) * a.cache_seq;
+  KV *vcache = static_cast<KV *>(a.vcache) + static_cast<int64_t>(b) * a.cache_seq;
   const size_t cache_head = (static_cast<size_t>(kvh) * a.n_ctx) * HD;
   if (has_new && tid < HD) {
     const int j = tid % (HD / 2);
     const float2 cs = rope[j];
     const float v0 = kn[j], v1 = kn[j + HD / 2];
-    const float k = tid < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x;
-    const float v = kn[HD + tid];
-    kcache[cache_head + static_cast<size_t>(pos) * HD + tid] = k;
-    vcache[cache_head + static_cast<size_t>(pos) * HD + tid] = v;
+    // the new row takes part as the cache holds it (rounded to fp16 in an fp16 cache)
+    const float k = KvIO<KV>::round(tid < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x);
+    const float v = KvIO<KV>::round(kn[HD + tid]);
+    KvIO<KV>::store(kcache + cache_head + static_cast<size_t>(pos) * HD + tid, k);
+    KvIO<KV>::store(vcache + cache_head + static_cast<size_t>(pos) * HD + tid, v);
     ks[(pos - t0) * (HD + 1) + tid] = k;
     vs[(pos - t0) * HD + tid] = v;
   }
   const int n_old = has_new ? nt - 1 : nt;
   {
-    const float4 *kc = reinterpret_cast<const float4 *>(kcache + cache_head + static_cast<size_t>(t0) * HD);
-    const float4 *vc = reinterpret_cast<const float4 *>(vcache + cache_head + static_cast<size_t>(t0) * HD);
+    const KV *kc = kcache + cache_head + static_cast<size_t>(t0) * HD;
+    const KV *vc = vcache + cache_head + static_cast<size_t>(t0) * HD;
     for (int i = tid; i < n_old * (HD / 4); i += blockDim.x) {
       const int t = i / (HD / 4), dd = (i - t * (HD / 4)) * 4;
-      const float4 kv = kc[i], vv = vc[i];
+      const float4 kv = KvIO<KV>::load4(kc + 4 * i), vv = KvIO<KV>::load4(vc + 4 * i);
       float *kd = ks + t * (HD + 1) + dd;
       kd[0] = kv.x;
       kd[1] = kv.y;
@@ -288,7 +293,8 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
 // and quantise the head's HD outputs into the Q8_1 input of the output projection.
 template <int HD>
 __global__ void __launch_bounds__(HD) attn_combine_quant_kernel(AttnParams a, uint8_t *__restrict__ xq,
-                                                                size_t d_off, size_t s_off, int nbp) {
+                                                                size_t d_off, size_t s_off, int nbp,
+                                                                float *__restrict__ pre) {
   grid_dep_launch();
   grid_dep_wait();
   const int G = a.n_head / a.n_kv;
@@ -307,6 +313,7 @@ __global__ void __launch_bounds__(HD) attn_combine_quant_kernel(AttnParams a, ui
     o += e * a.part_o[(ps * G + g) * HD + dd];
   }
   const float v = ns ? o / l : 0.f;
+  if (pre) pre[(static_cast<int64_t>(b) * a.n_head + h) * HD + dd] = v;
   const Q8View q = q8_vec(xq, a.n_head * HD, d_off, s_off, nbp, b);
   const int blk = (h * HD + dd) / 32;
   if (quant_block(v, lane, q.q, q.d, q.s, blk) && lane == 0) status_or(a.status, ST_NONFINITE_IN);
@@ -369,9 +376,12 @@ size_t attn_partial_smem(int group) {
 }
 
 ugb_status init_decode_kernels(ugb_ctx *ctx) {
-  return cuda_status(cudaFuncSetAttribute(attn_partial_kernel<kHeadDim>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8)))));
+  const int smem = static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8)));
+  if (cudaFuncSetAttribute(attn_partial_kernel<kHeadDim, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return UGB_EBACKEND;
+  return cuda_status(cudaFuncSetAttribute(attn_partial_kernel<kHeadDim, __half>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
 }
 
 ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,
@@ -380,28 +390,32 @@ ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int e
 }
 
 ugb_status launch_rmsnorm_quant(cudaStream_t s, bool pdl, float *x, const float *dx, const float *w, int n,
-                                int batch, float eps, uint8_t *xq, DecodeState *clear_keys, uint32_t *status) {
+                                int batch, float eps, uint8_t *xq, DecodeState *clear_keys, uint32_t *status,
+                                float *pre) {
   const Q8Act l = q8act_layout(n, batch);
   return launch_ex(rmsnorm_quant_kernel, dim3(batch), dim3(1024), 0, s, pdl, x, dx, w, n, eps, xq, l.d_off,
-                   l.s_off, static_cast<int>(l.nbp), clear_keys, status);
+                   l.s_off, static_cast<int>(l.nbp), clear_keys, status, pre);
 }
 
 ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff, int batch, uint8_t *hq,
-                             uint32_t *status) {
+                             uint32_t *status, float *pre) {
   const Q8Act l = q8act_layout(n_ff, batch);
   const int warps = static_cast<int>(l.nbp);
   return launch_ex(silu_quant_kernel, dim3((warps + 7) / 8, batch), dim3(256), 0, s, pdl, gu, n_ff, hq, l.d_off,
-                   l.s_off, warps, status);
+                   l.s_off, warps, status, pre);
 }
 
-ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq) {
+ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq, float *pre) {
   const int group = a.n_head / a.n_kv;
-  ugb_status st = launch_ex(attn_partial_kernel<kHeadDim>, dim3(a.n_kv, a.n_split, batch), dim3(256),
-                            attn_partial_smem(group), s, pdl, a);
+  const dim3 grid(a.n_kv, a.n_split, batch);
+  ugb_status st = a.kv16 ? launch_ex(attn_partial_kernel<kHeadDim, __half>, grid, dim3(256),
+                                     attn_partial_smem(group), s, pdl, a)
+                         : launch_ex(attn_partial_kernel<kHeadDim, float>, grid, dim3(256),
+                                     attn_partial_smem(group), s, pdl, a);
   if (st != UGB_OK) return st;
   const Q8Act l = q8act_layout(static_cast<int64_t>(a.n_head) * kHeadDim, batch);
   return launch_ex(attn_combine_quant_kernel<kHeadDim>, dim3(a.n_head, batch), dim3(kHeadDim), 0, s, pdl, a, xq,
-                   l.d_off, l.s_off, static_cast<int>(l.nbp));
+                   l.d_off, l.s_off, static_cast<int>(l.nbp), pre);
 }
 
 ugb_status launch_argmax(cudaStream_t s, bool pdl, const float *logits, int n, int batch, int id0,

@@ -24,12 +24,30 @@ struct DecodeState {
   unsigned long long key[kMaxSeq];  // greedy (value, complemented id) of the last head
 };
 
+// Trace of a decode step (ugb_decoder_set_trace): per layer one record of the fields of
+// ugb.h's UGB_TRACE_* list, each [batch][len] at its own 256-byte aligned offset; record
+// n_layer holds the residual, the output norm and the head's Q8_1 input.  Q8_1 fields use the
+// ugb_q8act layout of their length and the decoder's batch.
+struct TraceMap {
+  uint8_t *base = nullptr;  // null: tracing off
+  uint64_t rec = 0;         // bytes per record
+  uint64_t off[UGB_TRACE_FIELDS] = {};
+  uint64_t bytes[UGB_TRACE_FIELDS] = {};
+  // Q8_1 sub-offsets (scales, sums) of the fields of length n_embd, n_head*HD and n_ff
+  uint32_t d_e = 0, s_e = 0, d_q = 0, s_q = 0, d_f = 0, s_f = 0;
+  __host__ __device__ uint8_t *at(int layer, int field) const {
+    return base ? base + rec * static_cast<uint64_t>(layer) + off[field] : nullptr;
+  }
+  __host__ __device__ float *f32(int layer, int field) const { return reinterpret_cast<float *>(at(layer, field)); }
+};
+
 struct AttnParams {
   const float *qkv;       // [batch][n_head*HD (q) ; n_kv*HD (k) ; n_kv*HD (v)] of this layer
   const float *bias;      // [q ; k ; v] rows of this layer, or null
   const float2 *rope;     // [n_ctx][HD/2] (cos, sin)
-  float *kcache;          // sequence 0, this layer: [n_kv][n_ctx][HD] (rotated keys)
-  float *vcache;
+  void *kcache;           // sequence 0, this layer: [n_kv][n_ctx][HD] (rotated keys), f32 or f16
+  void *vcache;
+  bool kv16;              // the cache holds fp16 (rounded to nearest even on write)
   int64_t cache_seq;      // elements between sequences' caches
   float *part_m, *part_l; // [batch][n_kv][n_split][G]
   float *part_o;          // [batch][n_kv][n_split][G][HD]
@@ -40,13 +58,16 @@ struct AttnParams {
 
 size_t attn_partial_smem(int group);
 
+// `pre` (may be null): [batch][n] copy of the values before quantisation, for the trace.
 ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,
                         int batch, DecodeState *state, float *x, uint32_t *status);
 ugb_status launch_rmsnorm_quant(cudaStream_t s, bool pdl, float *x, const float *dx, const float *w, int n,
-                                int batch, float eps, uint8_t *xq, DecodeState *clear_keys, uint32_t *status);
+                                int batch, float eps, uint8_t *xq, DecodeState *clear_keys, uint32_t *status,
+                                float *pre = nullptr);
 ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff, int batch, uint8_t *hq,
-                             uint32_t *status);
-ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq);
+                             uint32_t *status, float *pre = nullptr);
+ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq,
+                            float *pre = nullptr);
 ugb_status launch_argmax(cudaStream_t s, bool pdl, const float *logits, int n, int batch, int id0,
                          DecodeState *state, int sm_count);
 ugb_status init_decode_kernels(ugb_ctx *ctx);
@@ -78,7 +99,7 @@ struct TokenStep {
   float *dxo, *dxd;           // O and down projections (read by the next phase's residual add)
   float *logits;              // [n_vocab]
   uint8_t *hq;                // Q8_1 of SiLU(gate) * up: quants [n_ff] | scales | sums
-  float *kcache, *vcache;     // [n_layer][n_kv][n_ctx][HD]
+  void *kcache, *vcache;      // [n_layer][n_kv][n_ctx][HD], f32 or (kv16) f16
   const float2 *rope;         // [n_ctx][HD/2]
   float *part_m, *part_l, *part_o;  // attention partials, [n_kv][n_split][G](.[HD])
   DecodeState *state;
@@ -88,6 +109,10 @@ struct TokenStep {
   float eps;
   uint32_t rb_e, rb_q, rb_f, rb_h, rb_tok;  // row bytes at K = n_embd, n_head*HD, n_ff; head; embedding
   int gu_blocks;              // FFN blocks a CTA holds at most
+  bool kv16;                  // fp16 KV cache
+  uint32_t unreachable;       // test hook: extra arrivals the first attention wait needs (0 normally)
+  uint64_t wait_ns;           // limit of every wait on other CTAs' progress
+  TraceMap trace;             // per-layer trace of the step (tracing off: trace.base null)
   uint32_t o_xres, o_xq, o_xd, o_xs, o_scr, o_layers, o_gu, o_ring, ring_bytes;
 };
 

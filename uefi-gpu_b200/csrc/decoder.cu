@@ -34,7 +34,8 @@ struct ugb_decoder {
   float *rlogits = nullptr, *rweights = nullptr;
   int32_t *rids = nullptr;
   uint8_t *xq = nullptr, *attq = nullptr, *hq = nullptr;
-  float *kcache = nullptr, *vcache = nullptr;
+  void *kcache = nullptr, *vcache = nullptr;  // f32 or (kv16) f16
+  bool kv16 = false;
   int64_t cache_seq = 0;   // elements of one sequence's cache (all layers)
   float2 *rope = nullptr;
   float *part_m = nullptr, *part_l = nullptr, *part_o = nullptr;
@@ -55,6 +56,9 @@ struct ugb_decoder {
   ugb::TokLayer *tok_layers = nullptr;
   int path = UGB_PATH_AUTO;
   ugb_comm *comm = nullptr;
+  ugb::TraceMap trace;     // step trace (ugb_decoder_set_trace); base null: off
+  uint64_t wait_ns = ugb::kWaitLimitNs;  // token kernel: limit of each wait on other CTAs
+  uint32_t unreachable = 0;              // token kernel test hook (ugb_decoder_test_unreachable_wait)
   // replay
   cudaStream_t cap = nullptr;
   cudaGraph_t graph = nullptr;
@@ -78,6 +82,7 @@ ugb_status check_config(const ugb_ctx *ctx, const ugb_decoder_config &c) {
       c.batch > kMaxSeq)
     return UGB_ESHAPE;
   if (!kind_ok(c.kind) || !kind_ok(c.head_kind)) return UGB_EQUANT;
+  if (c.kv_type != UGB_F32 && c.kv_type != UGB_F16) return UGB_EQUANT;
   if (ugb_row_bytes(c.kind, c.n_embd) < 0 || ugb_row_bytes(c.kind, static_cast<int64_t>(c.n_head) * c.head_dim) < 0 ||
       ugb_row_bytes(c.head_kind, c.n_embd) < 0)
     return UGB_ESHAPE;
@@ -107,13 +112,46 @@ void free_graph(ugb_decoder *d) {
 void free_all(ugb_decoder *d) {
   void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->rlogits, d->rweights, d->rids, d->xq, d->attq,
                   d->hq, d->kcache, d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->moe_ws, d->state,
-                  d->bias, d->dxd, d->tok_hq, d->tok_sync, d->tok_layers};
+                  d->bias, d->dxd, d->tok_hq, d->tok_sync, d->tok_layers, d->trace.base};
   for (void *b : bufs)
     if (b) cudaFree(b);
   for (void *b : d->owned) cudaFree(b);
   if (d->state_host) cudaFreeHost(d->state_host);
   free_graph(d);
   if (d->cap) cudaStreamDestroy(d->cap);
+}
+
+// Field sizes and offsets of one trace record (the buffer itself is allocated by set_trace).
+void plan_trace(ugb_decoder *d) {
+  const ugb_decoder_config &c = d->cfg;
+  const int64_t B = d->batch, E = c.n_embd, Q = static_cast<int64_t>(c.n_head) * c.head_dim;
+  const int64_t brow = Q + 2 * static_cast<int64_t>(c.n_head_kv) * c.head_dim;
+  const int64_t F = d->moe ? 0 : c.n_ff;
+  const Q8Act xe = q8act_layout(E, B), xq = q8act_layout(Q, B);
+  uint64_t *n = d->trace.bytes;
+  n[UGB_TRACE_X] = n[UGB_TRACE_ATTN_NORM] = n[UGB_TRACE_O] = n[UGB_TRACE_FFN_NORM] = n[UGB_TRACE_DOWN] = B * E * 4;
+  n[UGB_TRACE_ATTN_XQ] = n[UGB_TRACE_FFN_XQ] = xe.bytes;
+  n[UGB_TRACE_QKV] = B * brow * 4;
+  n[UGB_TRACE_ATT] = B * Q * 4;
+  n[UGB_TRACE_ATT_XQ] = xq.bytes;
+  n[UGB_TRACE_GATE_UP] = B * 2 * F * 4;
+  n[UGB_TRACE_H] = B * F * 4;
+  n[UGB_TRACE_H_XQ] = F ? q8act_layout(F, B).bytes : 0;
+  uint64_t o = 0;
+  for (int f = 0; f < UGB_TRACE_FIELDS; ++f) {
+    d->trace.off[f] = o;
+    o += round_up(n[f], 256);
+  }
+  d->trace.rec = o;
+  d->trace.d_e = static_cast<uint32_t>(xe.d_off);
+  d->trace.s_e = static_cast<uint32_t>(xe.s_off);
+  d->trace.d_q = static_cast<uint32_t>(xq.d_off);
+  d->trace.s_q = static_cast<uint32_t>(xq.s_off);
+  if (F) {
+    const Q8Act xf = q8act_layout(F, B);
+    d->trace.d_f = static_cast<uint32_t>(xf.d_off);
+    d->trace.s_f = static_cast<uint32_t>(xf.s_off);
+  }
 }
 
 }  // namespace
@@ -143,6 +181,8 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
   d->n_split = (c.n_ctx + kAttnChunk - 1) / kAttnChunk;
   d->cache_seq = static_cast<int64_t>(c.n_layer) * kvrows * c.n_ctx;
   const size_t kv = static_cast<size_t>(B) * d->cache_seq;
+  d->kv16 = c.kv_type == UGB_F16;
+  const size_t kv_bytes = kv * (d->kv16 ? sizeof(__half) : sizeof(float));
   const size_t parts = static_cast<size_t>(B) * c.n_head_kv * d->n_split * group;
   bool ok = dalloc(&d->x, static_cast<size_t>(B) * c.n_embd) == UGB_OK &&
             dalloc(&d->dx, static_cast<size_t>(B) * c.n_embd) == UGB_OK &&
@@ -150,7 +190,7 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
             dalloc(&d->logits, static_cast<size_t>(B) * d->n_vocab_local) == UGB_OK &&
             dalloc(&d->xq, q8act_layout(c.n_embd, B).bytes) == UGB_OK &&
             dalloc(&d->attq, q8act_layout(qrows, B).bytes) == UGB_OK &&
-            dalloc(&d->kcache, kv) == UGB_OK && dalloc(&d->vcache, kv) == UGB_OK &&
+            cudaMalloc(&d->kcache, kv_bytes) == cudaSuccess && cudaMalloc(&d->vcache, kv_bytes) == cudaSuccess &&
             dalloc(&d->rope, static_cast<size_t>(c.n_ctx) * (c.head_dim / 2)) == UGB_OK &&
             dalloc(&d->part_m, parts) == UGB_OK && dalloc(&d->part_l, parts) == UGB_OK &&
             dalloc(&d->part_o, parts * c.head_dim) == UGB_OK && dalloc(&d->state, 1) == UGB_OK &&
@@ -186,8 +226,7 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
       }
     ok = cudaMemcpy(d->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) == cudaSuccess &&
          cudaMemset(d->state, 0, sizeof(DecodeState)) == cudaSuccess &&
-         cudaMemset(d->kcache, 0, kv * sizeof(float)) == cudaSuccess &&
-         cudaMemset(d->vcache, 0, kv * sizeof(float)) == cudaSuccess &&
+         cudaMemset(d->kcache, 0, kv_bytes) == cudaSuccess && cudaMemset(d->vcache, 0, kv_bytes) == cudaSuccess &&
          cudaMemset(d->dx, 0, static_cast<size_t>(B) * c.n_embd * sizeof(float)) == cudaSuccess;
   }
   if (!ok) {
@@ -195,6 +234,7 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
     delete d;
     return UGB_EBACKEND;
   }
+  plan_trace(d);
   *out = d;
   return UGB_OK;
 }
@@ -430,6 +470,10 @@ bool token_step_of(const ugb_decoder *d, TokenStep &p) {
   p.hq = d->tok_hq;
   p.kcache = d->kcache;
   p.vcache = d->vcache;
+  p.kv16 = d->kv16;
+  p.trace = d->trace;
+  p.wait_ns = d->wait_ns;
+  p.unreachable = d->unreachable;
   p.rope = d->rope;
   p.part_m = d->part_m;
   p.part_l = d->part_l;
@@ -496,7 +540,13 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
   const int64_t qrows = static_cast<int64_t>(c.n_head) * c.head_dim;
   const int64_t kvrows = static_cast<int64_t>(c.n_head_kv) * c.head_dim;
   const int64_t brow = qrows + 2 * kvrows;
-  const size_t kv_layer = static_cast<size_t>(kvrows) * c.n_ctx;
+  const size_t kv_layer = static_cast<size_t>(kvrows) * c.n_ctx * (d->kv16 ? sizeof(__half) : sizeof(float));
+  const TraceMap &T = d->trace;
+  // Tracing: copy a device buffer into field f of record l after the kernel that wrote it.
+  auto tcopy = [&](int l, int f, const void *src) {
+    return T.base ? cuda_status(cudaMemcpyAsync(T.at(l, f), src, T.bytes[f], cudaMemcpyDeviceToDevice, stream))
+                  : UGB_OK;
+  };
   const bool ep_reduce = d->moe && d->comm && d->n_expert_local < c.n_expert;
   const bool vocab_reduce = d->comm && d->n_vocab_local < c.n_vocab;
   ugb_status st = launch_embed(stream, false, static_cast<const uint8_t *>(d->w.tok_embd), c.n_embd, c.n_vocab,
@@ -504,7 +554,10 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
   for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
     const ugb_layer_weights &L = d->layers[l];
     st = launch_rmsnorm_quant(stream, true, d->x, l == 0 ? nullptr : d->dx, static_cast<const float *>(L.attn_norm),
-                              c.n_embd, B, c.norm_eps, d->xq, l == 0 ? d->state : nullptr, status);
+                              c.n_embd, B, c.norm_eps, d->xq, l == 0 ? d->state : nullptr, status,
+                              T.f32(l, UGB_TRACE_ATTN_NORM));
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_X, d->x);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_ATTN_XQ, d->xq);
     if (st != UGB_OK) break;
     MatvecArgs a = mv_args(c.kind, c.n_embd, brow, B, d->xq, d->qkv);
     a.nseg = 3;
@@ -514,13 +567,15 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
     a.seg_rows[0] = qrows;
     a.seg_rows[1] = a.seg_rows[2] = kvrows;
     st = launch_matvec(ctx, stream, a);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_QKV, d->qkv);
     if (st != UGB_OK) break;
     AttnParams ap{};
     ap.qkv = d->qkv;
     ap.bias = d->bias ? d->bias + static_cast<size_t>(l) * brow : nullptr;
     ap.rope = d->rope;
-    ap.kcache = d->kcache + kv_layer * l;
-    ap.vcache = d->vcache + kv_layer * l;
+    ap.kcache = static_cast<uint8_t *>(d->kcache) + kv_layer * l;
+    ap.vcache = static_cast<uint8_t *>(d->vcache) + kv_layer * l;
+    ap.kv16 = d->kv16;
     ap.cache_seq = d->cache_seq;
     ap.part_m = d->part_m;
     ap.part_l = d->part_l;
@@ -531,14 +586,17 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
     ap.n_ctx = c.n_ctx;
     ap.n_split = d->n_split;
     ap.status = status;
-    st = launch_attention(stream, true, ap, B, d->attq);
+    st = launch_attention(stream, true, ap, B, d->attq, T.f32(l, UGB_TRACE_ATT));
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_ATT_XQ, d->attq);
     if (st != UGB_OK) break;
     a = mv_args(c.kind, qrows, c.n_embd, B, d->attq, d->dx);
     a.w = static_cast<const uint8_t *>(L.wo);
     st = launch_matvec(ctx, stream, a);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_O, d->dx);
     if (st != UGB_OK) break;
     st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(L.ffn_norm), c.n_embd, B,
-                              c.norm_eps, d->xq, nullptr, status);
+                              c.norm_eps, d->xq, nullptr, status, T.f32(l, UGB_TRACE_FFN_NORM));
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_FFN_XQ, d->xq);
     if (st != UGB_OK) break;
     if (d->moe) {
       a = mv_args(c.kind, c.n_embd, c.n_expert, B, d->xq, d->rlogits);
@@ -569,6 +627,7 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
       st = launch_moe_experts(ctx, stream, m);
       if (st == UGB_OK && ep_reduce)
         st = comm_allreduce_sum_f32(d->comm, d->dx, static_cast<size_t>(B) * c.n_embd, stream);
+      if (st == UGB_OK) st = tcopy(l, UGB_TRACE_DOWN, d->dx);
     } else {
       a = mv_args(c.kind, c.n_embd, 2 * static_cast<int64_t>(c.n_ff), B, d->xq, d->gu);
       a.nseg = 2;
@@ -576,17 +635,22 @@ extern "C" ugb_status ugb_decoder_step(ugb_decoder *d, ugb_stream stream) {
       a.ws[1] = static_cast<const uint8_t *>(L.w_up);
       a.seg_rows[0] = a.seg_rows[1] = c.n_ff;
       st = launch_matvec(ctx, stream, a);
+      if (st == UGB_OK) st = tcopy(l, UGB_TRACE_GATE_UP, d->gu);
       if (st != UGB_OK) break;
-      st = launch_silu_quant(stream, true, d->gu, c.n_ff, B, d->hq, status);
+      st = launch_silu_quant(stream, true, d->gu, c.n_ff, B, d->hq, status, T.f32(l, UGB_TRACE_H));
+      if (st == UGB_OK) st = tcopy(l, UGB_TRACE_H_XQ, d->hq);
       if (st != UGB_OK) break;
       a = mv_args(c.kind, c.n_ff, c.n_embd, B, d->hq, d->dx);
       a.w = static_cast<const uint8_t *>(L.w_down);
       st = launch_matvec(ctx, stream, a);
+      if (st == UGB_OK) st = tcopy(l, UGB_TRACE_DOWN, d->dx);
     }
   }
   if (st != UGB_OK) return st;
   st = launch_rmsnorm_quant(stream, true, d->x, d->dx, static_cast<const float *>(d->w.output_norm), c.n_embd, B,
-                            c.norm_eps, d->xq, nullptr, status);
+                            c.norm_eps, d->xq, nullptr, status, T.f32(c.n_layer, UGB_TRACE_ATTN_NORM));
+  if (st == UGB_OK) st = tcopy(c.n_layer, UGB_TRACE_X, d->x);
+  if (st == UGB_OK) st = tcopy(c.n_layer, UGB_TRACE_ATTN_XQ, d->xq);
   if (st != UGB_OK) return st;
   MatvecArgs a = mv_args(c.head_kind, c.n_embd, d->n_vocab_local, B, d->xq, d->logits);
   a.w = static_cast<const uint8_t *>(d->w.output);
@@ -667,24 +731,108 @@ extern "C" ugb_status ugb_decoder_logits(ugb_decoder *d, ugb_stream stream, floa
   return cuda_status(cudaStreamSynchronize(stream));
 }
 
-extern "C" ugb_status ugb_decoder_read_kv(ugb_decoder *d, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
-                                          int32_t count, float *k_host, float *v_host) {
-  if (!d || !k_host || !v_host) return UGB_ECONTEXT;
+namespace {
+
+// Copy `count` cached positions from `pos` of one sequence and layer between the cache and host
+// rows [n_kv][count][head_dim] of fp32 (converted to or from fp16 for an fp16 cache).
+ugb_status kv_copy(ugb_decoder *d, cudaStream_t stream, int32_t seq, int32_t layer, int32_t pos, int32_t count,
+                   float *k_out, float *v_out, const float *k_in, const float *v_in) {
   const ugb_decoder_config &c = d->cfg;
   if (seq < 0 || seq >= d->batch || layer < 0 || layer >= c.n_layer || pos < 0 || count < 1 || count > c.n_ctx - pos)
     return UGB_ESHAPE;
   cudaSetDevice(d->ctx->device);
   const size_t hd = static_cast<size_t>(c.head_dim);
-  const size_t off = static_cast<size_t>(seq) * d->cache_seq + static_cast<size_t>(layer) * c.n_head_kv * c.n_ctx * hd;
-  const size_t row = count * hd * sizeof(float);
+  const size_t esz = d->kv16 ? sizeof(__half) : sizeof(float);
+  const size_t off = static_cast<size_t>(seq) * d->cache_seq + static_cast<size_t>(layer) * c.n_head_kv * c.n_ctx * hd +
+                     static_cast<size_t>(pos) * hd;
+  const size_t n = static_cast<size_t>(c.n_head_kv) * count * hd;
+  const size_t row = count * hd * esz, pitch = c.n_ctx * hd * esz;
+  const bool out = k_out != nullptr;
+  std::vector<__half> stage(d->kv16 ? n : 0);
   for (int which = 0; which < 2; ++which) {
-    const float *src = (which ? d->vcache : d->kcache) + off + static_cast<size_t>(pos) * hd;
-    float *dst = which ? v_host : k_host;
-    // one row per KV head: [n_kv][n_ctx][hd] (pitch n_ctx*hd) -> [n_kv][count][hd]
-    if (cudaMemcpy2DAsync(dst, row, src, c.n_ctx * hd * sizeof(float), row, c.n_head_kv, cudaMemcpyDeviceToHost,
-                          stream) != cudaSuccess)
-      return UGB_EBACKEND;
+    uint8_t *dev = static_cast<uint8_t *>(which ? d->vcache : d->kcache) + off * esz;
+    float *host_out = which ? v_out : k_out;
+    const float *host_in = which ? v_in : k_in;
+    void *host = d->kv16 ? static_cast<void *>(stage.data()) : (out ? static_cast<void *>(host_out) : const_cast<float *>(host_in));
+    if (!out && d->kv16)
+      for (size_t i = 0; i < n; ++i) stage[i] = __float2half_rn(host_in[i]);
+    // one row per KV head: [n_kv][n_ctx][hd] (pitch n_ctx*hd) <-> [n_kv][count][hd]
+    const cudaError_t e = out ? cudaMemcpy2DAsync(host, row, dev, pitch, row, c.n_head_kv, cudaMemcpyDeviceToHost, stream)
+                              : cudaMemcpy2DAsync(dev, pitch, host, row, row, c.n_head_kv, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess || cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
+    if (out && d->kv16)
+      for (size_t i = 0; i < n; ++i) host_out[i] = __half2float(stage[i]);
   }
+  return UGB_OK;
+}
+
+}  // namespace
+
+extern "C" ugb_status ugb_decoder_read_kv(ugb_decoder *d, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
+                                          int32_t count, float *k_host, float *v_host) {
+  if (!d || !k_host || !v_host) return UGB_ECONTEXT;
+  return kv_copy(d, stream, seq, layer, pos, count, k_host, v_host, nullptr, nullptr);
+}
+
+extern "C" ugb_status ugb_decoder_write_kv(ugb_decoder *d, ugb_stream stream, int32_t seq, int32_t layer, int32_t pos,
+                                           int32_t count, const float *k_host, const float *v_host) {
+  if (!d || !k_host || !v_host) return UGB_ECONTEXT;
+  return kv_copy(d, stream, seq, layer, pos, count, nullptr, nullptr, k_host, v_host);
+}
+
+extern "C" ugb_status ugb_decoder_set_trace(ugb_decoder *d, int32_t enable) {
+  if (!d) return UGB_ECONTEXT;
+  cudaSetDevice(d->ctx->device);
+  const size_t bytes = d->trace.rec * (static_cast<size_t>(d->cfg.n_layer) + 1);
+  if (enable && !d->trace.base) {
+    void *p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return UGB_EBACKEND;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+      cudaFree(p);
+      return UGB_EBACKEND;
+    }
+    d->trace.base = static_cast<uint8_t *>(p);
+    free_graph(d);  // the captured step has no trace stores
+  } else if (!enable && d->trace.base) {
+    if (cudaDeviceSynchronize() != cudaSuccess) return UGB_EBACKEND;
+    cudaFree(d->trace.base);
+    d->trace.base = nullptr;
+    free_graph(d);
+  }
+  return UGB_OK;
+}
+
+extern "C" ugb_status ugb_decoder_set_wait_limit(ugb_decoder *d, uint64_t ns) {
+  if (!d) return UGB_ECONTEXT;
+  if (ns < 1000 || ns > 60ull * 1000000000ull) return UGB_ESHAPE;
+  d->wait_ns = ns;
+  free_graph(d);  // the captured step holds the old limit
+  return UGB_OK;
+}
+
+extern "C" ugb_status ugb_decoder_test_unreachable_wait(ugb_decoder *d, int32_t enable) {
+  if (!d) return UGB_ECONTEXT;
+  d->unreachable = enable ? 1u : 0u;
+  free_graph(d);
+  return UGB_OK;
+}
+
+extern "C" size_t ugb_decoder_trace_bytes(const ugb_decoder *d, int32_t field) {
+  if (!d || field < 0 || field >= UGB_TRACE_FIELDS) return 0;
+  return d->trace.bytes[field];
+}
+
+extern "C" ugb_status ugb_decoder_read_trace(ugb_decoder *d, ugb_stream stream, int32_t layer, int32_t field,
+                                             void *host, size_t bytes) {
+  if (!d || !host) return UGB_ECONTEXT;
+  if (!d->trace.base) return UGB_ECONTEXT;
+  if (field < 0 || field >= UGB_TRACE_FIELDS || layer < 0 || layer > d->cfg.n_layer) return UGB_ESHAPE;
+  if (layer == d->cfg.n_layer && field != UGB_TRACE_X && field != UGB_TRACE_ATTN_NORM && field != UGB_TRACE_ATTN_XQ)
+    return UGB_ESHAPE;
+  if (bytes != d->trace.bytes[field] || bytes == 0) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  if (cudaMemcpyAsync(host, d->trace.at(layer, field), bytes, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
   return cuda_status(cudaStreamSynchronize(stream));
 }
 

@@ -2,6 +2,7 @@
 // (decode.cu) and the persistent token kernel (token.cu): Q8_1 block quantisation of a
 // warp-held block, the greedy key, and warp reductions of row partials.
 #pragma once
+#include <cuda_fp16.h>
 #include <cfloat>
 #include <cmath>
 
@@ -107,6 +108,30 @@ __device__ __forceinline__ bool quant_blocks(const float (&v)[NB], const int (&b
   }
   return __any_sync(0xffffffffu, bad);
 }
+
+// Element access of a KV cache of fp32 or fp16 (round to nearest even on store).  round()
+// is the value a store followed by a load gives back.
+template <typename KV>
+struct KvIO;
+template <>
+struct KvIO<float> {
+  static __device__ __forceinline__ float round(float v) { return v; }
+  static __device__ __forceinline__ void store(float *p, float v) { *p = v; }
+  static __device__ __forceinline__ float load(const float *p) { return *p; }
+  static __device__ __forceinline__ float4 load4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+};
+template <>
+struct KvIO<__half> {
+  static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+  static __device__ __forceinline__ void store(__half *p, float v) { *p = __float2half_rn(v); }
+  static __device__ __forceinline__ float load(const __half *p) { return __half2float(*p); }
+  static __device__ __forceinline__ float4 load4(const __half *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+};
 
 // Greedy key: value bits made order-preserving as an unsigned integer, then the complemented
 // id, so the larger key is the larger value and, for equal values, the lower id (the

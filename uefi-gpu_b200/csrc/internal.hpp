@@ -84,6 +84,12 @@ ugb_status comm_allreduce_sum_f32(ugb_comm *c, float *buf, size_t n, cudaStream_
 ugb_status comm_allreduce_max_u64(ugb_comm *c, unsigned long long *buf, size_t n, cudaStream_t stream);
 int comm_world(const ugb_comm *c);
 
+// Entry-point prologue: a live context, and its device made current for this thread.
+ugb_status check_ctx(ugb_ctx *ctx);
+// Synchronise `stream`, return the context's device status bits (and clear them) as a status
+// code: TIMEOUT, then NONFINITE, then BADARG (as UGB_ESHAPE).
+ugb_status read_status_bits(ugb_ctx *ctx, cudaStream_t stream, uint32_t *bits);
+
 // Validation shared by entry points: kind supported by the matvec kernels, k a multiple of
 // its block, row_bytes consistent.
 ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_t k, int64_t m);

@@ -42,13 +42,14 @@ constexpr int kMaxDevices = 64;
 std::mutex g_addr_mu;
 void *g_addr[kMaxDevices] = {};
 
-// Address of the scratch array on ctx's device, looked up on the first call for that device
-// (with the device current) and cached.
-ugb_status scratch_address(ugb_ctx *ctx, uint8_t **out) {
+// Address of the scratch array on the current device (ctx's, made current by check_ctx), looked
+// up on the first call for that device and cached for the life of the process.  The cache
+// assumes the device's primary context lives that long: after cudaDeviceReset the array would
+// move, and this form must not be used again in that process.
+ugb_status scratch_address(const ugb_ctx *ctx, uint8_t **out) {
   if (ctx->device < 0 || ctx->device >= kMaxDevices) return UGB_ECONTEXT;
   std::lock_guard<std::mutex> lock(g_addr_mu);
   if (!g_addr[ctx->device]) {
-    if (cudaSetDevice(ctx->device) != cudaSuccess) return UGB_EBACKEND;
     void *p = nullptr;
     if (cudaGetSymbolAddress(&p, g_linear_scratch) != cudaSuccess || !p) return UGB_EBACKEND;
     g_addr[ctx->device] = p;
@@ -65,8 +66,9 @@ using namespace ugb;
 extern "C" ugb_status ugb_linear_static(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const void *w_dev,
                                         int64_t row_bytes, const float *x_host, float *y_host, int64_t k,
                                         int64_t m) {
-  if (!ctx || !ctx->status) return UGB_ECONTEXT;
-  ugb_status st = check_weights(kind, w_dev, row_bytes, k, m);
+  ugb_status st = check_ctx(ctx);  // ctx's device current on every call, as every entry point
+  if (st != UGB_OK) return st;
+  st = check_weights(kind, w_dev, row_bytes, k, m);
   if (st != UGB_OK) return st;
   if (k > kStaticMaxK || m > kStaticMaxM) return UGB_ESHAPE;  // beyond the fixed scratch
   if (!x_host || !y_host) return UGB_EALIGN;
@@ -95,13 +97,7 @@ extern "C" ugb_status ugb_linear_static(ugb_ctx *ctx, ugb_stream stream, uint32_
   a.batch = 1;
   st = launch_matvec(ctx, stream, a);
   if (st != UGB_OK) return st;
-  if (cudaMemcpyAsync(y_host, y_dev, static_cast<size_t>(m) * 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-      cudaMemcpyAsync(ctx->status_host, ctx->status, 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
-      cudaMemsetAsync(ctx->status, 0, 4, stream) != cudaSuccess || cudaStreamSynchronize(stream) != cudaSuccess)
+  if (cudaMemcpyAsync(y_host, y_dev, static_cast<size_t>(m) * 4, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
     return UGB_EBACKEND;
-  const uint32_t bits = *ctx->status_host;
-  if (bits & ST_TIMEOUT) return UGB_ETIMEOUT;
-  if (bits & (ST_NONFINITE_IN | ST_NONFINITE_OUT)) return UGB_ENONFINITE;
-  if (bits & ST_BADARG) return UGB_ESHAPE;
-  return UGB_OK;
+  return read_status_bits(ctx, stream, nullptr);  // synchronises the stream
 }

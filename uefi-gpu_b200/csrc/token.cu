@@ -108,7 +108,7 @@ __device__ bool spin_until(const TokenStep &p, int which, uint32_t target) {
     }
     if ((n & 15) == 0) {
       if (aborted(p)) return false;
-      if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      if (globaltimer_ns() - t0 > p.wait_ns) {
         abort_all(p);
         return false;
       }
@@ -142,7 +142,7 @@ __device__ bool mbar_wait_step(const TokenStep &p, uint32_t bar, uint32_t parity
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (aborted(p)) return false;
-    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+    if (globaltimer_ns() - t0 > p.wait_ns) {
       abort_all(p);
       return false;
     }
@@ -465,7 +465,11 @@ constexpr int kMaxEmbdPer = 16;  // n_embd <= 4096 = 16 * 256
 // x (shared) += dx (global, written by other CTAs) when dx is given; then the RMSNorm of x times
 // w, Q8_1-quantised into the shared activation (fused_resnorm + quant_act, gpu_fused.cu:28-35,
 // gpu_dp4a.cu:23-31).  Sum of squares in a fixed order.
-__device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const float *dx, const float *w) {
+// Tracing (CTA 0 only, else rec < 0): the residual, the norm output and its Q8_1 go to fields X,
+// ATTN_NORM / FFN_NORM (fn) and the Q8_1 field after it of trace record `rec`.
+template <bool TRACE>
+__device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const float *dx, const float *w,
+                           int rec, int fn) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = p.n_embd;
   float *x = reinterpret_cast<float *>(smem + p.o_xres);
@@ -477,6 +481,7 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
     d[k] = dx && i < n ? __ldcg(dx + i) : 0.f;
     wv[k] = b < n / 32 ? w[b * 32 + lane] : 0.f;
   }
+  float *tx = TRACE && rec >= 0 ? p.trace.f32(rec, UGB_TRACE_X) : nullptr;
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
@@ -484,6 +489,7 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
     if (i < n) {
       const float v = x[i] + d[k];
       x[i] = v;
+      if (TRACE && tx) tx[i] = v;
       ss += v * v;
     }
   }
@@ -513,6 +519,15 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
         v[k] = live[k] ? x[b[k] * 32 + lane] * scale * wv[k0 + k] : 0.f;
       }
       bad |= quant_blocks<kQ>(v, b, live, lane, q, qd, qs);
+      if (TRACE && rec >= 0) {  // the same arithmetic again, into the trace
+        float *tn = p.trace.f32(rec, fn);
+        uint8_t *tq = p.trace.at(rec, fn + 1);
+#pragma unroll
+        for (int k = 0; k < kQ; ++k)
+          if (live[k]) tn[b[k] * 32 + lane] = v[k];
+        quant_blocks<kQ>(v, b, live, lane, reinterpret_cast<int8_t *>(tq), reinterpret_cast<float *>(tq + p.trace.d_e),
+                         reinterpret_cast<int32_t *>(tq + p.trace.s_e));
+      }
     }
   }
   if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
@@ -521,15 +536,17 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
 
 // Ask L2 for the cached keys and values an attention unit of layer l will read (positions before
 // pos of its chunk), so phase B finds them there instead of in HBM.  One thread.
+template <typename KV>
 __device__ __forceinline__ void prefetch_unit(const TokenStep &p, int l, int kvh, int c, int pos) {
   constexpr int HD = kHeadDim;
   const int t0 = c * kAttnChunk;
   const int n_old = min(kAttnChunk, pos - t0);  // the row at pos is written in phase B
   if (n_old <= 0) return;
   const size_t row0 = ((static_cast<size_t>(l) * p.n_kv + kvh) * p.n_ctx + t0) * HD;
-  const uint32_t bytes = static_cast<uint32_t>(n_old) * HD * 4;
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.kcache + row0), "r"(bytes) : "memory");
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.vcache + row0), "r"(bytes) : "memory");
+  const uint32_t bytes = static_cast<uint32_t>(n_old) * HD * sizeof(KV);
+  const KV *k = static_cast<const KV *>(p.kcache) + row0, *v = static_cast<const KV *>(p.vcache) + row0;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(k), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(v), "r"(bytes) : "memory");
 }
 
 // One attention unit: KV head kvh, context chunk c (positions [64 c, 64 c + nt)) and query
@@ -545,6 +562,7 @@ constexpr int kMaxGroup = 4;
 
 __host__ __device__ constexpr int attn_subgroups(int G) { return (G + kMaxGroup - 1) / kMaxGroup; }
 
+template <typename KV>
 __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, int l, int kvh, int c, int sg,
                           int pos) {
   constexpr int HD = kHeadDim, C = kAttnChunk, GM = kMaxGroup;
@@ -560,7 +578,7 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
   const bool has_new = pos < t0 + C;
   const float2 *rope = p.rope + static_cast<size_t>(pos) * (HD / 2);
   const size_t cache_head = (static_cast<size_t>(l) * p.n_kv + kvh) * p.n_ctx * HD;
-  float *kcache = p.kcache + cache_head, *vcache = p.vcache + cache_head;
+  KV *kcache = static_cast<KV *>(p.kcache) + cache_head, *vcache = static_cast<KV *>(p.vcache) + cache_head;
   // Threads [0, GM*64) take rotation pair (g, j) = (tid / 64, tid % 64) of the padded
   // subgroup; in the chunk holding pos, threads [GM*64, GM*64 + 64) take key pair j and the next
   // HD threads one value element each.  Every load is issued before any is used.
@@ -579,18 +597,19 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
     const float b0 = bias ? bias[krow] : 0.f, b1 = bias ? bias[krow + HD / 2] : 0.f;
     const float k0 = __ldcg(p.qkv + krow) + b0, k1 = __ldcg(p.qkv + krow + HD / 2) + b1;
     const float2 cs = rope[j];
-    const float a = k0 * cs.x - k1 * cs.y, b = k0 * cs.y + k1 * cs.x;
+    // the new row takes part as the cache holds it (rounded to fp16 in an fp16 cache)
+    const float a = KvIO<KV>::round(k0 * cs.x - k1 * cs.y), b = KvIO<KV>::round(k0 * cs.y + k1 * cs.x);
     kn[j] = a;
     kn[j + HD / 2] = b;
     if (sg == 0) {
-      kcache[static_cast<size_t>(pos) * HD + j] = a;
-      kcache[static_cast<size_t>(pos) * HD + j + HD / 2] = b;
+      KvIO<KV>::store(kcache + static_cast<size_t>(pos) * HD + j, a);
+      KvIO<KV>::store(kcache + static_cast<size_t>(pos) * HD + j + HD / 2, b);
     }
   } else if (has_new && tid < GM * HD / 2 + HD / 2 + HD) {
     const int dd = tid - GM * HD / 2 - HD / 2, vrow = qr + kr + kvh * HD + dd;
-    const float v = __ldcg(p.qkv + vrow) + (bias ? bias[vrow] : 0.f);
+    const float v = KvIO<KV>::round(__ldcg(p.qkv + vrow) + (bias ? bias[vrow] : 0.f));
     kn[HD + dd] = v;
-    if (sg == 0) vcache[static_cast<size_t>(pos) * HD + dd] = v;
+    if (sg == 0) KvIO<KV>::store(vcache + static_cast<size_t>(pos) * HD + dd, v);
   }
   cbar();
   // Scores: 8 lanes per position (lane j of a group takes float4 columns j, j+8, j+16, j+24),
@@ -605,16 +624,24 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
 #pragma unroll
   for (int ps_i = 0; ps_i < kPass; ++ps_i) {
     const int tl = (ps_i * kCW + warp) * 4 + grp, t = t0 + min(tl, nt - 1);
-    const float4 *src = reinterpret_cast<const float4 *>(t == pos ? kn : kcache + static_cast<size_t>(t) * HD);
+    if constexpr (sizeof(KV) == 4) {
+      const float4 *src = reinterpret_cast<const float4 *>(t == pos ? kn : reinterpret_cast<const float *>(kcache) +
+                                                                              static_cast<size_t>(t) * HD);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) k4[ps_i][i] = src[sub + 8 * i];
+      for (int i = 0; i < 4; ++i) k4[ps_i][i] = src[sub + 8 * i];
+    } else {
+      const float4 *own = reinterpret_cast<const float4 *>(kn);
+      const KV *row = kcache + static_cast<size_t>(t) * HD;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) k4[ps_i][i] = t == pos ? own[sub + 8 * i] : KvIO<KV>::load4(row + 4 * (sub + 8 * i));
+    }
   }
   // P.V: thread (dd, sl) sums positions tl = sl, sl + kPV, ... of output dimension dd.
   float vv[C / kPV];
 #pragma unroll
   for (int m = 0; m < C / kPV; ++m) {
     const int tl = min(sl + kPV * m, nt - 1), t = t0 + tl;
-    vv[m] = t == pos ? 0.f : vcache[static_cast<size_t>(t) * HD + dd];
+    vv[m] = t == pos ? 0.f : KvIO<KV>::load(vcache + static_cast<size_t>(t) * HD + dd);
   }
 #pragma unroll
   for (int ps_i = 0; ps_i < kPass; ++ps_i) {
@@ -690,7 +717,9 @@ constexpr int kCombBlocks = 4;  // attention-output blocks a warp combines per p
 // warp forms the chunk weights exp(m_c - max) and the reciprocal of the denominator; then the
 // outputs (o * (1 / l), within an ulp of the launch chain's o / l), warp w taking 32-element
 // blocks w, w + kCW, ... (kCombBlocks per pass, two chunks per iteration).
-__device__ void combine_quant(const TokenStep &p, uint8_t *smem, int pos) {
+// Tracing (CTA 0 only, else rec < 0): the output and its Q8_1 go to fields ATT, ATT_XQ of record rec.
+template <bool TRACE>
+__device__ void combine_quant(const TokenStep &p, uint8_t *smem, int pos, int rec) {
   constexpr int HD = kHeadDim;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.n_head / p.n_kv;
@@ -769,6 +798,15 @@ __device__ void combine_quant(const TokenStep &p, uint8_t *smem, int pos) {
       v[k] = o[k] * den[hh[k]];
     }
     bad |= quant_blocks<kCombBlocks>(v, bb, live, lane, q, qd, qs);
+    if (TRACE && rec >= 0) {  // the same arithmetic again, into the trace
+      float *ta = p.trace.f32(rec, UGB_TRACE_ATT);
+      uint8_t *tq = p.trace.at(rec, UGB_TRACE_ATT_XQ);
+#pragma unroll
+      for (int k = 0; k < kCombBlocks; ++k)
+        if (live[k]) ta[bb[k] * 32 + lane] = v[k];
+      quant_blocks<kCombBlocks>(v, bb, live, lane, reinterpret_cast<int8_t *>(tq),
+                                reinterpret_cast<float *>(tq + p.trace.d_q), reinterpret_cast<int32_t *>(tq + p.trace.s_q));
+    }
   }
   if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
   cbar();
@@ -776,7 +814,9 @@ __device__ void combine_quant(const TokenStep &p, uint8_t *smem, int pos) {
 
 // The CTA's FFN blocks [b0, b1): h = SiLU(gate) * up (gateup_dp4a epilogue, gpu_dp4a.cu:63) from
 // the shared gate / up rows, quantised per 32-block into the global hq buffer.
-__device__ void silu_quant(const TokenStep &p, uint8_t *smem, int b0, int b1) {
+// Tracing (rec >= 0): every CTA writes its blocks of fields H and H_XQ of record rec.
+template <bool TRACE>
+__device__ void silu_quant(const TokenStep &p, uint8_t *smem, int b0, int b1, int rec) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float *gs = reinterpret_cast<const float *>(smem + p.o_gu);
   const float *us = gs + 32 * p.gu_blocks;
@@ -787,7 +827,14 @@ __device__ void silu_quant(const TokenStep &p, uint8_t *smem, int b0, int b1) {
   for (int b = b0 + warp; b < b1; b += kCW) {
     const int i = (b - b0) * 32 + lane;
     const float gv = gs[i], uv = us[i];
-    bad |= quant_block((gv / (1.0f + expf(-gv))) * uv, lane, q, d, s, b);
+    const float h = (gv / (1.0f + expf(-gv))) * uv;
+    bad |= quant_block(h, lane, q, d, s, b);
+    if (TRACE && rec >= 0) {  // the same arithmetic again, into the trace
+      uint8_t *tq = p.trace.at(rec, UGB_TRACE_H_XQ);
+      p.trace.f32(rec, UGB_TRACE_H)[b * 32 + lane] = h;
+      quant_block(h, lane, reinterpret_cast<int8_t *>(tq), reinterpret_cast<float *>(tq + p.trace.d_f),
+                  reinterpret_cast<int32_t *>(tq + p.trace.s_f), b);
+    }
   }
   if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
 }
@@ -814,7 +861,7 @@ __device__ void load_hq(const TokenStep &p, uint8_t *smem) {
 
 // Returns when the step is done or aborted; ms->consumed is not needed (the drain works from
 // the producer's count).
-template <int KIND, int HKIND>
+template <int KIND, int HKIND, typename KV, bool TRACE>
 __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokMisc *ms, const TokLayer *layers) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int P = gridDim.x, cta = blockIdx.x;
@@ -871,53 +918,61 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
   Cursor cur;
   Slots sl;
   uint32_t *status = p.status;
+  constexpr bool tracing = TRACE;
+  const bool tr0 = TRACE && cta == 0;  // replicated values are traced by CTA 0
   for (int l = 0; l < p.n_layer; ++l) {
     const TokLayer &L = layers[l];
     // A: residual + norm + Q8_1, then Q/K/V
     if (l > 0 && !phase_wait(p, ms, kCntE, Pu * l)) return;
     if (tid == 0)
       for (int u = cta; u < units; u += P)
-        if (u % nsg == 0) prefetch_unit(p, l, u / nsg / nch, u / nsg % nch, pos);
-    norm_quant(p, smem, ms, l > 0 ? p.dxd : nullptr, L.attn_norm);
+        if (u % nsg == 0) prefetch_unit<KV>(p, l, u / nsg / nch, u / nsg % nch, pos);
+    norm_quant<TRACE>(p, smem, ms, l > 0 ? p.dxd : nullptr, L.attn_norm, tr0 ? l : -1, UGB_TRACE_ATTN_NORM);
     make_slots(p, base, p.n_embd, p.rb_e, sl);
     bool ok = consume<KIND>(p, base, cur, pl, L, kSlotQKV, p.rb_e, sl, [&](int row, float v) {
       p.qkv[row] = v;
+      if (tracing) p.trace.f32(l, UGB_TRACE_QKV)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     if (!cbar_and(ok)) return;
     phase_arrive(p, kCntA, 1);
     // B: attention partials
     if (cta < units) {
-      if (!phase_wait(p, ms, kCntA, Pu * (l + 1))) return;
+      // p.unreachable > 0 (a test hook) asks for arrivals that no CTA makes, so the wait can end
+      // only by its time limit
+      if (!phase_wait(p, ms, kCntA, Pu * (l + 1) + (l == 0 ? p.unreachable : 0u))) return;
       uint32_t n = 0;
       for (int u = cta; u < units; u += P, ++n)
-        attn_unit(p, smem, L.bias, l, u / nsg / nch, u / nsg % nch, u % nsg, pos);
+        attn_unit<KV>(p, smem, L.bias, l, u / nsg / nch, u / nsg % nch, u % nsg, pos);
       phase_arrive(p, kCntB, n);
     }
     // C: combine + Q8_1, then O
     if (!phase_wait(p, ms, kCntB, static_cast<uint32_t>(units) * (l + 1))) return;
-    combine_quant(p, smem, pos);
+    combine_quant<TRACE>(p, smem, pos, tr0 ? l : -1);
     make_slots(p, base, qr, p.rb_q, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotO, p.rb_q, sl, [&](int row, float v) {
       p.dxo[row] = v;
+      if (tracing) p.trace.f32(l, UGB_TRACE_O)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     if (!cbar_and(ok)) return;
     phase_arrive(p, kCntC, 1);
     // D: residual + norm + Q8_1, then gate and up of whole blocks, SiLU * up + Q8_1
     if (!phase_wait(p, ms, kCntC, Pu * (l + 1))) return;
-    norm_quant(p, smem, ms, p.dxo, L.ffn_norm);
+    norm_quant<TRACE>(p, smem, ms, p.dxo, L.ffn_norm, tr0 ? l : -1, UGB_TRACE_FFN_NORM);
     make_slots(p, base, p.n_embd, p.rb_e, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotGate, p.rb_e, sl, [&](int row, float v) {
       gs[row - 32 * gb0] = v;
+      if (tracing) p.trace.f32(l, UGB_TRACE_GATE_UP)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     ok = consume<KIND>(p, base, cur, pl, L, kSlotUp, p.rb_e, sl, [&](int row, float v) {
       us[row - 32 * gb0] = v;
+      if (tracing) p.trace.f32(l, UGB_TRACE_GATE_UP)[p.n_ff + row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     }) && ok;
     if (!cbar_and(ok)) return;
-    silu_quant(p, smem, gb0, gb1);
+    silu_quant<TRACE>(p, smem, gb0, gb1, TRACE ? l : -1);
     phase_arrive(p, kCntD, 1);
     // E: down
     if (!phase_wait(p, ms, kCntD, Pu * (l + 1))) return;
@@ -925,6 +980,7 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
     make_slots(p, base, p.n_ff, p.rb_f, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotDown, p.rb_f, sl, [&](int row, float v) {
       p.dxd[row] = v;
+      if (tracing) p.trace.f32(l, UGB_TRACE_DOWN)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     if (!cbar_and(ok)) return;
@@ -932,7 +988,7 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
   }
   // Head: residual + output norm + Q8_1, logits of this CTA's rows, greedy key.
   if (!phase_wait(p, ms, kCntE, Pu * p.n_layer)) return;
-  norm_quant(p, smem, ms, p.dxd, p.out_norm);
+  norm_quant<TRACE>(p, smem, ms, p.dxd, p.out_norm, tr0 ? p.n_layer : -1, UGB_TRACE_ATTN_NORM);
   make_slots(p, base, p.n_embd, p.rb_h, sl);
   unsigned long long best = 0;
   const bool ok = consume<HKIND>(p, base, cur, pl, layers[0], kSlotHead, p.rb_h, sl, [&](int row, float v) {
@@ -954,7 +1010,7 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
   }
 }
 
-template <int KIND, int HKIND>
+template <int KIND, int HKIND, typename KV, bool TRACE>
 __global__ void __launch_bounds__(kTT, 1) token_kernel(const TokenStep p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
@@ -982,7 +1038,7 @@ __global__ void __launch_bounds__(kTT, 1) token_kernel(const TokenStep p) {
     if (lane == 0) ms->issued = produce(p, base, ms->plan, layers);
     __syncwarp();
   } else {
-    consumers<KIND, HKIND>(p, smem, base, ms, layers);
+    consumers<KIND, HKIND, KV, TRACE>(p, smem, base, ms, layers);
   }
   __syncthreads();
   if (tid == 0) {
@@ -1034,9 +1090,10 @@ bool token_layout(const ugb_ctx *ctx, TokenStep &p) {
   return true;
 }
 
-template <int KIND, int HKIND>
+template <int KIND, int HKIND, typename KV>
 ugb_status launch_kind(ugb_ctx *ctx, cudaStream_t stream, const TokenStep &p, size_t smem) {
-  auto *k = token_kernel<KIND, HKIND>;
+  // a traced step runs its own instantiation: the trace stores stay out of the untraced kernel
+  auto *k = p.trace.base ? token_kernel<KIND, HKIND, KV, true> : token_kernel<KIND, HKIND, KV, false>;
   if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
     return UGB_EBACKEND;
   int per_sm = 0;
@@ -1072,8 +1129,11 @@ ugb_status launch_token(ugb_ctx *ctx, cudaStream_t stream, uint32_t kind, uint32
   if (!token_supported(ctx, kind, head_kind, p)) return UGB_ESHAPE;
   token_layout(ctx, p);
   const size_t smem = p.o_ring + p.ring_bytes + kRingSlack;
-  if (kind == UGB_Q8_0) return launch_kind<UGB_Q8_0, UGB_Q8_0>(ctx, stream, p, smem);
-  return launch_kind<UGB_Q4_K, UGB_Q8_0>(ctx, stream, p, smem);
+  if (kind == UGB_Q8_0)
+    return p.kv16 ? launch_kind<UGB_Q8_0, UGB_Q8_0, __half>(ctx, stream, p, smem)
+                  : launch_kind<UGB_Q8_0, UGB_Q8_0, float>(ctx, stream, p, smem);
+  return p.kv16 ? launch_kind<UGB_Q4_K, UGB_Q8_0, __half>(ctx, stream, p, smem)
+                : launch_kind<UGB_Q4_K, UGB_Q8_0, float>(ctx, stream, p, smem);
 }
 
 }  // namespace ugb
