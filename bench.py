@@ -523,44 +523,87 @@ def c3_ops_per_step(c=C2, m=C3_TOKENS):
     return c["n_layer"] * sum(2 * m * n * k for _, n, k in c3_gemms(c))
 
 
-def c3_gpu(args, ugb, ctx, torch, rank, world, c=C2, m=C3_TOKENS):
-    dev = torch.device("cuda", torch.cuda.current_device())
-    gen = torch.Generator(device="cpu").manual_seed(11 + rank)
-    layers = []
+def c3_attn_flops(c=C2, m=C3_TOKENS):
+    """fp32 multiply-adds x 2 of the causal attention of an m-token prompt (scores and P.V)."""
+    return c["n_layer"] * c["n_head"] * 2 * 2 * c["head_dim"] * m * (m + 1) // 2
+
+
+def c3_gemm_kernel(ugb, ctx, torch, dev, cap, stream, c=C2, m=C3_TOKENS):
+    """Per-launch time of the fused gate/up prefill GEMM (512 x 17920 x 1536) on its own
+    operands, 28 launches back to back in one graph (each layer's weights are distinct)."""
+    _, n, k = c3_gemms(c)[2]
+    gen = torch.Generator(device="cpu").manual_seed(13)
+    ops = []
     for li in range(c["n_layer"]):
-        L = []
-        for gi, (name, n, k) in enumerate(c3_gemms(c)):
-            w = torch.empty(q8_bytes(k, n), dtype=torch.uint8, device=dev)
-            ctx.fill_synthetic(Q8_0, w, k, n, seed=7000 + 8 * li + gi)
-            wp = ugb.alloc_prefill(n, k, device=dev)
-            ctx.prefill_repack_q8_0(w, n, k, wp)  # one-time setup, outside timing (as the reference)
-            del w
-            x = torch.randn((m, k), generator=gen).to(dev)
-            L.append((name, n, k, wp, x, ugb.alloc_prefill(m, k, device=dev),
-                      torch.empty((m, n), dtype=torch.float32, device=dev)))
-        layers.append(L)
+        w = torch.empty(q8_bytes(k, n), dtype=torch.uint8, device=dev)
+        ctx.fill_synthetic(Q8_0, w, k, n, seed=7000 + li)
+        wp = ugb.alloc_prefill(n, k, device=dev)
+        ctx.prefill_repack_q8_0(w, n, k, wp)
+        del w
+        xp = ugb.alloc_prefill(m, k, device=dev)
+        ctx.prefill_quant(torch.randn((m, k), generator=gen).to(dev), m, k, xp)
+        ops.append((wp, xp, torch.empty((m, n), dtype=torch.float32, device=dev)))
     torch.cuda.synchronize()
+    ctx.set_pdl(True)
+    kgraph = ctx.capture(lambda: [ctx.prefill_gemm(wp, xp, y, m, n, k) for wp, xp, y in ops], cap)
+    ctx.set_pdl(False)
+    kgraph.launch(stream)
+    stream.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 4
+    e0.record(stream)
+    for _ in range(reps):
+        kgraph.launch(stream)
+    e1.record(stream)
+    stream.synchronize()
+    kgraph.close()
+    return e0.elapsed_time(e1) / (reps * len(ops)), 2 * m * n * k
+
+
+def int8_peak_tops(torch, dev):
+    """Measured INT8 tensor peak on this GPU: cuBLAS int8 GEMM 8192^3 (torch._int_mm), burst."""
+    a8 = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    b8 = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a8, b8)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(10):
+        torch._int_mm(a8, b8)
+    e1.record()
+    torch.cuda.synchronize()
+    return 2 * 8192 ** 3 / (e0.elapsed_time(e1) / 10 / 1e3) / 1e12
+
+
+def c3_gpu(args, ugb, ctx, torch, rank, world, c=C2, m=C3_TOKENS):
+    """The whole 512-token prefill of the 1.5B model (ugb_decoder_prefill_async, replayed from one
+    captured graph): embedding, 28 layers of norm / quant / Q-K-V GEMM / bias + RoPE + KV write /
+    causal attention / quant / O GEMM / norm / quant / gate-up GEMM / SiLU / quant / down GEMM, and
+    the last token through the output norm, the head and greedy selection."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    c = dict(c, kv_type=KV_TYPES[args.kv])
+    w = c2_device_weights(ctx, ugb, torch, seed=11 + rank, c=c)
+    dec = ugb.Decoder(ctx, **c)
+    dec.bind(w["tok_embd"], w["output_norm"], w["output"], w["layers"])
+    dec.prefill_prepare(m)  # one-time repack, outside timing (as the reference's init_swizzle)
+    prompt = np.random.default_rng(5 + rank).integers(0, c["n_vocab"], size=m).astype(np.int32)
+    toks = torch.from_numpy(prompt).to(dev)
     stream = torch.cuda.Stream()
     cap = torch.cuda.Stream()
-
-    def step():
-        for L in layers:
-            for _, n, k, wp, x, xp, y in L:
-                ctx.prefill_quant(x, m, k, xp)
-                ctx.prefill_gemm(wp, xp, y, m, n, k)
-
     ctx.set_pdl(True)
-    graph = ctx.capture(step, cap)
+    graph = ctx.capture(lambda: dec.prefill_async(toks, m, 0), cap)
     ctx.set_pdl(False)
+    kernels = graph.kernels()
+    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
+    sampler.start()
     for _ in range(args.warmup):
         graph.launch(stream)
     stream.synchronize()
     code, bits = ctx.status_read(stream)
     assert code == ugb.OK, ("status after warm-up", code, bits)
-    sampler = ClockSampler(int(os.environ.get("LOCAL_RANK", "0")) if world > 1 else torch.cuda.current_device())
     barrier(world, torch)
     torch.cuda.synchronize()
-    sampler.start()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
@@ -571,93 +614,50 @@ def c3_gpu(args, ugb, ctx, torch, rank, world, c=C2, m=C3_TOKENS):
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     ms_max = reduce_max(ms, world, torch)
-
-    # dominant kernel: the fused gate/up GEMM (512 x 17920 x 1536), 28 layers back to back
-    gu = [L[2] for L in layers]
-    kgraph = ctx.capture(lambda: [ctx.prefill_gemm(wp, xp, y, m, n, k) for _, n, k, wp, x, xp, y in gu], cap)
-    kgraph.launch(stream)
-    stream.synchronize()
-    reps = 4
-    e0.record(stream)
-    for _ in range(reps):
-        kgraph.launch(stream)
-    e1.record(stream)
-    stream.synchronize()
-    kern_ms = e0.elapsed_time(e1) / (reps * len(gu))
-    _, n_gu, k_gu = c3_gemms(c)[2]
-    kern_ops = 2 * m * n_gu * k_gu
-
-    # measured INT8 tensor peak on this GPU: cuBLAS int8 GEMM 8192^3 (torch._int_mm), burst
-    a8 = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
-    b8 = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
-    for _ in range(3):
-        torch._int_mm(a8, b8)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(10):
-        torch._int_mm(a8, b8)
-    e1.record()
-    torch.cuda.synchronize()
-    int8_tops = 2 * 8192 ** 3 / (e0.elapsed_time(e1) / 10 / 1e3) / 1e12
-    del a8, b8
-
-    # end to end: the prompt's activations come from pinned host memory (the first GEMM input)
-    # and the last GEMM's output goes back, around one step
-    x0 = layers[0][0][4]
-    y_last = layers[-1][-1][6]
-    x_host = torch.empty(x0.shape, dtype=torch.float32).pin_memory()
-    x_host.copy_(x0.cpu())
-    y_host = torch.empty(y_last.shape, dtype=torch.float32).pin_memory()
-    e2e_steps = max(3, min(args.steps, 10))
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        with torch.cuda.stream(stream):
-            x0.copy_(x_host, non_blocking=True)
-        graph.launch(stream)
-        with torch.cuda.stream(stream):
-            y_host.copy_(y_last, non_blocking=True)
-        stream.synchronize()
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
-    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
     code, bits = ctx.status_read(stream)
     assert code == ugb.OK, ("status after timing", code, bits)
     graph.close()
-    kgraph.close()
+    # end to end through the host-facing call: ugb_decoder_prefill (host prompt in, greedy next
+    # token out, status checked) every step
+    e2e_steps = max(3, min(args.steps, 10))
+    dec.prefill(list(prompt), 0)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        dec.prefill(list(prompt), 0)
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
+    dec.close()
+    kern_ms, kern_ops = c3_gemm_kernel(ugb, ctx, torch, dev, cap, stream, c, m)
     return {
         "value": world * m * args.steps / (ms_max / 1e3), "ms_per_step": ms_max / args.steps, "clocks": clocks,
-        "gpu_launches": 2 * len(c3_gemms(c)) * c["n_layer"] * args.steps,
-        "kernel_ms": kern_ms, "kernel_ops": kern_ops, "int8_tops": int8_tops,
-        "e2e": {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": x0.numel() * 4,
-                "d2h_bytes_per_step": y_last.numel() * 4},
+        "gpu_launches": kernels * args.steps,
+        "kernel_ms": kern_ms, "kernel_ops": kern_ops, "int8_tops": int8_peak_tops(torch, dev),
+        "step_gemm_ops": c3_ops_per_step(c, m), "step_attn_flops": c3_attn_flops(c, m),
+        "e2e": {"value": world * m / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": m * 4,
+                "d2h_bytes_per_step": 104 + 4},
     }
 
 
-def c3_cpu(budget_s: float, c=C2):
-    """The oracle's prefill GEMM (oracle/ugb_oracle.c, POSIX threads over tokens) on one layer's
-    four GEMMs for as many tokens as fit the budget; scaled to the 28 layers: (tok/s, tokens,
-    threads)."""
+def c3_cpu(budget_s: float, c=C2, kv_type=0):
+    """The oracle's whole-prompt prefill of the full-depth model (oracle/decode_ref.py
+    RefDecoder.prefill: batched oracle/ugb_oracle.c matvecs on POSIX threads, numpy glue) on a
+    prompt of as many tokens as fit the budget: (tok/s, tokens, threads)."""
     from oracle import pyoracle as orc
+    from oracle.decode_ref import RefDecoder
+    cfg = dict(c, kv_type=kv_type)
+    ref = RefDecoder(cfg, c2_host_weights(7, c), mt=True)
     rng = np.random.default_rng(3)
-    mats = []
-    for _, n, k in c3_gemms(c):
-        nb = k // 32
-        b = np.empty((n, nb, 34), dtype=np.uint8)
-        b[:, :, 2:] = rng.integers(-127, 128, size=(n, nb, 32), dtype=np.int8).view(np.uint8)
-        b[:, :, :2] = (0.002 * np.abs(rng.standard_normal((n, nb)))).astype(np.float16).view(np.uint8).reshape(n, nb, 2)
-        mats.append((b.reshape(-1), n, k))
-    threads = orc.lib(True).orc_threads()
-    tokens = threads
+    tokens = 4
     while True:
-        xs = [rng.standard_normal((tokens, k)).astype(np.float32) for _, _, k in mats]
+        prompt = rng.integers(0, c["n_vocab"], size=tokens)
         t0 = time.perf_counter()
-        for (w, n, k), x in zip(mats, xs):
-            orc.prefill_gemm_q8_0(w, n, k, x)
+        ref.prefill(prompt, 0)
         dt = time.perf_counter() - t0
-        if dt * 4 > budget_s or tokens >= C3_TOKENS:
+        if dt * 3 > budget_s or tokens >= C3_TOKENS:
             break
         tokens *= 2
-    return tokens / (dt * c["n_layer"]), tokens, threads
+    return tokens / dt, tokens, orc.lib(True).orc_threads()
 
 
 # ---- workloads c4 / c5: batched and sharded decode of the larger configs ---------------------
@@ -902,15 +902,18 @@ def main():
         base = {"metric": "decode tok/s", "unit": "tok/s",
                 "dtype": "int8 x int8 -> int32 (K-quant / Q8_0 x Q8_1), fp32 glue"}
     elif args.workload == "c3":
-        config = {"workload": "c3: Q8 prefill GEMMs of the Qwen2.5-1.5B-shaped Q8_0 model, 512-token prompt",
-                  "tokens": C3_TOKENS, "layers": C2["n_layer"],
+        config = {"workload": "c3: Q8 prefill of the Qwen2.5-1.5B-shaped Q8_0 model, 512-token prompt of seeded "
+                              "uniform token ids, the whole prefill graph",
+                  "tokens": C3_TOKENS, "layers": C2["n_layer"], "context": C2["n_ctx"],
+                  "kv_cache": "fp16" if args.kv == "f16" else "fp32",
                   "gemms_per_layer": "qkv 2048x1536, o 1536x1536, gate_up 17920x1536, down 1536x8960",
                   "per_gemm": "block-32 activation quant + tcgen05 INT8 GEMM with per-block fp32 rescale",
-                  "excluded": "prefill attention, norms, SiLU and the head (outside the hot-path scope)",
+                  "glue": "embedding, RMSNorm, bias + RoPE + KV write, causal attention (fp32), SiLU * up; "
+                          "the last token through the output norm, the head and greedy selection",
                   "l2": "inputs larger than L2 (1.4 GB of repacked weights per step)",
                   "parallelism": f"replicas x{world}"}
-        base = {"metric": "prefill tok/s (linear layers)", "unit": "tok/s",
-                "dtype": "int8 x int8 -> int32 per 32-block (tcgen05 kind::i8), fp32 rescale"}
+        base = {"metric": "prefill tok/s", "unit": "tok/s",
+                "dtype": "int8 x int8 -> int32 per 32-block (tcgen05 kind::i8), fp32 rescale and glue"}
     else:
         config = {"workload": "c1: Q8_0 matvec 8960x1536 + block-32 activation quantisation",
                   "rows": C1_M, "k": C1_K, "weight_copies_rotated": C1_ROTATE,
@@ -938,9 +941,9 @@ def main():
                       "threads), per-token time extrapolated to the full depth; one sequence at a time")
             ms = per_token * 1e3
         elif args.workload == "c3":
-            value, toks, cores = c3_cpu(max(30.0, args.cpu_seconds))
-            sample = (f"the four GEMMs of one layer for {toks} tokens (oracle/ugb_oracle.c prefill GEMM, POSIX "
-                      f"threads over tokens), scaled to 28 layers")
+            value, toks, cores = c3_cpu(max(30.0, args.cpu_seconds), kv_type=KV_TYPES[args.kv])
+            sample = (f"a {toks}-token prompt through the full 28-layer prefill (oracle/decode_ref.py "
+                      f"RefDecoder.prefill: batched oracle/ugb_oracle.c matvecs on POSIX threads, numpy glue)")
             ms = C3_TOKENS / value * 1e3
         else:
             value, cores = c1_cpu(300)
@@ -1003,6 +1006,10 @@ def main():
                 "peak_source": "measured in this run: cuBLAS int8 GEMM 8192^3 (torch._int_mm), burst",
                 "kernel": kernel, "kernel_ms": res["kernel_ms"], "ops_per_launch": res["kernel_ops"],
                 "traffic": traffic}
+        if "step_gemm_ops" in res:  # the GEMMs' share of the whole prefill step
+            step_tops = res["step_gemm_ops"] / (res["ms_per_step"] / 1e3) / 1e12
+            roof["step"] = {"gemm_int8_ops": res["step_gemm_ops"], "attention_fp32_flops": res["step_attn_flops"],
+                            "gemm_tops_over_step": step_tops, "frac": step_tops / res["int8_tops"]}
     else:
         achieved = res["kernel_bytes"] / (res["kernel_ms"] / 1e3) / 1e9
         roof = {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
@@ -1030,8 +1037,8 @@ def main():
             v, _, cores = big_cpu(args.cpu_seconds, args.workload, 1)
             sample = "1- and 2-layer oracle models, per-token time extrapolated to the full depth"
         elif args.workload == "c3":
-            v, toks, cores = c3_cpu(args.cpu_seconds)
-            sample = f"one layer's four GEMMs for {toks} tokens on the host threads, scaled to 28 layers"
+            v, toks, cores = c3_cpu(args.cpu_seconds, kv_type=KV_TYPES[args.kv])
+            sample = f"a {toks}-token prompt through the full 28-layer oracle prefill on the host threads"
         else:
             v, cores = c1_cpu(100)
             sample = "100 steps of quant_act + Q8_0 matvec 8960x1536 on the host cores"

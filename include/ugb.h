@@ -475,6 +475,42 @@ ugb_status ugb_decoder_tokens(ugb_decoder *dec, ugb_stream stream, const int32_t
 ugb_status ugb_decoder_token(ugb_decoder *dec, ugb_stream stream, int32_t token, int32_t pos,
                              int32_t *next_token);
 
+/* ---- whole-prompt prefill ------------------------------------------------------------------ */
+
+/* One-time preparation of ugb_decoder_prefill for the bound weights: repacks every layer's Q8_0
+ * matrices into the tensor-core operand layout (the reference's init_swizzle / prefill_repack,
+ * gpu_prefill.rs:58-94; Q/K/V and, when n_ff is a multiple of 128, gate/up become one operand
+ * each; about 1.06x the layer weights in device memory) and allocates the activations of up to
+ * max_tokens tokens (<= n_ctx).  Dense decoders with batch 1, Q8_0 layers and the whole head.
+ * Synchronous.  Binding other weights drops the preparation: prepare again after
+ * ugb_decoder_bind. */
+ugb_status ugb_decoder_prefill_prepare(ugb_decoder *dec, ugb_stream stream, int32_t max_tokens);
+
+/* Prefill n prompt tokens at positions pos0 .. pos0 + n - 1 in one pass (the reference's prefill
+ * graph, gpu_prefill.rs:122-150, kernels gpu_prefill.cu:10-101): per layer the RMSNorm, block-32
+ * quantisation of all n tokens, the Q/K/V, O, gate/up and down INT8 tensor-core GEMMs, bias +
+ * RoPE with the KV-cache write, causal attention over positions [0, pos0 + t] for token t, and
+ * SiLU * up; then only the last token through the final norm, the head and greedy selection
+ * (gpu_prefill.rs:138-148).  Afterwards the decoder's state is that of a decode step of the last
+ * prompt token at pos0 + n - 1 with its greedy choice, so ugb_decoder_step continues the
+ * sequence at pos0 + n, and ugb_decoder_logits returns the last token's logits.
+ * ugb_decoder_prefill: host tokens in, the greedy next token out (synchronous, status checked).
+ * ugb_decoder_prefill_async: tokens in device memory (caller-owned, live until the work is
+ * done), asynchronous on `stream` and capturable in a CUDA graph. */
+ugb_status ugb_decoder_prefill(ugb_decoder *dec, ugb_stream stream, const int32_t *tokens_host, int32_t n,
+                               int32_t pos0, int32_t *next_token);
+ugb_status ugb_decoder_prefill_async(ugb_decoder *dec, ugb_stream stream, const int32_t *tokens_dev, int32_t n,
+                                     int32_t pos0);
+
+/* Trace of the last prefill while tracing is on (ugb_decoder_set_trace): the fields of the step
+ * trace, each with max_tokens rows (the first n filled) instead of the batch: X, ATTN_NORM, QKV,
+ * ATT, O, FFN_NORM, GATE_UP, H, DOWN per layer (the packed Q8_1 operands are not recorded), and in
+ * record n_layer the last token's X, ATTN_NORM (row 0) and its head input ATTN_XQ (a ugb_q8act
+ * buffer of batch 1 at the field's start).  bytes may be less than the field's size. */
+size_t ugb_decoder_prefill_trace_bytes(const ugb_decoder *dec, int32_t field);
+ugb_status ugb_decoder_read_prefill_trace(ugb_decoder *dec, ugb_stream stream, int32_t layer, int32_t field,
+                                          void *host, size_t bytes);
+
 /* ---- host-buffer entry points (synchronous) --------------------------------------------- */
 
 /* y_host[m] = W x_host[k], synchronously: copy x to the device, quantise, matvec, copy y

@@ -129,6 +129,51 @@ class RefDecoder:
             out = (out + (np.float32(wgt) * v).astype(np.float32)).astype(np.float32)
         return out
 
+    # ---- a whole prompt ------------------------------------------------------------------
+
+    def prefill(self, tokens, pos0: int = 0):
+        """The reference's prefill graph (gpu_prefill.rs:122-150, kernels gpu_prefill.cu:60-101):
+        every layer over all prompt tokens at once -- per-token RMSNorm and block-32 quantisation,
+        the linear layers as one batched matvec per matrix (the same integer block dots), bias + RoPE
+        into the cache, causal attention of token t over positions [0, pos0 + t], SiLU * up -- then
+        only the last token through the final norm and the head (gpu_prefill.rs:138-148).  Dense
+        layers only.  Returns (last token's logits, greedy next token)."""
+        c, hd = self.c, self.hd
+        kind, nh, nkv = c["kind"], c["n_head"], c["n_head_kv"]
+        qrows, kvrows, e = nh * hd, nkv * hd, c["n_embd"]
+        n = len(tokens)
+        x = np.stack([self.embed(int(t)) for t in tokens])
+
+        def lin(w, xs, m):
+            q, d, s, _ = po.quant_act(xs)
+            k = xs.shape[1]
+            return po.matvec(kind, w, po.row_bytes(kind, k), q, d, s, k, m, xs.shape[0], mt=self.mt)
+
+        for li, L in enumerate(self.w["layers"]):
+            xn = np.stack([self.norm(x[t], L["attn_norm"]) for t in range(n)])
+            q, k, v = lin(L["wq"], xn, qrows), lin(L["wk"], xn, kvrows), lin(L["wv"], xn, kvrows)
+            if L.get("bq") is not None:
+                q, k, v = q + L["bq"], k + L["bk"], v + L["bv"]
+            att = np.empty((n, qrows), np.float32)
+            qr = np.empty((n, nh, hd), np.float32)
+            for t in range(n):
+                pos = pos0 + t
+                qr[t] = self.rotate(q[t].reshape(nh, hd), pos)
+                self.kcache[li, :, pos] = self.kv_round(self.rotate(k[t].reshape(nkv, hd), pos))
+                self.vcache[li, :, pos] = self.kv_round(v[t].reshape(nkv, hd))
+            for t in range(n):
+                pos = pos0 + t
+                att[t] = self.attend(qr[t], self.kcache[li, :, :pos + 1], self.vcache[li, :, :pos + 1]).reshape(-1)
+            x = (x + lin(L["wo"], att, e)).astype(np.float32)
+            xn = np.stack([self.norm(x[t], L["ffn_norm"]) for t in range(n)])
+            g, u = lin(L["w_gate"], xn, c["n_ff"]), lin(L["w_up"], xn, c["n_ff"])
+            with np.errstate(over="ignore"):
+                h = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
+            x = (x + lin(L["w_down"], h, e)).astype(np.float32)
+        xn = self.norm(x[-1], self.w["output_norm"])
+        logits = self.linear(c["head_kind"], self.w["output"], xn, c["n_vocab"])
+        return logits, int(np.argmax(logits))
+
     # ---- one token -----------------------------------------------------------------------
 
     def step(self, token: int, pos: int):

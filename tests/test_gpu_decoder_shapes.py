@@ -37,7 +37,9 @@ C2_POSITIONS = [0, 63, 64, 200, 447, 448, 511]
 C4_POSITIONS = [0, 64, 575, 1023]
 
 NORM_REL = 2e-5   # RMSNorm: the sum of squares in another order moves the scale by a few ulp
-ATT_REL = 2e-5    # attention: chunked log-sum-exp vs one softmax, dot products in another order
+# attention: chunked log-sum-exp vs one softmax and dot products in another order; score errors of a
+# few ulp of |score| (up to ~60 here) become relative errors of the probabilities (worst seen 3e-5)
+ATT_REL = 1e-4
 SILU_REL = 2e-6   # expf vs numpy's exp: an ulp or two
 ROPE_REL = 2e-6   # the rotation with or without a fused multiply-add
 
@@ -71,12 +73,13 @@ def matvec(orc, kind, w, xq, m):
 
 
 def seed_history(dec, cfg, rng):
-    """Random rotated keys and values at every position of every layer and sequence."""
+    """Random rotated keys and values (N(0, 1), as the step's own rows roughly are after RoPE)
+    at every position of every layer and sequence."""
     shape = (cfg["n_head_kv"], cfg["n_ctx"], cfg["head_dim"])
     for seq in range(cfg.get("batch", 1)):
         for layer in range(cfg["n_layer"]):
-            dec.write_kv(layer, 0, (4 * rng.standard_normal(shape)).astype(np.float32),
-                         (4 * rng.standard_normal(shape)).astype(np.float32), seq=seq)
+            dec.write_kv(layer, 0, rng.standard_normal(shape).astype(np.float32),
+                         rng.standard_normal(shape).astype(np.float32), seq=seq)
 
 
 def check_step(orc, ref, dec, host, cfg, toks, pos):

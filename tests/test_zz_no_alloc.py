@@ -64,14 +64,15 @@ def test_static_allocates_nothing(ugb, orc):
             assert_rows_close(y, _oracle_rows(orc, kind, w, rb, x, k, m))
     finally:
         ctx.close()
-    # Positive control: the same measurement sees ugb_linear grow its workspace.
+    # Positive control: the same measurement sees ugb_linear grow its workspace (a 16 MiB output
+    # staging buffer; allocations of a page or less can come from memory the driver holds already).
     ctx = ugb.Context(0)
     try:
-        w, rb = _weights(ctx, ugb, Q8_0, 16384, 8192, seed=8)
-        x = np.ones(16384, np.float32)
-        ctx.linear_static(Q8_0, w, rb, x, 16384, 8192)
+        m = 1 << 22
+        w, rb = _weights(ctx, ugb, Q8_0, 32, m, seed=8)
+        x = np.ones(32, np.float32)
         before = _free_bytes(torch)
-        ctx.linear(Q8_0, w, rb, x, 16384, 8192)
+        ctx.linear(Q8_0, w, rb, x, 32, m)
         after = _free_bytes(torch)
         assert after[0] < before[0], "the free-memory probe did not see ugb_linear's workspace"
     finally:

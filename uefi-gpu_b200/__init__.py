@@ -87,6 +87,11 @@ SIGNATURES = {
                                     _vp, _vp]),
     "ugb_decoder_set_trace": (_int, [_vp, ctypes.c_int32]),
     "ugb_decoder_set_wait_limit": (_int, [_vp, _u64]),
+    "ugb_decoder_prefill_prepare": (_int, [_vp, _vp, ctypes.c_int32]),
+    "ugb_decoder_prefill": (_int, [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int32)]),
+    "ugb_decoder_prefill_async": (_int, [_vp, _vp, _vp, ctypes.c_int32, ctypes.c_int32]),
+    "ugb_decoder_prefill_trace_bytes": (ctypes.c_size_t, [_vp, ctypes.c_int32]),
+    "ugb_decoder_read_prefill_trace": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_size_t]),
     "ugb_decoder_test_unreachable_wait": (_int, [_vp, ctypes.c_int32]),
     "ugb_decoder_trace_bytes": (ctypes.c_size_t, [_vp, ctypes.c_int32]),
     "ugb_decoder_read_trace": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_size_t]),
@@ -527,6 +532,46 @@ class Decoder:
         d = raw[d_off: d_off + b * nbp * 4].view(np.float32).reshape(b, nbp)[:, :nb]
         s = raw[s_off: s_off + b * nbp * 4].view(np.int32).reshape(b, nbp)[:, :nb]
         return q, d, s
+
+    def prefill_prepare(self, max_tokens: int, stream=None) -> None:
+        check("ugb_decoder_prefill_prepare", lib().ugb_decoder_prefill_prepare(self.handle, _stream(stream), max_tokens))
+        self.prefill_max = max_tokens
+
+    def prefill(self, tokens, pos0: int = 0, stream=None) -> int:
+        """Whole-prompt prefill of host tokens from position pos0; returns the greedy next token."""
+        arr = (ctypes.c_int32 * len(tokens))(*[int(t) for t in tokens])
+        nxt = ctypes.c_int32()
+        check("ugb_decoder_prefill", lib().ugb_decoder_prefill(self.handle, _stream(stream), arr, len(tokens), pos0,
+                                                                 ctypes.byref(nxt)))
+        return nxt.value
+
+    def prefill_async(self, tokens_dev, n: int, pos0: int = 0, stream=None) -> None:
+        """tokens_dev: int32 device tensor of at least n tokens."""
+        check("ugb_decoder_prefill_async", lib().ugb_decoder_prefill_async(self.handle, _stream(stream),
+                                                                             _ptr(tokens_dev), n, pos0))
+
+    def prefill_trace(self, layer: int, field: str, n: int, stream=None):
+        """One field of the last traced prefill: float32 [n, len] (record n_layer: [1, len] of the last
+        token, and ATTN_XQ as the (q, d, s) of its batch-1 Q8_1 head input)."""
+        import numpy as np
+        f = TRACE[field]
+        final = layer == self.cfg.n_layer
+        E = self.cfg.n_embd
+        if field == "ATTN_XQ":
+            assert final
+            nbytes = q8act_bytes(E, 1)
+        else:
+            total = lib().ugb_decoder_prefill_trace_bytes(self.handle, f)
+            nbytes = total // self.prefill_max * (1 if final else n)
+        raw = np.empty(nbytes, dtype=np.uint8)
+        check("ugb_decoder_read_prefill_trace", lib().ugb_decoder_read_prefill_trace(
+            self.handle, _stream(stream), layer, f, raw.ctypes.data, nbytes))
+        if field != "ATTN_XQ":
+            return raw.view(np.float32).reshape(1 if final else n, -1)
+        d_off, s_off = q8act_offsets(E, 1)
+        nb = E // 32
+        return (raw[:E].view(np.int8).reshape(1, E), raw[d_off:d_off + 4 * nb].view(np.float32).reshape(1, nb),
+                raw[s_off:s_off + 4 * nb].view(np.int32).reshape(1, nb))
 
     def tokens(self, tokens, pos: int, stream=None):
         b = self.cfg.batch

@@ -100,6 +100,7 @@ ugb_status ugb_init(int device, ugb_ctx **out) {
   ugb_status st = init_matvec_kernels(ctx);
   if (st == UGB_OK) st = init_decode_kernels(ctx);
   if (st == UGB_OK) st = init_prefill_kernels(ctx);
+  if (st == UGB_OK) st = init_prefill_step_kernels(ctx);
   if (st != UGB_OK) {
     ugb_destroy(ctx);
     return st;

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "decode.hpp"
+#include "prefill.hpp"
 
 struct ugb_decoder {
   ugb_ctx *ctx = nullptr;
@@ -59,6 +60,17 @@ struct ugb_decoder {
   ugb::TraceMap trace;     // step trace (ugb_decoder_set_trace); base null: off
   uint64_t wait_ns = ugb::kWaitLimitNs;  // token kernel: limit of each wait on other CTAs
   uint32_t unreachable = 0;              // token kernel test hook (ugb_decoder_test_unreachable_wait)
+  // whole-prompt prefill (ugb_decoder_prefill_prepare): packed Q8_0 operands of every layer and
+  // the activations of up to pf_max tokens
+  int pf_max = 0;
+  bool pf_gu_fused = false;  // gate and up packed as one operand (n_ff a multiple of 128)
+  uint8_t *pf_w = nullptr;   // all layers' packed weights
+  std::vector<size_t> pf_off;  // per layer: qkv, o, gate(/up), up (unfused), down
+  uint8_t *pf_ws = nullptr;  // workspace
+  float *pf_x = nullptr, *pf_y = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_gu = nullptr, *pf_tmp = nullptr;
+  uint8_t *pf_act = nullptr, *pf_xq = nullptr;
+  int32_t *pf_tokens = nullptr;
+  ugb::TraceMap ptrace;      // prefill trace, [pf_max] rows per field
   // replay
   cudaStream_t cap = nullptr;
   cudaGraph_t graph = nullptr;
@@ -112,7 +124,8 @@ void free_graph(ugb_decoder *d) {
 void free_all(ugb_decoder *d) {
   void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->rlogits, d->rweights, d->rids, d->xq, d->attq,
                   d->hq, d->kcache, d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->moe_ws, d->state,
-                  d->bias, d->dxd, d->tok_hq, d->tok_sync, d->tok_layers, d->trace.base};
+                  d->bias, d->dxd, d->tok_hq, d->tok_sync, d->tok_layers, d->trace.base, d->pf_w, d->pf_ws,
+                  d->ptrace.base};
   for (void *b : bufs)
     if (b) cudaFree(b);
   for (void *b : d->owned) cudaFree(b);
@@ -121,14 +134,15 @@ void free_all(ugb_decoder *d) {
   if (d->cap) cudaStreamDestroy(d->cap);
 }
 
-// Field sizes and offsets of one trace record (the buffer itself is allocated by set_trace).
-void plan_trace(ugb_decoder *d) {
+// Field sizes and offsets of one trace record of `rows` rows per field (the decode step: the
+// batch; a prefill: its token capacity).  The buffer itself is allocated by set_trace.
+void plan_trace(const ugb_decoder *d, TraceMap &t, int64_t rows) {
   const ugb_decoder_config &c = d->cfg;
-  const int64_t B = d->batch, E = c.n_embd, Q = static_cast<int64_t>(c.n_head) * c.head_dim;
+  const int64_t B = rows, E = c.n_embd, Q = static_cast<int64_t>(c.n_head) * c.head_dim;
   const int64_t brow = Q + 2 * static_cast<int64_t>(c.n_head_kv) * c.head_dim;
   const int64_t F = d->moe ? 0 : c.n_ff;
   const Q8Act xe = q8act_layout(E, B), xq = q8act_layout(Q, B);
-  uint64_t *n = d->trace.bytes;
+  uint64_t *n = t.bytes;
   n[UGB_TRACE_X] = n[UGB_TRACE_ATTN_NORM] = n[UGB_TRACE_O] = n[UGB_TRACE_FFN_NORM] = n[UGB_TRACE_DOWN] = B * E * 4;
   n[UGB_TRACE_ATTN_XQ] = n[UGB_TRACE_FFN_XQ] = xe.bytes;
   n[UGB_TRACE_QKV] = B * brow * 4;
@@ -139,18 +153,18 @@ void plan_trace(ugb_decoder *d) {
   n[UGB_TRACE_H_XQ] = F ? q8act_layout(F, B).bytes : 0;
   uint64_t o = 0;
   for (int f = 0; f < UGB_TRACE_FIELDS; ++f) {
-    d->trace.off[f] = o;
+    t.off[f] = o;
     o += round_up(n[f], 256);
   }
-  d->trace.rec = o;
-  d->trace.d_e = static_cast<uint32_t>(xe.d_off);
-  d->trace.s_e = static_cast<uint32_t>(xe.s_off);
-  d->trace.d_q = static_cast<uint32_t>(xq.d_off);
-  d->trace.s_q = static_cast<uint32_t>(xq.s_off);
+  t.rec = o;
+  t.d_e = static_cast<uint32_t>(xe.d_off);
+  t.s_e = static_cast<uint32_t>(xe.s_off);
+  t.d_q = static_cast<uint32_t>(xq.d_off);
+  t.s_q = static_cast<uint32_t>(xq.s_off);
   if (F) {
     const Q8Act xf = q8act_layout(F, B);
-    d->trace.d_f = static_cast<uint32_t>(xf.d_off);
-    d->trace.s_f = static_cast<uint32_t>(xf.s_off);
+    t.d_f = static_cast<uint32_t>(xf.d_off);
+    t.s_f = static_cast<uint32_t>(xf.s_off);
   }
 }
 
@@ -234,7 +248,7 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
     delete d;
     return UGB_EBACKEND;
   }
-  plan_trace(d);
+  plan_trace(d, d->trace, B);
   *out = d;
   return UGB_OK;
 }
@@ -336,6 +350,11 @@ extern "C" ugb_status ugb_decoder_bind(ugb_decoder *d, const ugb_model_weights *
           copy_bias(b + qrows + kvrows, L.bv, kvrows) != UGB_OK)
         return UGB_EBACKEND;
     }
+  }
+  if (d->pf_w) {  // the packed prefill weights are of the old tensors: prepare again
+    cudaDeviceSynchronize();
+    cudaFree(d->pf_w);
+    d->pf_w = nullptr;
   }
   d->w = *w;
   d->layers.assign(w->layers, w->layers + c.n_layer);
@@ -780,6 +799,12 @@ extern "C" ugb_status ugb_decoder_write_kv(ugb_decoder *d, ugb_stream stream, in
   return kv_copy(d, stream, seq, layer, pos, count, nullptr, nullptr, k_host, v_host);
 }
 
+namespace ugb {
+namespace {
+ugb_status sync_prefill_trace(ugb_decoder *d);
+}  // namespace
+}  // namespace ugb
+
 extern "C" ugb_status ugb_decoder_set_trace(ugb_decoder *d, int32_t enable) {
   if (!d) return UGB_ECONTEXT;
   cudaSetDevice(d->ctx->device);
@@ -799,7 +824,7 @@ extern "C" ugb_status ugb_decoder_set_trace(ugb_decoder *d, int32_t enable) {
     d->trace.base = nullptr;
     free_graph(d);
   }
-  return UGB_OK;
+  return sync_prefill_trace(d);
 }
 
 extern "C" ugb_status ugb_decoder_set_wait_limit(ugb_decoder *d, uint64_t ns) {
@@ -878,4 +903,263 @@ extern "C" ugb_status ugb_decoder_token(ugb_decoder *d, ugb_stream stream, int32
   const ugb_status st = ugb_decoder_tokens(d, stream, t, pos, n);
   *next_token = n[0];
   return st;
+}
+
+// ---- whole-prompt prefill ------------------------------------------------------------------
+
+namespace ugb {
+namespace {
+
+// (Re)allocate the prefill trace when tracing is on and a prefill is prepared.
+ugb_status sync_prefill_trace(ugb_decoder *d) {
+  const bool want = d->trace.base && d->pf_max > 0;
+  if (d->ptrace.base && (!want || d->ptrace.rec == 0)) {
+    cudaDeviceSynchronize();
+    cudaFree(d->ptrace.base);
+    d->ptrace.base = nullptr;
+  }
+  if (!want || d->ptrace.base) return UGB_OK;
+  plan_trace(d, d->ptrace, d->pf_max);
+  const size_t bytes = d->ptrace.rec * (static_cast<size_t>(d->cfg.n_layer) + 1);
+  void *p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) return UGB_EBACKEND;
+  if (cudaMemset(p, 0, bytes) != cudaSuccess) {
+    cudaFree(p);
+    return UGB_EBACKEND;
+  }
+  d->ptrace.base = static_cast<uint8_t *>(p);
+  return UGB_OK;
+}
+
+// Sequence 0's state after a prefill of n tokens from pos0: the last prompt token at position
+// pos0 + n - 1, greedy key cleared for the head's argmax.
+__global__ void prefill_state_kernel(const int32_t *__restrict__ tokens, int n, int pos0, DecodeState *state) {
+  state->token[0] = tokens[n - 1];
+  state->pos = pos0 + n - 1;
+  state->key[0] = 0;
+}
+
+// Every kernel of one prefill, enqueued on `s` (graph-capturable).
+ugb_status prefill_enqueue(ugb_decoder *d, cudaStream_t s, const int32_t *tokens, int n, int pos0) {
+  const ugb_decoder_config &c = d->cfg;
+  ugb_ctx *ctx = d->ctx;
+  uint32_t *status = ctx->status;
+  const int E = c.n_embd, Q = c.n_head * c.head_dim, KV = c.n_head_kv * c.head_dim, F = c.n_ff;
+  const int brow = Q + 2 * KV;
+  const size_t kv_layer = static_cast<size_t>(KV) * c.n_ctx * (d->kv16 ? sizeof(__half) : sizeof(float));
+  const TraceMap &T = d->ptrace;
+  // trace: the first n rows of field f of record l from a [n][len] buffer
+  auto tcopy = [&](int l, int f, const void *src, int64_t len) {
+    return T.base ? cuda_status(cudaMemcpyAsync(T.at(l, f), src, static_cast<size_t>(n) * len * 4,
+                                                cudaMemcpyDeviceToDevice, s))
+                  : UGB_OK;
+  };
+  auto gemm = [&](size_t w_off, const float *x, int64_t k, float *y, int64_t rows, int64_t ldy) {
+    ugb_status st = launch_prefill_quant(ctx, s, x, n, k, k, d->pf_act);
+    if (st == UGB_OK) st = launch_prefill_gemm(ctx, s, d->pf_w + w_off, d->pf_act, y, n, rows, k, ldy);
+    return st;
+  };
+  ugb_status st = launch_pf_embed(s, static_cast<const uint8_t *>(d->w.tok_embd), tokens, n, E, c.n_vocab, d->pf_x,
+                                  status);
+  for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
+    const ugb_layer_weights &L = d->layers[l];
+    const size_t *off = d->pf_off.data() + 5 * l;
+    st = launch_pf_rmsnorm(s, d->pf_x, l ? d->pf_tmp : nullptr, static_cast<const float *>(L.attn_norm), n, E,
+                           c.norm_eps, d->pf_y, status);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_X, d->pf_x, E);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_ATTN_NORM, d->pf_y, E);
+    if (st == UGB_OK) st = gemm(off[0], d->pf_y, E, d->pf_qkv, brow, brow);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_QKV, d->pf_qkv, brow);
+    PrefillAttn a{};
+    a.qkv = d->pf_qkv;
+    a.ld = brow;
+    a.bias = d->bias ? d->bias + static_cast<size_t>(l) * brow : nullptr;
+    a.rope = d->rope;
+    a.q = d->pf_q;
+    a.kcache = static_cast<uint8_t *>(d->kcache) + kv_layer * l;
+    a.vcache = static_cast<uint8_t *>(d->vcache) + kv_layer * l;
+    a.kv16 = d->kv16;
+    a.out = d->pf_y;
+    a.n = n;
+    a.pos0 = pos0;
+    a.n_head = c.n_head;
+    a.n_kv = c.n_head_kv;
+    a.n_ctx = c.n_ctx;
+    if (st == UGB_OK) st = launch_pf_rope_kv(s, a);
+    if (st == UGB_OK) st = launch_pf_attention(s, a);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_ATT, d->pf_y, Q);
+    if (st == UGB_OK) st = gemm(off[1], d->pf_y, Q, d->pf_tmp, E, E);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_O, d->pf_tmp, E);
+    if (st == UGB_OK)
+      st = launch_pf_rmsnorm(s, d->pf_x, d->pf_tmp, static_cast<const float *>(L.ffn_norm), n, E, c.norm_eps, d->pf_y,
+                             status);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_FFN_NORM, d->pf_y, E);
+    if (d->pf_gu_fused) {
+      if (st == UGB_OK) st = gemm(off[2], d->pf_y, E, d->pf_gu, 2 * F, 2 * F);
+    } else {
+      if (st == UGB_OK) st = gemm(off[2], d->pf_y, E, d->pf_gu, F, 2 * F);
+      if (st == UGB_OK) st = launch_prefill_gemm(ctx, s, d->pf_w + off[3], d->pf_act, d->pf_gu + F, n, F, E, 2 * F);
+    }
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_GATE_UP, d->pf_gu, 2 * F);
+    if (st == UGB_OK) st = launch_pf_silu(s, d->pf_gu, 2 * F, n, F, d->pf_y);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_H, d->pf_y, F);
+    if (st == UGB_OK) st = gemm(off[4], d->pf_y, F, d->pf_tmp, E, E);
+    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_DOWN, d->pf_tmp, E);
+  }
+  if (st != UGB_OK) return st;
+  // Only the last prompt token goes through the head (gpu_prefill.rs:138-148): its residual plus
+  // the last down projection, the output norm and Q8_1, the head matvec and greedy selection.
+  float *x_last = d->pf_x + static_cast<size_t>(n - 1) * E;
+  st = launch_rmsnorm_quant(s, false, x_last, d->pf_tmp + static_cast<size_t>(n - 1) * E,
+                            static_cast<const float *>(d->w.output_norm), E, 1, c.norm_eps, d->pf_xq, nullptr, status,
+                            T.f32(c.n_layer, UGB_TRACE_ATTN_NORM));
+  if (st == UGB_OK && T.base)
+    st = cuda_status(cudaMemcpyAsync(T.at(c.n_layer, UGB_TRACE_X), x_last, E * 4, cudaMemcpyDeviceToDevice, s));
+  if (st == UGB_OK && T.base)
+    st = cuda_status(cudaMemcpyAsync(T.at(c.n_layer, UGB_TRACE_ATTN_XQ), d->pf_xq, q8act_layout(E, 1).bytes,
+                                     cudaMemcpyDeviceToDevice, s));
+  if (st != UGB_OK) return st;
+  MatvecArgs a = mv_args(c.head_kind, E, c.n_vocab, 1, d->pf_xq, d->logits);
+  a.w = static_cast<const uint8_t *>(d->w.output);
+  a.pdl = false;
+  st = launch_matvec(ctx, s, a);
+  if (st != UGB_OK) return st;
+  prefill_state_kernel<<<1, 1, 0, s>>>(tokens, n, pos0, d->state);
+  st = cuda_status(cudaGetLastError());
+  if (st == UGB_OK) st = launch_argmax(s, false, d->logits, c.n_vocab, 1, 0, d->state, ctx->sm_count);
+  return st;
+}
+
+}  // namespace
+}  // namespace ugb
+
+extern "C" ugb_status ugb_decoder_prefill_prepare(ugb_decoder *d, ugb_stream stream, int32_t max_tokens) {
+  if (!d || !d->w.layers) return UGB_ECONTEXT;
+  const ugb_decoder_config &c = d->cfg;
+  if (d->moe || d->batch != 1 || c.kind != UGB_Q8_0 || d->n_vocab_local != c.n_vocab) return UGB_ESHAPE;
+  if (max_tokens < 1 || max_tokens > c.n_ctx) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return UGB_EBACKEND;
+  if (d->pf_w) cudaFree(d->pf_w);
+  if (d->pf_ws) cudaFree(d->pf_ws);
+  d->pf_w = d->pf_ws = nullptr;
+  d->pf_max = 0;
+  const int64_t E = c.n_embd, Q = static_cast<int64_t>(c.n_head) * c.head_dim,
+                KV = static_cast<int64_t>(c.n_head_kv) * c.head_dim, F = c.n_ff, brow = Q + 2 * KV;
+  d->pf_gu_fused = F % kPrefillTile == 0;
+  // packed weights: per layer qkv (one operand, the three matrices' 128-row tiles back to back),
+  // o, gate (with up when fused), up (unfused), down
+  d->pf_off.assign(5 * static_cast<size_t>(c.n_layer), 0);
+  size_t total = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = total;
+    total += round_up(bytes, 256);
+    return o;
+  };
+  for (int l = 0; l < c.n_layer; ++l) {
+    size_t *off = d->pf_off.data() + 5 * l;
+    off[0] = take(prefill_layout(brow, E).bytes);
+    off[1] = take(prefill_layout(E, Q).bytes);
+    off[2] = take(prefill_layout(d->pf_gu_fused ? 2 * F : F, E).bytes);
+    off[3] = d->pf_gu_fused ? 0 : take(prefill_layout(F, E).bytes);
+    off[4] = take(prefill_layout(E, F).bytes);
+  }
+  const int64_t M = max_tokens, W = std::max({E, Q, F});
+  size_t ws = 0;
+  auto wtake = [&](size_t bytes) {
+    const size_t o = ws;
+    ws += round_up(bytes, 256);
+    return o;
+  };
+  const size_t o_x = wtake(M * E * 4), o_y = wtake(M * W * 4), o_qkv = wtake(M * brow * 4), o_q = wtake(M * Q * 4),
+               o_gu = wtake(M * 2 * F * 4), o_tmp = wtake(M * E * 4), o_act = wtake(prefill_layout(M, W).bytes),
+               o_xq = wtake(q8act_layout(E, 1).bytes), o_tok = wtake(M * 4);
+  if (cudaMalloc(&d->pf_w, total) != cudaSuccess) return UGB_EBACKEND;
+  if (cudaMalloc(&d->pf_ws, ws) != cudaSuccess) {
+    cudaFree(d->pf_w);
+    d->pf_w = nullptr;
+    return UGB_EBACKEND;
+  }
+  d->pf_x = reinterpret_cast<float *>(d->pf_ws + o_x);
+  d->pf_y = reinterpret_cast<float *>(d->pf_ws + o_y);
+  d->pf_qkv = reinterpret_cast<float *>(d->pf_ws + o_qkv);
+  d->pf_q = reinterpret_cast<float *>(d->pf_ws + o_q);
+  d->pf_gu = reinterpret_cast<float *>(d->pf_ws + o_gu);
+  d->pf_tmp = reinterpret_cast<float *>(d->pf_ws + o_tmp);
+  d->pf_act = d->pf_ws + o_act;
+  d->pf_xq = d->pf_ws + o_xq;
+  d->pf_tokens = reinterpret_cast<int32_t *>(d->pf_ws + o_tok);
+  // repack: matrix `w` of `rows` rows at 128-row tile `tile0` of the operand at `off` of `all_rows`
+  ugb_status st = UGB_OK;
+  auto pack = [&](size_t off, int64_t all_rows, int64_t k, const void *w, int64_t rows, int64_t tile0) {
+    if (st != UGB_OK) return;
+    const PackedLayout p = prefill_layout(all_rows, k);
+    uint8_t *q = d->pf_w + off + static_cast<size_t>(tile0) * p.nb * kPrefillTileBytes;
+    float *sc = reinterpret_cast<float *>(d->pf_w + off + p.q_bytes) + static_cast<size_t>(tile0) * p.nb * kPrefillTile;
+    st = launch_prefill_repack(stream, static_cast<const uint8_t *>(w), rows, k, q, sc);
+  };
+  for (int l = 0; l < c.n_layer; ++l) {
+    const ugb_layer_weights &L = d->layers[l];
+    const size_t *off = d->pf_off.data() + 5 * l;
+    pack(off[0], brow, E, L.wq, Q, 0);
+    pack(off[0], brow, E, L.wk, KV, Q / kPrefillTile);
+    pack(off[0], brow, E, L.wv, KV, (Q + KV) / kPrefillTile);
+    pack(off[1], E, Q, L.wo, E, 0);
+    if (d->pf_gu_fused) {
+      pack(off[2], 2 * F, E, L.w_gate, F, 0);
+      pack(off[2], 2 * F, E, L.w_up, F, F / kPrefillTile);
+    } else {
+      pack(off[2], F, E, L.w_gate, F, 0);
+      pack(off[3], F, E, L.w_up, F, 0);
+    }
+    pack(off[4], E, F, L.w_down, E, 0);
+  }
+  if (st == UGB_OK) st = cuda_status(cudaStreamSynchronize(stream));
+  if (st != UGB_OK) return st;
+  d->pf_max = max_tokens;
+  return sync_prefill_trace(d);
+}
+
+extern "C" ugb_status ugb_decoder_prefill_async(ugb_decoder *d, ugb_stream stream, const int32_t *tokens_dev, int32_t n,
+                                                int32_t pos0) {
+  if (!d || !d->pf_w || !tokens_dev) return UGB_ECONTEXT;
+  if (n < 1 || n > d->pf_max || pos0 < 0 || pos0 + n > d->cfg.n_ctx) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  return prefill_enqueue(d, stream, tokens_dev, n, pos0);
+}
+
+extern "C" ugb_status ugb_decoder_prefill(ugb_decoder *d, ugb_stream stream, const int32_t *tokens_host, int32_t n,
+                                          int32_t pos0, int32_t *next_token) {
+  if (!d || !d->pf_w || !tokens_host || !next_token) return UGB_ECONTEXT;
+  if (n < 1 || n > d->pf_max || pos0 < 0 || pos0 + n > d->cfg.n_ctx) return UGB_ESHAPE;
+  for (int i = 0; i < n; ++i)
+    if (tokens_host[i] < 0 || tokens_host[i] >= d->cfg.n_vocab) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  if (cudaMemcpyAsync(d->pf_tokens, tokens_host, static_cast<size_t>(n) * 4, cudaMemcpyHostToDevice, stream) !=
+      cudaSuccess)
+    return UGB_EBACKEND;
+  ugb_status st = prefill_enqueue(d, stream, d->pf_tokens, n, pos0);
+  if (st != UGB_OK) return st;
+  if (cudaMemcpyAsync(d->state_host, d->state, sizeof(DecodeState), cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  st = ugb_status_read(d->ctx, stream, nullptr);  // synchronises the stream
+  if (st != UGB_OK) return st;
+  *next_token = next_of(d->state_host, 0);
+  return *next_token < 0 ? UGB_ENONFINITE : UGB_OK;
+}
+
+extern "C" size_t ugb_decoder_prefill_trace_bytes(const ugb_decoder *d, int32_t field) {
+  if (!d || field < 0 || field >= UGB_TRACE_FIELDS || !d->ptrace.base) return 0;
+  return d->ptrace.bytes[field];
+}
+
+extern "C" ugb_status ugb_decoder_read_prefill_trace(ugb_decoder *d, ugb_stream stream, int32_t layer, int32_t field,
+                                                     void *host, size_t bytes) {
+  if (!d || !host || !d->ptrace.base) return UGB_ECONTEXT;
+  if (field < 0 || field >= UGB_TRACE_FIELDS || layer < 0 || layer > d->cfg.n_layer) return UGB_ESHAPE;
+  if (bytes == 0 || bytes > d->ptrace.bytes[field]) return UGB_ESHAPE;
+  cudaSetDevice(d->ctx->device);
+  if (cudaMemcpyAsync(host, d->ptrace.at(layer, field), bytes, cudaMemcpyDeviceToHost, stream) != cudaSuccess)
+    return UGB_EBACKEND;
+  return cuda_status(cudaStreamSynchronize(stream));
 }

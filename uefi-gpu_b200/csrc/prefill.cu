@@ -478,21 +478,19 @@ ugb_status init_prefill_kernels(ugb_ctx *ctx) {
       cudaFuncSetAttribute(prefill_gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<64>::kSmem));
 }
 
-namespace {
-
-struct Packed {
-  int64_t tiles = 0, nb = 0;
-  size_t q_bytes = 0, bytes = 0;
-};
-
-Packed packed_layout(int64_t rows, int64_t k) {
-  Packed p;
+PackedLayout prefill_layout(int64_t rows, int64_t k) {
+  PackedLayout p;
   p.tiles = (rows + kPrefillTile - 1) / kPrefillTile;
   p.nb = k / 32;
   p.q_bytes = static_cast<size_t>(p.tiles * p.nb) * kPrefillTileBytes;
   p.bytes = p.q_bytes + static_cast<size_t>(p.tiles * p.nb) * kPrefillTile * sizeof(float);
   return p;
 }
+
+namespace {
+
+using Packed = PackedLayout;
+inline Packed packed_layout(int64_t rows, int64_t k) { return prefill_layout(rows, k); }
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -532,6 +530,42 @@ ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, 
 }
 
 }  // namespace
+
+ugb_status launch_prefill_repack(cudaStream_t stream, const uint8_t *w, int64_t n, int64_t k, uint8_t *q_out,
+                                 float *s_out) {
+  const Packed pw = packed_layout(n, k);
+  const int64_t total = pw.tiles * kPrefillTile * pw.nb * 2;
+  const int64_t blocks = (total + 255) / 256;
+  if (blocks > 0x7fffffff) return UGB_ESHAPE;
+  repack_q8_0_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(w, n, static_cast<int>(pw.nb), pw.tiles,
+                                                                        q_out, s_out);
+  return cuda_status(cudaGetLastError());
+}
+
+ugb_status launch_prefill_quant(ugb_ctx *ctx, cudaStream_t stream, const float *x, int64_t m, int64_t k, int64_t ldx,
+                                uint8_t *packed) {
+  const Packed px = packed_layout(m, k);
+  const int64_t warps = px.tiles * kPrefillTile * px.nb;
+  const int64_t blocks = (warps + 7) / 8;
+  if (blocks > 0x7fffffff) return UGB_ESHAPE;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_status(cudaLaunchKernelEx(&cfg, prefill_quant_kernel, x, m, k, ldx, px.tiles, packed,
+                                        reinterpret_cast<float *>(packed + px.q_bytes), ctx->status));
+}
+
+ugb_status launch_prefill_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, const void *x_packed,
+                               float *y, int64_t m, int64_t n, int64_t k, int64_t ldy) {
+  return launch_gemm(ctx, stream, w_packed, x_packed, y, nullptr, m, n, k, ldy);
+}
+
 }  // namespace ugb
 
 using namespace ugb;
@@ -550,13 +584,8 @@ ugb_status ugb_prefill_repack_q8_0(ugb_ctx *ctx, ugb_stream stream, const void *
   if (!w_dev || !packed_dev || !aligned16(packed_dev)) return UGB_EALIGN;
   const Packed pw = packed_layout(n, k);
   uint8_t *q = static_cast<uint8_t *>(packed_dev);
-  const int64_t total = pw.tiles * kPrefillTile * pw.nb * 2;
-  const int64_t blocks = (total + 255) / 256;
-  if (blocks > 0x7fffffff) return UGB_ESHAPE;
-  repack_q8_0_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
-      static_cast<const uint8_t *>(w_dev), n, static_cast<int>(pw.nb), pw.tiles, q,
-      reinterpret_cast<float *>(q + pw.q_bytes));
-  return cuda_status(cudaGetLastError());
+  return launch_prefill_repack(stream, static_cast<const uint8_t *>(w_dev), n, k, q,
+                               reinterpret_cast<float *>(q + pw.q_bytes));
 }
 
 ugb_status ugb_prefill_quant(ugb_ctx *ctx, ugb_stream stream, const float *x_dev, int64_t m, int64_t k,
@@ -564,22 +593,7 @@ ugb_status ugb_prefill_quant(ugb_ctx *ctx, ugb_stream stream, const float *x_dev
   if (!ctx || !ctx->status) return UGB_ECONTEXT;
   if (m < 1 || k < 32 || k % 32) return UGB_ESHAPE;
   if (!x_dev || !packed_dev || !aligned16(packed_dev)) return UGB_EALIGN;
-  const Packed px = packed_layout(m, k);
-  uint8_t *q = static_cast<uint8_t *>(packed_dev);
-  const int64_t warps = px.tiles * kPrefillTile * px.nb;
-  const int64_t blocks = (warps + 7) / 8;
-  if (blocks > 0x7fffffff) return UGB_ESHAPE;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
-  cfg.blockDim = dim3(256);
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cuda_status(cudaLaunchKernelEx(&cfg, prefill_quant_kernel, x_dev, m, k, k, px.tiles, q,
-                                        reinterpret_cast<float *>(q + px.q_bytes), ctx->status));
+  return launch_prefill_quant(ctx, stream, x_dev, m, k, k, static_cast<uint8_t *>(packed_dev));
 }
 
 ugb_status ugb_prefill_gemm_q8_0(ugb_ctx *ctx, ugb_stream stream, const void *w_packed, const void *x_packed,

@@ -481,7 +481,8 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
     d[k] = dx && i < n ? __ldcg(dx + i) : 0.f;
     wv[k] = b < n / 32 ? w[b * 32 + lane] : 0.f;
   }
-  float *tx = TRACE && rec >= 0 ? p.trace.f32(rec, UGB_TRACE_X) : nullptr;
+  // X is the residual entering a layer (or the head): the attention-side norm's input only
+  float *tx = TRACE && rec >= 0 && fn == UGB_TRACE_ATTN_NORM ? p.trace.f32(rec, UGB_TRACE_X) : nullptr;
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
