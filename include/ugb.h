@@ -511,6 +511,90 @@ size_t ugb_decoder_prefill_trace_bytes(const ugb_decoder *dec, int32_t field);
 ugb_status ugb_decoder_read_prefill_trace(ugb_decoder *dec, ugb_stream stream, int32_t layer, int32_t field,
                                           void *host, size_t bytes);
 
+/* ---- GGUF ingestion ------------------------------------------------------------------------ */
+
+/* A parsed GGUF v3 directory (one file, or one shard of a split model): metadata and tensor
+ * table, bounded and checked as the reference's Shard::parse (frontier_gguf.rs:145-200).  Tensor
+ * bodies are not read: the directory gives each tensor's absolute file range, and the caller
+ * copies the bytes it needs to the device.  The object copies what it keeps, so the prefix may be
+ * freed after parsing.  Host code only; no CUDA call. */
+typedef struct ugb_gguf ugb_gguf;
+
+/* Results of the ugb_gguf_* calls: 0 or the reference's frontier_gguf::Error variant
+ * (frontier_gguf.rs:7-8), in its order. */
+enum {
+  UGB_GGUF_OK = 0, UGB_GGUF_TRUNCATED, UGB_GGUF_MAGIC, UGB_GGUF_VERSION, UGB_GGUF_LIMIT, UGB_GGUF_TYPE,
+  UGB_GGUF_UTF8, UGB_GGUF_ALIGNMENT, UGB_GGUF_SHAPE, UGB_GGUF_OVERFLOW, UGB_GGUF_TENSOR_BOUNDS,
+  UGB_GGUF_OVERLAP, UGB_GGUF_DUPLICATE, UGB_GGUF_MISSING, UGB_GGUF_SPLIT
+};
+
+/* One tensor of the directory (Tensor, frontier_gguf.rs:84-88): dims[0] is the row length;
+ * offset is absolute in the file (data section start + the tensor's own offset); bytes =
+ * row_bytes x dims[1] x ... ; name is owned by the ugb_gguf. */
+typedef struct ugb_gguf_tensor {
+  const char *name;
+  uint64_t dims[4];
+  uint32_t rank, kind;
+  uint64_t offset, bytes, row_bytes;
+} ugb_gguf_tensor;
+
+/* Parse the header prefix of a file of logical_bytes bytes (the prefix must hold the whole
+ * directory, at most 16 MiB).  Limits: version 3, <= 4096 tensors, <= 1024 keys, keys and names
+ * <= 256 bytes, strings <= 16 MiB, arrays <= 1e6 elements and not nested, alignment a power of
+ * two <= 4096 (default 32), split.no < split.count <= 64, tensors rank 1..4 with non-zero dims,
+ * aligned offsets, row lengths whole blocks of their kind, every tensor inside the file, no two
+ * overlapping.  Kinds: those of ugb_row_bytes plus F16. */
+int32_t ugb_gguf_parse(const uint8_t *prefix, size_t prefix_len, uint64_t logical_bytes, ugb_gguf **out);
+void ugb_gguf_free(ugb_gguf *g);
+/* data_offset: start of the data section; split_no / split_count / total_tensors of the split
+ * set (0 / 1 / this file's count for an unsplit file). */
+int32_t ugb_gguf_info(const ugb_gguf *g, uint64_t *data_offset, uint64_t *split_no, uint64_t *split_count,
+                      uint64_t *total_tensors, int64_t *n_tensors);
+int32_t ugb_gguf_tensor_at(const ugb_gguf *g, int64_t index, ugb_gguf_tensor *out);
+int32_t ugb_gguf_find_tensor(const ugb_gguf *g, const char *name, ugb_gguf_tensor *out);
+/* Absolute file range of rows [start, start + count) (Tensor::rows), and of expert `id` of a
+ * rank-3 stacked expert tensor (Tensor::expert, frontier_gguf.rs:89-104). */
+int32_t ugb_gguf_tensor_rows(const ugb_gguf_tensor *t, uint64_t start, uint64_t count, uint64_t *offset,
+                             uint64_t *bytes);
+int32_t ugb_gguf_tensor_expert(const ugb_gguf_tensor *t, uint32_t id, uint64_t *offset, uint64_t *bytes);
+
+/* Metadata (Value, frontier_gguf.rs:42-72).  kind: the GGUF value type (0 u8 .. 12 f64).
+ * unsigned: u8 / u16 / u32 / u64 values; float: f32; string: copies at most cap bytes and gives
+ * the full length; array: element kind and count, and element `index` of an unsigned or string
+ * array.  UGB_GGUF_MISSING for an absent key, UGB_GGUF_TYPE for another kind. */
+int32_t ugb_gguf_meta_kind(const ugb_gguf *g, const char *key, uint32_t *kind);
+int32_t ugb_gguf_meta_unsigned(const ugb_gguf *g, const char *key, uint64_t *value);
+int32_t ugb_gguf_meta_float(const ugb_gguf *g, const char *key, float *value);
+int32_t ugb_gguf_meta_string(const ugb_gguf *g, const char *key, char *buf, size_t cap, size_t *len);
+int32_t ugb_gguf_meta_array(const ugb_gguf *g, const char *key, uint32_t *elem_kind, uint64_t *count);
+int32_t ugb_gguf_meta_array_unsigned(const ugb_gguf *g, const char *key, uint64_t index, uint64_t *value);
+int32_t ugb_gguf_meta_array_string(const ugb_gguf *g, const char *key, uint64_t index, char *buf, size_t cap,
+                                   size_t *len);
+
+/* A split model's shards as one directory (ModelIndex::new, frontier_gguf.rs:113-125): shard i
+ * must be split i of `count`, all with the same total tensor count, no name twice, and every
+ * tensor present (UGB_GGUF_SPLIT / UGB_GGUF_DUPLICATE otherwise).  inventory: on-disk bytes of
+ * ordinary tensors, of per_layer_token_embd.weight and of *_exps.weight tensors
+ * (ModelIndex::inventory). */
+int32_t ugb_gguf_check_index(ugb_gguf *const *shards, int32_t count);
+int32_t ugb_gguf_inventory(ugb_gguf *const *shards, int32_t count, uint64_t *counts /* [3] */);
+
+/* A Qwen2 / Qwen3-MoE decoder from a model's directory (shards as ugb_gguf_check_index accepts):
+ * ugb_gguf_decoder_config fills the shape from the architecture's metadata (<arch>.block_count,
+ * embedding_length, feed_forward_length, attention.head_count(_kv), context_length,
+ * rope.freq_base, attention.layer_norm_rms_epsilon, expert_count, expert_used_count,
+ * expert_feed_forward_length) and the kinds from the tensors; batch 1, all experts and head rows,
+ * fp32 KV.  ugb_gguf_model_weights points every tensor of cfg's layers into device copies of the
+ * shards' bytes: dev_bases[i] holds shard i's file bytes from file offset base_offsets[i]
+ * (normally its data_offset), dev_sizes[i] bytes of them; a tied model (no output.weight) reuses
+ * token_embd.weight.  layers: n_layer entries.  UGB_GGUF_MISSING names no tensor, and
+ * UGB_GGUF_SHAPE / UGB_GGUF_TYPE a tensor whose dims or kind do not fit cfg. */
+int32_t ugb_gguf_decoder_config(ugb_gguf *const *shards, int32_t count, ugb_decoder_config *cfg);
+int32_t ugb_gguf_model_weights(ugb_gguf *const *shards, int32_t count, const void *const *dev_bases,
+                               const uint64_t *base_offsets, const uint64_t *dev_sizes,
+                               const ugb_decoder_config *cfg, ugb_model_weights *weights,
+                               ugb_layer_weights *layers);
+
 /* ---- host-buffer entry points (synchronous) --------------------------------------------- */
 
 /* y_host[m] = W x_host[k], synchronously: copy x to the device, quantise, matvec, copy y

@@ -95,6 +95,27 @@ SIGNATURES = {
     "ugb_decoder_test_unreachable_wait": (_int, [_vp, ctypes.c_int32]),
     "ugb_decoder_trace_bytes": (ctypes.c_size_t, [_vp, ctypes.c_int32]),
     "ugb_decoder_read_trace": (_int, [_vp, _vp, ctypes.c_int32, ctypes.c_int32, _vp, ctypes.c_size_t]),
+    "ugb_gguf_parse": (ctypes.c_int32, [_vp, ctypes.c_size_t, _u64, ctypes.POINTER(_vp)]),
+    "ugb_gguf_free": (None, [_vp]),
+    "ugb_gguf_info": (ctypes.c_int32, [_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64), ctypes.POINTER(_u64),
+                                       ctypes.POINTER(_u64), ctypes.POINTER(_i64)]),
+    "ugb_gguf_tensor_at": (ctypes.c_int32, [_vp, _i64, _vp]),
+    "ugb_gguf_find_tensor": (ctypes.c_int32, [_vp, ctypes.c_char_p, _vp]),
+    "ugb_gguf_tensor_rows": (ctypes.c_int32, [_vp, _u64, _u64, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
+    "ugb_gguf_tensor_expert": (ctypes.c_int32, [_vp, _u32, ctypes.POINTER(_u64), ctypes.POINTER(_u64)]),
+    "ugb_gguf_meta_kind": (ctypes.c_int32, [_vp, ctypes.c_char_p, ctypes.POINTER(_u32)]),
+    "ugb_gguf_meta_unsigned": (ctypes.c_int32, [_vp, ctypes.c_char_p, ctypes.POINTER(_u64)]),
+    "ugb_gguf_meta_float": (ctypes.c_int32, [_vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_float)]),
+    "ugb_gguf_meta_string": (ctypes.c_int32, [_vp, ctypes.c_char_p, _vp, ctypes.c_size_t,
+                                              ctypes.POINTER(ctypes.c_size_t)]),
+    "ugb_gguf_meta_array": (ctypes.c_int32, [_vp, ctypes.c_char_p, ctypes.POINTER(_u32), ctypes.POINTER(_u64)]),
+    "ugb_gguf_meta_array_unsigned": (ctypes.c_int32, [_vp, ctypes.c_char_p, _u64, ctypes.POINTER(_u64)]),
+    "ugb_gguf_meta_array_string": (ctypes.c_int32, [_vp, ctypes.c_char_p, _u64, _vp, ctypes.c_size_t,
+                                                    ctypes.POINTER(ctypes.c_size_t)]),
+    "ugb_gguf_check_index": (ctypes.c_int32, [_vp, ctypes.c_int32]),
+    "ugb_gguf_inventory": (ctypes.c_int32, [_vp, ctypes.c_int32, _vp]),
+    "ugb_gguf_decoder_config": (ctypes.c_int32, [_vp, ctypes.c_int32, _vp]),
+    "ugb_gguf_model_weights": (ctypes.c_int32, [_vp, ctypes.c_int32, _vp, _vp, _vp, _vp, _vp, _vp]),
     "ugb_graph_begin": (_int, [_vp, _vp]),
     "ugb_graph_end": (_int, [_vp, _vp, ctypes.POINTER(_vp)]),
     "ugb_graph_launch": (_int, [_vp, _vp]),
@@ -585,6 +606,186 @@ class Decoder:
         check("ugb_decoder_token", lib().ugb_decoder_token(self.handle, _stream(stream), token, pos,
                                                              ctypes.byref(nxt)))
         return nxt.value
+
+
+GGUF_ERRORS = ("ok", "truncated", "magic", "version", "limit", "type", "utf8", "alignment", "shape", "overflow",
+               "tensor_bounds", "overlap", "duplicate", "missing", "split")
+
+
+class GgufError(ValueError):
+    def __init__(self, fn: str, code: int):
+        name = GGUF_ERRORS[code] if 0 <= code < len(GGUF_ERRORS) else str(code)
+        super().__init__(f"{fn} failed: {name} ({code})")
+        self.code = code
+        self.name = name
+
+
+def _gcheck(fn: str, code: int) -> None:
+    if code != 0:
+        raise GgufError(fn, code)
+
+
+class GgufTensor(ctypes.Structure):
+    """ugb_gguf_tensor."""
+    _fields_ = [("name", ctypes.c_char_p), ("dims", _u64 * 4), ("rank", _u32), ("kind", _u32),
+                ("offset", _u64), ("bytes", _u64), ("row_bytes", _u64)]
+
+
+class Gguf:
+    """A parsed GGUF directory (ugb_gguf_parse): one file or one shard of a split model."""
+
+    def __init__(self, prefix: bytes, logical_bytes: int | None = None):
+        buf = (ctypes.c_uint8 * len(prefix)).from_buffer_copy(prefix) if prefix else None
+        h = _vp()
+        total = len(prefix) if logical_bytes is None else logical_bytes
+        _gcheck("ugb_gguf_parse", lib().ugb_gguf_parse(buf, len(prefix), total, ctypes.byref(h)))
+        self.handle = h
+
+    @classmethod
+    def open(cls, path: str) -> "Gguf":
+        """Parse the directory of a file (its first 16 MiB hold it, as the format's limits require)."""
+        size = os.path.getsize(path)
+        with open(path, "rb") as f:
+            prefix = f.read(min(size, 16 * 1024 * 1024))
+        return cls(prefix, size)
+
+    def close(self) -> None:
+        if self.handle:
+            lib().ugb_gguf_free(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def info(self) -> dict:
+        v = [_u64() for _ in range(4)]
+        n = _i64()
+        _gcheck("ugb_gguf_info", lib().ugb_gguf_info(self.handle, *[ctypes.byref(x) for x in v], ctypes.byref(n)))
+        return dict(data_offset=v[0].value, split_no=v[1].value, split_count=v[2].value, total_tensors=v[3].value,
+                    n_tensors=n.value)
+
+    def tensors(self) -> list:
+        out = []
+        for i in range(self.info()["n_tensors"]):
+            t = GgufTensor()
+            _gcheck("ugb_gguf_tensor_at", lib().ugb_gguf_tensor_at(self.handle, i, ctypes.byref(t)))
+            out.append(t)
+        return out
+
+    def tensor(self, name: str) -> GgufTensor:
+        t = GgufTensor()
+        _gcheck("ugb_gguf_find_tensor", lib().ugb_gguf_find_tensor(self.handle, name.encode(), ctypes.byref(t)))
+        return t
+
+    @staticmethod
+    def rows(t: GgufTensor, start: int, count: int) -> tuple[int, int]:
+        o, n = _u64(), _u64()
+        _gcheck("ugb_gguf_tensor_rows", lib().ugb_gguf_tensor_rows(ctypes.byref(t), start, count, ctypes.byref(o),
+                                                                     ctypes.byref(n)))
+        return o.value, n.value
+
+    @staticmethod
+    def expert(t: GgufTensor, eid: int) -> tuple[int, int]:
+        o, n = _u64(), _u64()
+        _gcheck("ugb_gguf_tensor_expert", lib().ugb_gguf_tensor_expert(ctypes.byref(t), eid, ctypes.byref(o),
+                                                                         ctypes.byref(n)))
+        return o.value, n.value
+
+    def meta(self, key: str):
+        """A metadata value as Python: int (unsigned kinds), float (f32), str, or list (arrays of
+        unsigned or string elements)."""
+        k = key.encode()
+        kind = _u32()
+        _gcheck("ugb_gguf_meta_kind", lib().ugb_gguf_meta_kind(self.handle, k, ctypes.byref(kind)))
+        if kind.value in (0, 2, 4, 10):
+            v = _u64()
+            _gcheck("ugb_gguf_meta_unsigned", lib().ugb_gguf_meta_unsigned(self.handle, k, ctypes.byref(v)))
+            return v.value
+        if kind.value == 6:
+            f = ctypes.c_float()
+            _gcheck("ugb_gguf_meta_float", lib().ugb_gguf_meta_float(self.handle, k, ctypes.byref(f)))
+            return f.value
+        if kind.value == 8:
+            return self._string(lambda buf, cap, n: lib().ugb_gguf_meta_string(self.handle, k, buf, cap, n))
+        if kind.value == 9:
+            ek, count = _u32(), _u64()
+            _gcheck("ugb_gguf_meta_array", lib().ugb_gguf_meta_array(self.handle, k, ctypes.byref(ek),
+                                                                       ctypes.byref(count)))
+            out = []
+            for i in range(count.value):
+                if ek.value == 8:
+                    out.append(self._string(lambda buf, cap, n, i=i: lib().ugb_gguf_meta_array_string(
+                        self.handle, k, i, buf, cap, n)))
+                else:
+                    v = _u64()
+                    _gcheck("ugb_gguf_meta_array_unsigned",
+                            lib().ugb_gguf_meta_array_unsigned(self.handle, k, i, ctypes.byref(v)))
+                    out.append(v.value)
+            return out
+        raise GgufError("meta", 5)
+
+    @staticmethod
+    def _string(call) -> str:
+        n = ctypes.c_size_t()
+        _gcheck("ugb_gguf_meta_string", call(None, 0, ctypes.byref(n)))
+        buf = ctypes.create_string_buffer(max(1, n.value))
+        _gcheck("ugb_gguf_meta_string", call(buf, n.value, ctypes.byref(n)))
+        return buf.raw[:n.value].decode()
+
+
+def _handles(shards):
+    return (_vp * len(shards))(*[s.handle for s in shards])
+
+
+def gguf_check_index(shards) -> None:
+    _gcheck("ugb_gguf_check_index", lib().ugb_gguf_check_index(_handles(shards), len(shards)))
+
+
+def gguf_inventory(shards) -> list:
+    out = (_u64 * 3)()
+    _gcheck("ugb_gguf_inventory", lib().ugb_gguf_inventory(_handles(shards), len(shards), out))
+    return list(out)
+
+
+def gguf_decoder_config(shards) -> dict:
+    cfg = DecoderConfig()
+    _gcheck("ugb_gguf_decoder_config", lib().ugb_gguf_decoder_config(_handles(shards), len(shards),
+                                                                       ctypes.byref(cfg)))
+    return {name: getattr(cfg, name) for name, _ in DecoderConfig._fields_}
+
+
+def gguf_model_weights(shards, dev_bases, base_offsets, dev_sizes, cfg: dict):
+    """(ModelWeights, LayerWeights array) pointing into the shards' device copies."""
+    n = len(shards)
+    c = DecoderConfig(**cfg)
+    layers = (LayerWeights * c.n_layer)()
+    w = ModelWeights()
+    _gcheck("ugb_gguf_model_weights", lib().ugb_gguf_model_weights(
+        _handles(shards), n, (_vp * n)(*dev_bases), (_u64 * n)(*base_offsets), (_u64 * n)(*dev_sizes),
+        ctypes.byref(c), ctypes.byref(w), layers))
+    return w, layers
+
+
+def load_gguf_decoder(ctx: "Context", path: str, **overrides) -> "Decoder":
+    """A decoder bound to the weights of a GGUF file: the directory is parsed, the data section
+    is copied to the device once (owned by the returned decoder), and every tensor is bound in
+    place.  overrides replace configuration fields (e.g. n_ctx, batch, kv_type)."""
+    import numpy as np
+    import torch
+    g = Gguf.open(path)
+    info = g.info()
+    cfg = gguf_decoder_config([g])
+    cfg.update(overrides)
+    data = np.fromfile(path, dtype=np.uint8, offset=info["data_offset"])
+    dev = torch.from_numpy(data).to(torch.device("cuda", ctx.device))
+    w, layers = gguf_model_weights([g], [dev.data_ptr()], [info["data_offset"]], [dev.numel()], cfg)
+    dec = Decoder(ctx, **cfg)
+    check("ugb_decoder_bind", lib().ugb_decoder_bind(dec.handle, ctypes.byref(w)))
+    dec._keep = (w, layers, dev, g)
+    return dec
 
 
 class Graph:
