@@ -21,7 +21,13 @@ def strip_comments(text: str) -> str:
 
 
 def c_to_rust(ctype: str) -> str:
-    """'const void *const *' -> '*const *const c_void'."""
+    """'const void *const *' -> '*const *const c_void'; 'uint64_t[4]' -> '[u64; 4]'; a void
+    return -> '()'."""
+    arr = re.match(r"^(.*)\[(\d+)\]$", ctype)
+    if arr:
+        return f"[{c_to_rust(arr.group(1))}; {arr.group(2)}]"
+    if ctype.strip() == "void":
+        return "()"
     parts = ctype.replace("*", " * ").split()
     base, quals, i = [], [], 0
     while i < len(parts) and parts[i] != "*":
@@ -44,14 +50,15 @@ def c_to_rust(ctype: str) -> str:
 
 
 def _split_decl(decl: str):
-    """'const void *a, *b' -> [('const void *', 'a'), ('const void *', 'b')]."""
+    """'const void *a, *b' -> [('const void *', 'a'), ('const void *', 'b')]; an array field
+    'uint64_t dims[4]' -> [('uint64_t[4]', 'dims')]."""
     decl = " ".join(decl.split())
-    first = re.match(r"^(.*?)(\**)\s*(\w+)$", decl.split(",")[0].strip())
+    first = re.match(r"^(.*?)(\**)\s*(\w+)\s*(\[\d+\])?$", decl.split(",")[0].strip())
     base = first.group(1).strip()
-    out = [(f"{base} {first.group(2)}".strip(), first.group(3))]
+    out = [(f"{base} {first.group(2)}".strip() + (first.group(4) or ""), first.group(3))]
     for extra in decl.split(",")[1:]:
-        m = re.match(r"^\s*(\**)\s*(\w+)\s*$", extra)
-        out.append((f"{base} {m.group(1)}".strip(), m.group(2)))
+        m = re.match(r"^\s*(\**)\s*(\w+)\s*(\[\d+\])?\s*$", extra)
+        out.append((f"{base} {m.group(1)}".strip() + (m.group(3) or ""), m.group(2)))
     return out
 
 

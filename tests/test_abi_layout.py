@@ -56,15 +56,24 @@ def test_rust_constants_match_header():
     assert hc == rc
 
 
+def _rust_size_align(ty):
+    arr = __import__("re").match(r"^\[(.*); (\d+)\]$", ty)
+    if arr:
+        size, align = _rust_size_align(arr.group(1))
+        return size * int(arr.group(2)), align
+    size = 8 if ty.startswith("*") else RUST_SIZES[ty]
+    return size, size
+
+
 def _rust_layout(fields):
     """repr(C) offsets and size of a struct of the given Rust field types."""
     off, align, out = 0, 1, []
     for name, ty in fields:
-        size = 8 if ty.startswith("*") else RUST_SIZES[ty]
-        off = (off + size - 1) // size * size
+        size, a = _rust_size_align(ty)
+        off = (off + a - 1) // a * a
         out.append((name, off))
         off += size
-        align = max(align, size)
+        align = max(align, a)
     return out, (off + align - 1) // align * align
 
 
@@ -107,7 +116,8 @@ def test_c_layout_equals_rust_repr_c():
 def test_c_layout_equals_ctypes(ugb):
     c = _c_layout()
     binding = {"ugb_job": ugb.Job, "ugb_moe_args": ugb.MoeArgs, "ugb_decoder_config": ugb.DecoderConfig,
-               "ugb_layer_weights": ugb.LayerWeights, "ugb_model_weights": ugb.ModelWeights}
+               "ugb_layer_weights": ugb.LayerWeights, "ugb_model_weights": ugb.ModelWeights,
+               "ugb_gguf_tensor": ugb.GgufTensor}
     assert set(binding) == set(c)
     for name, cls in binding.items():
         size, offs = c[name]
