@@ -67,7 +67,10 @@ struct ugb_decoder {
   uint8_t *pf_w = nullptr;   // all layers' packed weights
   std::vector<size_t> pf_off;  // per layer: qkv, o, gate(/up), up (unfused), down
   uint8_t *pf_ws = nullptr;  // workspace
-  float *pf_x = nullptr, *pf_y = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_gu = nullptr, *pf_tmp = nullptr;
+  float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_gu = nullptr, *pf_tmp = nullptr;
+  float *pf_pm = nullptr, *pf_pl = nullptr, *pf_po = nullptr;  // attention partials
+  float *pf_last = nullptr;  // the last token's summed down projection
+  int pf_cpi = 1;            // attention chunks per partial
   uint8_t *pf_act = nullptr, *pf_xq = nullptr;
   int32_t *pf_tokens = nullptr;
   ugb::TraceMap ptrace;      // prefill trace, [pf_max] rows per field
@@ -939,7 +942,11 @@ __global__ void prefill_state_kernel(const int32_t *__restrict__ tokens, int n, 
   state->key[0] = 0;
 }
 
-// Every kernel of one prefill, enqueued on `s` (graph-capturable).
+// Every kernel of one prefill, enqueued on `s` (graph-capturable).  Per layer: RMSNorm +
+// quantisation into the packed operand, the Q/K/V GEMM, bias + RoPE + KV write, attention
+// (partials + combine + quantisation), the O GEMM, RMSNorm + quantisation, the gate/up GEMM,
+// SiLU * up + quantisation, the down GEMM.  A GEMM may be split over K; its consumer sums the
+// splits in order.
 ugb_status prefill_enqueue(ugb_decoder *d, cudaStream_t s, const int32_t *tokens, int n, int pos0) {
   const ugb_decoder_config &c = d->cfg;
   ugb_ctx *ctx = d->ctx;
@@ -948,38 +955,51 @@ ugb_status prefill_enqueue(ugb_decoder *d, cudaStream_t s, const int32_t *tokens
   const int brow = Q + 2 * KV;
   const size_t kv_layer = static_cast<size_t>(KV) * c.n_ctx * (d->kv16 ? sizeof(__half) : sizeof(float));
   const TraceMap &T = d->ptrace;
-  // trace: the first n rows of field f of record l from a [n][len] buffer
-  auto tcopy = [&](int l, int f, const void *src, int64_t len) {
-    return T.base ? cuda_status(cudaMemcpyAsync(T.at(l, f), src, static_cast<size_t>(n) * len * 4,
-                                                cudaMemcpyDeviceToDevice, s))
-                  : UGB_OK;
+  const int s_qkv = prefill_gemm_splits(ctx, n, brow, E), s_o = prefill_gemm_splits(ctx, n, E, Q),
+            s_gu = d->pf_gu_fused ? prefill_gemm_splits(ctx, n, 2 * F, E) : 1, s_dn = prefill_gemm_splits(ctx, n, E, F);
+  // the split-K outputs: [splits][n][len] (partial sums of the first n rows, split stride n * len)
+  const int64_t st_qkv = static_cast<int64_t>(n) * brow, st_e = static_cast<int64_t>(n) * E,
+                st_gu = static_cast<int64_t>(n) * 2 * F;
+  // trace: the sum of a split-K output, or a plain buffer, into field f of record l
+  auto tsum = [&](int l, int f, const float *src, int splits, int64_t len) {
+    return T.base ? launch_pf_sum_splits(s, src, splits, n * len, 0, n, len, T.f32(l, f)) : UGB_OK;
   };
-  auto gemm = [&](size_t w_off, const float *x, int64_t k, float *y, int64_t rows, int64_t ldy) {
-    ugb_status st = launch_prefill_quant(ctx, s, x, n, k, k, d->pf_act);
-    if (st == UGB_OK) st = launch_prefill_gemm(ctx, s, d->pf_w + w_off, d->pf_act, y, n, rows, k, ldy);
-    return st;
+  auto gemm = [&](size_t w_off, int64_t k, float *y, int64_t rows, int splits) {
+    return launch_prefill_gemm(ctx, s, d->pf_w + w_off, d->pf_act, y, n, rows, k, rows, splits);
   };
   ugb_status st = launch_pf_embed(s, static_cast<const uint8_t *>(d->w.tok_embd), tokens, n, E, c.n_vocab, d->pf_x,
                                   status);
   for (int l = 0; l < c.n_layer && st == UGB_OK; ++l) {
     const ugb_layer_weights &L = d->layers[l];
     const size_t *off = d->pf_off.data() + 5 * l;
-    st = launch_pf_rmsnorm(s, d->pf_x, l ? d->pf_tmp : nullptr, static_cast<const float *>(L.attn_norm), n, E,
-                           c.norm_eps, d->pf_y, status);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_X, d->pf_x, E);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_ATTN_NORM, d->pf_y, E);
-    if (st == UGB_OK) st = gemm(off[0], d->pf_y, E, d->pf_qkv, brow, brow);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_QKV, d->pf_qkv, brow);
+    // the residual entering the layer: x += the previous layer's down projection (its splits)
+    st = launch_pf_norm_quant(s, d->pf_x, l ? d->pf_tmp : nullptr, s_dn, st_e, static_cast<const float *>(L.attn_norm),
+                              n, E, c.norm_eps, d->pf_act, T.f32(l, UGB_TRACE_ATTN_NORM), status);
+    if (st == UGB_OK && T.base)
+      st = cuda_status(cudaMemcpyAsync(T.at(l, UGB_TRACE_X), d->pf_x, static_cast<size_t>(n) * E * 4,
+                                       cudaMemcpyDeviceToDevice, s));
+    if (st == UGB_OK && l) st = tsum(l - 1, UGB_TRACE_DOWN, d->pf_tmp, s_dn, E);
+    if (st == UGB_OK) st = gemm(off[0], E, d->pf_qkv, brow, s_qkv);
+    if (st == UGB_OK) st = tsum(l, UGB_TRACE_QKV, d->pf_qkv, s_qkv, brow);
     PrefillAttn a{};
     a.qkv = d->pf_qkv;
     a.ld = brow;
+    a.splits = s_qkv;
+    a.split_stride = st_qkv;
     a.bias = d->bias ? d->bias + static_cast<size_t>(l) * brow : nullptr;
     a.rope = d->rope;
     a.q = d->pf_q;
     a.kcache = static_cast<uint8_t *>(d->kcache) + kv_layer * l;
     a.vcache = static_cast<uint8_t *>(d->vcache) + kv_layer * l;
     a.kv16 = d->kv16;
-    a.out = d->pf_y;
+    a.part_m = d->pf_pm;
+    a.part_l = d->pf_pl;
+    a.part_o = d->pf_po;
+    a.cpi = d->pf_cpi;
+    a.out = T.f32(l, UGB_TRACE_ATT);
+    a.q_out = d->pf_act;
+    a.s_out = reinterpret_cast<float *>(d->pf_act + prefill_layout(n, Q).q_bytes);
+    a.status = status;
     a.n = n;
     a.pos0 = pos0;
     a.n_head = c.n_head;
@@ -987,32 +1007,32 @@ ugb_status prefill_enqueue(ugb_decoder *d, cudaStream_t s, const int32_t *tokens
     a.n_ctx = c.n_ctx;
     if (st == UGB_OK) st = launch_pf_rope_kv(s, a);
     if (st == UGB_OK) st = launch_pf_attention(s, a);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_ATT, d->pf_y, Q);
-    if (st == UGB_OK) st = gemm(off[1], d->pf_y, Q, d->pf_tmp, E, E);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_O, d->pf_tmp, E);
+    if (st == UGB_OK) st = gemm(off[1], Q, d->pf_tmp, E, s_o);
     if (st == UGB_OK)
-      st = launch_pf_rmsnorm(s, d->pf_x, d->pf_tmp, static_cast<const float *>(L.ffn_norm), n, E, c.norm_eps, d->pf_y,
-                             status);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_FFN_NORM, d->pf_y, E);
+      st = launch_pf_norm_quant(s, d->pf_x, d->pf_tmp, s_o, st_e, static_cast<const float *>(L.ffn_norm), n, E,
+                                c.norm_eps, d->pf_act, T.f32(l, UGB_TRACE_FFN_NORM), status);
+    if (st == UGB_OK) st = tsum(l, UGB_TRACE_O, d->pf_tmp, s_o, E);
     if (d->pf_gu_fused) {
-      if (st == UGB_OK) st = gemm(off[2], d->pf_y, E, d->pf_gu, 2 * F, 2 * F);
+      if (st == UGB_OK) st = gemm(off[2], E, d->pf_gu, 2 * F, s_gu);
     } else {
-      if (st == UGB_OK) st = gemm(off[2], d->pf_y, E, d->pf_gu, F, 2 * F);
-      if (st == UGB_OK) st = launch_prefill_gemm(ctx, s, d->pf_w + off[3], d->pf_act, d->pf_gu + F, n, F, E, 2 * F);
+      if (st == UGB_OK) st = launch_prefill_gemm(ctx, s, d->pf_w + off[2], d->pf_act, d->pf_gu, n, F, E, 2 * F, 1);
+      if (st == UGB_OK) st = launch_prefill_gemm(ctx, s, d->pf_w + off[3], d->pf_act, d->pf_gu + F, n, F, E, 2 * F, 1);
     }
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_GATE_UP, d->pf_gu, 2 * F);
-    if (st == UGB_OK) st = launch_pf_silu(s, d->pf_gu, 2 * F, n, F, d->pf_y);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_H, d->pf_y, F);
-    if (st == UGB_OK) st = gemm(off[4], d->pf_y, F, d->pf_tmp, E, E);
-    if (st == UGB_OK) st = tcopy(l, UGB_TRACE_DOWN, d->pf_tmp, E);
+    if (st == UGB_OK) st = tsum(l, UGB_TRACE_GATE_UP, d->pf_gu, s_gu, 2 * F);
+    if (st == UGB_OK)
+      st = launch_pf_silu_quant(s, d->pf_gu, 2 * F, s_gu, st_gu, n, F, d->pf_act, T.f32(l, UGB_TRACE_H), status);
+    if (st == UGB_OK) st = gemm(off[4], F, d->pf_tmp, E, s_dn);
   }
   if (st != UGB_OK) return st;
+  st = tsum(c.n_layer - 1, UGB_TRACE_DOWN, d->pf_tmp, s_dn, E);
   // Only the last prompt token goes through the head (gpu_prefill.rs:138-148): its residual plus
-  // the last down projection, the output norm and Q8_1, the head matvec and greedy selection.
+  // the last down projection (summed over its splits), the output norm and Q8_1, the head matvec
+  // and greedy selection.
   float *x_last = d->pf_x + static_cast<size_t>(n - 1) * E;
-  st = launch_rmsnorm_quant(s, false, x_last, d->pf_tmp + static_cast<size_t>(n - 1) * E,
-                            static_cast<const float *>(d->w.output_norm), E, 1, c.norm_eps, d->pf_xq, nullptr, status,
-                            T.f32(c.n_layer, UGB_TRACE_ATTN_NORM));
+  if (st == UGB_OK) st = launch_pf_sum_splits(s, d->pf_tmp, s_dn, st_e, n - 1, 1, E, d->pf_last);
+  if (st == UGB_OK)
+    st = launch_rmsnorm_quant(s, false, x_last, d->pf_last, static_cast<const float *>(d->w.output_norm), E, 1,
+                              c.norm_eps, d->pf_xq, nullptr, status, T.f32(c.n_layer, UGB_TRACE_ATTN_NORM));
   if (st == UGB_OK && T.base)
     st = cuda_status(cudaMemcpyAsync(T.at(c.n_layer, UGB_TRACE_X), x_last, E * 4, cudaMemcpyDeviceToDevice, s));
   if (st == UGB_OK && T.base)
@@ -1071,9 +1091,16 @@ extern "C" ugb_status ugb_decoder_prefill_prepare(ugb_decoder *d, ugb_stream str
     ws += round_up(bytes, 256);
     return o;
   };
-  const size_t o_x = wtake(M * E * 4), o_y = wtake(M * W * 4), o_qkv = wtake(M * brow * 4), o_q = wtake(M * Q * 4),
-               o_gu = wtake(M * 2 * F * 4), o_tmp = wtake(M * E * 4), o_act = wtake(prefill_layout(M, W).bytes),
-               o_xq = wtake(q8act_layout(E, 1).bytes), o_tok = wtake(M * 4);
+  // attention partials: at most kMaxAttnGroups chunk groups per (16-token tile, KV head)
+  constexpr int kMaxAttnGroups = 16;
+  const int chunks = (c.n_ctx + 63) / 64;
+  d->pf_cpi = (chunks + kMaxAttnGroups - 1) / kMaxAttnGroups;
+  const size_t part_o = pf_attn_partial_floats(max_tokens, c.n_head, c.n_ctx, kMaxAttnGroups);
+  const int64_t S = kMaxGemmSplits;
+  const size_t o_x = wtake(M * E * 4), o_qkv = wtake(S * M * brow * 4), o_q = wtake(M * Q * 4),
+               o_gu = wtake(S * M * 2 * F * 4), o_tmp = wtake(S * M * E * 4), o_act = wtake(prefill_layout(M, W).bytes),
+               o_xq = wtake(q8act_layout(E, 1).bytes), o_tok = wtake(M * 4), o_pm = wtake(part_o / kHeadDim * 4),
+               o_pl = wtake(part_o / kHeadDim * 4), o_po = wtake(part_o * 4), o_last = wtake(E * 4);
   if (cudaMalloc(&d->pf_w, total) != cudaSuccess) return UGB_EBACKEND;
   if (cudaMalloc(&d->pf_ws, ws) != cudaSuccess) {
     cudaFree(d->pf_w);
@@ -1081,7 +1108,10 @@ extern "C" ugb_status ugb_decoder_prefill_prepare(ugb_decoder *d, ugb_stream str
     return UGB_EBACKEND;
   }
   d->pf_x = reinterpret_cast<float *>(d->pf_ws + o_x);
-  d->pf_y = reinterpret_cast<float *>(d->pf_ws + o_y);
+  d->pf_pm = reinterpret_cast<float *>(d->pf_ws + o_pm);
+  d->pf_pl = reinterpret_cast<float *>(d->pf_ws + o_pl);
+  d->pf_po = reinterpret_cast<float *>(d->pf_ws + o_po);
+  d->pf_last = reinterpret_cast<float *>(d->pf_ws + o_last);
   d->pf_qkv = reinterpret_cast<float *>(d->pf_ws + o_qkv);
   d->pf_q = reinterpret_cast<float *>(d->pf_ws + o_q);
   d->pf_gu = reinterpret_cast<float *>(d->pf_ws + o_gu);

@@ -33,6 +33,7 @@
 #include "common.cuh"
 #include "internal.hpp"
 #include "prefill.hpp"
+#include "prefill_quant.cuh"
 
 namespace ugb {
 namespace {
@@ -164,11 +165,6 @@ __device__ __forceinline__ uint64_t cvt2_bias(uint32_t a, uint32_t b) {
   return sub2(pk2(__uint_as_float(a + kBiasBits), __uint_as_float(b + kBiasBits)), pk2(kBiasValue, kBiasValue));
 }
 
-// Byte offset of (row r, K byte j) inside one canonical 128 x 32-byte block.
-__host__ __device__ __forceinline__ uint32_t canon_off(int r, int j) {
-  return static_cast<uint32_t>((r >> 3) * 256 + (j >> 4) * 128 + (r & 7) * 16 + (j & 15));
-}
-
 // ---- repack: GGUF Q8_0 rows -> canonical K-major tiles -------------------------------------
 
 // One thread per (row, K-block, 16-byte half): 16 quant bytes to their canonical place, and
@@ -220,27 +216,7 @@ __global__ void __launch_bounds__(256) prefill_quant_kernel(const float *__restr
   const int b = static_cast<int>(gw % nb);
   const int64_t t = gw / nb;
   const float val = t < m ? x[t * ldx + b * 32 + lane] : 0.f;
-  const bool fin = isfinite(val);
-  float a = fin ? fabsf(val) : 0.f;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-  const float inv = a > 0.f ? 127.0f / a : 0.0f;
-  int qi = fin ? __float2int_rn(val * inv) : 0;
-  qi = max(-127, min(127, qi));
-  // gather four consecutive quants into lane 4w's word
-  uint32_t word = static_cast<uint32_t>(qi) & 0xFFu;
-  word |= (__shfl_down_sync(0xffffffffu, static_cast<uint32_t>(qi) & 0xFFu, 1) << 8);
-  word |= (__shfl_down_sync(0xffffffffu, static_cast<uint32_t>(qi) & 0xFFu, 2) << 16);
-  word |= (__shfl_down_sync(0xffffffffu, static_cast<uint32_t>(qi) & 0xFFu, 3) << 24);
-  const int64_t tile = t / kPrefillTile;
-  const int r = static_cast<int>(t % kPrefillTile);
-  if ((lane & 3) == 0)
-    *reinterpret_cast<uint32_t *>(q_out + (tile * nb + b) * kPrefillTileBytes + canon_off(r, lane)) = word;
-  const bool bad = __any_sync(0xffffffffu, !fin);
-  if (lane == 0) {
-    s_out[(tile * nb + b) * kPrefillTile + r] = a / 127.0f;
-    if (bad) status_or(status, ST_NONFINITE_IN);
-  }
+  if (pf_quant_block(val, lane, t, b, nb, q_out, s_out) && lane == 0) status_or(status, ST_NONFINITE_IN);
 }
 
 // ---- the GEMM ------------------------------------------------------------------------------
@@ -250,9 +226,11 @@ struct GemmParams {
   const float *as;    //                   [m_tiles][nb][128]
   const uint8_t *bq;  // weight tiles      [n_tiles][nb][4096]
   const float *bs;    //                   [n_tiles][nb][128]
-  float *y;           // [m][ldy]
+  float *y;           // [m][ldy]; split s of a split-K launch writes y + s * y_split
   int64_t ldy, m, n;
-  int nb;
+  int nb;             // K-blocks of the operands' rows
+  int nb_split;       // K-blocks one split sums (blockIdx.z takes blocks [z * nb_split, ...))
+  int64_t y_split;
   int32_t *dots;      // optional [nb][m][n] int32 block dots (test path)
   uint32_t *status;
 };
@@ -294,7 +272,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
   const int64_t n_col0 = static_cast<int64_t>(blockIdx.y) * BN;  // first output column
   const int64_t w_tile = n_col0 / kPrefillTile;                  // packed 128-row weight tile
   const int w_half = static_cast<int>((n_col0 % kPrefillTile) / BN);  // which BN rows of it
-  const int nb = p.nb;
+  // this CTA's K-blocks: [kb0, kb0 + nb) of the rows' p.nb (all of them unless split)
+  const int kb0 = static_cast<int>(blockIdx.z) * p.nb_split;
+  const int nb = min(p.nb_split, p.nb - kb0);
+  float *const y_out = p.y + static_cast<int64_t>(blockIdx.z) * p.y_split;
   const int n_stages = (nb + kKB - 1) / kKB;
 
   if (threadIdx.x == 0) {
@@ -325,10 +306,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     if (lane == 0) {
       grid_dep_wait();  // the activation tiles come from the preceding quant kernel
       const uint64_t pol = policy_evict_last();
-      const uint8_t *a_base = p.aq + m_tile * nb * kTileBytes;
-      const uint8_t *b_base = p.bq + w_tile * nb * kTileBytes + w_half * G::kBBytes;
-      const float *sa_base = p.as + m_tile * nb * kPrefillTile;
-      const float *sb_base = p.bs + w_tile * nb * kPrefillTile + w_half * BN;
+      const uint8_t *a_base = p.aq + (m_tile * p.nb + kb0) * kTileBytes;
+      const uint8_t *b_base = p.bq + (w_tile * p.nb + kb0) * kTileBytes + w_half * G::kBBytes;
+      const float *sa_base = p.as + (m_tile * p.nb + kb0) * kPrefillTile;
+      const float *sb_base = p.bs + (w_tile * p.nb + kb0) * kPrefillTile + w_half * BN;
       int issued = 0;
       for (int s = 0; s < n_stages; ++s) {
         const int slot = s % kStages;
@@ -411,7 +392,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       if (p.dots) {
         for (int i = 0; i < kC; ++i) {
           const int64_t nn = n_col0 + c0 + i;
-          if (t < p.m && nn < p.n) p.dots[(static_cast<int64_t>(b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
+          if (t < p.m && nn < p.n)
+            p.dots[(static_cast<int64_t>(kb0 + b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
         }
       }
 #pragma unroll
@@ -432,7 +414,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       }
     }
     if (ok && t < p.m) {
-      float *yrow = p.y + t * p.ldy + n_col0 + c0;
+      float *yrow = y_out + t * p.ldy + n_col0 + c0;
       const int64_t n_left = p.n - (n_col0 + c0);
       if (n_left >= kC && (reinterpret_cast<uintptr_t>(yrow) & 15) == 0) {
 #pragma unroll
@@ -495,7 +477,7 @@ inline Packed packed_layout(int64_t rows, int64_t k) { return prefill_layout(row
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, const void *x_packed, float *y,
-                       int32_t *dots, int64_t m, int64_t n, int64_t k, int64_t ldy) {
+                       int32_t *dots, int64_t m, int64_t n, int64_t k, int64_t ldy, int splits = 1) {
   if (!ctx || !ctx->status) return UGB_ECONTEXT;
   if (m < 1 || n < 1 || k < 32 || k % 32 || ldy < n || k / 32 > (1 << 20)) return UGB_ESHAPE;
   if (!w_packed || !x_packed || !y || !aligned16(w_packed) || !aligned16(x_packed)) return UGB_EALIGN;
@@ -511,12 +493,18 @@ ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, 
   p.m = m;
   p.n = n;
   p.nb = static_cast<int>(k / 32);
+  if (splits < 1 || splits > p.nb) return UGB_ESHAPE;
+  p.nb_split = (p.nb + splits - 1) / splits;
+  splits = (p.nb + p.nb_split - 1) / p.nb_split;  // no split without blocks
+  p.y_split = m * ldy;
   p.dots = dots;
   p.status = ctx->status;
-  // 64-row CTAs when 128-row tiles would leave SMs idle (twice the CTAs, same packed layout)
-  const bool narrow = px.tiles * pw.tiles < ctx->sm_count;
+  // 64-row CTAs when 128-row tiles would leave SMs idle (twice the CTAs, same packed layout);
+  // a split-K launch keeps whole tiles (its splits fill the SMs)
+  const bool narrow = splits == 1 && px.tiles * pw.tiles < ctx->sm_count;
   cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(px.tiles), static_cast<unsigned>(narrow ? 2 * pw.tiles : pw.tiles));
+  cfg.gridDim = dim3(static_cast<unsigned>(px.tiles), static_cast<unsigned>(narrow ? 2 * pw.tiles : pw.tiles),
+                     static_cast<unsigned>(splits));
   cfg.blockDim = dim3(kGemmThreads);
   cfg.dynamicSmemBytes = narrow ? Geo<64>::kSmem : Geo<128>::kSmem;
   cfg.stream = stream;
@@ -562,8 +550,25 @@ ugb_status launch_prefill_quant(ugb_ctx *ctx, cudaStream_t stream, const float *
 }
 
 ugb_status launch_prefill_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, const void *x_packed,
-                               float *y, int64_t m, int64_t n, int64_t k, int64_t ldy) {
-  return launch_gemm(ctx, stream, w_packed, x_packed, y, nullptr, m, n, k, ldy);
+                               float *y, int64_t m, int64_t n, int64_t k, int64_t ldy, int splits) {
+  return launch_gemm(ctx, stream, w_packed, x_packed, y, nullptr, m, n, k, ldy, splits);
+}
+
+int prefill_gemm_splits(const ugb_ctx *ctx, int64_t m, int64_t n, int64_t k) {
+  // Split K while that shortens the launch: waves of whole-tile CTAs x K-blocks per CTA (the
+  // per-block rescale bounds each CTA, so its time is proportional to its K-blocks).
+  const int64_t tiles = prefill_layout(m, k).tiles * prefill_layout(n, k).tiles, nb = k / 32;
+  int best = 1;
+  int64_t best_cost = INT64_MAX;
+  for (int s = 1; s <= kMaxGemmSplits && s <= nb; ++s) {
+    const int64_t waves = (tiles * s + ctx->sm_count - 1) / ctx->sm_count;
+    const int64_t cost = waves * ((nb + s - 1) / s);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 }  // namespace ugb

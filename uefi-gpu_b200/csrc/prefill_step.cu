@@ -9,6 +9,7 @@
 // RoPE over the pairs (i, i + 64) from the decoder's table, scores q.k / sqrt(128) with an exact
 // expf softmax, SiLU(g) * u.  Attention is computed in fp32 on the CUDA cores, with an online
 // (running max) softmax over 64-position chunks of the cache.
+#include <algorithm>
 #include <cfloat>
 #include <cmath>
 
@@ -16,6 +17,7 @@
 #include "decode.hpp"
 #include "glue.cuh"
 #include "prefill.hpp"
+#include "prefill_quant.cuh"
 
 namespace ugb {
 namespace {
@@ -42,22 +44,31 @@ __global__ void __launch_bounds__(256) pf_embed_kernel(const uint8_t *__restrict
   }
 }
 
-// Token t = blockIdx.x: x[t] += dx[t] (when dx is given); y[t] = x[t] * (1/sqrt(mean(x^2) +
-// eps)) * w (prefill_resnorm, gpu_prefill.cu:65-72).  The sum of squares is the decode kernel's
-// fixed-order tree.
-__global__ void __launch_bounds__(512) pf_rmsnorm_kernel(float *__restrict__ x, const float *__restrict__ dx,
-                                                         const float *__restrict__ w, int n, float eps,
-                                                         float *__restrict__ y, uint32_t *status) {
+// Sum of the `splits` partial outputs of a split-K GEMM at element i (split stride `stride`), in
+// split order: the same value every consumer of the product forms.
+__device__ __forceinline__ float split_sum(const float *p, int splits, int64_t stride, int64_t i) {
+  float v = p[i];
+  for (int s = 1; s < splits; ++s) v += p[s * stride + i];
+  return v;
+}
+
+// pf_rmsnorm fused with the quantisation of its output: x[t] += dx[t] (the sum of dx's splits),
+// then token t = blockIdx.x's normed row goes straight into the packed GEMM operand (quants q_out,
+// scales s_out) with prefill_quant's arithmetic, and into pre[t] (the trace) when given.  Same
+// values as pf_rmsnorm then prefill_quant, bit for bit.
+__global__ void __launch_bounds__(512) pf_norm_quant_kernel(float *__restrict__ x, const float *__restrict__ dx,
+                                                            int dx_splits, int64_t dx_stride,
+                                                            const float *__restrict__ w, int n, float eps,
+                                                            uint8_t *__restrict__ q_out, float *__restrict__ s_out,
+                                                            float *__restrict__ pre, uint32_t *status) {
   __shared__ float part[32];
   const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float *xt = x + static_cast<int64_t>(t) * n;
-  const float *dxt = dx ? dx + static_cast<int64_t>(t) * n : nullptr;
-  float *yt = y + static_cast<int64_t>(t) * n;
   float ss = 0.f;
   for (int i = tid; i < n; i += blockDim.x) {
     float v = xt[i];
-    if (dxt) {
-      v += dxt[i];
+    if (dx) {
+      v += split_sum(dx, dx_splits, dx_stride, static_cast<int64_t>(t) * n + i);
       xt[i] = v;
     }
     ss += v * v;
@@ -74,25 +85,55 @@ __global__ void __launch_bounds__(512) pf_rmsnorm_kernel(float *__restrict__ x, 
   }
   __syncthreads();
   const float scale = 1.0f / sqrtf(part[0] / static_cast<float>(n) + eps);
+  const int nb = n / 32;
   bool bad = false;
-  for (int i = tid; i < n; i += blockDim.x) {
+  for (int b = warp; b < nb; b += blockDim.x >> 5) {
+    const int i = b * 32 + lane;
     const float v = xt[i] * scale * w[i];
-    bad |= !isfinite(v);
-    yt[i] = v;
+    if (pre) pre[static_cast<int64_t>(t) * n + i] = v;
+    bad |= pf_quant_block(v, lane, t, b, nb, q_out, s_out);
   }
-  if (__any_sync(0xffffffffu, bad) && lane == 0) status_or(status, ST_NONFINITE_IN);
+  if (bad && lane == 0) status_or(status, ST_NONFINITE_IN);
 }
 
-// Thread (token t = blockIdx.x, pair j of head-pair slot): the query and key heads get their
-// bias and rotation (rope_bias / prefill_rope, gpu_prefill.cu:73-81), the rotated query goes to
-// q, the rotated key and the biased value into the cache at position pos0 + t (rounded to fp16
-// in an fp16 cache).
+// SiLU(g) * u of the gate / up GEMM rows (summed over its splits) quantised per 32-block into the
+// packed operand of the down GEMM; one warp per (token, block); pre[t] (the trace) when given.
+__global__ void __launch_bounds__(256) pf_silu_quant_kernel(const float *__restrict__ gu, int64_t ld, int splits,
+                                                            int64_t stride, int n, int n_ff,
+                                                            uint8_t *__restrict__ q_out, float *__restrict__ s_out,
+                                                            float *__restrict__ pre, uint32_t *status) {
+  const int lane = threadIdx.x & 31, nb = n_ff / 32;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  if (gw >= static_cast<int64_t>(n) * nb) return;  // warp-uniform
+  const int b = static_cast<int>(gw % nb);
+  const int64_t t = gw / nb;
+  const float g = split_sum(gu, splits, stride, t * ld + b * 32 + lane);
+  const float u = split_sum(gu, splits, stride, t * ld + n_ff + b * 32 + lane);
+  const float h = (g / (1.0f + expf(-g))) * u;
+  if (pre) pre[t * n_ff + b * 32 + lane] = h;
+  if (pf_quant_block(h, lane, t, b, nb, q_out, s_out) && lane == 0) status_or(status, ST_NONFINITE_IN);
+}
+
+// dst[r][i] = the sum of the splits of rows [row0, row0 + rows) of a split-K GEMM output [.][len].
+__global__ void __launch_bounds__(256) pf_sum_splits_kernel(const float *__restrict__ src, int splits, int64_t stride,
+                                                            int64_t row0, int64_t rows, int64_t len,
+                                                            float *__restrict__ dst) {
+  const int64_t total = rows * len;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    dst[i] = split_sum(src, splits, stride, row0 * len + i);
+}
+
+// Thread (token t = blockIdx.x, rotation pair or value element i): the query and key heads get
+// their bias and rotation (rope_bias / prefill_rope, gpu_prefill.cu:73-81) from the Q/K/V GEMM rows
+// (summed over its splits); the rotated query goes to q, the rotated key and the biased value into
+// the cache at position pos0 + t (rounded to fp16 in an fp16 cache).
 template <typename KV>
 __global__ void __launch_bounds__(256) pf_rope_kv_kernel(PrefillAttn a) {
   const int t = blockIdx.x;
   const int pos = a.pos0 + t;
   const int qr = a.n_head * kHD, kr = a.n_kv * kHD;
-  const float *row = a.qkv + static_cast<int64_t>(t) * a.ld;
+  const int64_t row = static_cast<int64_t>(t) * a.ld;
   const float2 *rope = a.rope + static_cast<size_t>(pos) * (kHD / 2);
   const int pairs = (a.n_head + a.n_kv) * (kHD / 2);
   KV *kc = static_cast<KV *>(a.kcache), *vc = static_cast<KV *>(a.vcache);
@@ -102,7 +143,8 @@ __global__ void __launch_bounds__(256) pf_rope_kv_kernel(PrefillAttn a) {
       const bool is_q = h < a.n_head;
       const int r0 = is_q ? h * kHD + j : qr + (h - a.n_head) * kHD + j;
       const float b0 = a.bias ? a.bias[r0] : 0.f, b1 = a.bias ? a.bias[r0 + kHD / 2] : 0.f;
-      const float u = row[r0] + b0, v = row[r0 + kHD / 2] + b1;
+      const float u = split_sum(a.qkv, a.splits, a.split_stride, row + r0) + b0;
+      const float v = split_sum(a.qkv, a.splits, a.split_stride, row + r0 + kHD / 2) + b1;
       const float2 cs = rope[j];
       const float lo = u * cs.x - v * cs.y, hi = u * cs.y + v * cs.x;
       if (is_q) {
@@ -117,132 +159,179 @@ __global__ void __launch_bounds__(256) pf_rope_kv_kernel(PrefillAttn a) {
     } else {
       const int e = i - pairs, kvh = e / kHD, d = e % kHD;
       const int r = qr + kr + e;
-      KvIO<KV>::store(vc + (static_cast<size_t>(kvh) * a.n_ctx + pos) * kHD + d, row[r] + (a.bias ? a.bias[r] : 0.f));
+      KvIO<KV>::store(vc + (static_cast<size_t>(kvh) * a.n_ctx + pos) * kHD + d,
+                      split_sum(a.qkv, a.splits, a.split_stride, row + r) + (a.bias ? a.bias[r] : 0.f));
     }
   }
 }
 
-// Causal attention of query head h = blockIdx.y for the kQT prompt tokens of tile blockIdx.x
-// over the cache positions [0, pos0 + t] of each (prefill_attention, gpu_prefill.cu:82-101;
-// fused_attention's arithmetic).  The cache is read in 64-position chunks into shared memory
-// as fp32; each query row keeps a running max m, a running sum l and its output o, rescaled by
-// exp(m_old - m_new) when a chunk raises the max.  Threads: 16 per query row; thread (r, c)
-// scores keys c, c + 16, c + 32, c + 48 of the chunk and owns output dims 8c .. 8c + 7.
-constexpr int kQT = 16;   // query tokens per CTA
-constexpr int kKC = 64;   // cache positions per chunk
-constexpr int kPadK = kHD + 1;
-// shared memory: queries [kQT][kHD], keys [kKC][kPadK], values [kKC][kHD], probabilities [kQT][kKC]
-constexpr size_t kAttnSmem = sizeof(float) * (kQT * kHD + kKC * kPadK + kKC * kHD + kQT * kKC);
-static_assert((kQT * kHD + kKC * kPadK) % 4 == 0, "values must start 16-byte aligned");
+// ---- causal attention: partial items and their combine ------------------------------------
+//
+// Item (query tile of kAQ tokens = blockIdx.x, KV head = blockIdx.y, chunk group = blockIdx.z):
+// the G query heads of the KV head for the tile's tokens (R = 16 G query rows, row g * 16 + token)
+// against the cache positions of chunks [z * cpi, (z + 1) * cpi) (kAK positions each) that any of
+// the tile's tokens sees.  Q, one chunk of K and of V sit in shared memory as fp32; thread
+// (tr, tc) of 16 x 16 scores rows g * 16 + tr (g < G) against keys tc + 16 j (j < 4) and owns
+// output dims 4 tc .. 4 tc + 3 and 64 + 4 tc .. 64 + 4 tc + 3 of its rows, so every shared load
+// feeds several FMAs.  Per row the item keeps a running max m, sum l and output o over its chunks
+// (rescaled by exp(m_old - m_new)) and writes them as one partial; the combine merges an item's
+// partials with the log-sum-exp rule (flash-decoding's) and quantises the result.
+constexpr int kAQ = 16;            // query tokens per item
+constexpr int kAK = 64;            // cache positions per chunk
+constexpr int kPadQ = kHD + 4;     // row pitch of Q and K in shared memory (float4 loads spread over banks)
 
-template <typename KV>
-__global__ void __launch_bounds__(256) pf_attention_kernel(PrefillAttn a) {
+__host__ __device__ constexpr size_t pf_attn_smem(int G) {
+  return sizeof(float) * (static_cast<size_t>(16 * G) * kPadQ + kAK * kPadQ + kAK * kHD + 16 * G * (kAK + 1));
+}
+
+template <int G, typename KV>
+__global__ void __launch_bounds__(256) pf_attn_partial_kernel(PrefillAttn a) {
+  constexpr int R = 16 * G;
   extern __shared__ __align__(16) float sm[];
-  float(*qs)[kHD] = reinterpret_cast<float(*)[kHD]>(sm);
-  float(*ks)[kPadK] = reinterpret_cast<float(*)[kPadK]>(sm + kQT * kHD);
-  float(*vs)[kHD] = reinterpret_cast<float(*)[kHD]>(sm + kQT * kHD + kKC * kPadK);
-  float(*ps)[kKC] = reinterpret_cast<float(*)[kKC]>(sm + kQT * kHD + kKC * kPadK + kKC * kHD);
-  const int tid = threadIdx.x, r = tid >> 4, c = tid & 15;
-  const int t0 = blockIdx.x * kQT, h = blockIdx.y;
-  const int G = a.n_head / a.n_kv, kvh = h / G;
+  float *qs = sm;                       // [R][kPadQ]
+  float *ks = qs + R * kPadQ;           // [kAK][kPadQ]
+  float *vs = ks + kAK * kPadQ;         // [kAK][kHD]
+  float *ps = vs + kAK * kHD;           // [R][kAK + 1]
+  const int tid = threadIdx.x, tr = tid >> 4, tc = tid & 15;
+  const int t0 = blockIdx.x * kAQ, kvh = blockIdx.y;
   const int qr = a.n_head * kHD;
-  const int t = t0 + r;                       // this thread's query token
-  const bool live = t < a.n;
-  const int my_pos = a.pos0 + min(t, a.n - 1);  // its position (the last token's for padding rows)
-  const int last = a.pos0 + min(t0 + kQT, a.n) - 1;  // the tile's last query position
-  for (int i = tid; i < kQT * kHD; i += blockDim.x) {
-    const int rr = i / kHD, d = i % kHD;
-    const int tt = min(t0 + rr, a.n - 1);
-    qs[rr][d] = a.q[static_cast<int64_t>(tt) * qr + h * kHD + d];
+  const int last = a.pos0 + min(t0 + kAQ, a.n) - 1;  // the tile's last query position
+  const int c_begin = blockIdx.z * a.cpi, c_end = min(c_begin + a.cpi, last / kAK + 1);
+  if (c_begin >= c_end) return;  // no token of the tile sees these chunks
+  const int my_pos = a.pos0 + min(t0 + tr, a.n - 1);  // padding rows act as the last token
+  for (int i = tid; i < R * (kHD / 4); i += blockDim.x) {
+    const int r = i / (kHD / 4), d = (i % (kHD / 4)) * 4, g = r / kAQ, tt = min(t0 + r % kAQ, a.n - 1);
+    *reinterpret_cast<float4 *>(qs + r * kPadQ + d) =
+        *reinterpret_cast<const float4 *>(a.q + static_cast<int64_t>(tt) * qr + (kvh * G + g) * kHD + d);
   }
   const KV *kc = static_cast<const KV *>(a.kcache) + static_cast<size_t>(kvh) * a.n_ctx * kHD;
   const KV *vc = static_cast<const KV *>(a.vcache) + static_cast<size_t>(kvh) * a.n_ctx * kHD;
   const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(kHD));
-  float m = -FLT_MAX, l = 0.f, o[8];
+  float m[G], l[G], o[G][8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = 0.f;
-  for (int p0 = 0; p0 <= last; p0 += kKC) {
-    const int np = min(kKC, last + 1 - p0);
-    __syncthreads();  // the previous chunk is consumed (and qs written, for the first)
-    for (int i = tid; i < kKC * (kHD / 4); i += blockDim.x) {
+  for (int g = 0; g < G; ++g) {
+    m[g] = -FLT_MAX;
+    l[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
+  }
+  for (int c = c_begin; c < c_end; ++c) {
+    const int p0 = c * kAK;
+    __syncthreads();  // the previous chunk's K, V and P are consumed (and Q is stored, the first time)
+    for (int i = tid; i < kAK * (kHD / 4); i += blockDim.x) {
       const int pp = i / (kHD / 4), d = (i % (kHD / 4)) * 4;
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (pp < np) {
+      if (p0 + pp <= last) {  // positions past the tile's last are not written yet: zeros
         kv = KvIO<KV>::load4(kc + static_cast<size_t>(p0 + pp) * kHD + d);
         vv = KvIO<KV>::load4(vc + static_cast<size_t>(p0 + pp) * kHD + d);
       }
-      ks[pp][d] = kv.x;
-      ks[pp][d + 1] = kv.y;
-      ks[pp][d + 2] = kv.z;
-      ks[pp][d + 3] = kv.w;
-      *reinterpret_cast<float4 *>(&vs[pp][d]) = vv;
+      *reinterpret_cast<float4 *>(ks + pp * kPadQ + d) = kv;
+      *reinterpret_cast<float4 *>(vs + pp * kHD + d) = vv;
     }
     __syncthreads();
-    float s[4];
+    float s[G][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) s[j] = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < kHD; ++d) {
-      const float qv = qs[r][d];
+    for (int g = 0; g < G; ++g)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) s[j] += qv * ks[c + 16 * j][d];
-    }
-    float cmax = -FLT_MAX;
+      for (int j = 0; j < 4; ++j) s[g][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < kHD; d += 4) {
+      float4 kf[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int pp = c + 16 * j;
-      s[j] = (pp < np && p0 + pp <= my_pos) ? s[j] * inv_sqrt : -FLT_MAX;  // causal mask
-      cmax = fmaxf(cmax, s[j]);
-    }
+      for (int j = 0; j < 4; ++j) kf[j] = *reinterpret_cast<const float4 *>(ks + (tc + 16 * j) * kPadQ + d);
 #pragma unroll
-    for (int off = 8; off > 0; off >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
-    const float m_new = fmaxf(m, cmax);  // finite: position 0 is never masked
-    const float resc = expf(m - m_new);
-    float csum = 0.f;
+      for (int g = 0; g < G; ++g) {
+        const float4 qf = *reinterpret_cast<const float4 *>(qs + (g * kAQ + tr) * kPadQ + d);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float e = s[j] == -FLT_MAX ? 0.f : expf(s[j] - m_new);
-      ps[r][c + 16 * j] = e;
-      csum += e;
+        for (int j = 0; j < 4; ++j) s[g][j] += qf.x * kf[j].x + qf.y * kf[j].y + qf.z * kf[j].z + qf.w * kf[j].w;
+      }
     }
 #pragma unroll
-    for (int off = 8; off > 0; off >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, off);
-    l = l * resc + csum;
-    m = m_new;
-    __syncwarp();
+    for (int g = 0; g < G; ++g) {
+      float cmax = -FLT_MAX;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] *= resc;
+      for (int j = 0; j < 4; ++j) {
+        const bool valid = p0 + tc + 16 * j <= my_pos;  // causal mask
+        s[g][j] = valid ? s[g][j] * inv_sqrt : -FLT_MAX;
+        cmax = fmaxf(cmax, s[g][j]);
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
+      const float m_new = fmaxf(m[g], cmax);
+      const float resc = m_new == -FLT_MAX ? 1.f : expf(m[g] - m_new);  // a row with nothing seen yet stays 0
+      float csum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float e = s[g][j] == -FLT_MAX ? 0.f : expf(s[g][j] - m_new);
+        ps[(g * kAQ + tr) * (kAK + 1) + tc + 16 * j] = e;
+        csum += e;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) csum += __shfl_xor_sync(0xffffffffu, csum, off);
+      l[g] = l[g] * resc + csum;
+      m[g] = m_new;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[g][i] *= resc;
+    }
+    __syncwarp();  // a row's probabilities are written and read by the same 16 lanes
+    const int np = min(kAK, last + 1 - p0);
     for (int pp = 0; pp < np; ++pp) {
-      const float pv = ps[r][pp];
-      const float4 v0 = *reinterpret_cast<const float4 *>(&vs[pp][8 * c]);
-      const float4 v1 = *reinterpret_cast<const float4 *>(&vs[pp][8 * c + 4]);
-      o[0] += pv * v0.x;
-      o[1] += pv * v0.y;
-      o[2] += pv * v0.z;
-      o[3] += pv * v0.w;
-      o[4] += pv * v1.x;
-      o[5] += pv * v1.y;
-      o[6] += pv * v1.z;
-      o[7] += pv * v1.w;
+      const float4 v0 = *reinterpret_cast<const float4 *>(vs + pp * kHD + 4 * tc);
+      const float4 v1 = *reinterpret_cast<const float4 *>(vs + pp * kHD + 64 + 4 * tc);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pv = ps[(g * kAQ + tr) * (kAK + 1) + pp];
+        o[g][0] += pv * v0.x;
+        o[g][1] += pv * v0.y;
+        o[g][2] += pv * v0.z;
+        o[g][3] += pv * v0.w;
+        o[g][4] += pv * v1.x;
+        o[g][5] += pv * v1.y;
+        o[g][6] += pv * v1.z;
+        o[g][7] += pv * v1.w;
+      }
     }
   }
-  if (live) {
-    const float inv = 1.0f / l;
-    float *out = a.out + static_cast<int64_t>(t) * qr + h * kHD + 8 * c;
-    *reinterpret_cast<float4 *>(out) = make_float4(o[0] * inv, o[1] * inv, o[2] * inv, o[3] * inv);
-    *reinterpret_cast<float4 *>(out + 4) = make_float4(o[4] * inv, o[5] * inv, o[6] * inv, o[7] * inv);
+  // partial of (tile, KV head, chunk group): m, l [R] and o [R][kHD]
+  const int64_t item = (static_cast<int64_t>(blockIdx.x) * a.n_kv + kvh) * gridDim.z + blockIdx.z;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int r = g * kAQ + tr;
+    if (tc == 0) {
+      a.part_m[item * R + r] = m[g];
+      a.part_l[item * R + r] = l[g];
+    }
+    float *po = a.part_o + (item * R + r) * kHD;
+    *reinterpret_cast<float4 *>(po + 4 * tc) = make_float4(o[g][0], o[g][1], o[g][2], o[g][3]);
+    *reinterpret_cast<float4 *>(po + 64 + 4 * tc) = make_float4(o[g][4], o[g][5], o[g][6], o[g][7]);
   }
 }
 
-// h[t][i] = SiLU(g) * u of the gate / up GEMM rows (silu_mul of the prefill graph).
-__global__ void __launch_bounds__(256) pf_silu_kernel(const float *__restrict__ gu, int64_t ld, int n_ff,
-                                                      float *__restrict__ h) {
-  const int t = blockIdx.y;
-  const float *row = gu + static_cast<int64_t>(t) * ld;
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_ff; i += gridDim.x * blockDim.x) {
-    const float g = row[i], u = row[n_ff + i];
-    h[static_cast<int64_t>(t) * n_ff + i] = (g / (1.0f + expf(-g))) * u;
+// Token t = blockIdx.x, query head h = blockIdx.y, thread = output dim: merge the token's partials
+// over the chunk groups that hold positions <= pos0 + t (max, then exp(m_z - max) weights), write
+// the output (trace) when asked and quantise it, warp w taking 32-block 4 h + w of the token, into
+// the O GEMM's packed operand.
+__global__ void __launch_bounds__(kHD) pf_attn_combine_kernel(PrefillAttn a, int groups) {
+  const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  const int G = a.n_head / a.n_kv, kvh = h / G, g = h - kvh * G, R = 16 * G;
+  const int r = g * kAQ + t % kAQ;
+  const int pos = a.pos0 + t;
+  const int nz = min(groups, (pos / kAK) / a.cpi + 1);  // chunk groups with positions <= pos
+  const int64_t item0 = (static_cast<int64_t>(t / kAQ) * a.n_kv + kvh) * groups;
+  float mx = -FLT_MAX;
+  for (int z = 0; z < nz; ++z) mx = fmaxf(mx, a.part_m[(item0 + z) * R + r]);
+  float l = 0.f, o = 0.f;
+  for (int z = 0; z < nz; ++z) {
+    const int64_t pi = (item0 + z) * R + r;
+    const float e = expf(a.part_m[pi] - mx);
+    l += e * a.part_l[pi];
+    o += e * a.part_o[pi * kHD + d];
   }
+  const float v = o / l;
+  const int qr = a.n_head * kHD;
+  if (a.out) a.out[static_cast<int64_t>(t) * qr + h * kHD + d] = v;
+  if (pf_quant_block(v, lane, t, 4 * h + warp, qr / 32, a.q_out, a.s_out) && lane == 0)
+    status_or(a.status, ST_NONFINITE_IN);
 }
 
 }  // namespace
@@ -250,12 +339,6 @@ __global__ void __launch_bounds__(256) pf_silu_kernel(const float *__restrict__ 
 ugb_status launch_pf_embed(cudaStream_t s, const uint8_t *tok_embd, const int32_t *tokens, int n, int embd, int vocab,
                            float *x, uint32_t *status) {
   pf_embed_kernel<<<n, 256, 0, s>>>(tok_embd, tokens, embd, vocab, x, status);
-  return cuda_status(cudaGetLastError());
-}
-
-ugb_status launch_pf_rmsnorm(cudaStream_t s, float *x, const float *dx, const float *w, int n, int embd, float eps,
-                             float *y, uint32_t *status) {
-  pf_rmsnorm_kernel<<<n, 512, 0, s>>>(x, dx, w, embd, eps, y, status);
   return cuda_status(cudaGetLastError());
 }
 
@@ -267,27 +350,93 @@ ugb_status launch_pf_rope_kv(cudaStream_t s, const PrefillAttn &a) {
   return cuda_status(cudaGetLastError());
 }
 
-ugb_status init_prefill_step_kernels(ugb_ctx *ctx) {
-  if (ctx->smem_optin < kAttnSmem) return UGB_EBACKEND;
-  if (cudaFuncSetAttribute(pf_attention_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(kAttnSmem)) != cudaSuccess)
-    return UGB_EBACKEND;
-  return cuda_status(cudaFuncSetAttribute(pf_attention_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(kAttnSmem)));
+namespace {
+
+template <int G, typename KV>
+ugb_status set_attn_smem(ugb_ctx *ctx) {
+  if (ctx->smem_optin < pf_attn_smem(G)) return UGB_EBACKEND;
+  return cuda_status(cudaFuncSetAttribute(pf_attn_partial_kernel<G, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(pf_attn_smem(G))));
 }
 
-ugb_status launch_pf_attention(cudaStream_t s, const PrefillAttn &a) {
-  const dim3 grid((a.n + kQT - 1) / kQT, a.n_head);
+template <int G>
+ugb_status launch_partial(cudaStream_t s, const PrefillAttn &a, dim3 grid) {
   if (a.kv16)
-    pf_attention_kernel<__half><<<grid, 256, kAttnSmem, s>>>(a);
+    pf_attn_partial_kernel<G, __half><<<grid, 256, pf_attn_smem(G), s>>>(a);
   else
-    pf_attention_kernel<float><<<grid, 256, kAttnSmem, s>>>(a);
+    pf_attn_partial_kernel<G, float><<<grid, 256, pf_attn_smem(G), s>>>(a);
   return cuda_status(cudaGetLastError());
 }
 
-ugb_status launch_pf_silu(cudaStream_t s, const float *gu, int64_t ld, int n, int n_ff, float *h) {
-  const dim3 grid((n_ff + 255) / 256, n);
-  pf_silu_kernel<<<grid, 256, 0, s>>>(gu, ld, n_ff, h);
+}  // namespace
+
+ugb_status init_prefill_step_kernels(ugb_ctx *ctx) {
+  ugb_status st = UGB_OK;
+#define UGB_ATTN_INIT(G)                                             \
+  if (st == UGB_OK) st = set_attn_smem<G, float>(ctx);               \
+  if (st == UGB_OK) st = set_attn_smem<G, __half>(ctx);
+  UGB_ATTN_INIT(1) UGB_ATTN_INIT(2) UGB_ATTN_INIT(3) UGB_ATTN_INIT(4)
+  UGB_ATTN_INIT(5) UGB_ATTN_INIT(6) UGB_ATTN_INIT(7) UGB_ATTN_INIT(8)
+#undef UGB_ATTN_INIT
+  return st;
+}
+
+int pf_attn_groups(int pos0, int n, int cpi) {
+  const int chunks = (pos0 + n + kAK - 1) / kAK;
+  return (chunks + cpi - 1) / cpi;
+}
+
+size_t pf_attn_partial_floats(int max_tokens, int n_head, int n_ctx, int max_groups) {
+  const size_t tiles = (max_tokens + kAQ - 1) / kAQ;
+  const int chunks = (n_ctx + kAK - 1) / kAK;
+  const size_t groups = std::min(chunks, max_groups);
+  return tiles * groups * 16 * static_cast<size_t>(n_head) * kHD;  // (n_kv x 16 G rows = 16 n_head) x 128
+}
+
+ugb_status launch_pf_attention(cudaStream_t s, const PrefillAttn &a) {
+  const int G = a.n_head / a.n_kv;
+  const int groups = pf_attn_groups(a.pos0, a.n, a.cpi);
+  const dim3 grid((a.n + kAQ - 1) / kAQ, a.n_kv, groups);
+  ugb_status st;
+  switch (G) {
+    case 1: st = launch_partial<1>(s, a, grid); break;
+    case 2: st = launch_partial<2>(s, a, grid); break;
+    case 3: st = launch_partial<3>(s, a, grid); break;
+    case 4: st = launch_partial<4>(s, a, grid); break;
+    case 5: st = launch_partial<5>(s, a, grid); break;
+    case 6: st = launch_partial<6>(s, a, grid); break;
+    case 7: st = launch_partial<7>(s, a, grid); break;
+    case 8: st = launch_partial<8>(s, a, grid); break;
+    default: return UGB_ESHAPE;
+  }
+  if (st != UGB_OK) return st;
+  pf_attn_combine_kernel<<<dim3(a.n, a.n_head), kHD, 0, s>>>(a, groups);
+  return cuda_status(cudaGetLastError());
+}
+
+ugb_status launch_pf_norm_quant(cudaStream_t s, float *x, const float *dx, int dx_splits, int64_t dx_stride,
+                                const float *w, int n, int embd, float eps, uint8_t *packed, float *pre,
+                                uint32_t *status) {
+  const PackedLayout p = prefill_layout(n, embd);
+  pf_norm_quant_kernel<<<n, 512, 0, s>>>(x, dx, dx_splits, dx_stride, w, embd, eps, packed,
+                                         reinterpret_cast<float *>(packed + p.q_bytes), pre, status);
+  return cuda_status(cudaGetLastError());
+}
+
+ugb_status launch_pf_silu_quant(cudaStream_t s, const float *gu, int64_t ld, int splits, int64_t stride, int n,
+                                int n_ff, uint8_t *packed, float *pre, uint32_t *status) {
+  const PackedLayout p = prefill_layout(n, n_ff);
+  const int64_t warps = static_cast<int64_t>(n) * (n_ff / 32);
+  pf_silu_quant_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, s>>>(
+      gu, ld, splits, stride, n, n_ff, packed, reinterpret_cast<float *>(packed + p.q_bytes), pre, status);
+  return cuda_status(cudaGetLastError());
+}
+
+ugb_status launch_pf_sum_splits(cudaStream_t s, const float *src, int splits, int64_t stride, int64_t row0,
+                                int64_t rows, int64_t len, float *dst) {
+  const int64_t total = rows * len;
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((total + 255) / 256, 4096));
+  pf_sum_splits_kernel<<<blocks, 256, 0, s>>>(src, splits, stride, row0, rows, len, dst);
   return cuda_status(cudaGetLastError());
 }
 
