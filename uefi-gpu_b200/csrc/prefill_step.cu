@@ -47,8 +47,13 @@ __global__ void __launch_bounds__(256) pf_embed_kernel(const uint8_t *__restrict
 // Sum of the `splits` partial outputs of a split-K GEMM at element i (split stride `stride`), in
 // split order: the same value every consumer of the product forms.
 __device__ __forceinline__ float split_sum(const float *p, int splits, int64_t stride, int64_t i) {
-  float v = p[i];
-  for (int s = 1; s < splits; ++s) v += p[s * stride + i];
+  float t[kMaxGemmSplits];  // every split's load issued before the first add
+#pragma unroll
+  for (int s = 0; s < kMaxGemmSplits; ++s) t[s] = s < splits ? p[s * stride + i] : 0.f;
+  float v = t[0];
+#pragma unroll
+  for (int s = 1; s < kMaxGemmSplits; ++s)
+    if (s < splits) v += t[s];
   return v;
 }
 
@@ -97,21 +102,47 @@ __global__ void __launch_bounds__(512) pf_norm_quant_kernel(float *__restrict__ 
 }
 
 // SiLU(g) * u of the gate / up GEMM rows (summed over its splits) quantised per 32-block into the
-// packed operand of the down GEMM; one warp per (token, block); pre[t] (the trace) when given.
+// packed operand of the down GEMM; pre[t] (the trace) when given.  One warp per kSiluBlocks
+// consecutive blocks of a token, every load issued before the first use.
+constexpr int kSiluBlocks = 4;
+
 __global__ void __launch_bounds__(256) pf_silu_quant_kernel(const float *__restrict__ gu, int64_t ld, int splits,
                                                             int64_t stride, int n, int n_ff,
                                                             uint8_t *__restrict__ q_out, float *__restrict__ s_out,
                                                             float *__restrict__ pre, uint32_t *status) {
   const int lane = threadIdx.x & 31, nb = n_ff / 32;
+  const int per_token = (nb + kSiluBlocks - 1) / kSiluBlocks;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
-  if (gw >= static_cast<int64_t>(n) * nb) return;  // warp-uniform
-  const int b = static_cast<int>(gw % nb);
-  const int64_t t = gw / nb;
-  const float g = split_sum(gu, splits, stride, t * ld + b * 32 + lane);
-  const float u = split_sum(gu, splits, stride, t * ld + n_ff + b * 32 + lane);
-  const float h = (g / (1.0f + expf(-g))) * u;
-  if (pre) pre[t * n_ff + b * 32 + lane] = h;
-  if (pf_quant_block(h, lane, t, b, nb, q_out, s_out) && lane == 0) status_or(status, ST_NONFINITE_IN);
+  if (gw >= static_cast<int64_t>(n) * per_token) return;  // warp-uniform
+  const int b0 = static_cast<int>(gw % per_token) * kSiluBlocks;
+  const int64_t t = gw / per_token;
+  const float *row = gu + t * ld;
+  float g[kSiluBlocks][kMaxGemmSplits], u[kSiluBlocks][kMaxGemmSplits];
+#pragma unroll
+  for (int k = 0; k < kSiluBlocks; ++k) {
+    const int i = min(b0 + k, nb - 1) * 32 + lane;
+#pragma unroll
+    for (int sp = 0; sp < kMaxGemmSplits; ++sp) {
+      g[k][sp] = sp < splits ? row[sp * stride + i] : 0.f;
+      u[k][sp] = sp < splits ? row[sp * stride + n_ff + i] : 0.f;
+    }
+  }
+  bool bad = false;
+#pragma unroll
+  for (int k = 0; k < kSiluBlocks; ++k) {
+    if (b0 + k >= nb) break;  // warp-uniform
+    float gv = g[k][0], uv = u[k][0];
+#pragma unroll
+    for (int sp = 1; sp < kMaxGemmSplits; ++sp)
+      if (sp < splits) {
+        gv += g[k][sp];
+        uv += u[k][sp];
+      }
+    const float h = (gv / (1.0f + expf(-gv))) * uv;
+    if (pre) pre[t * n_ff + (b0 + k) * 32 + lane] = h;
+    bad |= pf_quant_block(h, lane, t, b0 + k, nb, q_out, s_out);
+  }
+  if (bad && lane == 0) status_or(status, ST_NONFINITE_IN);
 }
 
 // dst[r][i] = the sum of the splits of rows [row0, row0 + rows) of a split-K GEMM output [.][len].
@@ -307,31 +338,49 @@ __global__ void __launch_bounds__(256) pf_attn_partial_kernel(PrefillAttn a) {
   }
 }
 
-// Token t = blockIdx.x, query head h = blockIdx.y, thread = output dim: merge the token's partials
-// over the chunk groups that hold positions <= pos0 + t (max, then exp(m_z - max) weights), write
-// the output (trace) when asked and quantise it, warp w taking 32-block 4 h + w of the token, into
-// the O GEMM's packed operand.
-__global__ void __launch_bounds__(kHD) pf_attn_combine_kernel(PrefillAttn a, int groups) {
-  const int t = blockIdx.x, h = blockIdx.y, d = threadIdx.x, lane = d & 31, warp = d >> 5;
-  const int G = a.n_head / a.n_kv, kvh = h / G, g = h - kvh * G, R = 16 * G;
-  const int r = g * kAQ + t % kAQ;
+// Token t = blockIdx.x, KV head blockIdx.y: merge the token's partials of the G query heads over
+// the chunk groups holding positions <= pos0 + t (max, then exp(m_z - max) weights), write the
+// output (trace) when asked and quantise it into the O GEMM's packed operand.  Warp w takes the
+// 32-blocks w, w + 8, ... of the KV head's G * 128 outputs (block 4 g + j is dims 32 j .. of head
+// kvh * G + g); the per-head weights are formed once, by warp g, into shared memory.
+__global__ void __launch_bounds__(256) pf_attn_combine_kernel(PrefillAttn a, int groups) {
+  constexpr int kMaxZ = 16;
+  __shared__ float wz[8][kMaxZ];  // [head of the group][chunk group] weight exp(m_z - max) / L
+  const int t = blockIdx.x, kvh = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = a.n_head / a.n_kv, R = 16 * G;
   const int pos = a.pos0 + t;
   const int nz = min(groups, (pos / kAK) / a.cpi + 1);  // chunk groups with positions <= pos
   const int64_t item0 = (static_cast<int64_t>(t / kAQ) * a.n_kv + kvh) * groups;
-  float mx = -FLT_MAX;
-  for (int z = 0; z < nz; ++z) mx = fmaxf(mx, a.part_m[(item0 + z) * R + r]);
-  float l = 0.f, o = 0.f;
-  for (int z = 0; z < nz; ++z) {
-    const int64_t pi = (item0 + z) * R + r;
-    const float e = expf(a.part_m[pi] - mx);
-    l += e * a.part_l[pi];
-    o += e * a.part_o[pi * kHD + d];
+  if (warp < G) {
+    const int r = warp * kAQ + t % kAQ;
+    const float m = lane < nz ? a.part_m[(item0 + lane) * R + r] : -FLT_MAX;
+    const float l = lane < nz ? a.part_l[(item0 + lane) * R + r] : 0.f;
+    float mx = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float e = lane < nz ? expf(m - mx) : 0.f;
+    float L = e * l;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane < kMaxZ) wz[warp][lane] = e / L;
   }
-  const float v = o / l;
-  const int qr = a.n_head * kHD;
-  if (a.out) a.out[static_cast<int64_t>(t) * qr + h * kHD + d] = v;
-  if (pf_quant_block(v, lane, t, 4 * h + warp, qr / 32, a.q_out, a.s_out) && lane == 0)
-    status_or(a.status, ST_NONFINITE_IN);
+  __syncthreads();
+  const int qr = a.n_head * kHD, nb = qr / 32;
+  bool bad = false;
+  for (int blk = warp; blk < 4 * G; blk += 8) {  // warp-uniform
+    const int g = blk / 4, d = (blk % 4) * 32 + lane, h = kvh * G + g;
+    const int64_t p0 = (item0 * R + g * kAQ + t % kAQ) * kHD + d;
+    float ov[kMaxZ];
+#pragma unroll
+    for (int z = 0; z < kMaxZ; ++z) ov[z] = z < nz ? a.part_o[p0 + static_cast<int64_t>(z) * R * kHD] : 0.f;
+    float v = 0.f;
+#pragma unroll
+    for (int z = 0; z < kMaxZ; ++z)
+      if (z < nz) v += wz[g][z] * ov[z];
+    if (a.out) a.out[static_cast<int64_t>(t) * qr + h * kHD + d] = v;
+    bad |= pf_quant_block(v, lane, t, 4 * h + blk % 4, nb, a.q_out, a.s_out);
+  }
+  if (bad && lane == 0) status_or(a.status, ST_NONFINITE_IN);
 }
 
 }  // namespace
@@ -410,7 +459,8 @@ ugb_status launch_pf_attention(cudaStream_t s, const PrefillAttn &a) {
     default: return UGB_ESHAPE;
   }
   if (st != UGB_OK) return st;
-  pf_attn_combine_kernel<<<dim3(a.n, a.n_head), kHD, 0, s>>>(a, groups);
+  if (groups > 16) return UGB_ESHAPE;  // the combine weighs at most 16 chunk groups
+  pf_attn_combine_kernel<<<dim3(a.n, a.n_kv), 256, 0, s>>>(a, groups);
   return cuda_status(cudaGetLastError());
 }
 
@@ -426,7 +476,7 @@ ugb_status launch_pf_norm_quant(cudaStream_t s, float *x, const float *dx, int d
 ugb_status launch_pf_silu_quant(cudaStream_t s, const float *gu, int64_t ld, int splits, int64_t stride, int n,
                                 int n_ff, uint8_t *packed, float *pre, uint32_t *status) {
   const PackedLayout p = prefill_layout(n, n_ff);
-  const int64_t warps = static_cast<int64_t>(n) * (n_ff / 32);
+  const int64_t warps = static_cast<int64_t>(n) * ((n_ff / 32 + kSiluBlocks - 1) / kSiluBlocks);
   pf_silu_quant_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, s>>>(
       gu, ld, splits, stride, n, n_ff, packed, reinterpret_cast<float *>(packed + p.q_bytes), pre, status);
   return cuda_status(cudaGetLastError());
