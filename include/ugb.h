@@ -285,15 +285,31 @@ ugb_status ugb_prefill_block_dots(ugb_ctx *ctx, ugb_stream stream, const void *w
 
 /* ---- collectives (NCCL over NVLink) for sharded decoding -------------------------------- */
 
-/* A communicator over the devices of one sharded decoder (one process or thread per GPU).
- * NCCL is loaded at run time; without it these return UGB_EBACKEND.  Rank 0 makes the id
- * with ugb_comm_unique_id and the caller hands it to every rank (e.g. over its own process
- * group); ugb_comm_init is collective: every rank calls it at the same time. */
+/* A communicator over the devices of one sharded decoder (one process or thread per GPU, at
+ * most 8, all able to map each other's memory: one NVLink / NVSwitch node).  NCCL is loaded at
+ * run time to create it; without NCCL these return UGB_EBACKEND.  Rank 0 makes the id with
+ * ugb_comm_unique_id and the caller hands it to every rank (e.g. over its own process group);
+ * ugb_comm_init is collective: every rank calls it at the same time.  It allocates each rank's
+ * receive area and maps every peer's (CUDA IPC), so the collectives below are the library's own
+ * kernels over peer memory (replacing the reference's single-GPU expert loop and vocabulary
+ * projection, frontier_forward.rs:164-199, gpu_greedy.cu:13-27, when they are sharded).
+ * ugb_comm_destroy is collective too. */
 typedef struct ugb_comm ugb_comm;
 #define UGB_COMM_ID_BYTES 128
+#define UGB_COMM_MAX_WORDS 32768
 ugb_status ugb_comm_unique_id(uint8_t *id_out /* UGB_COMM_ID_BYTES */);
 ugb_status ugb_comm_init(ugb_ctx *ctx, int rank, int world, const uint8_t *id, ugb_comm **out);
 ugb_status ugb_comm_destroy(ugb_comm *comm);
+
+/* In-place all-reduce of n values of a 16-byte aligned device buffer over the communicator's
+ * ranks, asynchronous on `stream` and capturable: every rank pushes its data into every rank's
+ * receive area with peer stores, raises a flag there, waits (bounded by the wait limit; on
+ * expiry the context's status word gets UGB_STATUS_TIMEOUT and the result is not valid) for
+ * every rank's flag, and reduces the ranks' data in rank order, so all ranks hold the same bits.
+ * f32: sum, n <= UGB_COMM_MAX_WORDS.  u64: maximum, n <= UGB_COMM_MAX_WORDS / 2.  Every rank must
+ * make the same sequence of calls. */
+ugb_status ugb_comm_allreduce_f32(ugb_comm *comm, ugb_stream stream, float *buf_dev, int64_t n);
+ugb_status ugb_comm_allreduce_max_u64(ugb_comm *comm, ugb_stream stream, uint64_t *buf_dev, int64_t n);
 
 /* ---- decoder (the per-token graph around the matvecs) ------------------------------------ */
 

@@ -41,7 +41,7 @@ def _load(name: str) -> ctypes.CDLL:
     lib.orc_quant_act.argtypes = [_c_f32p, _c_i8p, _c_f32p, _c_i32p, ctypes.c_long]
     lib.orc_block_dots.restype = ctypes.c_int
     lib.orc_block_dots.argtypes = [ctypes.c_uint32, _c_u8p, _c_i8p, ctypes.c_long, _c_i32p]
-    for fn in (lib.orc_matvec, lib.orc_matvec_mt):
+    for fn in (lib.orc_matvec, lib.orc_matvec_mt, lib.orc_matvec_terms_mt):
         fn.restype = ctypes.c_int
         fn.argtypes = [ctypes.c_uint32, _c_u8p, ctypes.c_long, _c_i8p, _c_f32p, _c_i32p, _c_f32p,
                        ctypes.c_long, ctypes.c_long, ctypes.c_long]
@@ -131,6 +131,21 @@ def matvec(kind: int, w: np.ndarray, row_bytes_: int, q: np.ndarray, d: np.ndarr
             _p(y, _c_f32p), k, m, batch)
     if rc:
         raise ValueError(f"orc_matvec rc={rc}")
+    return y
+
+
+def matvec_terms(kind: int, w: np.ndarray, row_bytes_: int, q: np.ndarray, d: np.ndarray, s: np.ndarray,
+                 k: int, m: int, batch: int = 1) -> np.ndarray:
+    """Per (vector, row): the sum of the magnitudes of the row's block terms."""
+    w = np.ascontiguousarray(w, dtype=np.uint8).reshape(-1)
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    d = np.ascontiguousarray(d, dtype=np.float32)
+    s = np.ascontiguousarray(s, dtype=np.int32)
+    y = np.empty((batch, m), dtype=np.float32)
+    rc = lib(True).orc_matvec_terms_mt(kind, _p(w, _c_u8p), row_bytes_, _p(q, _c_i8p), _p(d, _c_f32p),
+                                       _p(s, _c_i32p), _p(y, _c_f32p), k, m, batch)
+    if rc:
+        raise ValueError(f"orc_matvec_terms rc={rc}")
     return y
 
 

@@ -209,15 +209,18 @@ int orc_block_dots(uint32_t kind, const uint8_t *row, const int8_t *q, long k, i
   return 0;
 }
 
+/* The scaled row dot; with `absolute` set, the sum of the magnitudes of its block terms instead
+ * (the scale against which any reordering of the fp32 sum is judged). */
 static float row_dot(uint32_t kind, const uint8_t *row, const int8_t *q, const float *d,
-                     const int32_t *s, long k) {
+                     const int32_t *s, long k, int absolute) {
   float y = 0.0f;
   for (long b = 0; b < k / 32; b++) {
     int32_t isum = block_dot(kind, row, q, b);
+    float term = 0.0f;
     switch (kind) {
       case ORC_Q8_0: {
         float dw = orc_half(rd16(row + b * 34));
-        y += (float)isum * (dw * d[b]);
+        term = (float)isum * (dw * d[b]);
         break;
       }
       case ORC_Q4_K: {
@@ -226,16 +229,17 @@ static float row_dot(uint32_t kind, const uint8_t *row, const int8_t *q, const f
         q4k_scale_min(sb + 4, (int)(b % 8), &sc, &mn);
         float dl = orc_half(rd16(sb)) * (float)sc;
         float ml = orc_half(rd16(sb + 2)) * (float)mn;
-        y += d[b] * (dl * (float)isum - ml * (float)s[b]);
+        term = d[b] * (dl * (float)isum - ml * (float)s[b]);
         break;
       }
       case ORC_Q3_K: {
         const uint8_t *sb = row + (b / 8) * 110;
         float dsb = orc_half(rd16(sb + 108));
-        y += (float)isum * (dsb * d[b]);
+        term = (float)isum * (dsb * d[b]);
         break;
       }
     }
+    y += absolute ? fabsf(term) : term;
   }
   return y;
 }
@@ -248,6 +252,7 @@ typedef struct {
   const float *d;
   const int32_t *s;
   float *y;
+  int absolute;
 } mv_span;
 
 /* Rows [begin, end) of the flattened (batch, row) index space. */
@@ -257,14 +262,14 @@ static void *mv_span_run(void *arg) {
   for (long i = t->begin; i < t->end; i++) {
     long v = i / t->m, r = i % t->m;
     t->y[i] = row_dot(t->kind, t->w + r * t->row_bytes, t->q + v * t->k, t->d + v * nb,
-                      t->s + v * nb, t->k);
+                      t->s + v * nb, t->k, t->absolute);
   }
   return NULL;
 }
 
 static int matvec_impl(uint32_t kind, const uint8_t *w, long row_bytes, const int8_t *q,
                        const float *d, const int32_t *s, float *y, long k, long m, long batch,
-                       int threads) {
+                       int threads, int absolute) {
   long rb = orc_row_bytes(kind, k);
   if (rb < 0) return (int)rb;
   if (kind == ORC_F32 || !has_decoder(kind)) return -1;
@@ -277,7 +282,7 @@ static int matvec_impl(uint32_t kind, const uint8_t *w, long row_bytes, const in
   pthread_t tids[256];
   for (int t = 0; t < threads; t++) {
     mv_span sp = {kind, w, row_bytes, k, m, batch, total * t / threads,
-                  total * (t + 1) / threads, q, d, s, y};
+                  total * (t + 1) / threads, q, d, s, y, absolute};
     spans[t] = sp;
   }
   if (threads == 1) {
@@ -299,12 +304,17 @@ int orc_threads(void) {
 
 int orc_matvec(uint32_t kind, const uint8_t *w, long row_bytes, const int8_t *q, const float *d,
                const int32_t *s, float *y, long k, long m, long batch) {
-  return matvec_impl(kind, w, row_bytes, q, d, s, y, k, m, batch, 1);
+  return matvec_impl(kind, w, row_bytes, q, d, s, y, k, m, batch, 1, 0);
 }
 
 int orc_matvec_mt(uint32_t kind, const uint8_t *w, long row_bytes, const int8_t *q,
                   const float *d, const int32_t *s, float *y, long k, long m, long batch) {
-  return matvec_impl(kind, w, row_bytes, q, d, s, y, k, m, batch, orc_threads());
+  return matvec_impl(kind, w, row_bytes, q, d, s, y, k, m, batch, orc_threads(), 0);
+}
+
+int orc_matvec_terms_mt(uint32_t kind, const uint8_t *w, long row_bytes, const int8_t *q,
+                        const float *d, const int32_t *s, float *y, long k, long m, long batch) {
+  return matvec_impl(kind, w, row_bytes, q, d, s, y, k, m, batch, orc_threads(), 1);
 }
 
 int orc_matvec_dequant_f32(uint32_t kind, const uint8_t *w, long row_bytes, const float *x,

@@ -25,10 +25,18 @@ Q8_0 = 8
 
 
 def quant_matvec(orc, kind, w, x, m):
-    """The oracle's matvec of its own quantisation of x [n, k]."""
+    """The oracle's matvec of its own quantisation of x [n, k], and the sums of the magnitudes of
+    each row's block terms (the prefill's GEMMs may add a row's blocks in another order: split
+    over K)."""
     q, d, s, _ = orc.quant_act(x)
     n, k = x.shape
-    return orc.matvec(kind, w, orc.row_bytes(kind, k), q, d, s, k, m, n, mt=True)
+    rb = orc.row_bytes(kind, k)
+    return orc.matvec(kind, w, rb, q, d, s, k, m, n, mt=True), orc.matvec_terms(kind, w, rb, q, d, s, k, m, n)
+
+
+def rows_close(gpu, want_terms):
+    want, terms = want_terms
+    assert_rows_close(gpu, want, terms=terms)
 
 
 def check_prefill(orc, ref, dec, host, cfg, toks, pos0):
@@ -46,10 +54,8 @@ def check_prefill(orc, ref, dec, host, cfg, toks, pos0):
             np.testing.assert_array_equal(x, np.stack([ref.embed(int(t)) for t in toks]))
         for t in range(n):
             assert_close(tr["ATTN_NORM"][t], ref.norm(x[t], L["attn_norm"]), NORM_REL, f"L{li} t{t} attn norm")
-        want = np.concatenate([quant_matvec(orc, kind, L["wq"], tr["ATTN_NORM"], Q),
-                               quant_matvec(orc, kind, L["wk"], tr["ATTN_NORM"], KV),
-                               quant_matvec(orc, kind, L["wv"], tr["ATTN_NORM"], KV)], axis=1)
-        assert_rows_close(tr["QKV"], want)
+        parts = [quant_matvec(orc, kind, L[w], tr["ATTN_NORM"], rows) for w, rows in (("wq", Q), ("wk", KV), ("wv", KV))]
+        rows_close(tr["QKV"], (np.concatenate([p[0] for p in parts], axis=1), np.concatenate([p[1] for p in parts], axis=1)))
         keys, vals = dec.read_kv(li, 0, pos0 + n)
         kv_rel = 1e-3 if cfg.get("kv_type", F32) == F16 else ROPE_REL
         for t in range(n):
@@ -62,18 +68,17 @@ def check_prefill(orc, ref, dec, host, cfg, toks, pos0):
             assert_close(vals[:, pos], ref.kv_round(v), 0.0, f"L{li} t{t} cached value")
             assert_close(tr["ATT"][t], ref.attend(q, keys[:, :pos + 1], vals[:, :pos + 1]).reshape(-1), ATT_REL,
                          f"L{li} t{t} attention")
-        assert_rows_close(tr["O"], quant_matvec(orc, kind, L["wo"], tr["ATT"], E))
+        rows_close(tr["O"], quant_matvec(orc, kind, L["wo"], tr["ATT"], E))
         mid = (x + tr["O"]).astype(np.float32)
         for t in range(n):
             assert_close(tr["FFN_NORM"][t], ref.norm(mid[t], L["ffn_norm"]), NORM_REL, f"L{li} t{t} ffn norm")
-        gu = np.concatenate([quant_matvec(orc, kind, L["w_gate"], tr["FFN_NORM"], F),
-                             quant_matvec(orc, kind, L["w_up"], tr["FFN_NORM"], F)], axis=1)
-        assert_rows_close(tr["GATE_UP"], gu)
+        g_, u_ = quant_matvec(orc, kind, L["w_gate"], tr["FFN_NORM"], F), quant_matvec(orc, kind, L["w_up"], tr["FFN_NORM"], F)
+        rows_close(tr["GATE_UP"], (np.concatenate([g_[0], u_[0]], axis=1), np.concatenate([g_[1], u_[1]], axis=1)))
         g, u = tr["GATE_UP"][:, :F], tr["GATE_UP"][:, F:]
         with np.errstate(over="ignore"):
             h = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
         assert_close(tr["H"], h, SILU_REL, f"L{li} silu")
-        assert_rows_close(tr["DOWN"], quant_matvec(orc, kind, L["w_down"], tr["H"], E))
+        rows_close(tr["DOWN"], quant_matvec(orc, kind, L["w_down"], tr["H"], E))
         x_next = (mid + tr["DOWN"]).astype(np.float32)
         if li + 1 < cfg["n_layer"]:
             np.testing.assert_array_equal(dec.prefill_trace(li + 1, "X", n), x_next, err_msg=f"L{li} residual")

@@ -76,6 +76,8 @@ SIGNATURES = {
     "ugb_comm_unique_id": (_int, [_vp]),
     "ugb_comm_init": (_int, [_vp, _int, _int, _vp, ctypes.POINTER(_vp)]),
     "ugb_comm_destroy": (_int, [_vp]),
+    "ugb_comm_allreduce_f32": (_int, [_vp, _vp, _vp, _i64]),
+    "ugb_comm_allreduce_max_u64": (_int, [_vp, _vp, _vp, _i64]),
     "ugb_decoder_get_state": (_int, [_vp, _vp, ctypes.POINTER(ctypes.c_int32),
                                      ctypes.POINTER(ctypes.c_int32), ctypes.POINTER(ctypes.c_int32)]),
     "ugb_decoder_logits": (_int, [_vp, _vp, _vp]),
@@ -413,6 +415,16 @@ class Comm:
         if self.handle:
             lib().ugb_comm_destroy(self.handle)
             self.handle = None
+
+    def allreduce_f32(self, buf, stream=None) -> None:
+        """In-place sum over the ranks of a float32 device tensor (rank order, deterministic)."""
+        check("ugb_comm_allreduce_f32", lib().ugb_comm_allreduce_f32(self.handle, _stream(stream), _ptr(buf),
+                                                                       buf.numel()))
+
+    def allreduce_max_u64(self, buf, stream=None) -> None:
+        """In-place maximum over the ranks of an int64 device tensor read as unsigned 64-bit."""
+        check("ugb_comm_allreduce_max_u64", lib().ugb_comm_allreduce_max_u64(self.handle, _stream(stream),
+                                                                               _ptr(buf), buf.numel()))
 
 
 def comm_unique_id() -> bytes:
