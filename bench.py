@@ -777,6 +777,33 @@ def big_gpu(args, ugb, ctx, torch, rank, world, workload):
     e2e_s = (time.perf_counter() - t0) / e2e_steps
     e2e_s = reduce_max(e2e_s * 1e3, world, torch) / 1e3
     barrier(world, torch)
+    collective = None
+    if comm:
+        # the step's collective alone, back to back on the stream: the MoE layer output (sum of
+        # batch x hidden f32) or the greedy keys (max of batch u64)
+        if workload == "c5":
+            cbuf = torch.zeros(batch * c["n_embd"], dtype=torch.float32, device="cuda")
+            call, what, per_step = comm.allreduce_f32, f"sum of {batch}x{c['n_embd']} f32", c["n_layer"]
+        else:
+            cbuf = torch.zeros(batch, dtype=torch.int64, device="cuda")
+            call, what, per_step = comm.allreduce_max_u64, f"max of {batch} u64 greedy keys", 1
+        for _ in range(5):
+            call(cbuf, stream)
+        stream.synchronize()
+        barrier(world, torch)
+        reps = 200
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(reps):
+            call(cbuf, stream)
+        c1.record(stream)
+        torch.cuda.synchronize()
+        us = reduce_max(c0.elapsed_time(c1) * 1e3 / reps, world, torch)
+        collective = {"op": "ugb_comm one-shot all-reduce over NVLink peer memory: " + what, "us_per_call": us,
+                      "calls_per_step": per_step, "share_of_step": per_step * us / 1e3 / (ms_max / K)}
+        code, bits = ctx.status_read(stream)
+        assert code == ugb.OK, ("status after the collective timing", code, bits)
+        barrier(world, torch)
     graph.close()
     dec.close()  # releases the decoder's own captured graph before the communicator goes
     if comm:
@@ -786,8 +813,29 @@ def big_gpu(args, ugb, ctx, torch, rank, world, workload):
         "gpu_launches": kernels * K, "step_bytes": step_bytes, "batch": batch, "path": active,
         "e2e": {"value": batch / e2e_s, "unit": "tok/s", "h2d_bytes_per_step": 8 * 4 + 8,
                 "d2h_bytes_per_step": 112 + 4},
-        "config": c,
+        "config": c, "collective": collective,
     }
+
+
+SHARDED = (("c4_b8_head_rows_split", "c4", 8), ("c5_b1_experts_split", "c5", 1), ("c5_b8_experts_split", "c5", 8))
+
+
+def sharded_gpu(args, ugb, ctx, torch, rank, world):
+    """The configs that shard (BASELINE configs 4 and 5) at this process group's size: C4 batch 8
+    with the head rows split over the GPUs, C5 batch 1 and 8 with the experts split.  tok/s of the
+    whole group, per-step time, and the time of the step's collective measured alone."""
+    import copy
+    out = {}
+    for name, wl, batch in SHARDED:
+        a = copy.copy(args)
+        a.batch, a.path, a.layers = batch, "auto", 0
+        res = big_gpu(a, ugb, ctx, torch, rank, world, wl)
+        out[name] = {"value": res["value"], "unit": "tok/s", "ms_per_step": res["ms_per_step"], "n_gpus": world,
+                     "batch": batch, "roofline_frac": res["step_bytes"] / (res["ms_per_step"] / 1e3) / 1e9 /
+                     load_peaks()[0], "collective": res["collective"],
+                     "path": "token kernel" if res["path"] == ugb.PATH_TOKEN else "launch chain (captured graph)"}
+        torch.cuda.empty_cache()
+    return out
 
 
 def host_quant_matrix(rng, kind, k, m):
@@ -864,6 +912,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0,
                     help="c4 / c5: decode this many layers instead of the config's (profiling captures only)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--sharded", choices=["auto", "on", "off"], default="auto",
+                    help="c2: also measure the sharding configs (c4 batch 8 head split, c5 batch 1 / 8 experts "
+                         "split) at this --gpus; auto = when more than one GPU")
     ap.add_argument("--kv", choices=sorted(KV_TYPES), default="f16",
                     help="c2 / c4 / c5 KV cache element type (BASELINE config 2: fp16; the reference keeps fp32)")
     ap.add_argument("--path", choices=sorted(PATHS), default="auto",
@@ -1025,6 +1076,8 @@ def main():
         line["decoder_path"] = decoder_path
     if res.get("kv_other"):
         line["kv_fp32"] = res["kv_other"]
+    if args.workload == "c2" and (args.sharded == "on" or (args.sharded == "auto" and world > 1)):
+        line["sharded"] = sharded_gpu(args, ugb, ctx, torch, rank, world)
     if "token_bytes" in res:
         step_gbs = res["token_bytes"] / (res["ms_per_step"] / 1e3) / 1e9
         line["roofline"]["step"] = {"bytes_per_token": res["token_bytes"], "achieved": step_gbs,

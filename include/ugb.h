@@ -301,7 +301,7 @@ ugb_status ugb_comm_unique_id(uint8_t *id_out /* UGB_COMM_ID_BYTES */);
 ugb_status ugb_comm_init(ugb_ctx *ctx, int rank, int world, const uint8_t *id, ugb_comm **out);
 ugb_status ugb_comm_destroy(ugb_comm *comm);
 
-/* In-place all-reduce of n values of a 16-byte aligned device buffer over the communicator's
+/* In-place all-reduce of n values of a device buffer (aligned to its element) over the communicator's
  * ranks, asynchronous on `stream` and capturable: every rank pushes its data into every rank's
  * receive area with peer stores, raises a flag there, waits (bounded by the wait limit; on
  * expiry the context's status word gets UGB_STATUS_TIMEOUT and the result is not valid) for

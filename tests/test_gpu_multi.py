@@ -3,6 +3,8 @@
 Each rank is a process on its own GPU with the library's NCCL communicator; a gloo process
 group carries the communicator id and a barrier (with a timeout) before every step, so a rank
 that fails is noticed on the host before the other enters a collective.
+* the library's own all-reduce over NVLink peer memory (sum f32, max u64) gives every rank the
+  rank-order result bit for bit, across repeated calls and sizes up to 32768 values;
 * vocabulary split: each rank holds half of the head rows; the greedy keys are all-reduced
   inside the token step.  The next tokens equal a single-GPU decoder's, and each rank's
   logits equal that decoder's logits over the held rows, bit for bit.
@@ -54,6 +56,22 @@ def _worker(rank, world, port, out):
     dist.broadcast_object_list(uid, src=0)
     comm = ugb.Comm(ctx, rank, world, uid[0])
     res = {}
+    # -- the collectives themselves: every rank gets the rank-order sum / maximum, bit for bit,
+    # over several calls (both buffer parities), unaligned and multi-slice sizes included --
+    ok_sum, ok_max = True, True
+    for call, n in enumerate([1, 4096, 4099, 32768, 7, 4096]):
+        data = [np.random.default_rng(100 * call + r).standard_normal(n).astype(np.float32) for r in range(world)]
+        want = data[0].copy()
+        for r in range(1, world):
+            want = (want + data[r]).astype(np.float32)
+        buf = torch.from_numpy(data[rank].copy()).cuda()
+        comm.allreduce_f32(buf)
+        ok_sum &= bool(np.array_equal(buf.cpu().numpy().view(np.uint32), want.view(np.uint32)))
+        keys = [np.random.default_rng(7 * call + r).integers(0, 2 ** 62, size=max(1, n // 1024)) for r in range(world)]
+        kbuf = torch.from_numpy(keys[rank].copy()).cuda()
+        comm.allreduce_max_u64(kbuf)
+        ok_max &= bool(np.array_equal(kbuf.cpu().numpy(), np.max(np.stack(keys), axis=0)))
+    res["allreduce_sum"], res["allreduce_max"] = ok_sum, ok_max
     # -- vocabulary split --
     half = SMALL["n_vocab"] // world
     shard = ugb.Decoder(ctx, **dict(SMALL, vocab0=rank * half, n_vocab_local=half))
@@ -119,6 +137,7 @@ def test_sharded_decoder_two_gpus():
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     for r in range(world):
         res = out[r]
+        assert res["allreduce_sum"] and res["allreduce_max"], res
         assert res["vocab_tokens"] and res["vocab_logits"], res
         errs = np.array(res["ep_errs"])
         assert errs.max() <= 5e-2 and (errs <= 1e-4).mean() >= 0.6, errs

@@ -116,11 +116,13 @@ __global__ void __launch_bounds__(256) p2p_allreduce_kernel(const AllReduceArgs 
   const uint32_t e = a.epochs[c] + 1;
   const int par = e & 1;
   // 1. this rank's slice into slot [par][rank] of every rank's area (the own one included)
+  const bool vec = (reinterpret_cast<uintptr_t>(a.buf) & 15) == 0;  // slots are 16-byte aligned
   for (int r = 0; r < a.world; ++r) {
     uint32_t *dst = a.peers.base[r] + (static_cast<int64_t>(par) * kCommMaxRanks + a.rank) * kCommCapWords + w0;
-    for (int i = tid; i < len / 4; i += blockDim.x)
+    const int nv = vec ? len / 4 : 0;
+    for (int i = tid; i < nv; i += blockDim.x)
       reinterpret_cast<uint4 *>(dst)[i] = reinterpret_cast<const uint4 *>(a.buf + w0)[i];
-    for (int i = (len / 4) * 4 + tid; i < len; i += blockDim.x) dst[i] = a.buf[w0 + i];
+    for (int i = nv * 4 + tid; i < len; i += blockDim.x) dst[i] = a.buf[w0 + i];
   }
   __syncthreads();
   if (tid == 0) {
@@ -166,7 +168,7 @@ __global__ void __launch_bounds__(256) p2p_allreduce_kernel(const AllReduceArgs 
 ugb_status launch_allreduce(ugb_comm *c, int op, uint32_t *buf, int64_t words, cudaStream_t stream) {
   if (!c || !c->area) return UGB_EBACKEND;
   if (words < 1 || words > kCommCapWords || (op == kOpMaxU64 && (words & 1))) return UGB_ESHAPE;
-  if ((reinterpret_cast<uintptr_t>(buf) & 15) != 0) return UGB_EALIGN;
+  if ((reinterpret_cast<uintptr_t>(buf) & (op == kOpMaxU64 ? 7 : 3)) != 0) return UGB_EALIGN;
   AllReduceArgs a;
   a.peers = c->peers;
   a.buf = buf;

@@ -113,23 +113,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
 }
-// 8 consecutive TMEM columns of this warp's 32 lanes.
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-               : "r"(taddr));
-}
-template <int N>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[N]) {
-  if constexpr (N == 32) {
-    tmem_ld32(taddr, r);
-  } else if constexpr (N == 16) {
-    tmem_ld16(taddr, r);
-  } else {
-    static_assert(N == 8, "8, 16 or 32 columns");
-    tmem_ld8(taddr, r);
-  }
-}
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor of one 128 x 32-byte K-major operand block in the canonical
@@ -267,23 +250,6 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   }
 }
 
-// acc[OFF/2 + i/2] (pairs of fp32) += (float)r[i] * (dw[i] * dx) for the H columns of one half-block:
-// fmaf((float)I, dw * dx, acc) per lane, two columns per instruction; half the conversions by the
-// conversion instruction and half by the bias trick, so neither pipe alone bounds the epilogue.
-template <int H, int OFF, int NACC>
-__device__ __forceinline__ void rescale_half(const uint32_t (&r)[H], const float4 *dw4, uint64_t dx2,
-                                             uint64_t (&acc)[NACC]) {
-#pragma unroll
-  for (int i = 0; i < H; i += 4) {
-    const float4 w = dw4[(OFF + i) / 4];  // same address across the warp: broadcast
-    const uint64_t s01 = mul2(pk2(w.x, w.y), dx2), s23 = mul2(pk2(w.z, w.w), dx2);
-    const uint64_t f01 = cvt2_i2f(r[i], r[i + 1]);
-    const uint64_t f23 = cvt2_bias(r[i + 2], r[i + 3]);
-    acc[(OFF + i) / 2] = fma2(f01, s01, acc[(OFF + i) / 2]);
-    acc[(OFF + i) / 2 + 1] = fma2(f23, s23, acc[(OFF + i) / 2 + 1]);
-  }
-}
-
 template <int BN>
 __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParams p) {
   using G = Geo<BN>;
@@ -395,69 +361,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     }
   } else {
     // ---- epilogue: rescale every block's int32 tile into fp32 accumulators ----
-    // Pipelined by half-blocks: the TMEM load of the next half is in flight while the current half
-    // is rescaled, and a block's accumulator is handed back to the MMA warp as soon as its second
-    // half is in registers (before it is rescaled).  Blocks are summed in order, as the reference.
     constexpr int kC = G::kCols;           // columns of this warp (32 or 16)
-    constexpr int kH = kC / 2;             // per half-block load
     const int q = warp & 3;                // TMEM lane quarter this warp may access
     const int h = (warp - 2) >> 2;         // column quarter
     const int t_local = q * 32 + lane;     // token row of the tile
     const int c0 = h * kC;                 // first column of this warp
     const int64_t t = m_tile * kBM + t_local;
-    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0);
-    auto taddr = [&](int b, int half) { return lane_base + static_cast<uint32_t>((b % kAcc) * BN + half * kH); };
-    auto dump = [&](const uint32_t(&r)[kH], int b, int half) {  // test path: the raw int32 block dots
-#pragma unroll
-      for (int i = 0; i < kH; ++i) {
-        const int64_t nn = n_col0 + c0 + half * kH + i;
-        if (t < p.m && nn < p.n)
-          p.dots[(static_cast<int64_t>(kb0 + b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
-      }
-    };
     uint64_t acc[kC / 2];                  // pairs of fp32 accumulators
 #pragma unroll
     for (int i = 0; i < kC / 2; ++i) acc[i] = 0ull;
-    uint32_t ra[kH], rb[kH];
-    bool ok = wait_or_abort(smem_u32(&tfull[0]), 0, abort_flag);
-    if (ok) {
-      tc_fence_after();
-      tmem_ld<kH>(taddr(0, 0), ra);
-      tmem_ld_wait();
-    }
+    bool ok = true;
     for (int b = 0; b < nb && ok; ++b) {
-      const int s = b / kKB, slot = s % kStages, kb = b % kKB;
-      tmem_ld<kH>(taddr(b, 1), rb);  // second half of block b, in flight while the first is rescaled
-      if (kb == 0 && !wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag)) {
-        tmem_ld_wait();  // no load may be outstanding when the CTA gives up
-        ok = false;
-        break;
-      }
+      const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc;
+      if (kb == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
+      if (ok) ok = wait_or_abort(smem_u32(&tfull[j]), (b / kAcc) & 1, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
       const uint8_t *st = smem + slot * G::kStageBytes;
       const float dx = reinterpret_cast<const float *>(st + kOffSA)[kb * kPrefillTile + t_local];
       const float4 *dw4 = reinterpret_cast<const float4 *>(st + kOffSB + (kb * BN + c0) * 4);
       const uint64_t dx2 = pk2(dx, dx);
-      if (p.dots) dump(ra, b, 0);
-      rescale_half<kH, 0>(ra, dw4, dx2, acc);
-      tmem_ld_wait();  // block b is in registers: its accumulator goes back to the MMA warp
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&tempty[b % kAcc]));
-      const bool more = b + 1 < nb;
-      if (more) {
-        ok = wait_or_abort(smem_u32(&tfull[(b + 1) % kAcc]), ((b + 1) / kAcc) & 1, abort_flag);
-        if (ok) {
-          tc_fence_after();
-          tmem_ld<kH>(taddr(b + 1, 0), ra);  // first half of the next block, in flight meanwhile
+      uint32_t r[kC];
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * BN + c0);
+      if constexpr (kC == 32) {
+        tmem_ld32(taddr, r);
+      } else {
+        tmem_ld16(taddr, r);
+      }
+      tmem_ld_wait();
+      if (p.dots) {
+        for (int i = 0; i < kC; ++i) {
+          const int64_t nn = n_col0 + c0 + i;
+          if (t < p.m && nn < p.n)
+            p.dots[(static_cast<int64_t>(kb0 + b) * p.m + t) * p.n + nn] = static_cast<int32_t>(r[i]);
         }
       }
-      if (p.dots) dump(rb, b, 1);
-      rescale_half<kH, kH>(rb, dw4, dx2, acc);
-      if (kb == kKB - 1 || b == nb - 1) {  // the stage's scales are read
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&empty[slot]));
+#pragma unroll
+      for (int i = 0; i < kC; i += 4) {
+        const float4 w = dw4[i / 4];  // same address across the warp: broadcast
+        // fmaf((float)I, dw * dx, acc) per lane, two columns per instruction
+        const uint64_t s01 = mul2(pk2(w.x, w.y), dx2), s23 = mul2(pk2(w.z, w.w), dx2);
+        const uint64_t f01 = cvt2_i2f(r[i], r[i + 1]);
+        const uint64_t f23 = cvt2_bias(r[i + 2], r[i + 3]);
+        acc[i / 2] = fma2(f01, s01, acc[i / 2]);
+        acc[i / 2 + 1] = fma2(f23, s23, acc[i / 2 + 1]);
       }
-      if (more && ok) tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(smem_u32(&tempty[j]));
+        if (kb == kKB - 1 || b == nb - 1) mbar_arrive(smem_u32(&empty[slot]));
+      }
     }
     if (ok && t < p.m) {
       float *yrow = y_out + t * p.ldy + n_col0 + c0;
