@@ -16,7 +16,7 @@
 //     canonical K-major layout, so no tensor map is needed;
 //   * warp 1 issues one tcgen05.mma.kind::i8 (M=128, N=128, K=32) per K-block into one of four
 //     TMEM accumulators (128 columns each, overwrite mode): every block's int32 dot lands alone;
-//   * warps 2..9 (two per TMEM lane quarter, 64 columns each) read each block's int32 tile with
+//   * warps 2..17 (four per TMEM lane quarter, 32 columns each) read each block's int32 tile with
 //     tcgen05.ld, scale it by dw*dx and accumulate in fp32 registers, then store the tile.
 // Per-block scales are why the accumulator cannot stay in TMEM across K: the fp32 rescale of
 // every 32-deep block is the bound of this kernel, not the tensor pipe.
@@ -144,25 +144,15 @@ __device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
-__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
-  uint64_t d;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
-  return d;
-}
 
-// int32 -> fp32 of a block dot, two ways that give the same (exact) value: the conversion
-// instruction (a quarter-rate pipe on sm_100), and the bias trick on the integer and fp32 pipes
-// -- the bits of i + 0x4B400000 read as a float equal 2^23 + 2^22 + i exactly for
-// |i| < 2^22, so subtracting 12582912 leaves i.  A block dot is at most 32 * 127 * 127 in
-// magnitude.  The epilogue converts half of its values each way, so neither pipe alone bounds it.
-constexpr uint32_t kBiasBits = 0x4B400000u;
-constexpr float kBiasValue = 12582912.0f;
-static_assert(32 * 127 * 127 < (1 << 22), "block dots fit the bias trick");
+// int32 -> fp32 of a block dot with the conversion instruction.  Measured on the 512 x 17920 x
+// 1536 GEMM: converting every value this way (108.8 us) beats converting half of them through the
+// bias trick on the integer and fp32 pipes (110.8 us), all of them that way (129.5 us), and
+// seeding the accumulators with the bias so no conversion is needed (133 us: the fp32 pipe then
+// carries three operations per value).  The epilogue's bound is its per-block chain (waits,
+// tensor-memory load, rescale, arrive), not the conversion pipe.
 __device__ __forceinline__ uint64_t cvt2_i2f(uint32_t a, uint32_t b) {
   return pk2(static_cast<float>(static_cast<int32_t>(a)), static_cast<float>(static_cast<int32_t>(b)));
-}
-__device__ __forceinline__ uint64_t cvt2_bias(uint32_t a, uint32_t b) {
-  return sub2(pk2(__uint_as_float(a + kBiasBits), __uint_as_float(b + kBiasBits)), pk2(kBiasValue, kBiasValue));
 }
 
 // ---- repack: GGUF Q8_0 rows -> canonical K-major tiles -------------------------------------
@@ -402,7 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
         // fmaf((float)I, dw * dx, acc) per lane, two columns per instruction
         const uint64_t s01 = mul2(pk2(w.x, w.y), dx2), s23 = mul2(pk2(w.z, w.w), dx2);
         const uint64_t f01 = cvt2_i2f(r[i], r[i + 1]);
-        const uint64_t f23 = cvt2_bias(r[i + 2], r[i + 3]);
+        const uint64_t f23 = cvt2_i2f(r[i + 2], r[i + 3]);
         acc[i / 2] = fma2(f01, s01, acc[i / 2]);
         acc[i / 2 + 1] = fma2(f23, s23, acc[i / 2 + 1]);
       }
