@@ -50,13 +50,21 @@ typedef enum ugb_status {
   UGB_ECONTEXT = 7    /* bad or missing context / not initialised (Error::Context) */
 } ugb_status;
 
-/* GGML type ids, the same numbers the reference uses for `kind` (frontier_core.rs:146-151). */
+/* GGML type ids, the same numbers the reference uses for `kind` (frontier_core.rs:54-57).
+ * Q8_0, Q4_K and Q3_K are the configurations' formats; Q6_K, IQ3_XXS, IQ4_NL and IQ4_XS are the
+ * reference's other block formats (frontier_core.rs:85-103), accepted by the matvec entry points
+ * (ugb_matvec, ugb_matvec_f32, ugb_matvec_jobs, ugb_linear, ugb_block_dots) and as the MoE expert
+ * kind. */
 enum {
   UGB_F32 = 0,
   UGB_F16 = 1,
   UGB_Q8_0 = 8,
   UGB_Q3_K = 11,
-  UGB_Q4_K = 12
+  UGB_Q4_K = 12,
+  UGB_Q6_K = 14,
+  UGB_IQ3_XXS = 18,
+  UGB_IQ4_NL = 20,
+  UGB_IQ4_XS = 23
 };
 
 /* Device status-word bits reported by ugb_status_read(). */
@@ -90,7 +98,7 @@ ugb_status ugb_status_read(ugb_ctx *ctx, ugb_stream stream, uint32_t *bits);
 /* ---- formats ----------------------------------------------------------------------------- */
 
 /* Bytes of one row of n elements of GGML type `kind`, or a negative value: -1 unknown kind,
- * -2 n not a positive multiple of the block.  frontier_core.rs:146-151 row_bytes(), with
+ * -2 n not a positive multiple of the block.  frontier_core.rs:54-57 row_bytes(), with
  * the same table (F32, BF16, Q8_0, Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS) plus Q4_K and Q3_K. */
 int64_t ugb_row_bytes(uint32_t kind, int64_t n);
 

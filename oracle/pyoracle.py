@@ -15,6 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 BUILD = os.path.join(HERE, "_build")
 
 Q8_0, Q3_K, Q4_K = 8, 11, 12
+Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS = 14, 18, 20, 23  # the reference's other formats (frontier_core.rs:54-55)
 
 _c_u8p = ctypes.POINTER(ctypes.c_uint8)
 _c_i8p = ctypes.POINTER(ctypes.c_int8)
@@ -62,7 +63,22 @@ def _load(name: str) -> ctypes.CDLL:
                                           _c_f32p, ctypes.c_int]
     lib.orc_silu_mul.restype = ctypes.c_float
     lib.orc_silu_mul.argtypes = [ctypes.c_float, ctypes.c_float]
+    lib.orc_set_iq3_grid.restype = None
+    lib.orc_set_iq3_grid.argtypes = [ctypes.POINTER(ctypes.c_uint32)]
+    grid = iq3_grid()
+    lib.orc_set_iq3_grid(grid.ctypes.data_as(ctypes.POINTER(ctypes.c_uint32)))
     return lib
+
+
+def iq3_grid() -> np.ndarray:
+    """The IQ3_XXS grid as 256 little-endian words of four magnitudes, decoded from the compact
+    form the third-party gguf package (0.19.0) ships (IQ3_XXS.grid_map / grid_hex) -- an
+    independent source from the table compiled into libugb."""
+    from gguf import quants
+
+    quants.IQ3_XXS.init_grid()
+    g = np.asarray(quants.IQ3_XXS.grid, dtype=np.float32).reshape(256, 4).astype(np.uint32)
+    return np.ascontiguousarray(g[:, 0] | (g[:, 1] << 8) | (g[:, 2] << 16) | (g[:, 3] << 24))
 
 
 _LIBS: dict[str, ctypes.CDLL] = {}

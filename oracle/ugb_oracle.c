@@ -14,7 +14,7 @@
 /* ---- fp16 ------------------------------------------------------------------------------ */
 
 float orc_half(uint16_t h) {
-  /* frontier_core.rs:153-158 */
+  /* frontier_core.rs:60-65 */
   uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
   uint32_t exp = (h >> 10) & 31u;
   uint32_t frac = h & 1023u;
@@ -30,16 +30,73 @@ float orc_half(uint16_t h) {
 }
 
 static uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+static uint32_t rd32(const uint8_t *p) { return (uint32_t)rd16(p) | ((uint32_t)rd16(p + 2) << 16); }
+
+/* ---- the reference's other formats (frontier_core.rs:68-101) ------------------------------ */
+
+/* frontier_core.rs:68 IQ4 code book. */
+static const int8_t kIq4[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+static uint32_t g_iq3_grid[256];
+static int g_iq3_set = 0;
+
+void orc_set_iq3_grid(const uint32_t *grid) {
+  memcpy(g_iq3_grid, grid, sizeof g_iq3_grid);
+  g_iq3_set = 1;
+}
+
+/* IQ4_NL element j (0..31) of an 18-byte block: code-book index = nibble j/16 of byte 2 + j%16
+ * (frontier_core.rs:80-82). */
+static int iq4nl_value(const uint8_t *blk, int j) {
+  return kIq4[(blk[2 + j % 16] >> (4 * (j / 16))) & 15];
+}
+
+/* IQ4_XS sub-block scale (sc, 0..63) of sub-block sb and element j (0..255) value index
+ * (frontier_core.rs:83-87). */
+static int iq4xs_scale(const uint8_t *sb, int s) {
+  return ((sb[4 + s / 2] >> (4 * (s % 2))) & 15) | (((rd16(sb + 2) >> (2 * s)) & 3) << 4);
+}
+static int iq4xs_value(const uint8_t *sb, int j) {
+  return kIq4[(sb[8 + (j / 32) * 16 + j % 16] >> (4 * ((j % 32) / 16))) & 15];
+}
+
+/* Q6_K element j (0..255): signed 6-bit quant and its int8 scale (frontier_core.rs:88-93). */
+static int q6k_quant(const uint8_t *sb, int j) {
+  int sub = j / 128, l = j % 32, group = (j % 128) / 32;
+  int low = sb[sub * 64 + l + (group % 2) * 32];
+  int high = sb[128 + sub * 32 + l];
+  return (((low >> (4 * (group / 2))) & 15) | (((high >> (2 * group)) & 3) << 4)) - 32;
+}
+static int q6k_scale(const uint8_t *sb, int j) {
+  int sub = j / 128, l = j % 32, group = (j % 128) / 32;
+  return (int8_t)sb[192 + sub * 8 + l / 16 + group * 2];
+}
+
+/* IQ3_XXS element j (0..255): signed grid magnitude; the sub-block scale d*(0.5+s)*0.5
+ * (frontier_core.rs:94-101). */
+static int iq3xxs_value(const uint8_t *sb, int j) {
+  int s = j / 32, group = (j % 32) / 8;
+  uint32_t aux = rd32(sb + 66 + s * 4);
+  uint32_t signs7 = (aux >> (7 * group)) & 127u;
+  uint32_t par = (uint32_t)__builtin_popcount(signs7) & 1u;
+  uint32_t signs = signs7 | (par << 7);
+  int index = sb[2 + s * 8 + group * 2 + (j % 8) / 4];
+  int q = (int)((g_iq3_grid[index] >> (8 * (j % 4))) & 255u);
+  return (signs & (1u << (j % 8))) ? -q : q;
+}
+static float iq3xxs_scale(const uint8_t *sb, int s) {
+  uint32_t aux = rd32(sb + 66 + s * 4);
+  return orc_half(rd16(sb)) * (0.5f + (float)(aux >> 28)) * 0.5f;
+}
 
 /* ---- sizes ----------------------------------------------------------------------------- */
 
-/* Block geometry.  Kinds 14/18/20/23/30 are the reference's other formats
- * (frontier_core.rs:147-148); only their sizes are restated, so row_bytes() answers the
- * reference's known-answer cases, but they have no decoder here. */
+/* Block geometry (frontier_core.rs:54-55).  BF16 (30) has no decoder here: only its size is
+ * restated, so row_bytes() answers every known-answer case of the reference. */
 static int block_of(uint32_t kind, long *elems, long *bytes) {
   switch (kind) {
     case ORC_F32: *elems = 1; *bytes = 4; return 0;
-    case ORC_Q8_0: *elems = 32; *bytes = 34; return 0;   /* frontier_core.rs:147 */
+    case ORC_Q8_0: *elems = 32; *bytes = 34; return 0;   /* frontier_core.rs:54 */
     case ORC_Q4_K: *elems = 256; *bytes = 144; return 0; /* ggml block_q4_K */
     case ORC_Q3_K: *elems = 256; *bytes = 110; return 0; /* ggml block_q3_K */
     case 14: *elems = 256; *bytes = 210; return 0;       /* Q6_K */
@@ -52,11 +109,13 @@ static int block_of(uint32_t kind, long *elems, long *bytes) {
 }
 
 static int has_decoder(uint32_t kind) {
-  return kind == ORC_F32 || kind == ORC_Q8_0 || kind == ORC_Q4_K || kind == ORC_Q3_K;
+  if (kind == ORC_IQ3_XXS) return g_iq3_set;
+  return kind == ORC_F32 || kind == ORC_Q8_0 || kind == ORC_Q4_K || kind == ORC_Q3_K || kind == ORC_Q6_K ||
+         kind == ORC_IQ4_NL || kind == ORC_IQ4_XS;
 }
 
 long orc_row_bytes(uint32_t kind, long n) {
-  /* frontier_core.rs:146-151 */
+  /* frontier_core.rs:53-58 */
   long e, b;
   if (block_of(kind, &e, &b)) return -1;
   if (n <= 0 || n % e != 0) return -2;
@@ -113,7 +172,7 @@ int orc_dequantize(uint32_t kind, const uint8_t *in, long nbytes, float *out, lo
         out[i] = v;
         break;
       }
-      case ORC_Q8_0: { /* frontier_core.rs:172 */
+      case ORC_Q8_0: { /* frontier_core.rs:79 */
         const uint8_t *p = in + (i / 32) * 34;
         out[i] = orc_half(rd16(p)) * (float)(int8_t)p[2 + i % 32];
         break;
@@ -132,6 +191,31 @@ int orc_dequantize(uint32_t kind, const uint8_t *in, long nbytes, float *out, lo
         int j = (int)(i % 256);
         float dl = orc_half(rd16(sb + 108)) * (float)q3k_scale(sb, j / 16);
         out[i] = dl * (float)q3k_quant(sb, j);
+        break;
+      }
+      case ORC_IQ4_NL: { /* frontier_core.rs:80-82: half(d) * IQ4[q] */
+        const uint8_t *p = in + (i / 32) * 18;
+        out[i] = orc_half(rd16(p)) * (float)iq4nl_value(p, (int)(i % 32));
+        break;
+      }
+      case ORC_IQ4_XS: { /* frontier_core.rs:83-87: (half(d) * (sc-32)) * IQ4[q] */
+        const uint8_t *sb = in + (i / 256) * 136;
+        int j = (int)(i % 256);
+        out[i] = (orc_half(rd16(sb)) * (float)(iq4xs_scale(sb, j / 32) - 32)) * (float)iq4xs_value(sb, j);
+        break;
+      }
+      case ORC_Q6_K: { /* frontier_core.rs:88-93: (half(d) * sc) * q */
+        const uint8_t *sb = in + (i / 256) * 210;
+        int j = (int)(i % 256);
+        out[i] = (orc_half(rd16(sb + 208)) * (float)q6k_scale(sb, j)) * (float)q6k_quant(sb, j);
+        break;
+      }
+      case ORC_IQ3_XXS: { /* frontier_core.rs:94-101: (scale * q) * sign */
+        const uint8_t *sb = in + (i / 256) * 98;
+        int j = (int)(i % 256);
+        int v = iq3xxs_value(sb, j);
+        float mag = iq3xxs_scale(sb, j / 32) * (float)(v < 0 ? -v : v);
+        out[i] = v < 0 ? -mag : mag;
         break;
       }
     }
@@ -197,6 +281,31 @@ static int32_t block_dot(uint32_t kind, const uint8_t *row, const int8_t *q, lon
       acc = q3k_scale(sb, sub) * lo + q3k_scale(sb, sub + 1) * hi;
       return acc;
     }
+    case ORC_Q6_K: {
+      const uint8_t *sb = row + (b / 8) * 210;
+      int base = (int)(b % 8) * 32;
+      int32_t lo = 0, hi = 0;
+      for (int j = 0; j < 16; j++) lo += q6k_quant(sb, base + j) * (int32_t)q[b * 32 + j];
+      for (int j = 16; j < 32; j++) hi += q6k_quant(sb, base + j) * (int32_t)q[b * 32 + j];
+      return q6k_scale(sb, base) * lo + q6k_scale(sb, base + 16) * hi;
+    }
+    case ORC_IQ4_NL: {
+      const uint8_t *p = row + b * 18;
+      for (int j = 0; j < 32; j++) acc += iq4nl_value(p, j) * (int32_t)q[b * 32 + j];
+      return acc;
+    }
+    case ORC_IQ4_XS: {
+      const uint8_t *sb = row + (b / 8) * 136;
+      int base = (int)(b % 8) * 32;
+      for (int j = 0; j < 32; j++) acc += iq4xs_value(sb, base + j) * (int32_t)q[b * 32 + j];
+      return acc;
+    }
+    case ORC_IQ3_XXS: {
+      const uint8_t *sb = row + (b / 8) * 98;
+      int base = (int)(b % 8) * 32;
+      for (int j = 0; j < 32; j++) acc += iq3xxs_value(sb, base + j) * (int32_t)q[b * 32 + j];
+      return acc;
+    }
   }
   return 0;
 }
@@ -236,6 +345,26 @@ static float row_dot(uint32_t kind, const uint8_t *row, const int8_t *q, const f
         const uint8_t *sb = row + (b / 8) * 110;
         float dsb = orc_half(rd16(sb + 108));
         term = (float)isum * (dsb * d[b]);
+        break;
+      }
+      case ORC_Q6_K: {
+        const uint8_t *sb = row + (b / 8) * 210;
+        term = (float)isum * (orc_half(rd16(sb + 208)) * d[b]);
+        break;
+      }
+      case ORC_IQ4_NL: {
+        term = (float)isum * (orc_half(rd16(row + b * 18)) * d[b]);
+        break;
+      }
+      case ORC_IQ4_XS: {
+        const uint8_t *sb = row + (b / 8) * 136;
+        float dl = orc_half(rd16(sb)) * (float)(iq4xs_scale(sb, (int)(b % 8)) - 32);
+        term = (float)isum * (dl * d[b]);
+        break;
+      }
+      case ORC_IQ3_XXS: {
+        const uint8_t *sb = row + (b / 8) * 98;
+        term = (float)isum * (iq3xxs_scale(sb, (int)(b % 8)) * d[b]);
         break;
       }
     }

@@ -7,8 +7,9 @@ Python port of ggml's block formats, which is not available on the GPU box):
 
 Outputs (all small .npz files):
 
-* ``dequant_<kind>.npz``: seeded random raw blocks of Q8_0 / Q4_K / Q3_K and the values
-  ``gguf.quants.dequantize`` decodes them to.  The oracle's decoders (oracle/ugb_oracle.c)
+* ``dequant_<kind>.npz``: seeded random raw blocks of Q8_0 / Q4_K / Q3_K, and of the reference's
+  other formats Q6_K / IQ3_XXS / IQ4_NL / IQ4_XS, and the values ``gguf.quants.dequantize``
+  decodes them to.  The oracle's decoders (oracle/ugb_oracle.c)
   and the CUDA block decoders are checked against these.  fp16 scales are drawn from a set
   that includes zero, subnormal, negative and large values.
 * ``fixture_q8_0.npz``: the reference's own xorshift operator fixture
@@ -62,9 +63,10 @@ def reference_fixture_q8_0(n: int, m: int) -> np.ndarray:
 
 
 def random_blocks(kind: T, nblocks: int, rng: np.random.Generator) -> np.ndarray:
-    bsize = {T.Q8_0: 34, T.Q4_K: 144, T.Q3_K: 110}[kind]
+    bsize = {T.Q8_0: 34, T.Q4_K: 144, T.Q3_K: 110, T.Q6_K: 210, T.IQ3_XXS: 98, T.IQ4_NL: 18, T.IQ4_XS: 136}[kind]
     raw = rng.integers(0, 256, size=(nblocks, bsize), dtype=np.uint8)
-    scale_offsets = {T.Q8_0: [0], T.Q4_K: [0, 2], T.Q3_K: [108]}[kind]
+    scale_offsets = {T.Q8_0: [0], T.Q4_K: [0, 2], T.Q3_K: [108], T.Q6_K: [208], T.IQ3_XXS: [0],
+                     T.IQ4_NL: [0], T.IQ4_XS: [0]}[kind]
     for b in range(nblocks):
         for off in scale_offsets:
             h = int(SCALE_BITS[rng.integers(0, len(SCALE_BITS))])
@@ -122,6 +124,16 @@ def main() -> None:
     x = activation_cases(rng)
     q, d, s = quant_act_numpy(x)
     np.savez_compressed(os.path.join(HERE, "quant_act.npz"), x=x, q=q, d=d, s=s)
+
+    # the reference's other formats, from a generator of their own so the files above keep
+    # their bytes
+    rng2 = np.random.default_rng(20261202)
+    for kind, name, nblocks in [(T.Q6_K, "q6_k", 12), (T.IQ3_XXS, "iq3_xxs", 12), (T.IQ4_NL, "iq4_nl", 96),
+                                (T.IQ4_XS, "iq4_xs", 12)]:
+        raw = random_blocks(kind, nblocks, rng2)
+        values = gguf.quants.dequantize(raw.reshape(-1), kind).astype(np.float32).reshape(-1)
+        np.savez_compressed(os.path.join(HERE, f"dequant_{name}.npz"), raw=raw.reshape(-1),
+                            values=values, kind=np.int32(int(kind)))
     print("golden vectors written to", HERE, "gguf", gguf.__file__)
 
 

@@ -42,7 +42,7 @@ def test_python_binding_covers_header(ugb):
 
 
 def test_row_bytes_abi(ugb):
-    # frontier_core.rs:222-227 plus the configs' shapes
+    # frontier_core.rs:129-134 plus the configs' shapes and the other formats' block sizes
     assert ugb.row_bytes(23, 640) == -2
     assert ugb.row_bytes(20, 160) == 90
     assert ugb.row_bytes(18, 2560) == 980
@@ -51,6 +51,10 @@ def test_row_bytes_abi(ugb):
     assert ugb.row_bytes(ugb.Q8_0, 8960) == 9520
     assert ugb.row_bytes(ugb.Q4_K, 18944) == 74 * 144
     assert ugb.row_bytes(ugb.Q3_K, 1536) == 660
+    assert ugb.row_bytes(ugb.Q6_K, 4096) == 16 * 210
+    assert ugb.row_bytes(ugb.IQ3_XXS, 1536) == 6 * 98
+    assert ugb.row_bytes(ugb.IQ4_NL, 96) == 3 * 18
+    assert ugb.row_bytes(ugb.IQ4_XS, 4096) == 16 * 136
 
 
 def test_q8act_layout(ugb):

@@ -4,7 +4,8 @@ Integer block dots must be bit-exact; fp32 rows within 1e-3 relative (assert_row
 activation quants and scales bit-exact.  Shapes cover the configs (C1 8960x1536 Q8_0, the
 1.5B / 7B / MoE matrices) and ragged edges: row counts that are not a multiple of the row
 group, rows whose byte length is not a multiple of 16 (tail bytes past the last 16-byte
-boundary), single-block rows, and batches 1..8 including non-powers of two.
+boundary), single-block rows, and batches 1..8 including non-powers of two.  The reference's
+other formats (Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS; frontier_core.rs:80-101) take the same checks.
 """
 from __future__ import annotations
 
@@ -16,7 +17,8 @@ from conftest import assert_rows_close, golden
 pytestmark = pytest.mark.gpu
 
 Q8_0, Q3_K, Q4_K = 8, 11, 12
-ELEMS = {Q8_0: 32, Q4_K: 256, Q3_K: 256}
+Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS = 14, 18, 20, 23
+ELEMS = {Q8_0: 32, Q4_K: 256, Q3_K: 256, Q6_K: 256, IQ3_XXS: 256, IQ4_NL: 32, IQ4_XS: 256}
 
 
 def _torch():
@@ -99,6 +101,14 @@ SHAPES = [
     (Q3_K, 65536, 5),      # K-chunked Q3_K at UGB_MAX_K
     (Q8_0, 3584, 100),     # 7B output-head row length
     (Q8_0, 8960, 37),      # rows spread over all lanes, two per item, ragged last item
+    (Q6_K, 4096, 200),     # the reference's other formats: Q6_K
+    (Q6_K, 1536, 37),      # 1260-byte rows (not 16-byte multiples), ragged row group
+    (IQ4_NL, 1536, 300),   # IQ4_NL: 18-byte blocks
+    (IQ4_NL, 96, 13),      # 54-byte rows, tail bytes
+    (IQ4_NL, 32768, 9),    # K-chunked IQ4_NL
+    (IQ4_XS, 4096, 129),   # IQ4_XS: 136-byte super-blocks
+    (IQ3_XXS, 1536, 129),  # IQ3_XXS: 588-byte rows
+    (IQ3_XXS, 65536, 5),   # K-chunked IQ3_XXS at UGB_MAX_K
 ]
 
 

@@ -21,6 +21,7 @@ from conftest import assert_rows_close
 pytestmark = pytest.mark.gpu
 
 Q8_0, Q3_K, Q4_K = 8, 11, 12
+Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS = 14, 18, 20, 23
 
 
 def _torch():
@@ -60,7 +61,8 @@ def oracle_mv(orc, ugb, kind, w_np, k, m, q, d, s, batch=1):
 def test_jobs_equal_single_launches(ctx, ugb, orc, batch):
     torch = _torch()
     shapes = [(Q8_0, 1536, 300), (Q3_K, 4096, 1536), (Q4_K, 1536, 700), (Q8_0, 1536, 8), (Q3_K, 4096, 96),
-              (Q3_K, 1536, 4096)]
+              (Q3_K, 1536, 4096), (Q6_K, 4096, 200), (IQ3_XXS, 1536, 300), (IQ4_NL, 1536, 64),
+              (IQ4_XS, 4096, 96)]
     rng = np.random.default_rng(batch)
     jobs, outs, singles, xs = [], [], [], {}
     for i, (kind, k, m) in enumerate(shapes):
@@ -172,7 +174,8 @@ def run_experts(ctx, ugb, kind, hidden, ffn, n_total, top_k, batch, shards, seed
 
 @pytest.mark.parametrize("kind,hidden,ffn,n_total,top_k,batch", [
     (Q3_K, 1024, 512, 16, 4, 1), (Q3_K, 1024, 512, 16, 4, 3), (Q8_0, 512, 256, 8, 2, 8),
-    (Q4_K, 512, 256, 12, 3, 2)])
+    (Q4_K, 512, 256, 12, 3, 2), (IQ3_XXS, 1024, 512, 16, 4, 1), (Q6_K, 512, 256, 8, 2, 3),
+    (IQ4_XS, 512, 256, 8, 2, 2), (IQ4_NL, 512, 256, 8, 2, 1)])
 def test_moe_experts_stagewise(ctx, ugb, orc, kind, hidden, ffn, n_total, top_k, batch):
     r = run_experts(ctx, ugb, kind, hidden, ffn, n_total, top_k, batch, [(0, n_total)], seed=7)
     lay = ugb.moe_workspace_layout(hidden, ffn, top_k, batch)

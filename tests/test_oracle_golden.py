@@ -2,11 +2,13 @@
 
 * Decoders vs the gguf 0.19.0 golden vectors (llama.cpp's Python port of ggml's formats), and
   vs the reference's own operator fixture (frontier_gpu.rs:37-50).
-* fp16 decode vs IEEE binary16 for all 65536 bit patterns (frontier_core.rs:153-158).
+* fp16 decode vs IEEE binary16 for all 65536 bit patterns (frontier_core.rs:60-65).
 * Activation quantiser vs an independent numpy float32 statement (gpu_dp4a.cu:23-31).
 * Integer block dots vs independent numpy integer decodes of the raw bytes.
 * row_bytes and the descriptor ABI vs the reference's own unit tests
-  (frontier_core.rs:222-227, frontier_dispatch.rs:33-71).
+  (frontier_core.rs:129-134, frontier_dispatch.rs:33-71).
+* The reference's other formats (Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS, frontier_core.rs:80-101): the
+  same three pins, and the IQ3_XXS grid compiled into libugb vs the gguf package's.
 """
 from __future__ import annotations
 
@@ -16,6 +18,8 @@ import pytest
 from conftest import golden
 
 Q8_0, Q3_K, Q4_K = 8, 11, 12
+Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS = 14, 18, 20, 23
+IQ4 = np.array([-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113], dtype=np.int64)
 
 
 # ---- independent numpy integer decoders (restating gguf's reshape-based bit maps) ----------
@@ -59,9 +63,71 @@ def q3_k_ints(raw: np.ndarray):
     return d, sc, q  # q [n, 256], sc [n, 16]
 
 
+def _f16(b: np.ndarray) -> np.ndarray:
+    return b.copy().view(np.float16).astype(np.float32).reshape(-1)
+
+
+def q6_k_ints(raw: np.ndarray):
+    """q [n, 256] in [-32, 31] and the int8 scale of each element's 16-group."""
+    b = raw.reshape(-1, 210)
+    n = b.shape[0]
+    ql, qh = b[:, :128].astype(np.int64), b[:, 128:192].astype(np.int64)
+    sc = b[:, 192:208].view(np.int8).astype(np.int64)
+    d = _f16(b[:, 208:210])
+    q = np.empty((n, 256), np.int64)
+    s = np.empty((n, 256), np.int64)
+    for h in range(2):
+        for g in range(4):
+            low = (ql[:, 64 * h + 32 * (g % 2): 64 * h + 32 * (g % 2) + 32] >> (4 * (g // 2))) & 15
+            high = (qh[:, 32 * h: 32 * h + 32] >> (2 * g)) & 3
+            q[:, 128 * h + 32 * g: 128 * h + 32 * g + 32] = (low | (high << 4)) - 32
+            s[:, 128 * h + 32 * g: 128 * h + 32 * g + 16] = sc[:, 8 * h + 2 * g, None]
+            s[:, 128 * h + 32 * g + 16: 128 * h + 32 * g + 32] = sc[:, 8 * h + 2 * g + 1, None]
+    return d, s, q
+
+
+def iq4_nl_ints(raw: np.ndarray):
+    b = raw.reshape(-1, 18)
+    qs = b[:, 2:].astype(np.int64)
+    idx = np.concatenate([qs & 15, qs >> 4], axis=1)
+    return _f16(b[:, :2]), IQ4[idx]  # values [n, 32]
+
+
+def iq4_xs_ints(raw: np.ndarray):
+    b = raw.reshape(-1, 136)
+    n = b.shape[0]
+    d = _f16(b[:, :2])
+    sh = (b[:, 2].astype(np.int64) | (b[:, 3].astype(np.int64) << 8))
+    sl = b[:, 4:8].astype(np.int64)
+    sc = np.stack([((sl[:, j // 2] >> (4 * (j % 2))) & 15) | (((sh >> (2 * j)) & 3) << 4) for j in range(8)], axis=1)
+    qs = b[:, 8:].reshape(n, 8, 16).astype(np.int64)
+    idx = np.concatenate([qs & 15, qs >> 4], axis=2)  # [n, 8, 32]
+    return d, sc - 32, IQ4[idx]
+
+
+def iq3_xxs_ints(raw: np.ndarray, grid_words: np.ndarray):
+    b = raw.reshape(-1, 98)
+    n = b.shape[0]
+    d = _f16(b[:, :2])
+    idx = b[:, 2:66].astype(np.int64).reshape(n, 8, 8)
+    aux = b[:, 66:98].copy().view(np.uint32).astype(np.int64).reshape(n, 8)
+    mag = (grid_words[idx][..., None] >> (8 * np.arange(4))) & 255  # [n, 8, 8, 4]
+    mag = mag.reshape(n, 8, 32)
+    signs = np.empty((n, 8, 32), np.int64)
+    for g in range(4):
+        s7 = (aux >> (7 * g)) & 127
+        par = np.array([bin(int(v)).count("1") & 1 for v in s7.reshape(-1)], np.int64).reshape(n, 8)
+        s8 = s7 | (par << 7)
+        for e in range(8):
+            signs[:, :, 8 * g + e] = np.where((s8 >> e) & 1, -1, 1)
+    scale = d[:, None] * (np.float32(0.5) + (aux >> 28).astype(np.float32)) * np.float32(0.5)
+    return scale.astype(np.float32), mag * signs  # values [n, 8, 32]
+
+
 # ---- decoders vs gguf --------------------------------------------------------------------
 
-@pytest.mark.parametrize("name,kind", [("q8_0", Q8_0), ("q4_k", Q4_K), ("q3_k", Q3_K)])
+@pytest.mark.parametrize("name,kind", [("q8_0", Q8_0), ("q4_k", Q4_K), ("q3_k", Q3_K), ("q6_k", Q6_K),
+                                       ("iq3_xxs", IQ3_XXS), ("iq4_nl", IQ4_NL), ("iq4_xs", IQ4_XS)])
 def test_dequant_matches_gguf_bit_exact(orc, name, kind):
     g = golden(f"dequant_{name}.npz")
     raw, values = g["raw"], g["values"]
@@ -160,17 +226,73 @@ def test_block_dots_q3_k(orc):
                                   g["values"].view(np.uint32))
 
 
+def test_block_dots_q6_k(orc):
+    g = golden("dequant_q6_k.npz")
+    raw = g["raw"]
+    x = _rand_act(np.random.default_rng(6), raw.size // 210 * 256)
+    d, s, q = q6_k_ints(raw)
+    halves = (q.reshape(-1, 16) * x.astype(np.int64).reshape(-1, 16)).sum(axis=1) * s.reshape(-1, 16)[:, 0]
+    np.testing.assert_array_equal(orc.block_dots(Q6_K, raw, x), halves.reshape(-1, 2).sum(axis=1))
+    vals = ((d[:, None] * s.astype(np.float32)) * q.astype(np.float32)).reshape(-1)
+    np.testing.assert_array_equal(vals.view(np.uint32), g["values"].view(np.uint32))
+
+
+def test_block_dots_iq4_nl(orc):
+    g = golden("dequant_iq4_nl.npz")
+    raw = g["raw"]
+    x = _rand_act(np.random.default_rng(7), raw.size // 18 * 32)
+    d, v = iq4_nl_ints(raw)
+    np.testing.assert_array_equal(orc.block_dots(IQ4_NL, raw, x), (v * x.astype(np.int64).reshape(-1, 32)).sum(axis=1))
+    vals = (d[:, None] * v.astype(np.float32)).reshape(-1)
+    np.testing.assert_array_equal(vals.view(np.uint32), g["values"].view(np.uint32))
+
+
+def test_block_dots_iq4_xs(orc):
+    g = golden("dequant_iq4_xs.npz")
+    raw = g["raw"]
+    x = _rand_act(np.random.default_rng(8), raw.size // 136 * 256)
+    d, sc, v = iq4_xs_ints(raw)
+    np.testing.assert_array_equal(orc.block_dots(IQ4_XS, raw, x),
+                                  (v.reshape(-1, 32) * x.astype(np.int64).reshape(-1, 32)).sum(axis=1))
+    vals = ((d[:, None] * sc.astype(np.float32))[:, :, None] * v.astype(np.float32)).reshape(-1)
+    np.testing.assert_array_equal(vals.view(np.uint32), g["values"].view(np.uint32))
+
+
+def test_block_dots_iq3_xxs(orc):
+    g = golden("dequant_iq3_xxs.npz")
+    raw = g["raw"]
+    x = _rand_act(np.random.default_rng(9), raw.size // 98 * 256)
+    scale, v = iq3_xxs_ints(raw, orc.iq3_grid().astype(np.int64))
+    np.testing.assert_array_equal(orc.block_dots(IQ3_XXS, raw, x),
+                                  (v.reshape(-1, 32) * x.astype(np.int64).reshape(-1, 32)).sum(axis=1))
+    vals = (scale[:, :, None] * np.abs(v).astype(np.float32)) * np.where(v < 0, -1, 1).astype(np.float32)
+    np.testing.assert_array_equal(vals.reshape(-1).view(np.uint32), g["values"].view(np.uint32))
+
+
+def test_iq3_grid_compiled_equals_gguf(orc):
+    """The grid compiled into libugb (csrc/iq3_grid.inc, generated by csrc/gen_iq3_grid.py) is the
+    one the gguf package decodes; its first entries are the reference's IQ3_GRID values."""
+    import os
+    import re
+    inc = os.path.join(os.path.dirname(__file__), "..", "uefi-gpu_b200", "csrc", "iq3_grid.inc")
+    words = np.array([int(w, 16) for w in re.findall(r"0x([0-9a-f]{8})u", open(inc).read())], np.uint32)
+    np.testing.assert_array_equal(words, orc.iq3_grid())
+    assert list(words[:4]) == [0x04040404, 0x04040414, 0x04040424, 0x04040C0C]
+
+
 # ---- scaled matvec ---------------------------------------------------------------------------
 
 @pytest.mark.parametrize("name,kind,elems,bsz", [("q8_0", Q8_0, 32, 34), ("q4_k", Q4_K, 256, 144),
-                                                 ("q3_k", Q3_K, 256, 110)])
+                                                 ("q3_k", Q3_K, 256, 110), ("q6_k", Q6_K, 256, 210),
+                                                 ("iq3_xxs", IQ3_XXS, 256, 98), ("iq4_nl", IQ4_NL, 32, 18),
+                                                 ("iq4_xs", IQ4_XS, 256, 136)])
 def test_matvec_vs_float64(orc, name, kind, elems, bsz):
     """The oracle's fp32 block-order sum vs an fp64 sum of dequantised weight x dequantised
     activation: the only difference is fp32 rounding."""
     g = golden(f"dequant_{name}.npz")
     raw = g["raw"]
     nblk = raw.size // bsz
-    m = 4 if kind == Q8_0 else 3
+    m = 4 if elems == 32 else 3
     k = nblk * elems // m
     k -= k % elems
     rb = k // elems * bsz
@@ -200,7 +322,7 @@ def test_matvec_mt_identical(orc):
 # ---- reference unit-test known answers -------------------------------------------------------
 
 def test_row_bytes_reference_cases(orc):
-    # frontier_core.rs:222-227 rejects_bad_quant
+    # frontier_core.rs:129-134 rejects_bad_quant
     assert orc.row_bytes(23, 640) == -2  # Err(Shape)
     assert orc.row_bytes(20, 160) == 90
     assert orc.row_bytes(18, 2560) == 980

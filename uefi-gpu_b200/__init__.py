@@ -18,6 +18,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libugb.so")
 
 F32, F16, Q8_0, Q3_K, Q4_K = 0, 1, 8, 11, 12
+Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS = 14, 18, 20, 23  # the reference's other block formats
 MAX_BATCH = 8
 LINEAR_STATIC_MAX_K, LINEAR_STATIC_MAX_M = 16384, 524288  # ugb_linear_static's fixed scratch
 

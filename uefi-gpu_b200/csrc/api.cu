@@ -13,7 +13,7 @@
 namespace ugb {
 
 ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_t k, int64_t m) {
-  if (kind != UGB_Q8_0 && kind != UGB_Q4_K && kind != UGB_Q3_K) return UGB_EQUANT;
+  if (!matvec_kind(kind)) return UGB_EQUANT;
   if (k <= 0 || k > UGB_MAX_K || m <= 0 || m > (int64_t{1} << 31) - 64) return UGB_ESHAPE;
   const int64_t rb = ugb_row_bytes(kind, k);
   if (rb < 0 || rb != row_bytes) return UGB_ESHAPE;
@@ -143,7 +143,7 @@ ugb_status ugb_status_read(ugb_ctx *ctx, ugb_stream stream, uint32_t *bits) {
 }
 
 int64_t ugb_row_bytes(uint32_t kind, int64_t n) {
-  // frontier_core.rs:146-151, plus ggml's Q4_K / Q3_K.
+  // frontier_core.rs:54-57, plus ggml's Q4_K / Q3_K.
   int64_t block, bytes;
   switch (kind) {
     case 0: block = 1; bytes = 4; break;      // F32

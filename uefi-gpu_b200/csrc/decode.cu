@@ -38,7 +38,7 @@ __device__ __forceinline__ Q8View q8_vec(uint8_t *buf, int n, size_t d_off, size
 
 // Sequence b = blockIdx.x: its token is the previous step's greedy choice when there is one,
 // else the host-provided token; x[b] = dequantised Q8_0 embedding row (embedding_q8,
-// gpu_embedding.cu:3-9; frontier_core.rs:172).  When the keys are set the shared position
+// gpu_embedding.cu:3-9; frontier_core.rs:79).  When the keys are set the shared position
 // advances (sequence 0's CTA moves it); a position that would run past the KV cache is pinned
 // to its last slot and flagged, so no later kernel of the step indexes outside the cache.
 // The keys are cleared by the next kernel, after every sequence has read its own.

@@ -104,7 +104,7 @@ ugb_status check_config(const ugb_ctx *ctx, const ugb_decoder_config &c) {
   if (c.n_expert == 0) {
     if (c.n_ff < 32 || c.n_ff % 32 || ugb_row_bytes(c.kind, c.n_ff) < 0) return UGB_ESHAPE;
   } else {
-    if (!kind_ok(c.expert_kind)) return UGB_EQUANT;
+    if (!matvec_kind(c.expert_kind)) return UGB_EQUANT;  // any matvec format for the experts
     const int local = c.n_expert_local ? c.n_expert_local : c.n_expert;
     if (c.n_expert < 1 || c.n_expert > 4096 || c.top_k < 1 || c.top_k > 32 || c.top_k > c.n_expert ||
         c.n_ff_expert < 32 || c.n_ff_expert % 32 || ugb_row_bytes(c.expert_kind, c.n_ff_expert) < 0 ||

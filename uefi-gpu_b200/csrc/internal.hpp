@@ -90,6 +90,12 @@ ugb_status check_ctx(ugb_ctx *ctx);
 // code: TIMEOUT, then NONFINITE, then BADARG (as UGB_ESHAPE).
 ugb_status read_status_bits(ugb_ctx *ctx, cudaStream_t stream, uint32_t *bits);
 
+// Kinds the matvec kernels read: Q8_0, Q3_K, Q4_K, Q6_K, IQ3_XXS, IQ4_NL, IQ4_XS.
+inline bool matvec_kind(uint32_t kind) {
+  return kind == UGB_Q8_0 || kind == UGB_Q3_K || kind == UGB_Q4_K || kind == UGB_Q6_K || kind == UGB_IQ3_XXS ||
+         kind == UGB_IQ4_NL || kind == UGB_IQ4_XS;
+}
+
 // Validation shared by entry points: kind supported by the matvec kernels, k a multiple of
 // its block, row_bytes consistent.
 ugb_status check_weights(uint32_t kind, const void *w, int64_t row_bytes, int64_t k, int64_t m);

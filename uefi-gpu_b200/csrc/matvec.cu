@@ -727,9 +727,18 @@ uint64_t elems_to_bytes(uint32_t kind, uint64_t e) {
   switch (kind) {
     case UGB_Q8_0: return bytes_of<UGB_Q8_0>(e);
     case UGB_Q4_K: return bytes_of<UGB_Q4_K>(e);
-    default: return bytes_of<UGB_Q3_K>(e);
+    case UGB_Q3_K: return bytes_of<UGB_Q3_K>(e);
+    case UGB_Q6_K: return bytes_of<UGB_Q6_K>(e);
+    case UGB_IQ3_XXS: return bytes_of<UGB_IQ3_XXS>(e);
+    case UGB_IQ4_NL: return bytes_of<UGB_IQ4_NL>(e);
+    default: return bytes_of<UGB_IQ4_XS>(e);
   }
 }
+
+// The configurations' formats get every kernel form; the reference's other formats (Q6_K,
+// IQ3_XXS, IQ4_NL, IQ4_XS) go through the streaming kernel, which serves every batch, the job
+// table and the routed experts alike.
+bool all_forms(uint32_t kind) { return kind == UGB_Q8_0 || kind == UGB_Q4_K || kind == UGB_Q3_K; }
 
 size_t x_bytes(uint32_t kind, int64_t k, int nb) {
   const size_t nbp = round_up(static_cast<uint64_t>(k / 32), 4);
@@ -754,7 +763,7 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
   const int64_t units = k / 32;
   // Batch 1, whole rows: the rows kernel with the largest rows-per-warp whose item fits a
   // stage and whose slots fit the register budget.
-  if (nb == 1 && !dots) {
+  if (nb == 1 && !dots && all_forms(kind)) {
     for (int rw : {4, 2, 1}) {
       const int64_t slots = (rw * units + 31) / 32;
       if (rb * kWarps * rw <= kItemTarget && slots <= kSlots) {
@@ -791,7 +800,8 @@ Plan make_plan(uint32_t kind, int64_t k, int64_t m, int nb, bool dots, size_t sm
       pl.stage_bytes = static_cast<uint32_t>(round_up(rb * pl.rows + 32, 128));
     } else {
       // K chunks sized so the item's row chunks fill about one stage.
-      const int gran = kind == UGB_Q8_0 ? 128 : 256;  // chunk starts keep x arrays 16B aligned
+      // chunk starts keep x arrays 16B aligned and fall on block boundaries
+      const int gran = (kind == UGB_Q8_0 || kind == UGB_IQ4_NL) ? 128 : 256;
       const int nch = static_cast<int>((rb * pl.rows + target - 1) / target);
       pl.kc = static_cast<int>(round_up((k + nch - 1) / nch, gran));
       pl.nch = static_cast<int>((k + pl.kc - 1) / pl.kc);
@@ -878,6 +888,11 @@ const void *stream_kernel_ptr(int nb, bool dots, int rw) {
 }
 
 template <int KIND, class P>
+const void *select_stream(const Plan &pl, int nb, bool dots) {
+  return pl.rows_kernel || pl.split ? nullptr : stream_kernel_ptr<KIND, P>(nb, dots, pl.rw);
+}
+
+template <int KIND, class P>
 const void *select_for(const Plan &pl, int nb, bool dots) {
   return pl.rows_kernel ? rows_kernel_ptr<KIND, P>(pl.rw, pl.slots, pl.burst)
          : pl.split     ? split_kernel_ptr<KIND, P>(pl.rw, pl.slots)
@@ -891,6 +906,10 @@ const void *select_kernel(uint32_t kind, const Plan &pl, int nb, bool dots, bool
     case UGB_Q8_0: return table ? select_for<UGB_Q8_0, MvParamsT>(pl, nb, dots) : select_for<UGB_Q8_0, MvParams>(pl, nb, dots);
     case UGB_Q4_K: return table ? select_for<UGB_Q4_K, MvParamsT>(pl, nb, dots) : select_for<UGB_Q4_K, MvParams>(pl, nb, dots);
     case UGB_Q3_K: return table ? select_for<UGB_Q3_K, MvParamsT>(pl, nb, dots) : select_for<UGB_Q3_K, MvParams>(pl, nb, dots);
+#define UGB_STREAM_ONLY(K) \
+    case K: return table ? select_stream<K, MvParamsT>(pl, nb, dots) : select_stream<K, MvParams>(pl, nb, dots);
+    UGB_STREAM_ONLY(UGB_Q6_K) UGB_STREAM_ONLY(UGB_IQ3_XXS) UGB_STREAM_ONLY(UGB_IQ4_NL) UGB_STREAM_ONLY(UGB_IQ4_XS)
+#undef UGB_STREAM_ONLY
     default: return nullptr;
   }
 }
@@ -902,6 +921,17 @@ ugb_status allow_smem(const void *f, size_t bytes) {
 }  // namespace
 
 ugb_status init_matvec_kernels(ugb_ctx *ctx) {
+  for (uint32_t kind : {UGB_Q6_K, UGB_IQ3_XXS, UGB_IQ4_NL, UGB_IQ4_XS}) {
+    Plan pl;
+    for (int rw : {1, 2}) {
+      pl.rw = rw;
+      for (int nb : {1, 2, 4, 8})
+        for (bool table : {false, true})
+          if (allow_smem(select_kernel(kind, pl, nb, false, table), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+    }
+    pl.rw = 1;
+    if (allow_smem(select_kernel(kind, pl, 1, true), ctx->smem_optin) != UGB_OK) return UGB_EBACKEND;
+  }
   for (uint32_t kind : {UGB_Q8_0, UGB_Q4_K, UGB_Q3_K}) {
     Plan pl;
     for (int rw : {1, 2, 4})

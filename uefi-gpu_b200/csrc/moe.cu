@@ -363,7 +363,7 @@ ugb_status ugb_moe_experts(ugb_ctx *ctx, ugb_stream stream, const ugb_moe_args *
       m->n_expert_total < m->expert0 + m->n_expert)
     return UGB_ESHAPE;
   const int64_t rb_in = ugb_row_bytes(m->kind, m->hidden), rb_ff = ugb_row_bytes(m->kind, m->ffn);
-  if (rb_in == -1 || rb_ff == -1) return UGB_EQUANT;
+  if (!matvec_kind(m->kind)) return UGB_EQUANT;
   if (rb_in < 0 || rb_ff < 0) return UGB_ESHAPE;
   if (!m->gate || !m->up || !m->down || !m->xq || !m->ids || !m->weights || !m->out || !m->workspace)
     return UGB_EALIGN;

@@ -59,7 +59,8 @@ __device__ __forceinline__ uint8_t synth_byte(uint64_t seed, uint64_t b, int j) 
     const uint32_t r = hash32(seed, b, j) & 0xffff;
     return static_cast<uint8_t>(static_cast<int8_t>(static_cast<int>((r * 255u) >> 16) - 127));
   } else {
-    constexpr int d_at = KIND == UGB_Q4_K ? 0 : 108;
+    // where the block's fp16 scale d sits; every other byte is uniform (all patterns are valid)
+    constexpr int d_at = KIND == UGB_Q3_K ? 108 : KIND == UGB_Q6_K ? 208 : 0;
     if (j >= d_at && j < d_at + 2) {
       const uint16_t h = kScaleTable[hash32(seed, b, 1000) & 255];
       return static_cast<uint8_t>(j == d_at ? h & 0xff : h >> 8);
@@ -100,6 +101,10 @@ ugb_status launch_fill_synthetic(ugb_ctx *, cudaStream_t stream, uint32_t kind, 
     case UGB_Q8_0: fill_kernel<UGB_Q8_0, 34><<<grid, 256, 0, stream>>>(w, total, seed); break;
     case UGB_Q4_K: fill_kernel<UGB_Q4_K, 144><<<grid, 256, 0, stream>>>(w, total, seed); break;
     case UGB_Q3_K: fill_kernel<UGB_Q3_K, 110><<<grid, 256, 0, stream>>>(w, total, seed); break;
+    case UGB_Q6_K: fill_kernel<UGB_Q6_K, 210><<<grid, 256, 0, stream>>>(w, total, seed); break;
+    case UGB_IQ3_XXS: fill_kernel<UGB_IQ3_XXS, 98><<<grid, 256, 0, stream>>>(w, total, seed); break;
+    case UGB_IQ4_NL: fill_kernel<UGB_IQ4_NL, 18><<<grid, 256, 0, stream>>>(w, total, seed); break;
+    case UGB_IQ4_XS: fill_kernel<UGB_IQ4_XS, 136><<<grid, 256, 0, stream>>>(w, total, seed); break;
     default: return UGB_EQUANT;
   }
   return cuda_status(cudaGetLastError());
