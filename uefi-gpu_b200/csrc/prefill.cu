@@ -15,7 +15,8 @@
 //     copies -- both operands were written by the repack / quant kernels directly in the UMMA
 //     canonical K-major layout, so no tensor map is needed;
 //   * warp 1 issues one tcgen05.mma.kind::i8 (M=128, N=128, K=32) per K-block into one of four
-//     TMEM accumulators (128 columns each, overwrite mode): every block's int32 dot lands alone;
+//     TMEM accumulators (128 columns each, overwrite mode): every block's int32 dot lands alone,
+//     and the accumulators change hands with the epilogue two blocks at a time;
 //   * warps 2..17 (four per TMEM lane quarter, 32 columns each) read each block's int32 tile with
 //     tcgen05.ld, scale it by dw*dx and accumulate in fp32 registers, then store the tile.
 // Per-block scales are why the accumulator cannot stay in TMEM across K: the fp32 rescale of
@@ -42,6 +43,8 @@ constexpr int kBM = kPrefillTile;         // tokens per tile (UMMA M, TMEM lanes
 constexpr int kKB = 4;                    // K-blocks (of 32) per stage
 constexpr int kStages = 4;
 constexpr int kAcc = 4;                   // TMEM accumulators
+constexpr int kPairs = kAcc / 2;          // accumulator pairs: the unit of MMA / epilogue hand-off
+static_assert(kAcc % 2 == 0 && kKB % 2 == 0, "pairs of blocks never straddle a stage or an accumulator set");
 constexpr int kTileBytes = kPrefillTileBytes;         // 4096: one 128 x 32 B operand block
 constexpr int kScaleBytes = kPrefillTile * 4;          // 512
 constexpr int kEpiWarps = 16;
@@ -247,9 +250,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
   uint8_t *ctl = smem + kStages * G::kStageBytes;
   uint64_t *full = reinterpret_cast<uint64_t *>(ctl);  // [kStages] bulk data landed
   uint64_t *empty = full + kStages;                    // [kStages] MMAs done + scales read
-  uint64_t *tfull = empty + kStages;                   // [kAcc] block's int32 tile ready
-  uint64_t *tempty = tfull + kAcc;                     // [kAcc] tile read by the epilogue
-  uint64_t *drain = tempty + kAcc;                     // [1] final commit on abort
+  uint64_t *tfull = empty + kStages;                   // [kPairs] a pair's int32 tiles ready
+  uint64_t *tempty = tfull + kPairs;                   // [kPairs] a pair's tiles read by the epilogue
+  uint64_t *drain = tempty + kPairs;                   // [1] final commit on abort
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
   // stage layout: [A: kKB x 4096][B: kKB x BN*32][dx: kKB x 128 f32][dw: kKB x BN f32]
@@ -273,7 +276,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
       mbar_init(smem_u32(&full[i]), 1);
       mbar_init(smem_u32(&empty[i]), kEpiWarps + 1);
     }
-    for (int i = 0; i < kAcc; ++i) {
+    for (int i = 0; i < kPairs; ++i) {
       mbar_init(smem_u32(&tfull[i]), 1);
       mbar_init(smem_u32(&tempty[i]), kEpiWarps);
     }
@@ -329,19 +332,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
         mbar_wait_bounded(smem_u32(&full[s % kStages]), (s / kStages) & 1);
     }
   } else if (warp == 1) {
-    // ---- MMA issuer: one tcgen05.mma per K-block into accumulator b % kAcc ----
+    // ---- MMA issuer: one tcgen05.mma per K-block into accumulator b % kAcc; blocks go to the
+    // epilogue in pairs (2p, 2p + 1), one commit per pair ----
     if (lane == 0) {
       bool ok = true;
       for (int b = 0; b < nb && ok; ++b) {
-        const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc;
+        const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc, pr = b / 2, P = pr % kPairs;
         if (kb == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
-        if (ok && b >= kAcc) ok = wait_or_abort(smem_u32(&tempty[j]), ((b / kAcc) - 1) & 1, abort_flag);
+        if (ok && b % 2 == 0 && pr >= kPairs)  // the pair kPairs back has been read out
+          ok = wait_or_abort(smem_u32(&tempty[P]), ((pr / kPairs) - 1) & 1, abort_flag);
         if (!ok) break;
         tc_fence_after();
         const uint32_t st = smem_u32(smem + slot * G::kStageBytes);
         mma_i8(tmem_base + static_cast<uint32_t>(j * BN), smem_desc(st + kb * kTileBytes),
                smem_desc(st + kOffB + kb * G::kBBytes), G::kIdesc, 0u);
-        mma_commit(smem_u32(&tfull[j]));
+        if (b % 2 == 1 || b == nb - 1) mma_commit(smem_u32(&tfull[P]));
         if (kb == kKB - 1 || b == nb - 1) mma_commit(smem_u32(&empty[slot]));
       }
       // The last stages' release phases (commit + epilogue arrivals) are waited here, so no
@@ -360,14 +365,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     uint64_t acc[kC / 2];                  // pairs of fp32 accumulators
 #pragma unroll
     for (int i = 0; i < kC / 2; ++i) acc[i] = 0ull;
-    bool ok = true;
-    for (int b = 0; b < nb && ok; ++b) {
-      const int s = b / kKB, slot = s % kStages, kb = b % kKB, j = b % kAcc;
-      if (kb == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
-      if (ok) ok = wait_or_abort(smem_u32(&tfull[j]), (b / kAcc) & 1, abort_flag);
-      if (!ok) break;
-      tc_fence_after();
-      const uint8_t *st = smem + slot * G::kStageBytes;
+    // One block's int32 tile (already committed) into the accumulators.
+    auto rescale = [&](int b) {
+      const int kb = b % kKB, j = b % kAcc;
+      const uint8_t *st = smem + ((b / kKB) % kStages) * G::kStageBytes;
       const float dx = reinterpret_cast<const float *>(st + kOffSA)[kb * kPrefillTile + t_local];
       const float4 *dw4 = reinterpret_cast<const float4 *>(st + kOffSB + (kb * BN + c0) * 4);
       const uint64_t dx2 = pk2(dx, dx);
@@ -396,11 +397,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
         acc[i / 2] = fma2(f01, s01, acc[i / 2]);
         acc[i / 2 + 1] = fma2(f23, s23, acc[i / 2 + 1]);
       }
+    };
+    // Pairs of blocks: one wait for both tiles and one release of both accumulators per pair,
+    // since these waits, fences and arrivals (not the arithmetic) are most of a warp's chain per
+    // block; the two blocks are still added in block order.
+    bool ok = true;
+    for (int b0 = 0; b0 < nb && ok; b0 += 2) {
+      const int s = b0 / kKB, slot = s % kStages, pr = b0 / 2, P = pr % kPairs;
+      const bool two = b0 + 1 < nb;
+      if (b0 % kKB == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
+      if (ok) ok = wait_or_abort(smem_u32(&tfull[P]), (pr / kPairs) & 1, abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int b = b0; b < b0 + (two ? 2 : 1); ++b) rescale(b);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(smem_u32(&tempty[j]));
-        if (kb == kKB - 1 || b == nb - 1) mbar_arrive(smem_u32(&empty[slot]));
+        mbar_arrive(smem_u32(&tempty[P]));
+        const int bl = two ? b0 + 1 : b0;
+        if (bl % kKB == kKB - 1 || bl == nb - 1) mbar_arrive(smem_u32(&empty[slot]));
       }
     }
     if (ok && t < p.m) {
