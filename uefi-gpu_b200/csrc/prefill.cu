@@ -243,7 +243,7 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   }
 }
 
-template <int BN>
+template <int BN, bool DOTS>
 __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParams p) {
   using G = Geo<BN>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -380,7 +380,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
         tmem_ld16(taddr, r);
       }
       tmem_ld_wait();
-      if (p.dots) {
+      if (DOTS) {
         for (int i = 0; i < kC; ++i) {
           const int64_t nn = n_col0 + c0 + i;
           if (t < p.m && nn < p.n)
@@ -459,11 +459,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
 
 ugb_status init_prefill_kernels(ugb_ctx *ctx) {
   if (ctx->smem_optin < static_cast<size_t>(Geo<128>::kSmem)) return UGB_EBACKEND;
-  ugb_status st = cuda_status(
-      cudaFuncSetAttribute(prefill_gemm_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<128>::kSmem));
-  if (st != UGB_OK) return st;
-  return cuda_status(
-      cudaFuncSetAttribute(prefill_gemm_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<64>::kSmem));
+  for (const void *f : {reinterpret_cast<const void *>(prefill_gemm_kernel<128, false>),
+                        reinterpret_cast<const void *>(prefill_gemm_kernel<128, true>)})
+    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<128>::kSmem) != cudaSuccess)
+      return UGB_EBACKEND;
+  for (const void *f : {reinterpret_cast<const void *>(prefill_gemm_kernel<64, false>),
+                        reinterpret_cast<const void *>(prefill_gemm_kernel<64, true>)})
+    if (cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<64>::kSmem) != cudaSuccess)
+      return UGB_EBACKEND;
+  return UGB_OK;
 }
 
 PackedLayout prefill_layout(int64_t rows, int64_t k) {
@@ -519,8 +523,11 @@ ugb_status launch_gemm(ugb_ctx *ctx, cudaStream_t stream, const void *w_packed, 
   attr[0].val.programmaticStreamSerializationAllowed = ctx->pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cuda_status(narrow ? cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<64>, p)
-                            : cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<128>, p));
+  if (p.dots)
+    return cuda_status(narrow ? cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<64, true>, p)
+                              : cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<128, true>, p));
+  return cuda_status(narrow ? cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<64, false>, p)
+                            : cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<128, false>, p));
 }
 
 }  // namespace
