@@ -116,7 +116,7 @@ struct TokenStep {
   uint32_t o_xres, o_xq, o_xd, o_xs, o_scr, o_layers, o_gu, o_ring, ring_bytes;
 };
 
-constexpr size_t token_sync_words() { return 8 * 32; }
+constexpr size_t token_sync_words() { return 8 * 32 + 32; }  // counters, then combine tickets
 
 // Whether the token kernel serves this decoder on this device (kinds, shapes, row alignment,
 // shared memory).

@@ -7,7 +7,7 @@
 //    then the head) into a byte ring in shared memory with cp.async.bulk, in the order the
 //    consumers use it.  Weights do not depend on activations, so the stream waits only for
 //    ring space, never for a layer boundary, and HBM stays busy across the glue phases;
-//  * eight consumer warps run the step's phases.  A phase that needs every CTA's outputs
+//  * sixteen consumer warps run the step's phases.  A phase that needs every CTA's outputs
 //    waits on a device-wide completion counter instead of a kernel boundary.  Every wait is
 //    bounded, and an abort flag ends all of them at once.
 // Phases of layer l:
@@ -16,7 +16,9 @@
 //      the CTA's Q/K/V rows -> qkv
 //   B  attention partials of (KV head, 64-position chunk) units: bias, RoPE, KV-cache write,
 //      scores, chunk softmax, P.V (the launch chain's attn_partial_kernel, per CTA)
-//   C  every CTA combines all heads' partials and quantises them; the CTA's O rows -> dx_o
+//      and the last unit of each (KV head, query subgroup) combines that subgroup's chunks and
+//      writes its heads' quantised attention output (a ticket per subgroup picks the last unit)
+//   C  every CTA loads the quantised attention output; the CTA's O rows -> dx_o
 //   D  x += dx_o; RMSNorm; Q8_1; the CTA's gate and up rows of whole 32-row blocks, so the
 //      CTA forms SiLU(gate) * up of those blocks and their Q8_1 blocks itself -> hq
 //   E  hq into shared memory; the CTA's down rows -> dx_down
@@ -48,7 +50,11 @@ static_assert(kCT % kHeadDim == 0 && kAttnChunk % kPV == 0, "P.V thread layout")
 // Device-wide counters of a step (TokenStep::sync), zero between launches: the last CTA to
 // leave zeroes them for the next launch.
 enum : int { kStart, kCntA, kCntB, kCntC, kCntD, kCntE, kAbort, kExit, kNumSync };
-static_assert(kNumSync * kSyncStride <= token_sync_words(), "counter block too small");
+// After the counters: one ticket per (KV head, query subgroup), counting the attention units of
+// the subgroup that have written their partials (the last one combines them); zero between uses.
+constexpr int kTicket0 = kNumSync * kSyncStride;
+constexpr int kMaxTickets = 32;
+static_assert(kTicket0 + kMaxTickets <= token_sync_words(), "counter block too small");
 
 // Matrices of a layer, in the order the producer streams them.
 enum : int { kSlotQKV, kSlotO, kSlotGate, kSlotUp, kSlotDown, kSlotHead };
@@ -267,9 +273,10 @@ __device__ __forceinline__ bool overlaps(uint32_t a0, uint32_t alen, uint32_t b0
 // Per-CTA scratch at the start of shared memory, after the mbarriers.
 struct TokMisc {
   int ok;            // result of the last phase wait, broadcast to the consumer warps
+  int last;          // this CTA's attention unit was its subgroup's last (it combines)
   int tok, pos;
   uint32_t issued;   // items the producer issued
-  uint32_t pad[4];
+  uint32_t pad[3];
   float red[32];
   unsigned long long key[32];
   TokPlan plan;
@@ -710,28 +717,35 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
   cbar();  // the scratch is free for the next unit
 }
 
-constexpr int kCombBlocks = 4;  // attention-output blocks a warp combines per pass
-
-// Every CTA: combine the chunk partials of all query heads (log-sum-exp, the launch chain's
-// attn_combine_quant_kernel arithmetic) and quantise the attention output into the shared
-// activation.  Warp w takes heads w, w + kCW, ...: lane c loads chunk c's max and sum, and the
-// warp forms the chunk weights exp(m_c - max) and the reciprocal of the denominator; then the
-// outputs (o * (1 / l), within an ulp of the launch chain's o / l), warp w taking 32-element
-// blocks w, w + kCW, ... (kCombBlocks per pass, two chunks per iteration).
-// Tracing (CTA 0 only, else rec < 0): the output and its Q8_1 go to fields ATT, ATT_XQ of record rec.
+// The attention unit just finished (KV head kvh, subgroup sg, one of nch chunks) takes its
+// subgroup's ticket; the last of the nch units to do so combines the subgroup's chunk partials
+// (log-sum-exp: weights exp(m_c - max), the launch chain's attn_combine_quant_kernel arithmetic
+// and order) and writes the gn heads' attention output, quantised per 32-block, into the Q8_1
+// vector at p.hq (free in phases B and C: its FFN contents were consumed in the previous
+// layer's phase E).  Phase C of every CTA then loads that vector instead of combining all heads
+// itself.  Tracing (rec >= 0): the unit writes its heads' slice of fields ATT and ATT_XQ.
 template <bool TRACE>
-__device__ void combine_quant(const TokenStep &p, uint8_t *smem, int pos, int rec) {
-  constexpr int HD = kHeadDim;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.n_head / p.n_kv;
-  const int ns = pos / kAttnChunk + 1;
-  const int nh = p.n_head;
-  float *cw = reinterpret_cast<float *>(smem + p.o_scr);  // [nh][ns] chunk weights
-  float *den = cw + nh * ns;                              // [nh] 1 / denominator
-  for (int h = warp; h < nh; h += kCW) {
-    const int kvh = h / G, g = h - kvh * G;
-    const size_t p0 = static_cast<size_t>(kvh) * p.n_split * G + g;
-    // lane sp holds chunk sp (and sp + 32, ... beyond 32 chunks, read again after the max)
+__device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int kvh, int sg, int nch, int rec) {
+  constexpr int HD = kHeadDim, GM = kMaxGroup;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int G = p.n_head / p.n_kv, nsg = attn_subgroups(G);
+  const int g0 = G * sg / nsg, gn = G * (sg + 1) / nsg - g0;
+  if (tid == 0) {
+    uint32_t *ticket = p.sync + kTicket0 + kvh * nsg + sg;
+    uint32_t t;
+    // acq_rel: this CTA's partials (ordered before by the unit's last consumer barrier) are
+    // published with the ticket, and the last unit sees every other unit's
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(t) : "l"(ticket) : "memory");
+    ms->last = t + 1 == static_cast<uint32_t>(nch) ? 1 : 0;
+    if (ms->last) atomicExch(ticket, 0u);  // ready for the next layer's units
+  }
+  cbar();
+  if (!ms->last) return;
+  const int ns = nch;
+  float *cw = reinterpret_cast<float *>(smem + p.o_scr);  // [GM][ns] chunk weights
+  float *den = cw + GM * ns;                              // [GM] 1 / denominator
+  if (warp < gn) {
+    const size_t p0 = static_cast<size_t>(kvh) * p.n_split * G + g0 + warp;
     const bool one = lane < ns;
     const float m1 = one ? __ldcg(p.part_m + p0 + static_cast<size_t>(lane) * G) : -FLT_MAX;
     const float l1 = one ? __ldcg(p.part_l + p0 + static_cast<size_t>(lane) * G) : 0.f;
@@ -742,74 +756,69 @@ __device__ void combine_quant(const TokenStep &p, uint8_t *smem, int pos, int re
     float l = 0.f;
     if (one) {
       const float e = expf(m1 - mx);
-      cw[h * ns + lane] = e;
+      cw[warp * ns + lane] = e;
       l = e * l1;
     }
     for (int sp = lane + 32; sp < ns; sp += 32) {
       const size_t pi = p0 + static_cast<size_t>(sp) * G;
       const float e = expf(__ldcg(p.part_m + pi) - mx);
-      cw[h * ns + sp] = e;
+      cw[warp * ns + sp] = e;
       l += e * __ldcg(p.part_l + pi);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) den[h] = 1.0f / l;
+    if (lane == 0) den[warp] = 1.0f / l;
   }
   cbar();
-  int8_t *q = reinterpret_cast<int8_t *>(smem + p.o_xq);
-  float *qd = reinterpret_cast<float *>(smem + p.o_xd);
-  int32_t *qs = reinterpret_cast<int32_t *>(smem + p.o_xs);
-  const int nb = nh * HD / 32;
+  // thread (w, d) = (tid / HD, tid % HD) of the gn heads; a warp holds one 32-block of one head
   bool bad = false;
-  for (int b0 = warp; b0 < nb; b0 += kCW * kCombBlocks) {
-    float o[kCombBlocks];
-    int hh[kCombBlocks];
-    size_t base_o[kCombBlocks];
+  if (tid < gn * HD) {
+    const int w = tid / HD, d = tid % HD;
+    const size_t base = (static_cast<size_t>(kvh) * p.n_split * G + g0 + w) * HD + d;
+    float o = 0.f;
+    constexpr int kBatch = 8;  // chunk loads in flight together
+    for (int s0 = 0; s0 < ns; s0 += kBatch) {
+      float pv[kBatch];
 #pragma unroll
-    for (int k = 0; k < kCombBlocks; ++k) {
-      const int b = min(b0 + k * kCW, nb - 1);
-      const int i = b * 32 + lane, h = i / HD, kvh = h / G, g = h - kvh * G;
-      o[k] = 0.f;
-      hh[k] = h;
-      base_o[k] = (static_cast<size_t>(kvh) * p.n_split * G + g) * HD + (i - h * HD);
+      for (int j = 0; j < kBatch; ++j)
+        pv[j] = __ldcg(p.part_o + base + static_cast<size_t>(min(s0 + j, ns - 1)) * G * HD);
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (s0 + j < ns) o += cw[w * ns + s0 + j] * pv[j];
     }
-    // kChunkBatch chunks of every block loaded before any is used (all in flight together)
-    constexpr int kChunkBatch = 4;
-    for (int s0 = 0; s0 < ns; s0 += kChunkBatch) {
-      float pv[kChunkBatch][kCombBlocks];
-#pragma unroll
-      for (int j = 0; j < kChunkBatch; ++j) {
-        const size_t sp = static_cast<size_t>(min(s0 + j, ns - 1));
-#pragma unroll
-        for (int k = 0; k < kCombBlocks; ++k) pv[j][k] = __ldcg(p.part_o + base_o[k] + sp * G * HD);
-      }
-#pragma unroll
-      for (int j = 0; j < kChunkBatch; ++j)
-        if (s0 + j < ns)
-#pragma unroll
-          for (int k = 0; k < kCombBlocks; ++k) o[k] += cw[hh[k] * ns + s0 + j] * pv[j][k];
-    }
-    float v[kCombBlocks];
-    int bb[kCombBlocks];
-    bool live[kCombBlocks];
-#pragma unroll
-    for (int k = 0; k < kCombBlocks; ++k) {
-      bb[k] = b0 + k * kCW;
-      live[k] = bb[k] < nb;
-      v[k] = o[k] * den[hh[k]];
-    }
-    bad |= quant_blocks<kCombBlocks>(v, bb, live, lane, q, qd, qs);
+    const float v = o * den[w];
+    const int blk = ((kvh * G + g0 + w) * HD + d) >> 5;
+    int8_t *q = reinterpret_cast<int8_t *>(p.hq);
+    float *dq = reinterpret_cast<float *>(p.hq + p.n_ff);
+    int32_t *sq = reinterpret_cast<int32_t *>(p.hq + p.n_ff + 4 * (p.n_ff / 32));
+    bad = quant_block(v, lane, q, dq, sq, blk);
     if (TRACE && rec >= 0) {  // the same arithmetic again, into the trace
-      float *ta = p.trace.f32(rec, UGB_TRACE_ATT);
       uint8_t *tq = p.trace.at(rec, UGB_TRACE_ATT_XQ);
-#pragma unroll
-      for (int k = 0; k < kCombBlocks; ++k)
-        if (live[k]) ta[bb[k] * 32 + lane] = v[k];
-      quant_blocks<kCombBlocks>(v, bb, live, lane, reinterpret_cast<int8_t *>(tq),
-                                reinterpret_cast<float *>(tq + p.trace.d_q), reinterpret_cast<int32_t *>(tq + p.trace.s_q));
+      p.trace.f32(rec, UGB_TRACE_ATT)[blk * 32 + lane] = v;
+      quant_block(v, lane, reinterpret_cast<int8_t *>(tq), reinterpret_cast<float *>(tq + p.trace.d_q),
+                  reinterpret_cast<int32_t *>(tq + p.trace.s_q), blk);
     }
   }
   if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
+  cbar();  // the scratch is free for the next unit
+}
+
+// Every CTA: the attention output's Q8_1 vector (written by the subgroups' last units) into the
+// shared activation.
+__device__ void load_att(const TokenStep &p, uint8_t *smem) {
+  const int tid = threadIdx.x;
+  const int qr = p.n_head * kHeadDim, nq16 = qr / 16, nb = qr / 32;
+  const uint4 *src = reinterpret_cast<const uint4 *>(p.hq);
+  uint4 *dst = reinterpret_cast<uint4 *>(smem + p.o_xq);
+  for (int i = tid; i < nq16; i += kCT) dst[i] = __ldcg(src + i);
+  const float *sd = reinterpret_cast<const float *>(p.hq + p.n_ff);
+  const int32_t *ss = reinterpret_cast<const int32_t *>(p.hq + p.n_ff + 4 * (p.n_ff / 32));
+  float *dd = reinterpret_cast<float *>(smem + p.o_xd);
+  int32_t *ds = reinterpret_cast<int32_t *>(smem + p.o_xs);
+  for (int i = tid; i < nb; i += kCT) {
+    dd[i] = __ldcg(sd + i);
+    ds[i] = __ldcg(ss + i);
+  }
   cbar();
 }
 
@@ -943,13 +952,15 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
       // only by its time limit
       if (!phase_wait(p, ms, kCntA, Pu * (l + 1) + (l == 0 ? p.unreachable : 0u))) return;
       uint32_t n = 0;
-      for (int u = cta; u < units; u += P, ++n)
+      for (int u = cta; u < units; u += P, ++n) {
         attn_unit<KV>(p, smem, L.bias, l, u / nsg / nch, u / nsg % nch, u % nsg, pos);
+        attn_finish<TRACE>(p, smem, ms, u / nsg / nch, u % nsg, nch, TRACE ? l : -1);
+      }
       phase_arrive(p, kCntB, n);
     }
-    // C: combine + Q8_1, then O
+    // C: the quantised attention output, then O
     if (!phase_wait(p, ms, kCntB, static_cast<uint32_t>(units) * (l + 1))) return;
-    combine_quant<TRACE>(p, smem, pos, tr0 ? l : -1);
+    load_att(p, smem);
     make_slots(p, base, qr, p.rb_q, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotO, p.rb_q, sl, [&](int row, float v) {
       p.dxo[row] = v;
@@ -1050,6 +1061,7 @@ __global__ void __launch_bounds__(kTT, 1) token_kernel(const TokenStep p) {
     __threadfence();
     if (atomicAdd(sync_word(p, kExit), 1u) == gridDim.x - 1) {
       for (int i = 0; i < kNumSync; ++i) sync_word(p, i)[0] = 0;  // ready for the next launch
+      for (int i = 0; i < kMaxTickets; ++i) p.sync[kTicket0 + i] = 0;  // (an aborted step may leave some)
       __threadfence();
     }
   }
@@ -1067,7 +1079,7 @@ bool token_layout(const ugb_ctx *ctx, TokenStep &p) {
   const int kq = std::max({p.n_embd, qr, p.n_ff});
   const size_t xq_bytes = kq + 8 * static_cast<size_t>(kq / 32);
   const size_t attn = 4 * static_cast<size_t>(kPV * kMaxGroup * kHeadDim + 2 * kHeadDim + kMaxGroup * kAttnChunk);
-  const size_t comb = 4 * static_cast<size_t>(p.n_head * p.n_split + p.n_head);
+  const size_t comb = 4 * static_cast<size_t>(kMaxGroup * p.n_split + kMaxGroup);  // attn_finish
   p.gu_blocks = (p.n_ff / 32 + ctx->sm_count - 1) / ctx->sm_count;
   size_t o = 16 * kNS + kMiscBytes;
   p.o_xres = static_cast<uint32_t>(o);
@@ -1118,7 +1130,9 @@ ugb_status launch_kind(ugb_ctx *ctx, cudaStream_t stream, const TokenStep &p, si
 bool token_supported(const ugb_ctx *ctx, uint32_t kind, uint32_t head_kind, TokenStep p) {
   if ((kind != UGB_Q8_0 && kind != UGB_Q4_K) || head_kind != UGB_Q8_0) return false;
   if (p.n_head % p.n_kv || p.n_head / p.n_kv > 8 || p.n_embd % 32 || p.n_ff % 32) return false;
-  if (p.n_embd > 4096 || p.n_head * kHeadDim / 32 > 64 * kCW * kCombBlocks || p.n_layer > kMaxTokLayers)
+  // one combine ticket per (KV head, subgroup); the attention output travels in the hq buffer
+  if (p.n_kv * attn_subgroups(p.n_head / p.n_kv) > kMaxTickets || p.n_head * kHeadDim > p.n_ff) return false;
+  if (p.n_embd > 4096 || p.n_layer > kMaxTokLayers)
     return false;
   const uint32_t rbs[4] = {p.rb_e, p.rb_q, p.rb_f, p.rb_h};
   for (uint32_t rb : rbs)
