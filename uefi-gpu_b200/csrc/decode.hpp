@@ -96,7 +96,9 @@ struct TokenStep {
   const uint8_t *head;        // head_kind [n_vocab][n_embd]
   const float *out_norm;
   float *qkv;                 // [q; k; v] of the current layer
-  float *dxo, *dxd;           // O and down projections (read by the next phase's residual add)
+  unsigned long long *tdx;    // [2][n_embd] O then down projections as (tag << 32 | fp32 bits)
+                              // words: the next phase's residual add reads them until every
+                              // tag is the current layer's (no device-wide wait of its own)
   float *logits;              // [n_vocab]
   uint8_t *hq;                // Q8_1 of SiLU(gate) * up: quants [n_ff] | scales | sums
   void *kcache, *vcache;      // [n_layer][n_kv][n_ctx][HD], f32 or (kv16) f16
@@ -116,7 +118,7 @@ struct TokenStep {
   uint32_t o_xres, o_xq, o_xd, o_xs, o_scr, o_layers, o_gu, o_ring, ring_bytes;
 };
 
-constexpr size_t token_sync_words() { return 8 * 32 + 32; }  // counters, then combine tickets
+constexpr size_t token_sync_words() { return 8 * 32 + 64; }  // counters, combine tickets, epoch
 
 // Whether the token kernel serves this decoder on this device (kinds, shapes, row alignment,
 // shared memory).

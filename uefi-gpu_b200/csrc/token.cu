@@ -54,7 +54,14 @@ enum : int { kStart, kCntA, kCntB, kCntC, kCntD, kCntE, kAbort, kExit, kNumSync 
 // the subgroup that have written their partials (the last one combines them); zero between uses.
 constexpr int kTicket0 = kNumSync * kSyncStride;
 constexpr int kMaxTickets = 32;
-static_assert(kTicket0 + kMaxTickets <= token_sync_words(), "counter block too small");
+// Then the launch epoch: the tags of the exchanged O / down outputs are epoch * 256 + layer + 1,
+// so a word left from an earlier layer or launch (or the zeroed start) never matches the current
+// one.  The last CTA out advances it.
+constexpr int kEpochWord = kTicket0 + kMaxTickets;
+static_assert(kEpochWord < static_cast<int>(token_sync_words()), "counter block too small");
+__host__ __device__ constexpr uint32_t dx_tag(uint32_t epoch, int layer) {
+  return epoch * 256u + static_cast<uint32_t>(layer) + 1u;
+}
 
 // Matrices of a layer, in the order the producer streams them.
 enum : int { kSlotQKV, kSlotO, kSlotGate, kSlotUp, kSlotDown, kSlotHead };
@@ -90,6 +97,18 @@ __device__ __forceinline__ bool aborted(const TokenStep &p) { return ld_relaxed(
 __device__ __forceinline__ void abort_all(const TokenStep &p) {
   atomicExch(sync_word(p, kAbort), 1u);
   status_or(p.status, ST_TIMEOUT);
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One exchanged output: value and tag in one 64-bit store, so a reader sees both or neither.
+__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, uint32_t tag) {
+  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p) {
@@ -276,7 +295,8 @@ struct TokMisc {
   int last;          // this CTA's attention unit was its subgroup's last (it combines)
   int tok, pos;
   uint32_t issued;   // items the producer issued
-  uint32_t pad[3];
+  uint32_t epoch;    // the launch epoch (tags of the exchanged outputs)
+  uint32_t pad[2];
   float red[32];
   unsigned long long key[32];
   TokPlan plan;
@@ -474,19 +494,57 @@ constexpr int kMaxEmbdPer = 16;  // n_embd <= 4096 = 16 * 256
 // gpu_dp4a.cu:23-31).  Sum of squares in a fixed order.
 // Tracing (CTA 0 only, else rec < 0): the residual, the norm output and its Q8_1 go to fields X,
 // ATTN_NORM / FFN_NORM (fn) and the Q8_1 field after it of trace record `rec`.
+// dx (tagged words, or null at the first layer): each thread reads its elements until every tag
+// is `tag` -- the other CTAs' outputs of the previous phase, all written -- with the step's wait
+// limit; false (on every consumer thread) when the step was aborted or the limit passed.
 template <bool TRACE>
-__device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const float *dx, const float *w,
-                           int rec, int fn) {
+__device__ bool norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const unsigned long long *dx,
+                           uint32_t tag, const float *w, int rec, int fn) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = p.n_embd;
   float *x = reinterpret_cast<float *>(smem + p.o_xres);
   constexpr int kPer = kMaxEmbdPer / (kCW / 8);  // elements (and blocks) of x per thread (warp)
   float d[kPer], wv[kPer];
+  uint32_t pend = 0;  // elements whose tag is not yet the current one
 #pragma unroll
   for (int k = 0; k < kPer; ++k) {
     const int i = tid + k * kCT, b = warp + k * kCW;
-    d[k] = dx && i < n ? __ldcg(dx + i) : 0.f;
+    d[k] = 0.f;
+    if (dx && i < n) {
+      const unsigned long long v = ld_relaxed64(dx + i);
+      if (static_cast<uint32_t>(v >> 32) == tag) {
+        d[k] = __uint_as_float(static_cast<uint32_t>(v));
+      } else {
+        pend |= 1u << k;
+      }
+    }
     wv[k] = b < n / 32 ? w[b * 32 + lane] : 0.f;
+  }
+  bool ok = true;
+  if (pend) {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1; pend; ++it) {
+#pragma unroll
+      for (int k = 0; k < kPer; ++k)
+        if (pend & (1u << k)) {
+          const unsigned long long v = ld_relaxed64(dx + tid + k * kCT);
+          if (static_cast<uint32_t>(v >> 32) == tag) {
+            d[k] = __uint_as_float(static_cast<uint32_t>(v));
+            pend &= ~(1u << k);
+          }
+        }
+      if (pend && (it & 15) == 0) {
+        if (aborted(p)) {
+          ok = false;
+          break;
+        }
+        if (globaltimer_ns() - t0 > p.wait_ns) {
+          abort_all(p);
+          ok = false;
+          break;
+        }
+      }
+    }
   }
   // X is the residual entering a layer (or the head): the attention-side norm's input only
   float *tx = TRACE && rec >= 0 && fn == UGB_TRACE_ATTN_NORM ? p.trace.f32(rec, UGB_TRACE_X) : nullptr;
@@ -504,7 +562,7 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if (lane == 0) ms->red[warp] = ss;
-  cbar();
+  if (!cbar_and(ok)) return false;
   float tot = 0.f;
 #pragma unroll
   for (int i = 0; i < kCW; ++i) tot += ms->red[i];
@@ -540,6 +598,7 @@ __device__ void norm_quant(const TokenStep &p, uint8_t *smem, TokMisc *ms, const
   }
   if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
   cbar();  // the activation is complete, and ms->red may be reused
+  return true;
 }
 
 // Ask L2 for the cached keys and values an attention unit of layer l will read (positions before
@@ -892,6 +951,7 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
     }
     ms->tok = tok;
     ms->pos = pos;
+    ms->epoch = ld_relaxed(p.sync + kEpochWord);
     atomicAdd(sync_word(p, kStart), 1u);
     ms->ok = 1;
     if (cta == 0) {
@@ -906,6 +966,8 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
   }
   cbar();
   const int pos = ms->pos, tok = ms->tok;
+  const uint32_t epoch = ms->epoch;
+  unsigned long long *const tdx_o = p.tdx, *const tdx_d = p.tdx + p.n_embd;
   if (!cbar_and(ms->ok != 0)) return;
   float *x = reinterpret_cast<float *>(smem + p.o_xres);
   {  // x = the token's Q8_0 embedding row (embedding_q8, gpu_embedding.cu:3-9)
@@ -933,11 +995,13 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
   for (int l = 0; l < p.n_layer; ++l) {
     const TokLayer &L = layers[l];
     // A: residual + norm + Q8_1, then Q/K/V
-    if (l > 0 && !phase_wait(p, ms, kCntE, Pu * l)) return;
+    // (the previous layer's down outputs are waited for inside the norm, by their tags)
     if (tid == 0)
       for (int u = cta; u < units; u += P)
         if (u % nsg == 0) prefetch_unit<KV>(p, l, u / nsg / nch, u / nsg % nch, pos);
-    norm_quant<TRACE>(p, smem, ms, l > 0 ? p.dxd : nullptr, L.attn_norm, tr0 ? l : -1, UGB_TRACE_ATTN_NORM);
+    if (!norm_quant<TRACE>(p, smem, ms, l > 0 ? tdx_d : nullptr, dx_tag(epoch, l - 1), L.attn_norm, tr0 ? l : -1,
+                           UGB_TRACE_ATTN_NORM))
+      return;
     make_slots(p, base, p.n_embd, p.rb_e, sl);
     bool ok = consume<KIND>(p, base, cur, pl, L, kSlotQKV, p.rb_e, sl, [&](int row, float v) {
       p.qkv[row] = v;
@@ -963,15 +1027,14 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
     load_att(p, smem);
     make_slots(p, base, qr, p.rb_q, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotO, p.rb_q, sl, [&](int row, float v) {
-      p.dxo[row] = v;
+      st_tagged(tdx_o + row, v, dx_tag(epoch, l));
       if (tracing) p.trace.f32(l, UGB_TRACE_O)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     if (!cbar_and(ok)) return;
-    phase_arrive(p, kCntC, 1);
     // D: residual + norm + Q8_1, then gate and up of whole blocks, SiLU * up + Q8_1
-    if (!phase_wait(p, ms, kCntC, Pu * (l + 1))) return;
-    norm_quant<TRACE>(p, smem, ms, p.dxo, L.ffn_norm, tr0 ? l : -1, UGB_TRACE_FFN_NORM);
+    if (!norm_quant<TRACE>(p, smem, ms, tdx_o, dx_tag(epoch, l), L.ffn_norm, tr0 ? l : -1, UGB_TRACE_FFN_NORM))
+      return;
     make_slots(p, base, p.n_embd, p.rb_e, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotGate, p.rb_e, sl, [&](int row, float v) {
       gs[row - 32 * gb0] = v;
@@ -991,16 +1054,16 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
     load_hq(p, smem);
     make_slots(p, base, p.n_ff, p.rb_f, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotDown, p.rb_f, sl, [&](int row, float v) {
-      p.dxd[row] = v;
+      st_tagged(tdx_d + row, v, dx_tag(epoch, l));
       if (tracing) p.trace.f32(l, UGB_TRACE_DOWN)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     if (!cbar_and(ok)) return;
-    phase_arrive(p, kCntE, 1);
   }
   // Head: residual + output norm + Q8_1, logits of this CTA's rows, greedy key.
-  if (!phase_wait(p, ms, kCntE, Pu * p.n_layer)) return;
-  norm_quant<TRACE>(p, smem, ms, p.dxd, p.out_norm, tr0 ? p.n_layer : -1, UGB_TRACE_ATTN_NORM);
+  if (!norm_quant<TRACE>(p, smem, ms, tdx_d, dx_tag(epoch, p.n_layer - 1), p.out_norm, tr0 ? p.n_layer : -1,
+                         UGB_TRACE_ATTN_NORM))
+    return;
   make_slots(p, base, p.n_embd, p.rb_h, sl);
   unsigned long long best = 0;
   const bool ok = consume<HKIND>(p, base, cur, pl, layers[0], kSlotHead, p.rb_h, sl, [&](int row, float v) {
@@ -1062,6 +1125,7 @@ __global__ void __launch_bounds__(kTT, 1) token_kernel(const TokenStep p) {
     if (atomicAdd(sync_word(p, kExit), 1u) == gridDim.x - 1) {
       for (int i = 0; i < kNumSync; ++i) sync_word(p, i)[0] = 0;  // ready for the next launch
       for (int i = 0; i < kMaxTickets; ++i) p.sync[kTicket0 + i] = 0;  // (an aborted step may leave some)
+      p.sync[kEpochWord] += 1;  // a new tag space for the next launch
       __threadfence();
     }
   }
