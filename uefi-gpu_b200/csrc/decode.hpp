@@ -95,7 +95,8 @@ struct TokenStep {
   const uint8_t *tok_embd;    // Q8_0 [n_vocab][n_embd]
   const uint8_t *head;        // head_kind [n_vocab][n_embd]
   const float *out_norm;
-  float *qkv;                 // [q; k; v] of the current layer
+  unsigned long long *tqkv;   // [q; k; v] of the current layer as tagged words (read by the
+                              // attention units until every tag they need is current)
   unsigned long long *tdx;    // [2][n_embd] O then down projections as (tag << 32 | fp32 bits)
                               // words: the next phase's residual add reads them until every
                               // tag is the current layer's (no device-wide wait of its own)

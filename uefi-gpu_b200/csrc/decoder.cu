@@ -52,6 +52,7 @@ struct ugb_decoder {
   std::vector<void *> owned;
   // persistent token kernel (dense, batch 1): its own buffers and the per-layer tensor table
   unsigned long long *tok_tdx = nullptr;  // token kernel: tagged O / down outputs [2][n_embd]
+  unsigned long long *tok_tqkv = nullptr; // token kernel: tagged Q/K/V rows
   uint8_t *tok_hq = nullptr;
   uint32_t *tok_sync = nullptr;
   ugb::TokLayer *tok_layers = nullptr;
@@ -127,7 +128,7 @@ void free_graph(ugb_decoder *d) {
 void free_all(ugb_decoder *d) {
   void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->rlogits, d->rweights, d->rids, d->xq, d->attq,
                   d->hq, d->kcache, d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->moe_ws, d->state,
-                  d->bias, d->tok_tdx, d->tok_hq, d->tok_sync, d->tok_layers, d->trace.base, d->pf_w, d->pf_ws,
+                  d->bias, d->tok_tdx, d->tok_tqkv, d->tok_hq, d->tok_sync, d->tok_layers, d->trace.base, d->pf_w, d->pf_ws,
                   d->ptrace.base};
   for (void *b : bufs)
     if (b) cudaFree(b);
@@ -225,6 +226,9 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
     if (ok && B == 1)
       ok = dalloc(&d->tok_tdx, 2 * static_cast<size_t>(c.n_embd)) == UGB_OK &&
            cudaMemset(d->tok_tdx, 0, 2 * sizeof(unsigned long long) * c.n_embd) == cudaSuccess &&
+           dalloc(&d->tok_tqkv, static_cast<size_t>(c.head_dim) * (c.n_head + 2 * c.n_head_kv)) == UGB_OK &&
+           cudaMemset(d->tok_tqkv, 0, sizeof(unsigned long long) * c.head_dim * (c.n_head + 2 * c.n_head_kv)) ==
+               cudaSuccess &&
            dalloc(&d->tok_hq, c.n_ff + 8 * (c.n_ff / 32)) == UGB_OK &&
            dalloc(&d->tok_sync, token_sync_words()) == UGB_OK &&
            dalloc(&d->tok_layers, c.n_layer) == UGB_OK &&
@@ -487,7 +491,7 @@ bool token_step_of(const ugb_decoder *d, TokenStep &p) {
   p.tok_embd = static_cast<const uint8_t *>(d->w.tok_embd);
   p.head = static_cast<const uint8_t *>(d->w.output);
   p.out_norm = static_cast<const float *>(d->w.output_norm);
-  p.qkv = d->qkv;
+  p.tqkv = d->tok_tqkv;
   p.tdx = d->tok_tdx;
   p.logits = d->logits;
   p.hq = d->tok_hq;

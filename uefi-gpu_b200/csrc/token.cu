@@ -7,9 +7,11 @@
 //    then the head) into a byte ring in shared memory with cp.async.bulk, in the order the
 //    consumers use it.  Weights do not depend on activations, so the stream waits only for
 //    ring space, never for a layer boundary, and HBM stays busy across the glue phases;
-//  * sixteen consumer warps run the step's phases.  A phase that needs every CTA's outputs
-//    waits on a device-wide completion counter instead of a kernel boundary.  Every wait is
-//    bounded, and an abort flag ends all of them at once.
+//  * sixteen consumer warps run the step's phases.  A phase that needs other CTAs' outputs
+//    either waits on a device-wide completion counter (attention output, SiLU output) or reads
+//    them as tagged 64-bit words (Q/K/V rows, O and down outputs: value and launch/layer tag in
+//    one store) until every tag it needs is current -- no kernel boundary either way.  Every
+//    wait is bounded, and an abort flag ends all of them at once.
 // Phases of layer l:
 //   A  x += dx_down (x = the token's embedding row at l = 0); RMSNorm; Q8_1 into shared
 //      memory (every CTA keeps its own copy of the residual stream and of the activation);
@@ -99,6 +101,7 @@ __device__ __forceinline__ void abort_all(const TokenStep &p) {
   status_or(p.status, ST_TIMEOUT);
 }
 
+
 __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long long *p) {
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -109,6 +112,27 @@ __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long l
 __device__ __forceinline__ void st_tagged(unsigned long long *p, float v, uint32_t tag) {
   const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+// A tagged word written by another CTA in this phase: read until its tag is `tag` (false when the
+// step was aborted or the wait limit passed, then the value is 0).
+__device__ __forceinline__ float poll_tagged(const TokenStep &p, const unsigned long long *w, uint32_t tag, bool &ok) {
+  unsigned long long v = ld_relaxed64(w);
+  if (static_cast<uint32_t>(v >> 32) == tag) return __uint_as_float(static_cast<uint32_t>(v));
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    v = ld_relaxed64(w);
+    if (static_cast<uint32_t>(v >> 32) == tag) return __uint_as_float(static_cast<uint32_t>(v));
+    if ((it & 15) == 0) {
+      if (aborted(p)) break;
+      if (globaltimer_ns() - t0 > p.wait_ns) {
+        abort_all(p);
+        break;
+      }
+    }
+  }
+  ok = false;
+  return 0.f;
 }
 
 __device__ __forceinline__ uint32_t ld_acquire(const uint32_t *p) {
@@ -630,8 +654,8 @@ constexpr int kMaxGroup = 4;
 __host__ __device__ constexpr int attn_subgroups(int G) { return (G + kMaxGroup - 1) / kMaxGroup; }
 
 template <typename KV>
-__device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, int l, int kvh, int c, int sg,
-                          int pos) {
+__device__ bool attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, int l, int kvh, int c, int sg,
+                          int pos, uint32_t tag) {
   constexpr int HD = kHeadDim, C = kAttnChunk, GM = kMaxGroup;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.n_head / p.n_kv, nsg = attn_subgroups(G);
@@ -650,11 +674,12 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
   // subgroup; in the chunk holding pos, threads [GM*64, GM*64 + 64) take key pair j and the next
   // HD threads one value element each.  Every load is issued before any is used.
   static_assert(GM * HD / 2 + HD / 2 + HD <= kCT, "attention load layout");
+  bool ok = true;  // the Q/K/V rows arrive as tagged words, read until current (bounded)
   if (tid < GM * HD / 2) {
     const int g = tid / (HD / 2), j = tid % (HD / 2);
     const int qrow = (kvh * G + g0 + min(g, gn - 1)) * HD + j;
     const float b0 = bias ? bias[qrow] : 0.f, b1 = bias ? bias[qrow + HD / 2] : 0.f;
-    const float q0 = __ldcg(p.qkv + qrow) + b0, q1 = __ldcg(p.qkv + qrow + HD / 2) + b1;
+    const float q0 = poll_tagged(p, p.tqkv + qrow, tag, ok) + b0, q1 = poll_tagged(p, p.tqkv + qrow + HD / 2, tag, ok) + b1;
     const float2 cs = rope[j];
     const bool live = g < gn;
     qs[g * HD + j] = live ? q0 * cs.x - q1 * cs.y : 0.f;
@@ -662,7 +687,7 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
   } else if (has_new && tid < GM * HD / 2 + HD / 2) {
     const int j = tid - GM * HD / 2, krow = qr + kvh * HD + j;
     const float b0 = bias ? bias[krow] : 0.f, b1 = bias ? bias[krow + HD / 2] : 0.f;
-    const float k0 = __ldcg(p.qkv + krow) + b0, k1 = __ldcg(p.qkv + krow + HD / 2) + b1;
+    const float k0 = poll_tagged(p, p.tqkv + krow, tag, ok) + b0, k1 = poll_tagged(p, p.tqkv + krow + HD / 2, tag, ok) + b1;
     const float2 cs = rope[j];
     // the new row takes part as the cache holds it (rounded to fp16 in an fp16 cache)
     const float a = KvIO<KV>::round(k0 * cs.x - k1 * cs.y), b = KvIO<KV>::round(k0 * cs.y + k1 * cs.x);
@@ -674,11 +699,11 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
     }
   } else if (has_new && tid < GM * HD / 2 + HD / 2 + HD) {
     const int dd = tid - GM * HD / 2 - HD / 2, vrow = qr + kr + kvh * HD + dd;
-    const float v = KvIO<KV>::round(__ldcg(p.qkv + vrow) + (bias ? bias[vrow] : 0.f));
+    const float v = KvIO<KV>::round(poll_tagged(p, p.tqkv + vrow, tag, ok) + (bias ? bias[vrow] : 0.f));
     kn[HD + dd] = v;
     if (sg == 0) KvIO<KV>::store(vcache + static_cast<size_t>(pos) * HD + dd, v);
   }
-  cbar();
+  if (!cbar_and(ok)) return false;
   // Scores: 8 lanes per position (lane j of a group takes float4 columns j, j+8, j+16, j+24),
   // 4 positions per warp, all padded heads (zero queries score 0 and are not stored).  The
   // values for P.V are loaded right after the keys, so both are in flight together.
@@ -774,6 +799,7 @@ __device__ void attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
       if (g < gn) p.part_o[(part * G + g0 + g) * HD + dd] = o;
     }
   cbar();  // the scratch is free for the next unit
+  return true;
 }
 
 // The attention unit just finished (KV head kvh, subgroup sg, one of nch chunks) takes its
@@ -1004,26 +1030,24 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
       return;
     make_slots(p, base, p.n_embd, p.rb_e, sl);
     bool ok = consume<KIND>(p, base, cur, pl, L, kSlotQKV, p.rb_e, sl, [&](int row, float v) {
-      p.qkv[row] = v;
+      st_tagged(p.tqkv + row, v, dx_tag(epoch, l));
       if (tracing) p.trace.f32(l, UGB_TRACE_QKV)[row] = v;
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     });
     if (!cbar_and(ok)) return;
-    phase_arrive(p, kCntA, 1);
     // B: attention partials
+    // (no device-wide wait: a unit reads its Q/K/V rows by their tags)
     if (cta < units) {
-      // p.unreachable > 0 (a test hook) asks for arrivals that no CTA makes, so the wait can end
-      // only by its time limit
-      if (!phase_wait(p, ms, kCntA, Pu * (l + 1) + (l == 0 ? p.unreachable : 0u))) return;
       uint32_t n = 0;
       for (int u = cta; u < units; u += P, ++n) {
-        attn_unit<KV>(p, smem, L.bias, l, u / nsg / nch, u / nsg % nch, u % nsg, pos);
+        if (!attn_unit<KV>(p, smem, L.bias, l, u / nsg / nch, u / nsg % nch, u % nsg, pos, dx_tag(epoch, l))) return;
         attn_finish<TRACE>(p, smem, ms, u / nsg / nch, u % nsg, nch, TRACE ? l : -1);
       }
       phase_arrive(p, kCntB, n);
     }
-    // C: the quantised attention output, then O
-    if (!phase_wait(p, ms, kCntB, static_cast<uint32_t>(units) * (l + 1))) return;
+    // C: the quantised attention output, then O.  p.unreachable > 0 (a test hook) asks the first
+    // layer's wait for arrivals that no CTA makes, so it can end only by its time limit.
+    if (!phase_wait(p, ms, kCntB, static_cast<uint32_t>(units) * (l + 1) + (l == 0 ? p.unreachable : 0u))) return;
     load_att(p, smem);
     make_slots(p, base, qr, p.rb_q, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotO, p.rb_q, sl, [&](int row, float v) {
