@@ -101,7 +101,10 @@ struct TokenStep {
                               // words: the next phase's residual add reads them until every
                               // tag is the current layer's (no device-wide wait of its own)
   float *logits;              // [n_vocab]
-  uint8_t *hq;                // Q8_1 of SiLU(gate) * up: quants [n_ff] | scales | sums
+  // Q8_1 vectors exchanged between CTAs as tagged words, kQ8TagWords per 32-block: eight of four
+  // quants each, then the scale, then the sum (each word: tag << 32 | 32 data bits)
+  unsigned long long *thq;    // SiLU(gate) * up, n_ff / 32 blocks
+  unsigned long long *tatt;   // the attention output, n_head * HD / 32 blocks
   void *kcache, *vcache;      // [n_layer][n_kv][n_ctx][HD], f32 or (kv16) f16
   const float2 *rope;         // [n_ctx][HD/2]
   float *part_m, *part_l, *part_o;  // attention partials, [n_kv][n_split][G](.[HD])
@@ -119,6 +122,7 @@ struct TokenStep {
   uint32_t o_xres, o_xq, o_xd, o_xs, o_scr, o_layers, o_gu, o_ring, ring_bytes;
 };
 
+constexpr int kQ8TagWords = 10;
 constexpr size_t token_sync_words() { return 8 * 32 + 64; }  // counters, combine tickets, epoch
 
 // Whether the token kernel serves this decoder on this device (kinds, shapes, row alignment,

@@ -53,7 +53,8 @@ struct ugb_decoder {
   // persistent token kernel (dense, batch 1): its own buffers and the per-layer tensor table
   unsigned long long *tok_tdx = nullptr;  // token kernel: tagged O / down outputs [2][n_embd]
   unsigned long long *tok_tqkv = nullptr; // token kernel: tagged Q/K/V rows
-  uint8_t *tok_hq = nullptr;
+  unsigned long long *tok_thq = nullptr;  // token kernel: tagged Q8_1 of SiLU(gate) * up
+  unsigned long long *tok_tatt = nullptr; // token kernel: tagged Q8_1 of the attention output
   uint32_t *tok_sync = nullptr;
   ugb::TokLayer *tok_layers = nullptr;
   int path = UGB_PATH_AUTO;
@@ -128,7 +129,7 @@ void free_graph(ugb_decoder *d) {
 void free_all(ugb_decoder *d) {
   void *bufs[] = {d->x, d->dx, d->qkv, d->gu, d->logits, d->rlogits, d->rweights, d->rids, d->xq, d->attq,
                   d->hq, d->kcache, d->vcache, d->rope, d->part_m, d->part_l, d->part_o, d->moe_ws, d->state,
-                  d->bias, d->tok_tdx, d->tok_tqkv, d->tok_hq, d->tok_sync, d->tok_layers, d->trace.base, d->pf_w, d->pf_ws,
+                  d->bias, d->tok_tdx, d->tok_tqkv, d->tok_thq, d->tok_tatt, d->tok_sync, d->tok_layers, d->trace.base, d->pf_w, d->pf_ws,
                   d->ptrace.base};
   for (void *b : bufs)
     if (b) cudaFree(b);
@@ -229,7 +230,11 @@ extern "C" ugb_status ugb_decoder_create(ugb_ctx *ctx, const ugb_decoder_config 
            dalloc(&d->tok_tqkv, static_cast<size_t>(c.head_dim) * (c.n_head + 2 * c.n_head_kv)) == UGB_OK &&
            cudaMemset(d->tok_tqkv, 0, sizeof(unsigned long long) * c.head_dim * (c.n_head + 2 * c.n_head_kv)) ==
                cudaSuccess &&
-           dalloc(&d->tok_hq, c.n_ff + 8 * (c.n_ff / 32)) == UGB_OK &&
+           dalloc(&d->tok_thq, kQ8TagWords * static_cast<size_t>(c.n_ff / 32)) == UGB_OK &&
+           cudaMemset(d->tok_thq, 0, 8 * kQ8TagWords * static_cast<size_t>(c.n_ff / 32)) == cudaSuccess &&
+           dalloc(&d->tok_tatt, kQ8TagWords * static_cast<size_t>(c.n_head * c.head_dim / 32)) == UGB_OK &&
+           cudaMemset(d->tok_tatt, 0, 8 * kQ8TagWords * static_cast<size_t>(c.n_head * c.head_dim / 32)) ==
+               cudaSuccess &&
            dalloc(&d->tok_sync, token_sync_words()) == UGB_OK &&
            dalloc(&d->tok_layers, c.n_layer) == UGB_OK &&
            cudaMemset(d->tok_sync, 0, token_sync_words() * sizeof(uint32_t)) == cudaSuccess;
@@ -494,7 +499,8 @@ bool token_step_of(const ugb_decoder *d, TokenStep &p) {
   p.tqkv = d->tok_tqkv;
   p.tdx = d->tok_tdx;
   p.logits = d->logits;
-  p.hq = d->tok_hq;
+  p.thq = d->tok_thq;
+  p.tatt = d->tok_tatt;
   p.kcache = d->kcache;
   p.vcache = d->vcache;
   p.kv16 = d->kv16;

@@ -57,19 +57,28 @@ __device__ __forceinline__ float div_by_127(float a) {
 // [-127, 127], s = sum(q).  The block maximum is one redux over the bit patterns of |v| (for
 // non-negative floats the bit order is the value order).  Writes quants, scale and sum of
 // block b.
-__device__ __forceinline__ bool quant_block(float v, int lane, int8_t *q, float *d, int32_t *s, int b) {
+// The values alone: this lane's quant, and (every lane) the block's scale and sum.
+__device__ __forceinline__ bool quant_block_values(float v, int &qi, float &d, int &sum) {
   const bool fin = isfinite(v);
   const float a = __uint_as_float(__reduce_max_sync(0xffffffffu, fin ? __float_as_uint(fabsf(v)) : 0u));
   const float inv = a > 0.f ? div_127_by(a) : 0.0f;
-  int qi = fin ? __float2int_rn(v * inv) : 0;
+  qi = fin ? __float2int_rn(v * inv) : 0;
   qi = max(-127, min(127, qi));
+  sum = __reduce_add_sync(0xffffffffu, qi);
+  d = div_by_127(a);
+  return __any_sync(0xffffffffu, !fin);
+}
+
+__device__ __forceinline__ bool quant_block(float v, int lane, int8_t *q, float *d, int32_t *s, int b) {
+  int qi, sum;
+  float dd;
+  const bool bad = quant_block_values(v, qi, dd, sum);
   q[b * 32 + lane] = static_cast<int8_t>(qi);
-  const int sum = __reduce_add_sync(0xffffffffu, qi);
   if (lane == 0) {
-    d[b] = div_by_127(a);
+    d[b] = dd;
     s[b] = sum;
   }
-  return __any_sync(0xffffffffu, !fin);
+  return bad;
 }
 
 // NB blocks quantised together by one warp (block k's value in v[k], lane = element): the same

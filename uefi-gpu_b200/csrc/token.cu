@@ -8,10 +8,10 @@
 //    consumers use it.  Weights do not depend on activations, so the stream waits only for
 //    ring space, never for a layer boundary, and HBM stays busy across the glue phases;
 //  * sixteen consumer warps run the step's phases.  A phase that needs other CTAs' outputs
-//    either waits on a device-wide completion counter (attention output, SiLU output) or reads
-//    them as tagged 64-bit words (Q/K/V rows, O and down outputs: value and launch/layer tag in
-//    one store) until every tag it needs is current -- no kernel boundary either way.  Every
-//    wait is bounded, and an abort flag ends all of them at once.
+//    reads them as tagged 64-bit words -- 32 data bits and a launch/layer tag in one store: the
+//    Q/K/V rows, the O and down outputs, and the Q8_1 attention and SiLU outputs -- until every
+//    tag it needs is current.  There is no device-wide barrier between phases: each waits only
+//    for the words it reads.  Every wait is bounded, and an abort flag ends all of them at once.
 // Phases of layer l:
 //   A  x += dx_down (x = the token's embedding row at l = 0); RMSNorm; Q8_1 into shared
 //      memory (every CTA keeps its own copy of the residual stream and of the activation);
@@ -50,7 +50,8 @@ constexpr int kPV = kCT / kHeadDim;      // threads per output dimension in the 
 static_assert(kCT % kHeadDim == 0 && kAttnChunk % kPV == 0, "P.V thread layout");
 
 // Device-wide counters of a step (TokenStep::sync), zero between launches: the last CTA to
-// leave zeroes them for the next launch.
+// leave zeroes them for the next launch.  (Words kCntA..kCntE are kept in the layout, unused:
+// the phases now hand over through tagged words.)
 enum : int { kStart, kCntA, kCntB, kCntC, kCntD, kCntE, kAbort, kExit, kNumSync };
 // After the counters: one ticket per (KV head, query subgroup), counting the attention units of
 // the subgroup that have written their partials (the last one combines them); zero between uses.
@@ -109,10 +110,32 @@ __device__ __forceinline__ unsigned long long ld_relaxed64(const unsigned long l
 }
 
 // One exchanged output: value and tag in one 64-bit store, so a reader sees both or neither.
-__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, uint32_t tag) {
-  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+__device__ __forceinline__ void st_tagged_bits(unsigned long long *p, uint32_t bits, uint32_t tag) {
+  const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | bits;
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+__device__ __forceinline__ void st_tagged(unsigned long long *p, float v, uint32_t tag) {
+  st_tagged_bits(p, __float_as_uint(v), tag);
+}
+
+// One warp, one element per lane: the block-32 quantisation of quant_block, stored as the
+// block's kQ8TagWords tagged words at w (lanes 4j store quants 4j..4j+3, lane 0 the scale and the
+// sum).  Returns whether any element was non-finite.
+__device__ __forceinline__ bool quant_block_tagged(float v, int lane, unsigned long long *w, uint32_t tag) {
+  int qi, sum;
+  float d;
+  const bool bad = quant_block_values(v, qi, d, sum);
+  const uint32_t b = static_cast<uint32_t>(qi) & 0xffu;
+  const uint32_t word = b | (__shfl_down_sync(0xffffffffu, b, 1) << 8) | (__shfl_down_sync(0xffffffffu, b, 2) << 16) |
+                        (__shfl_down_sync(0xffffffffu, b, 3) << 24);
+  if ((lane & 3) == 0) st_tagged_bits(w + (lane >> 2), word, tag);
+  if (lane == 0) {
+    st_tagged_bits(w + 8, __float_as_uint(d), tag);
+    st_tagged_bits(w + 9, static_cast<uint32_t>(sum), tag);
+  }
+  return bad;
+}
+static_assert(kQ8TagWords == 10, "tagged Q8_1 block: 8 quant words, scale, sum");
 
 // A tagged word written by another CTA in this phase: read until its tag is `tag` (false when the
 // step was aborted or the wait limit passed, then the value is 0).
@@ -163,25 +186,6 @@ __device__ bool spin_until(const TokenStep &p, int which, uint32_t target) {
       }
     }
   }
-}
-
-// Consumer threads: wait for a phase's inputs.  Every consumer thread gets the same answer
-// (M is the CTA scratch block holding the broadcast flag).
-template <class M>
-__device__ bool phase_wait(const TokenStep &p, M *ms, int which, uint32_t target) {
-  if (threadIdx.x == 0) ms->ok = spin_until(p, which, target) ? 1 : 0;
-  cbar();
-  const bool ok = ms->ok != 0;
-  cbar();  // nobody overwrites ms->ok before every thread has read it
-  return ok;
-}
-
-// Consumer threads: publish this CTA's writes of a phase and count `n` completions (the
-// consumer barrier orders every thread's writes before thread 0's release).
-__device__ void phase_arrive(const TokenStep &p, int which, uint32_t n) {
-  cbar();
-  if (threadIdx.x == 0)
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(sync_word(p, which)), "r"(n) : "memory");
 }
 
 // Bounded wait on an mbarrier phase that also ends when the step is aborted.
@@ -805,12 +809,12 @@ __device__ bool attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
 // The attention unit just finished (KV head kvh, subgroup sg, one of nch chunks) takes its
 // subgroup's ticket; the last of the nch units to do so combines the subgroup's chunk partials
 // (log-sum-exp: weights exp(m_c - max), the launch chain's attn_combine_quant_kernel arithmetic
-// and order) and writes the gn heads' attention output, quantised per 32-block, into the Q8_1
-// vector at p.hq (free in phases B and C: its FFN contents were consumed in the previous
-// layer's phase E).  Phase C of every CTA then loads that vector instead of combining all heads
-// itself.  Tracing (rec >= 0): the unit writes its heads' slice of fields ATT and ATT_XQ.
+// and order) and writes the gn heads' attention output, quantised per 32-block, as tagged
+// words into p.tatt.  Phase C of every CTA then reads that vector (by its tags) instead of
+// combining all heads itself.  Tracing (rec >= 0): the unit writes its heads' slice of fields ATT and ATT_XQ.
 template <bool TRACE>
-__device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int kvh, int sg, int nch, int rec) {
+__device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int kvh, int sg, int nch, uint32_t tag,
+                            int rec) {
   constexpr int HD = kHeadDim, GM = kMaxGroup;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int G = p.n_head / p.n_kv, nsg = attn_subgroups(G);
@@ -873,10 +877,7 @@ __device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int 
     }
     const float v = o * den[w];
     const int blk = ((kvh * G + g0 + w) * HD + d) >> 5;
-    int8_t *q = reinterpret_cast<int8_t *>(p.hq);
-    float *dq = reinterpret_cast<float *>(p.hq + p.n_ff);
-    int32_t *sq = reinterpret_cast<int32_t *>(p.hq + p.n_ff + 4 * (p.n_ff / 32));
-    bad = quant_block(v, lane, q, dq, sq, blk);
+    bad = quant_block_tagged(v, lane, p.tatt + blk * kQ8TagWords, tag);
     if (TRACE && rec >= 0) {  // the same arithmetic again, into the trace
       uint8_t *tq = p.trace.at(rec, UGB_TRACE_ATT_XQ);
       p.trace.f32(rec, UGB_TRACE_ATT)[blk * 32 + lane] = v;
@@ -888,42 +889,81 @@ __device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int 
   cbar();  // the scratch is free for the next unit
 }
 
-// Every CTA: the attention output's Q8_1 vector (written by the subgroups' last units) into the
-// shared activation.
-__device__ void load_att(const TokenStep &p, uint8_t *smem) {
+// Every consumer thread: nb tagged Q8_1 blocks at w (written by other CTAs) into the shared
+// activation, each word read until its tag is `tag`; false (on every consumer thread) when the
+// step was aborted or the wait limit passed.  Words go in passes of kPer per thread, all of a
+// pass in flight together.
+__device__ bool load_q8_tagged(const TokenStep &p, uint8_t *smem, const unsigned long long *w, int nb, uint32_t tag) {
   const int tid = threadIdx.x;
-  const int qr = p.n_head * kHeadDim, nq16 = qr / 16, nb = qr / 32;
-  const uint4 *src = reinterpret_cast<const uint4 *>(p.hq);
-  uint4 *dst = reinterpret_cast<uint4 *>(smem + p.o_xq);
-  for (int i = tid; i < nq16; i += kCT) dst[i] = __ldcg(src + i);
-  const float *sd = reinterpret_cast<const float *>(p.hq + p.n_ff);
-  const int32_t *ss = reinterpret_cast<const int32_t *>(p.hq + p.n_ff + 4 * (p.n_ff / 32));
+  uint8_t *q = smem + p.o_xq;
   float *dd = reinterpret_cast<float *>(smem + p.o_xd);
   int32_t *ds = reinterpret_cast<int32_t *>(smem + p.o_xs);
-  for (int i = tid; i < nb; i += kCT) {
-    dd[i] = __ldcg(sd + i);
-    ds[i] = __ldcg(ss + i);
+  const int nw = nb * kQ8TagWords;
+  constexpr int kPer = 8;
+  bool ok = true;
+  for (int i0 = 0; i0 < nw && ok; i0 += kPer * kCT) {
+    unsigned long long v[kPer];
+    uint32_t pend = 0;
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = i0 + k * kCT + tid;
+      v[k] = i < nw ? ld_relaxed64(w + i) : 0ull;
+      if (i < nw && static_cast<uint32_t>(v[k] >> 32) != tag) pend |= 1u << k;
+    }
+    if (pend) {
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t it = 1; pend; ++it) {
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+          if (pend & (1u << k)) {
+            v[k] = ld_relaxed64(w + i0 + k * kCT + tid);
+            if (static_cast<uint32_t>(v[k] >> 32) == tag) pend &= ~(1u << k);
+          }
+        if (pend && (it & 15) == 0) {
+          if (aborted(p)) {
+            ok = false;
+            break;
+          }
+          if (globaltimer_ns() - t0 > p.wait_ns) {
+            abort_all(p);
+            ok = false;
+            break;
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+      const int i = i0 + k * kCT + tid;
+      if (i >= nw) continue;
+      const int b = i / kQ8TagWords, j = i - b * kQ8TagWords;
+      const uint32_t bits = static_cast<uint32_t>(v[k]);
+      if (j < 8) {
+        *reinterpret_cast<uint32_t *>(q + b * 32 + 4 * j) = bits;
+      } else if (j == 8) {
+        dd[b] = __uint_as_float(bits);
+      } else {
+        ds[b] = static_cast<int32_t>(bits);
+      }
+    }
   }
-  cbar();
+  return cbar_and(ok);
 }
 
 // The CTA's FFN blocks [b0, b1): h = SiLU(gate) * up (gateup_dp4a epilogue, gpu_dp4a.cu:63) from
 // the shared gate / up rows, quantised per 32-block into the global hq buffer.
 // Tracing (rec >= 0): every CTA writes its blocks of fields H and H_XQ of record rec.
 template <bool TRACE>
-__device__ void silu_quant(const TokenStep &p, uint8_t *smem, int b0, int b1, int rec) {
+__device__ void silu_quant(const TokenStep &p, uint8_t *smem, int b0, int b1, uint32_t tag, int rec) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float *gs = reinterpret_cast<const float *>(smem + p.o_gu);
   const float *us = gs + 32 * p.gu_blocks;
-  int8_t *q = reinterpret_cast<int8_t *>(p.hq);
-  float *d = reinterpret_cast<float *>(p.hq + p.n_ff);
-  int32_t *s = reinterpret_cast<int32_t *>(p.hq + p.n_ff + 4 * (p.n_ff / 32));
   bool bad = false;
   for (int b = b0 + warp; b < b1; b += kCW) {
     const int i = (b - b0) * 32 + lane;
     const float gv = gs[i], uv = us[i];
     const float h = (gv / (1.0f + expf(-gv))) * uv;
-    bad |= quant_block(h, lane, q, d, s, b);
+    bad |= quant_block_tagged(h, lane, p.thq + b * kQ8TagWords, tag);
     if (TRACE && rec >= 0) {  // the same arithmetic again, into the trace
       uint8_t *tq = p.trace.at(rec, UGB_TRACE_H_XQ);
       p.trace.f32(rec, UGB_TRACE_H)[b * 32 + lane] = h;
@@ -934,23 +974,6 @@ __device__ void silu_quant(const TokenStep &p, uint8_t *smem, int b0, int b1, in
   if (bad && lane == 0) status_or(p.status, ST_NONFINITE_IN);
 }
 
-// Every CTA: the whole Q8_1 hq vector (written by all CTAs) into the shared activation.
-__device__ void load_hq(const TokenStep &p, uint8_t *smem) {
-  const int tid = threadIdx.x;
-  const int nq16 = p.n_ff / 16, nb = p.n_ff / 32;
-  const uint4 *src = reinterpret_cast<const uint4 *>(p.hq);
-  uint4 *dst = reinterpret_cast<uint4 *>(smem + p.o_xq);
-  for (int i = tid; i < nq16; i += kCT) dst[i] = __ldcg(src + i);
-  const float *sd = reinterpret_cast<const float *>(p.hq + p.n_ff);
-  const int32_t *ss = reinterpret_cast<const int32_t *>(p.hq + p.n_ff + 4 * nb);
-  float *dd = reinterpret_cast<float *>(smem + p.o_xd);
-  int32_t *ds = reinterpret_cast<int32_t *>(smem + p.o_xs);
-  for (int i = tid; i < nb; i += kCT) {
-    dd[i] = __ldcg(sd + i);
-    ds[i] = __ldcg(ss + i);
-  }
-  cbar();
-}
 
 // ---- the consumers' step -------------------------------------------------------------------
 
@@ -1038,17 +1061,15 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
     // B: attention partials
     // (no device-wide wait: a unit reads its Q/K/V rows by their tags)
     if (cta < units) {
-      uint32_t n = 0;
-      for (int u = cta; u < units; u += P, ++n) {
+      for (int u = cta; u < units; u += P) {
         if (!attn_unit<KV>(p, smem, L.bias, l, u / nsg / nch, u / nsg % nch, u % nsg, pos, dx_tag(epoch, l))) return;
-        attn_finish<TRACE>(p, smem, ms, u / nsg / nch, u % nsg, nch, TRACE ? l : -1);
+        attn_finish<TRACE>(p, smem, ms, u / nsg / nch, u % nsg, nch, dx_tag(epoch, l), TRACE ? l : -1);
       }
-      phase_arrive(p, kCntB, n);
     }
-    // C: the quantised attention output, then O.  p.unreachable > 0 (a test hook) asks the first
-    // layer's wait for arrivals that no CTA makes, so it can end only by its time limit.
-    if (!phase_wait(p, ms, kCntB, static_cast<uint32_t>(units) * (l + 1) + (l == 0 ? p.unreachable : 0u))) return;
-    load_att(p, smem);
+    // C: the quantised attention output (by its tags), then O.  p.unreachable > 0 (a test hook)
+    // makes the first layer wait for a tag no CTA writes, so the wait ends only by its time limit.
+    if (!load_q8_tagged(p, smem, p.tatt, qr / 32, dx_tag(epoch, l) ^ (l == 0 && p.unreachable ? 0x80000000u : 0u)))
+      return;
     make_slots(p, base, qr, p.rb_q, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotO, p.rb_q, sl, [&](int row, float v) {
       st_tagged(tdx_o + row, v, dx_tag(epoch, l));
@@ -1071,11 +1092,9 @@ __device__ void consumers(const TokenStep &p, uint8_t *smem, uint32_t base, TokM
       if (!isfinite(v)) status_or(status, ST_NONFINITE_OUT);
     }) && ok;
     if (!cbar_and(ok)) return;
-    silu_quant<TRACE>(p, smem, gb0, gb1, TRACE ? l : -1);
-    phase_arrive(p, kCntD, 1);
-    // E: down
-    if (!phase_wait(p, ms, kCntD, Pu * (l + 1))) return;
-    load_hq(p, smem);
+    silu_quant<TRACE>(p, smem, gb0, gb1, dx_tag(epoch, l), TRACE ? l : -1);
+    // E: hq (by its tags), then down
+    if (!load_q8_tagged(p, smem, p.thq, p.n_ff / 32, dx_tag(epoch, l))) return;
     make_slots(p, base, p.n_ff, p.rb_f, sl);
     ok = consume<KIND>(p, base, cur, pl, L, kSlotDown, p.rb_f, sl, [&](int row, float v) {
       st_tagged(tdx_d + row, v, dx_tag(epoch, l));
@@ -1218,8 +1237,8 @@ ugb_status launch_kind(ugb_ctx *ctx, cudaStream_t stream, const TokenStep &p, si
 bool token_supported(const ugb_ctx *ctx, uint32_t kind, uint32_t head_kind, TokenStep p) {
   if ((kind != UGB_Q8_0 && kind != UGB_Q4_K) || head_kind != UGB_Q8_0) return false;
   if (p.n_head % p.n_kv || p.n_head / p.n_kv > 8 || p.n_embd % 32 || p.n_ff % 32) return false;
-  // one combine ticket per (KV head, subgroup); the attention output travels in the hq buffer
-  if (p.n_kv * attn_subgroups(p.n_head / p.n_kv) > kMaxTickets || p.n_head * kHeadDim > p.n_ff) return false;
+  // one combine ticket per (KV head, subgroup)
+  if (p.n_kv * attn_subgroups(p.n_head / p.n_kv) > kMaxTickets) return false;
   if (p.n_embd > 4096 || p.n_layer > kMaxTokLayers)
     return false;
   const uint32_t rbs[4] = {p.rb_e, p.rb_q, p.rb_f, p.rb_h};
