@@ -678,6 +678,30 @@ __device__ bool attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
   // subgroup; in the chunk holding pos, threads [GM*64, GM*64 + 64) take key pair j and the next
   // HD threads one value element each.  Every load is issued before any is used.
   static_assert(GM * HD / 2 + HD / 2 + HD <= kCT, "attention load layout");
+  // The chunk's cached keys (scores: 8 lanes per position, lane j of a group takes float4
+  // columns j, j+8, j+16, j+24, 4 positions per warp) and values (P.V: thread (dd, sl) takes
+  // positions tl = sl, sl + kPV, ... of output dimension dd), requested first: they do not
+  // depend on this step's Q/K/V rows, so both round trips overlap.  The row at pos is not in the
+  // cache yet; the new key replaces it below and P.V takes the new value.
+  const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(HD));
+  const int sub = lane & 7, grp = lane >> 3;
+  constexpr int kPass = C / (kCW * 4);
+  static_assert(kPass * kCW * 4 == C, "score passes");
+  const int dd = tid & (HD - 1), sl = tid / HD;
+  float4 k4[kPass][4];
+#pragma unroll
+  for (int ps_i = 0; ps_i < kPass; ++ps_i) {
+    const int tl = (ps_i * kCW + warp) * 4 + grp, t = t0 + min(tl, nt - 1);
+    const KV *row = kcache + static_cast<size_t>(t) * HD;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) k4[ps_i][i] = KvIO<KV>::load4(row + 4 * (sub + 8 * i));
+  }
+  float vv[C / kPV];
+#pragma unroll
+  for (int m = 0; m < C / kPV; ++m) {
+    const int tl = min(sl + kPV * m, nt - 1), t = t0 + tl;
+    vv[m] = KvIO<KV>::load(vcache + static_cast<size_t>(t) * HD + dd);
+  }
   bool ok = true;  // the Q/K/V rows arrive as tagged words, read until current (bounded)
   if (tid < GM * HD / 2) {
     const int g = tid / (HD / 2), j = tid % (HD / 2);
@@ -708,36 +732,15 @@ __device__ bool attn_unit(const TokenStep &p, uint8_t *smem, const float *bias, 
     if (sg == 0) KvIO<KV>::store(vcache + static_cast<size_t>(pos) * HD + dd, v);
   }
   if (!cbar_and(ok)) return false;
-  // Scores: 8 lanes per position (lane j of a group takes float4 columns j, j+8, j+16, j+24),
-  // 4 positions per warp, all padded heads (zero queries score 0 and are not stored).  The
-  // values for P.V are loaded right after the keys, so both are in flight together.
-  const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(HD));
-  const int sub = lane & 7, grp = lane >> 3;
-  constexpr int kPass = C / (kCW * 4);
-  static_assert(kPass * kCW * 4 == C, "score passes");
-  const int dd = tid & (HD - 1), sl = tid / HD;
-  float4 k4[kPass][4];
+  // Scores of all padded heads (zero queries score 0 and are not stored).
 #pragma unroll
-  for (int ps_i = 0; ps_i < kPass; ++ps_i) {
+  for (int ps_i = 0; ps_i < kPass; ++ps_i) {  // the row at pos: the new key (all rows of kn now written)
     const int tl = (ps_i * kCW + warp) * 4 + grp, t = t0 + min(tl, nt - 1);
-    if constexpr (sizeof(KV) == 4) {
-      const float4 *src = reinterpret_cast<const float4 *>(t == pos ? kn : reinterpret_cast<const float *>(kcache) +
-                                                                              static_cast<size_t>(t) * HD);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) k4[ps_i][i] = src[sub + 8 * i];
-    } else {
+    if (t == pos) {
       const float4 *own = reinterpret_cast<const float4 *>(kn);
-      const KV *row = kcache + static_cast<size_t>(t) * HD;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) k4[ps_i][i] = t == pos ? own[sub + 8 * i] : KvIO<KV>::load4(row + 4 * (sub + 8 * i));
+      for (int i = 0; i < 4; ++i) k4[ps_i][i] = own[sub + 8 * i];
     }
-  }
-  // P.V: thread (dd, sl) sums positions tl = sl, sl + kPV, ... of output dimension dd.
-  float vv[C / kPV];
-#pragma unroll
-  for (int m = 0; m < C / kPV; ++m) {
-    const int tl = min(sl + kPV * m, nt - 1), t = t0 + tl;
-    vv[m] = t == pos ? 0.f : KvIO<KV>::load(vcache + static_cast<size_t>(t) * HD + dd);
   }
 #pragma unroll
   for (int ps_i = 0; ps_i < kPass; ++ps_i) {
