@@ -836,6 +836,17 @@ __device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int 
   const int ns = nch;
   float *cw = reinterpret_cast<float *>(smem + p.o_scr);  // [GM][ns] chunk weights
   float *den = cw + GM * ns;                              // [GM] 1 / denominator
+  // thread (w, d) = (tid / HD, tid % HD) of the gn heads; a warp holds one 32-block of one head.
+  // Its first chunk outputs are requested now, with the maxima and sums below, so the two loads
+  // share one round trip.
+  const bool owner = tid < gn * HD;
+  const int w = tid / HD, d = tid % HD;
+  const size_t obase = (static_cast<size_t>(kvh) * p.n_split * G + g0 + w) * HD + d;
+  constexpr int kBatch = 8;  // chunk loads in flight together
+  float pv[kBatch];
+#pragma unroll
+  for (int j = 0; j < kBatch; ++j)
+    pv[j] = owner ? __ldcg(p.part_o + obase + static_cast<size_t>(min(j, ns - 1)) * G * HD) : 0.f;
   if (warp < gn) {
     const size_t p0 = static_cast<size_t>(kvh) * p.n_split * G + g0 + warp;
     const bool one = lane < ns;
@@ -862,18 +873,15 @@ __device__ void attn_finish(const TokenStep &p, uint8_t *smem, TokMisc *ms, int 
     if (lane == 0) den[warp] = 1.0f / l;
   }
   cbar();
-  // thread (w, d) = (tid / HD, tid % HD) of the gn heads; a warp holds one 32-block of one head
   bool bad = false;
-  if (tid < gn * HD) {
-    const int w = tid / HD, d = tid % HD;
-    const size_t base = (static_cast<size_t>(kvh) * p.n_split * G + g0 + w) * HD + d;
+  if (owner) {
     float o = 0.f;
-    constexpr int kBatch = 8;  // chunk loads in flight together
     for (int s0 = 0; s0 < ns; s0 += kBatch) {
-      float pv[kBatch];
+      if (s0 > 0) {
 #pragma unroll
-      for (int j = 0; j < kBatch; ++j)
-        pv[j] = __ldcg(p.part_o + base + static_cast<size_t>(min(s0 + j, ns - 1)) * G * HD);
+        for (int j = 0; j < kBatch; ++j)
+          pv[j] = __ldcg(p.part_o + obase + static_cast<size_t>(min(s0 + j, ns - 1)) * G * HD);
+      }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j)
         if (s0 + j < ns) o += cw[w * ns + s0 + j] * pv[j];
