@@ -30,6 +30,7 @@
 //   scales [tile][kblock][128] f32 (dw converted exactly from fp16; dx = amax/127).
 // Rows / tokens past the matrix are zero (quant 0, scale 0).
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "internal.hpp"
@@ -365,19 +366,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
     uint64_t acc[kC / 2];                  // pairs of fp32 accumulators
 #pragma unroll
     for (int i = 0; i < kC / 2; ++i) acc[i] = 0ull;
-    // One block's int32 tile (already committed) into the accumulators.
-    auto rescale = [&](int b) {
-      const int kb = b % kKB, j = b % kAcc;
-      const uint8_t *st = smem + ((b / kKB) % kStages) * G::kStageBytes;
+    // Block kb of the stage at st (its tile in accumulator kb: a stage's kKB blocks go to the kAcc
+    // accumulators in order) into the fp32 accumulators; kb is a compile-time constant, so the
+    // scale and tensor-memory addresses are fixed offsets.
+    const uint32_t tq = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(c0);
+    auto rescale = [&](const uint8_t *st, auto kbc, int b) {
+      constexpr int kb = decltype(kbc)::value;
       const float dx = reinterpret_cast<const float *>(st + kOffSA)[kb * kPrefillTile + t_local];
       const float4 *dw4 = reinterpret_cast<const float4 *>(st + kOffSB + (kb * BN + c0) * 4);
       const uint64_t dx2 = pk2(dx, dx);
       uint32_t r[kC];
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(j * BN + c0);
       if constexpr (kC == 32) {
-        tmem_ld32(taddr, r);
+        tmem_ld32(tq + kb * BN, r);
       } else {
-        tmem_ld16(taddr, r);
+        tmem_ld16(tq + kb * BN, r);
       }
       tmem_ld_wait();
       if (DOTS) {
@@ -398,26 +400,32 @@ __global__ void __launch_bounds__(kGemmThreads, 1) prefill_gemm_kernel(GemmParam
         acc[i / 2 + 1] = fma2(f23, s23, acc[i / 2 + 1]);
       }
     };
-    // Pairs of blocks: one wait for both tiles and one release of both accumulators per pair,
-    // since these waits, fences and arrivals (not the arithmetic) are most of a warp's chain per
-    // block; the two blocks are still added in block order.
-    bool ok = true;
-    for (int b0 = 0; b0 < nb && ok; b0 += 2) {
-      const int s = b0 / kKB, slot = s % kStages, pr = b0 / 2, P = pr % kPairs;
-      const bool two = b0 + 1 < nb;
-      if (b0 % kKB == 0) ok = wait_or_abort(smem_u32(&full[slot]), s / kStages & 1, abort_flag);
-      if (ok) ok = wait_or_abort(smem_u32(&tfull[P]), (pr / kPairs) & 1, abort_flag);
-      if (!ok) break;
+    // A pair (kb, kb + 1) of the stage: one wait for both tiles and one release of both
+    // accumulators, since these waits, fences and arrivals (not the arithmetic) are most of a
+    // warp's chain per block; the two blocks are still added in block order.
+    auto pair = [&](const uint8_t *st, int s, auto kbc, int nblk) -> bool {
+      constexpr int kb = decltype(kbc)::value;
+      const int pr = (s * kKB + kb) / 2, P = pr % kPairs;
+      if (!wait_or_abort(smem_u32(&tfull[P]), (pr / kPairs) & 1, abort_flag)) return false;
       tc_fence_after();
-#pragma unroll 1
-      for (int b = b0; b < b0 + (two ? 2 : 1); ++b) rescale(b);
+      rescale(st, std::integral_constant<int, kb>{}, s * kKB + kb);
+      if (kb + 1 < nblk) rescale(st, std::integral_constant<int, kb + 1>{}, s * kKB + kb + 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(smem_u32(&tempty[P]));
-        const int bl = two ? b0 + 1 : b0;
-        if (bl % kKB == kKB - 1 || bl == nb - 1) mbar_arrive(smem_u32(&empty[slot]));
+        if (kb + 2 >= nblk) mbar_arrive(smem_u32(&empty[s % kStages]));
       }
+      return true;
+    };
+    static_assert(kKB == 4 && kAcc == kKB, "a stage's blocks map one to one onto the accumulators");
+    bool ok = true;
+    for (int s = 0; s < n_stages && ok; ++s) {
+      const uint8_t *st = smem + (s % kStages) * G::kStageBytes;
+      const int nblk = min(kKB, nb - s * kKB);
+      ok = wait_or_abort(smem_u32(&full[s % kStages]), s / kStages & 1, abort_flag);
+      if (ok) ok = pair(st, s, std::integral_constant<int, 0>{}, nblk);
+      if (ok && nblk > 2) ok = pair(st, s, std::integral_constant<int, 2>{}, nblk);
     }
     if (ok && t < p.m) {
       float *yrow = y_out + t * p.ldy + n_col0 + c0;
