@@ -67,9 +67,18 @@ def assert_quant(orc, xq, pre, what):
 
 
 def matvec(orc, kind, w, xq, m):
+    """The oracle's rows and, per row, the sum of its block terms' magnitudes: the GPU adds a
+    row's blocks in another order (lane-strided units, K-split partials), which a row that
+    cancels to near zero may show at the 2^-24 * terms level."""
     q, d, s = xq
     b, k = q.shape
-    return orc.matvec(kind, w, orc.row_bytes(kind, k), q, d, s, k, m, b, mt=True)
+    rb = orc.row_bytes(kind, k)
+    return orc.matvec(kind, w, rb, q, d, s, k, m, b, mt=True), orc.matvec_terms(kind, w, rb, q, d, s, k, m, b)
+
+
+def rows_close(gpu, want_terms):
+    want, terms = want_terms
+    assert_rows_close(gpu, want, terms=terms)
 
 
 def seed_history(dec, cfg, rng):
@@ -98,9 +107,9 @@ def check_step(orc, ref, dec, host, cfg, toks, pos):
         for b in range(B):
             assert_close(tr["ATTN_NORM"][b], ref.norm(x[b], L["attn_norm"]), NORM_REL, f"L{li} attn norm")
         assert_quant(orc, tr["ATTN_XQ"], tr["ATTN_NORM"], f"L{li} attn xq")
-        want = np.concatenate([matvec(orc, kind, L["wq"], tr["ATTN_XQ"], Q), matvec(orc, kind, L["wk"], tr["ATTN_XQ"], KV),
-                               matvec(orc, kind, L["wv"], tr["ATTN_XQ"], KV)], axis=1)
-        assert_rows_close(tr["QKV"], want)
+        parts = [matvec(orc, kind, L["wq"], tr["ATTN_XQ"], Q), matvec(orc, kind, L["wk"], tr["ATTN_XQ"], KV),
+                 matvec(orc, kind, L["wv"], tr["ATTN_XQ"], KV)]
+        rows_close(tr["QKV"], tuple(np.concatenate([p[i] for p in parts], axis=1) for i in range(2)))
         for b in range(B):
             qkv = tr["QKV"][b]
             q = ref.rotate((qkv[:Q] + L["bq"]).reshape(nh, hd), pos)
@@ -112,20 +121,19 @@ def check_step(orc, ref, dec, host, cfg, toks, pos):
             assert_close(vals[:, pos], ref.kv_round(v), 0.0, f"L{li} cached value")  # the same fp32 add and rounding
             assert_close(tr["ATT"][b], ref.attend(q, keys, vals).reshape(-1), ATT_REL, f"L{li} attention")
         assert_quant(orc, tr["ATT_XQ"], tr["ATT"], f"L{li} att xq")
-        assert_rows_close(tr["O"], matvec(orc, kind, L["wo"], tr["ATT_XQ"], E))
+        rows_close(tr["O"], matvec(orc, kind, L["wo"], tr["ATT_XQ"], E))
         mid = (x + tr["O"]).astype(np.float32)
         for b in range(B):
             assert_close(tr["FFN_NORM"][b], ref.norm(mid[b], L["ffn_norm"]), NORM_REL, f"L{li} ffn norm")
         assert_quant(orc, tr["FFN_XQ"], tr["FFN_NORM"], f"L{li} ffn xq")
-        gu = np.concatenate([matvec(orc, kind, L["w_gate"], tr["FFN_XQ"], F),
-                             matvec(orc, kind, L["w_up"], tr["FFN_XQ"], F)], axis=1)
-        assert_rows_close(tr["GATE_UP"], gu)
+        parts = [matvec(orc, kind, L["w_gate"], tr["FFN_XQ"], F), matvec(orc, kind, L["w_up"], tr["FFN_XQ"], F)]
+        rows_close(tr["GATE_UP"], tuple(np.concatenate([p[i] for p in parts], axis=1) for i in range(2)))
         g, u = tr["GATE_UP"][:, :F], tr["GATE_UP"][:, F:]
         with np.errstate(over="ignore"):
             h = (g / (np.float32(1.0) + np.exp(-g)) * u).astype(np.float32)
         assert_close(tr["H"], h, SILU_REL, f"L{li} silu")
         assert_quant(orc, tr["H_XQ"], tr["H"], f"L{li} h xq")
-        assert_rows_close(tr["DOWN"], matvec(orc, kind, L["w_down"], tr["H_XQ"], E))
+        rows_close(tr["DOWN"], matvec(orc, kind, L["w_down"], tr["H_XQ"], E))
         x_next = dec.trace(li + 1, "X")
         np.testing.assert_array_equal(x_next, (mid + tr["DOWN"]).astype(np.float32), err_msg=f"L{li} residual")
     li = cfg["n_layer"]
@@ -134,8 +142,8 @@ def check_step(orc, ref, dec, host, cfg, toks, pos):
         assert_close(xn[b], ref.norm(x[b], host["output_norm"]), NORM_REL, "output norm")
     assert_quant(orc, xq, xn, "head xq")
     logits = dec.logits().reshape(B, -1)
-    want = matvec(orc, cfg["head_kind"], host["output"], xq, cfg["n_vocab"])
-    assert_rows_close(logits, want)
+    want, terms = matvec(orc, cfg["head_kind"], host["output"], xq, cfg["n_vocab"])
+    assert_rows_close(logits, want, terms=terms)
     for b in range(B):
         assert nxt[b] == int(np.argmax(logits[b])), "greedy token is not the first maximum of the logits"
         top = np.sort(want[b])[-2:]

@@ -302,3 +302,43 @@ def test_matvec_f32_nonfinite_sets_status(ctx, ugb):
     ctx.matvec_f32(Q8_0, w, rb, x, scratch, y, k, m, 1)
     code, bits = ctx.status_read()
     assert code == ugb.ENONFINITE and bits & 1
+
+
+@pytest.mark.parametrize("k,rows,batch", [
+    (3584, (3584, 512, 512), 8),   # 7B Q/K/V: 36 tiles, K split into 4 chunks
+    (3584, (18944, 18944), 8),     # 7B gate/up: 296 tiles, whole rows per CTA
+    (18944, (3584,), 8),           # 7B down: 28 tiles x 5 chunks of 15 super-blocks
+    (3584, (3584,), 5),            # O projection with 5 vectors
+    (4096, (1000, 77), 6),         # ragged last tile; a matrix boundary inside a tile
+    (256, (130,), 7),              # one super-block per row, two tiles
+    (24576, (9,), 8),              # one tile of 9 rows, 96 chunks of one super-block
+])
+def test_matvec_tc_q4k(ctx, ugb, orc, k, rows, batch):
+    """Q4_K batches of 5..8 vectors run on the tensor cores (mv_tc.cu): every row against the
+    oracle, and the same bits on a second run (the K-split partials add in a fixed order)."""
+    torch = _torch()
+    ws = []
+    for i, m in enumerate(rows):
+        w, rb = make_weights(ctx, ugb, Q4_K, k, m, seed=k + 31 * i + m)
+        ws.append(w)
+    rng = np.random.default_rng(k + batch)
+    x = (rng.standard_normal((batch, k)) * rng.uniform(0.1, 10)).astype(np.float32)
+    xq = quantize(ctx, ugb, x)
+    total = sum(rows)
+    outs = []
+    for _ in range(2):
+        y = torch.full((batch, total), float("nan"), dtype=torch.float32, device="cuda")
+        if len(rows) == 1:
+            ctx.matvec(Q4_K, ws[0], rb, xq, y, k, rows[0], batch)
+        else:
+            ctx.matvec_multi(Q4_K, ws, rows, rb, xq, y, k, batch)
+        outs.append(y.cpu().numpy())
+        code, bits = ctx.status_read()
+        assert code == ugb.OK, bits
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    q, d, s = host_act(ugb, xq, k, batch)
+    r0 = 0
+    for w, m in zip(ws, rows):
+        ref = orc.matvec(Q4_K, w.cpu().numpy(), rb, q, d, s, k, m, batch)
+        assert_rows_close(outs[0][:, r0:r0 + m], ref)
+        r0 += m

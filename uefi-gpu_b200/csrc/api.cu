@@ -97,7 +97,16 @@ ugb_status ugb_init(int device, ugb_ctx **out) {
     ugb_destroy(ctx);
     return UGB_EBACKEND;
   }
+  ctx->mv_part_floats = size_t(1) << 20;  // 4 MB: 1024 tile chunks of 8 x 128 partials
+  ctx->mv_ntickets = 4096;
+  if (cudaMalloc(reinterpret_cast<void **>(&ctx->mv_part), ctx->mv_part_floats * 4) != cudaSuccess ||
+      cudaMalloc(reinterpret_cast<void **>(&ctx->mv_tickets), ctx->mv_ntickets * 4) != cudaSuccess ||
+      cudaMemset(ctx->mv_tickets, 0, ctx->mv_ntickets * 4) != cudaSuccess) {
+    ugb_destroy(ctx);
+    return UGB_EBACKEND;
+  }
   ugb_status st = init_matvec_kernels(ctx);
+  if (st == UGB_OK) st = init_matvec_tc_kernels(ctx);
   if (st == UGB_OK) st = init_decode_kernels(ctx);
   if (st == UGB_OK) st = init_prefill_kernels(ctx);
   if (st == UGB_OK) st = init_prefill_step_kernels(ctx);
@@ -116,6 +125,8 @@ ugb_status ugb_destroy(ugb_ctx *ctx) {
   if (ctx->status) cudaFree(ctx->status);
   if (ctx->status_host) cudaFreeHost(ctx->status_host);
   if (ctx->work) cudaFree(ctx->work);
+  if (ctx->mv_part) cudaFree(ctx->mv_part);
+  if (ctx->mv_tickets) cudaFree(ctx->mv_tickets);
   if (ctx->pinned) cudaFreeHost(ctx->pinned);
   delete ctx;
   return UGB_OK;

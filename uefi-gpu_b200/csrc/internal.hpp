@@ -19,6 +19,13 @@ struct ugb_ctx {
   float *pinned = nullptr;      // pinned host staging for ugb_linear
   size_t pinned_bytes = 0;
   bool pdl = false;             // programmatic dependent launch for every kernel
+  // K-split workspace of the tensor-core batched matvec (mv_tc.cu): chunk partials and one
+  // ticket per 128-row tile (zero between launches).  Launches that use it are ordered on one
+  // stream, as every launch of a decode step is.
+  float *mv_part = nullptr;
+  size_t mv_part_floats = 0;
+  uint32_t *mv_tickets = nullptr;
+  size_t mv_ntickets = 0;
   std::mutex mu;
 };
 
@@ -78,6 +85,11 @@ ugb_status launch_quant_q8_1(ugb_ctx *ctx, cudaStream_t stream, const float *x, 
 ugb_status launch_fill_synthetic(ugb_ctx *ctx, cudaStream_t stream, uint32_t kind, uint8_t *w,
                                  int64_t k, int64_t m, uint64_t seed);
 ugb_status init_matvec_kernels(ugb_ctx *ctx);
+// Tensor-core form of a Q4_K batch launch (vectors [done, done + nb)); *used is false when the
+// launch does not qualify and the dp4a kernels must serve it.
+ugb_status launch_matvec_tc(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a, int64_t done, int nb,
+                            bool *used);
+ugb_status init_matvec_tc_kernels(ugb_ctx *ctx);
 
 // Collectives of a sharded decode step (comm.cu).
 ugb_status comm_allreduce_sum_f32(ugb_comm *c, float *buf, size_t n, cudaStream_t stream);

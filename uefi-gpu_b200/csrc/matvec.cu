@@ -1004,6 +1004,15 @@ ugb_status launch_matvec(ugb_ctx *ctx, cudaStream_t stream, const MatvecArgs &a_
   int64_t done = 0;
   while (done < a.batch) {
     const int64_t rest = a.batch - done;
+    if (mode == kSegments && !dots && rest >= 5) {  // Q4_K batches of 5..8 on the tensor cores
+      bool used = false;
+      const ugb_status st = launch_matvec_tc(ctx, stream, a, done, static_cast<int>(std::min<int64_t>(rest, 8)), &used);
+      if (st != UGB_OK) return st;
+      if (used) {
+        done += std::min<int64_t>(rest, 8);
+        continue;
+      }
+    }
     int nb = dots ? 1 : (rest >= 8 ? 8 : rest >= 4 ? 4 : rest >= 2 ? 2 : 1);
     while (nb > 1 && x_bytes(a.kind, a.k, nb) > kXBudget) nb /= 2;
     Plan pl = make_plan(a.kind, a.k, a.m, nb, dots, ctx->smem_optin, ctx->sm_count);
