@@ -174,15 +174,24 @@ __global__ void __launch_bounds__(256) silu_quant_kernel(const float *__restrict
 // unnormalised partials (max, sum of exp, exp-weighted V) for the combine step.  Scores are
 // q.k / sqrt(HD) with an exact expf softmax (fused_attention, gpu_attention.cu:2-26;
 // llm.rs:358-368).
+// Keys and values stay in shared memory in the cache's element type (an fp16 cache takes half the
+// space, so twice the CTAs fit an SM); key rows are padded to an odd word count, so the lanes of
+// a warp (consecutive positions) read distinct banks.
+template <typename KV>
+struct AttnSmem {
+  static constexpr int kKeyStride = sizeof(KV) == 2 ? kHeadDim + 2 : kHeadDim + 1;  // elements
+};
+
 template <int HD, typename KV>
 __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
   extern __shared__ __align__(16) float sm[];
+  constexpr int KS = AttnSmem<KV>::kKeyStride;
   const int G = a.n_head / a.n_kv;
   float *q_s = sm;                          // [G][HD] (raw, then rotated)
   float *r_s = q_s + G * HD;                // [G][HD] raw q before rotation
-  float *ks = r_s + G * HD;                 // [CH][HD + 1]
-  float *vs = ks + kAttnChunk * (HD + 1);   // [CH][HD]
-  float *ps = vs + kAttnChunk * HD;         // [G][CH]
+  KV *ks = reinterpret_cast<KV *>(r_s + G * HD);  // [CH][KS]
+  KV *vs = ks + kAttnChunk * KS;            // [CH][HD]
+  float *ps = reinterpret_cast<float *>(vs + kAttnChunk * HD);  // [G][CH]
   float *kn = ps + G * kAttnChunk;          // [2][HD] new key / value (raw)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kvh = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
@@ -233,8 +242,8 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
     const float v = KvIO<KV>::round(kn[HD + tid]);
     KvIO<KV>::store(kcache + cache_head + static_cast<size_t>(pos) * HD + tid, k);
     KvIO<KV>::store(vcache + cache_head + static_cast<size_t>(pos) * HD + tid, v);
-    ks[(pos - t0) * (HD + 1) + tid] = k;
-    vs[(pos - t0) * HD + tid] = v;
+    KvIO<KV>::store(ks + (pos - t0) * KS + tid, k);  // exact: k and v are already rounded
+    KvIO<KV>::store(vs + (pos - t0) * HD + tid, v);
   }
   const int n_old = has_new ? nt - 1 : nt;
   {
@@ -242,24 +251,47 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
     const KV *vc = vcache + cache_head + static_cast<size_t>(t0) * HD;
     for (int i = tid; i < n_old * (HD / 4); i += blockDim.x) {
       const int t = i / (HD / 4), dd = (i - t * (HD / 4)) * 4;
-      const float4 kv = KvIO<KV>::load4(kc + 4 * i), vv = KvIO<KV>::load4(vc + 4 * i);
-      float *kd = ks + t * (HD + 1) + dd;
-      kd[0] = kv.x;
-      kd[1] = kv.y;
-      kd[2] = kv.z;
-      kd[3] = kv.w;
-      *reinterpret_cast<float4 *>(vs + t * HD + dd) = vv;
+      KV *kd = ks + t * KS + dd;
+      if constexpr (sizeof(KV) == 2) {  // 8 bytes each; key rows are 4-byte aligned
+        const uint2 kv = *reinterpret_cast<const uint2 *>(kc + 4 * i), vv = *reinterpret_cast<const uint2 *>(vc + 4 * i);
+        reinterpret_cast<uint32_t *>(kd)[0] = kv.x;
+        reinterpret_cast<uint32_t *>(kd)[1] = kv.y;
+        *reinterpret_cast<uint2 *>(vs + t * HD + dd) = vv;
+      } else {
+        const float4 kv = KvIO<KV>::load4(kc + 4 * i), vv = KvIO<KV>::load4(vc + 4 * i);
+        kd[0] = kv.x;
+        kd[1] = kv.y;
+        kd[2] = kv.z;
+        kd[3] = kv.w;
+        *reinterpret_cast<float4 *>(vs + t * HD + dd) = vv;
+      }
     }
   }
   __syncthreads();
   const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(HD));
+  // Scores: one (query head, position) per thread; four partial sums shorten the FMA chain.
   for (int i = tid; i < G * nt; i += blockDim.x) {
     const int g = i / nt, t = i - g * nt;
-    const float *qg = q_s + g * HD, *kt = ks + t * (HD + 1);
-    float dot = 0.f;
+    const float *qg = q_s + g * HD;
+    const KV *kt = ks + t * KS;
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll 8
-    for (int dd = 0; dd < HD; ++dd) dot += qg[dd] * kt[dd];
-    ps[g * kAttnChunk + t] = dot * inv_sqrt;
+    for (int dd = 0; dd < HD; dd += 4) {
+      const float4 q4 = *reinterpret_cast<const float4 *>(qg + dd);  // same address across the warp
+      float k0, k1, k2, k3;
+      if constexpr (sizeof(KV) == 2) {
+        const float2 a01 = __half22float2(*reinterpret_cast<const __half2 *>(kt + dd));
+        const float2 a23 = __half22float2(*reinterpret_cast<const __half2 *>(kt + dd + 2));
+        k0 = a01.x, k1 = a01.y, k2 = a23.x, k3 = a23.y;
+      } else {
+        k0 = kt[dd], k1 = kt[dd + 1], k2 = kt[dd + 2], k3 = kt[dd + 3];
+      }
+      d0 = fmaf(q4.x, k0, d0);
+      d1 = fmaf(q4.y, k1, d1);
+      d2 = fmaf(q4.z, k2, d2);
+      d3 = fmaf(q4.w, k3, d3);
+    }
+    ps[g * kAttnChunk + t] = ((d0 + d1) + (d2 + d3)) * inv_sqrt;
   }
   __syncthreads();
   if (warp < G) {
@@ -281,11 +313,22 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnParams a) {
     }
   }
   __syncthreads();
+  // Probability-weighted values: one (query head, dimension) per thread, four partial sums.
   for (int i = tid; i < G * HD; i += blockDim.x) {
     const int g = i / HD, dd = i - g * HD;
-    float acc = 0.f;
-    for (int t = 0; t < nt; ++t) acc += ps[g * kAttnChunk + t] * vs[t * HD + dd];
-    po[i] = acc;
+    const float *pg = ps + g * kAttnChunk;
+    const KV *vd = vs + dd;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int t = 0;
+    for (; t + 4 <= nt; t += 4) {
+      const float4 p4 = *reinterpret_cast<const float4 *>(pg + t);  // same address across the warp
+      a0 = fmaf(p4.x, KvIO<KV>::load(vd + t * HD), a0);
+      a1 = fmaf(p4.y, KvIO<KV>::load(vd + (t + 1) * HD), a1);
+      a2 = fmaf(p4.z, KvIO<KV>::load(vd + (t + 2) * HD), a2);
+      a3 = fmaf(p4.w, KvIO<KV>::load(vd + (t + 3) * HD), a3);
+    }
+    for (; t < nt; ++t) a0 = fmaf(pg[t], KvIO<KV>::load(vd + t * HD), a0);
+    po[i] = (a0 + a1) + (a2 + a3);
   }
 }
 
@@ -370,18 +413,20 @@ ugb_status launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
 
 }  // namespace
 
-size_t attn_partial_smem(int group) {
-  return sizeof(float) * (2 * group * kHeadDim + kAttnChunk * (kHeadDim + 1) + kAttnChunk * kHeadDim +
-                          group * kAttnChunk + 2 * kHeadDim);
+size_t attn_partial_smem(int group, bool kv16) {
+  const size_t kv = kv16 ? sizeof(__half) * kAttnChunk * (AttnSmem<__half>::kKeyStride + kHeadDim)
+                         : sizeof(float) * kAttnChunk * (AttnSmem<float>::kKeyStride + kHeadDim);
+  return sizeof(float) * (2 * group * kHeadDim + group * kAttnChunk + 2 * kHeadDim) + kv;
 }
 
 ugb_status init_decode_kernels(ugb_ctx *ctx) {
-  const int smem = static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8)));
   if (cudaFuncSetAttribute(attn_partial_kernel<kHeadDim, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           smem) != cudaSuccess)
+                           static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8, false)))) !=
+      cudaSuccess)
     return UGB_EBACKEND;
-  return cuda_status(cudaFuncSetAttribute(attn_partial_kernel<kHeadDim, __half>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  return cuda_status(cudaFuncSetAttribute(
+      attn_partial_kernel<kHeadDim, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8, true)))));
 }
 
 ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,
@@ -409,9 +454,9 @@ ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int b
   const int group = a.n_head / a.n_kv;
   const dim3 grid(a.n_kv, a.n_split, batch);
   ugb_status st = a.kv16 ? launch_ex(attn_partial_kernel<kHeadDim, __half>, grid, dim3(256),
-                                     attn_partial_smem(group), s, pdl, a)
+                                     attn_partial_smem(group, true), s, pdl, a)
                          : launch_ex(attn_partial_kernel<kHeadDim, float>, grid, dim3(256),
-                                     attn_partial_smem(group), s, pdl, a);
+                                     attn_partial_smem(group, false), s, pdl, a);
   if (st != UGB_OK) return st;
   const Q8Act l = q8act_layout(static_cast<int64_t>(a.n_head) * kHeadDim, batch);
   return launch_ex(attn_combine_quant_kernel<kHeadDim>, dim3(a.n_head, batch), dim3(kHeadDim), 0, s, pdl, a, xq,

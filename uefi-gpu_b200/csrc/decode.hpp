@@ -56,7 +56,7 @@ struct AttnParams {
   uint32_t *status;
 };
 
-size_t attn_partial_smem(int group);
+size_t attn_partial_smem(int group, bool kv16);
 
 // `pre` (may be null): [batch][n] copy of the values before quantisation, for the trace.
 ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,
