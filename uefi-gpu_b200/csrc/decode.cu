@@ -174,6 +174,133 @@ __global__ void __launch_bounds__(256) silu_quant_kernel(const float *__restrict
 // unnormalised partials (max, sum of exp, exp-weighted V) for the combine step.  Scores are
 // q.k / sqrt(HD) with an exact expf softmax (fused_attention, gpu_attention.cu:2-26;
 // llm.rs:358-368).
+// Batch-1 form: keys and values converted to fp32 as they are staged, one accumulator per dot.
+// With few CTAs (one sequence: n_kv x chunks) it measured faster than the form below (C5 batch 1:
+// 181.2 vs 172.1 tok/s, A/B on one box); with a batch the form below fits twice the CTAs per SM
+// and wins (C4 batch 8: attention 30.8 -> 20.2 us per launch).
+// Flash-decoding over one KV head (blockIdx.x) and one context chunk of kAttnChunk positions
+// (blockIdx.y) of sequence b = blockIdx.z: the G query heads of the group get their bias and
+// RoPE (rope_bias, gpu_ops.cu:9-20: a = v0*c - v1*s, b = v0*s + v1*c over pairs
+// (i, i + HD/2)), the chunk holding `pos` also biases, rotates and stores the new key and
+// value (fp32 cache as the reference keeps it, gpu_attention.cu:1, or fp16), and every chunk writes
+// unnormalised partials (max, sum of exp, exp-weighted V) for the combine step.  Scores are
+// q.k / sqrt(HD) with an exact expf softmax (fused_attention, gpu_attention.cu:2-26;
+// llm.rs:358-368).
+template <int HD, typename KV>
+__global__ void __launch_bounds__(256) attn_partial_f32_kernel(AttnParams a) {
+  extern __shared__ __align__(16) float sm[];
+  const int G = a.n_head / a.n_kv;
+  float *q_s = sm;                          // [G][HD] (raw, then rotated)
+  float *r_s = q_s + G * HD;                // [G][HD] raw q before rotation
+  float *ks = r_s + G * HD;                 // [CH][HD + 1]
+  float *vs = ks + kAttnChunk * (HD + 1);   // [CH][HD]
+  float *ps = vs + kAttnChunk * HD;         // [G][CH]
+  float *kn = ps + G * kAttnChunk;          // [2][HD] new key / value (raw)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kvh = blockIdx.x, sp = blockIdx.y, b = blockIdx.z;
+  grid_dep_launch();
+  grid_dep_wait();
+  const int pos = a.state->pos;
+  const int t0 = sp * kAttnChunk;
+  const size_t part = (static_cast<size_t>(b) * a.n_kv + kvh) * a.n_split + sp;
+  float *pm = a.part_m + part * G;
+  float *pl = a.part_l + part * G;
+  float *po = a.part_o + part * G * HD;
+  if (pos < 0 || pos >= a.n_ctx) {  // the embedding step pins pos; this is a second guard
+    if (tid == 0 && sp == 0 && kvh == 0 && b == 0) status_or(a.status, ST_BADARG);
+    return;
+  }
+  if (t0 > pos) return;  // the combine step only reads chunks <= pos / kAttnChunk
+  const int nt = min(kAttnChunk, pos + 1 - t0);
+  const int qrows = a.n_head * HD, kvrows = a.n_kv * HD;
+  const float *qkv = a.qkv + static_cast<int64_t>(b) * (qrows + 2 * kvrows);
+  const float2 *rope = a.rope + static_cast<size_t>(pos) * (HD / 2);
+  const bool has_new = pos < t0 + kAttnChunk;
+  for (int i = tid; i < G * HD; i += blockDim.x) {
+    const int row = (kvh * G) * HD + i;
+    r_s[i] = qkv[row] + (a.bias ? a.bias[row] : 0.f);
+  }
+  if (has_new) {
+    for (int i = tid; i < 2 * HD; i += blockDim.x) {
+      const int row = qrows + (i < HD ? 0 : kvrows) + kvh * HD + (i % HD);
+      kn[i] = qkv[row] + (a.bias ? a.bias[row] : 0.f);
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * HD; i += blockDim.x) {
+    const int dd = i % HD, base = i - dd, j = dd % (HD / 2);
+    const float2 cs = rope[j];
+    const float v0 = r_s[base + j], v1 = r_s[base + j + HD / 2];
+    q_s[i] = dd < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x;
+  }
+  KV *kcache = static_cast<KV *>(a.kcache) + static_cast<int64_t>(b) * a.cache_seq;
+  KV *vcache = static_cast<KV *>(a.vcache) + static_cast<int64_t>(b) * a.cache_seq;
+  const size_t cache_head = (static_cast<size_t>(kvh) * a.n_ctx) * HD;
+  if (has_new && tid < HD) {
+    const int j = tid % (HD / 2);
+    const float2 cs = rope[j];
+    const float v0 = kn[j], v1 = kn[j + HD / 2];
+    // the new row takes part as the cache holds it (rounded to fp16 in an fp16 cache)
+    const float k = KvIO<KV>::round(tid < HD / 2 ? v0 * cs.x - v1 * cs.y : v0 * cs.y + v1 * cs.x);
+    const float v = KvIO<KV>::round(kn[HD + tid]);
+    KvIO<KV>::store(kcache + cache_head + static_cast<size_t>(pos) * HD + tid, k);
+    KvIO<KV>::store(vcache + cache_head + static_cast<size_t>(pos) * HD + tid, v);
+    ks[(pos - t0) * (HD + 1) + tid] = k;
+    vs[(pos - t0) * HD + tid] = v;
+  }
+  const int n_old = has_new ? nt - 1 : nt;
+  {
+    const KV *kc = kcache + cache_head + static_cast<size_t>(t0) * HD;
+    const KV *vc = vcache + cache_head + static_cast<size_t>(t0) * HD;
+    for (int i = tid; i < n_old * (HD / 4); i += blockDim.x) {
+      const int t = i / (HD / 4), dd = (i - t * (HD / 4)) * 4;
+      const float4 kv = KvIO<KV>::load4(kc + 4 * i), vv = KvIO<KV>::load4(vc + 4 * i);
+      float *kd = ks + t * (HD + 1) + dd;
+      kd[0] = kv.x;
+      kd[1] = kv.y;
+      kd[2] = kv.z;
+      kd[3] = kv.w;
+      *reinterpret_cast<float4 *>(vs + t * HD + dd) = vv;
+    }
+  }
+  __syncthreads();
+  const float inv_sqrt = 1.0f / sqrtf(static_cast<float>(HD));
+  for (int i = tid; i < G * nt; i += blockDim.x) {
+    const int g = i / nt, t = i - g * nt;
+    const float *qg = q_s + g * HD, *kt = ks + t * (HD + 1);
+    float dot = 0.f;
+#pragma unroll 8
+    for (int dd = 0; dd < HD; ++dd) dot += qg[dd] * kt[dd];
+    ps[g * kAttnChunk + t] = dot * inv_sqrt;
+  }
+  __syncthreads();
+  if (warp < G) {
+    float mx = -FLT_MAX;
+    for (int t = lane; t < nt; t += 32) mx = fmaxf(mx, ps[warp * kAttnChunk + t]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float e = expf(ps[warp * kAttnChunk + t] - mx);
+      ps[warp * kAttnChunk + t] = e;
+      sum += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (lane == 0) {
+      pm[warp] = mx;
+      pl[warp] = sum;
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < G * HD; i += blockDim.x) {
+    const int g = i / HD, dd = i - g * HD;
+    float acc = 0.f;
+    for (int t = 0; t < nt; ++t) acc += ps[g * kAttnChunk + t] * vs[t * HD + dd];
+    po[i] = acc;
+  }
+}
+
 // Keys and values stay in shared memory in the cache's element type (an fp16 cache takes half the
 // space, so twice the CTAs fit an SM); key rows are padded to an odd word count, so the lanes of
 // a warp (consecutive positions) read distinct banks.
@@ -413,6 +540,11 @@ ugb_status launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
 
 }  // namespace
 
+size_t attn_partial_f32_smem(int group) {
+  return sizeof(float) * (2 * group * kHeadDim + kAttnChunk * (kHeadDim + 1) + kAttnChunk * kHeadDim +
+                          group * kAttnChunk + 2 * kHeadDim);
+}
+
 size_t attn_partial_smem(int group, bool kv16) {
   const size_t kv = kv16 ? sizeof(__half) * kAttnChunk * (AttnSmem<__half>::kKeyStride + kHeadDim)
                          : sizeof(float) * kAttnChunk * (AttnSmem<float>::kKeyStride + kHeadDim);
@@ -420,6 +552,12 @@ size_t attn_partial_smem(int group, bool kv16) {
 }
 
 ugb_status init_decode_kernels(ugb_ctx *ctx) {
+  const int f32_smem = static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_f32_smem(8)));
+  if (cudaFuncSetAttribute(attn_partial_f32_kernel<kHeadDim, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           f32_smem) != cudaSuccess ||
+      cudaFuncSetAttribute(attn_partial_f32_kernel<kHeadDim, __half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           f32_smem) != cudaSuccess)
+    return UGB_EBACKEND;
   if (cudaFuncSetAttribute(attn_partial_kernel<kHeadDim, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(std::min<size_t>(ctx->smem_optin, attn_partial_smem(8, false)))) !=
       cudaSuccess)
@@ -453,10 +591,18 @@ ugb_status launch_silu_quant(cudaStream_t s, bool pdl, const float *gu, int n_ff
 ugb_status launch_attention(cudaStream_t s, bool pdl, const AttnParams &a, int batch, uint8_t *xq, float *pre) {
   const int group = a.n_head / a.n_kv;
   const dim3 grid(a.n_kv, a.n_split, batch);
-  ugb_status st = a.kv16 ? launch_ex(attn_partial_kernel<kHeadDim, __half>, grid, dim3(256),
-                                     attn_partial_smem(group, true), s, pdl, a)
-                         : launch_ex(attn_partial_kernel<kHeadDim, float>, grid, dim3(256),
-                                     attn_partial_smem(group, false), s, pdl, a);
+  ugb_status st;
+  if (batch == 1) {  // few CTAs: the fp32-staging form (see attn_partial_f32_kernel)
+    st = a.kv16 ? launch_ex(attn_partial_f32_kernel<kHeadDim, __half>, grid, dim3(256), attn_partial_f32_smem(group),
+                            s, pdl, a)
+                : launch_ex(attn_partial_f32_kernel<kHeadDim, float>, grid, dim3(256), attn_partial_f32_smem(group),
+                            s, pdl, a);
+  } else {
+    st = a.kv16 ? launch_ex(attn_partial_kernel<kHeadDim, __half>, grid, dim3(256), attn_partial_smem(group, true), s,
+                            pdl, a)
+                : launch_ex(attn_partial_kernel<kHeadDim, float>, grid, dim3(256), attn_partial_smem(group, false), s,
+                            pdl, a);
+  }
   if (st != UGB_OK) return st;
   const Q8Act l = q8act_layout(static_cast<int64_t>(a.n_head) * kHeadDim, batch);
   return launch_ex(attn_combine_quant_kernel<kHeadDim>, dim3(a.n_head, batch), dim3(kHeadDim), 0, s, pdl, a, xq,

@@ -57,6 +57,7 @@ struct AttnParams {
 };
 
 size_t attn_partial_smem(int group, bool kv16);
+size_t attn_partial_f32_smem(int group);  // the batch-1 form, the larger of the two
 
 // `pre` (may be null): [batch][n] copy of the values before quantisation, for the trace.
 ugb_status launch_embed(cudaStream_t s, bool pdl, const uint8_t *tok_embd, int embd, int vocab, int n_ctx,

@@ -115,7 +115,7 @@ ugb_status check_config(const ugb_ctx *ctx, const ugb_decoder_config &c) {
   }
   const int vl = c.n_vocab_local ? c.n_vocab_local : c.n_vocab;
   if (c.vocab0 < 0 || vl < 1 || c.vocab0 + vl > c.n_vocab) return UGB_ESHAPE;
-  if (attn_partial_smem(c.n_head / c.n_head_kv, false) > ctx->smem_optin) return UGB_ESHAPE;  // the larger form
+  if (attn_partial_f32_smem(c.n_head / c.n_head_kv) > ctx->smem_optin) return UGB_ESHAPE;
   return UGB_OK;
 }
 
