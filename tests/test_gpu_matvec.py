@@ -309,7 +309,8 @@ def test_matvec_f32_nonfinite_sets_status(ctx, ugb):
     (3584, (18944, 18944), 8),     # 7B gate/up: 296 tiles, whole rows per CTA
     (18944, (3584,), 8),           # 7B down: 28 tiles x 5 chunks of 15 super-blocks
     (3584, (3584,), 5),            # O projection with 5 vectors
-    (4096, (1000, 77), 6),         # ragged last tile; a matrix boundary inside a tile
+    (4096, (1024, 77), 6),         # a matrix boundary on a tile edge, ragged last tile, 16 chunks
+    (4096, (1000, 77), 6),         # a matrix boundary inside a tile: the dp4a kernels serve it
     (256, (130,), 7),              # one super-block per row, two tiles
     (24576, (9,), 8),              # one tile of 9 rows, 96 chunks of one super-block
 ])
