@@ -149,8 +149,8 @@ ugb_status ugb_matvec_f32(ugb_ctx *ctx, ugb_stream stream, uint32_t kind, const 
  * w_devs (host array) holds the count device pointers, rows the count row counts.
  * Replaces qkv_dp4a / gateup_dp4a (gpu_dp4a.cu:53-64, the fused Q/K/V and gate/up launches
  * over separate GGUF tensors) and Gpu::batch (llm.rs:226-245, up to 3 tensors sharing one
- * input).  Results are bit-identical to one ugb_matvec per matrix, except Q4_K with 5..8
- * vectors: that form splits K by the launch's total rows, so the fp32 sums may associate
+ * input).  Results are bit-identical to one ugb_matvec per matrix, except Q4_K / Q8_0 with
+ * 5..8 vectors: that form splits K by the launch's total rows, so the fp32 sums may associate
  * differently from the single launches' (same block dots, each within fp32 rounding). */
 ugb_status ugb_matvec_multi(ugb_ctx *ctx, ugb_stream stream, uint32_t kind,
                             const void *const *w_devs, const int64_t *rows, int count,
