@@ -34,7 +34,15 @@ ugb_status read_status_bits(ugb_ctx *ctx, cudaStream_t stream, uint32_t *bits) {
   if (cudaStreamSynchronize(stream) != cudaSuccess || !copied || !cleared) return UGB_EBACKEND;
   const uint32_t b = *ctx->status_host;
   if (bits) *bits = b;
-  if (b & ST_TIMEOUT) return UGB_ETIMEOUT;
+  if (b & ST_TIMEOUT) {
+    // A launch that gave up may have left tile tickets of the tensor-core matvec's K split
+    // partly counted (mv_tc.cu); clear them so the next launches count from zero.
+    if (ctx->mv_tickets &&
+        (cudaMemsetAsync(ctx->mv_tickets, 0, ctx->mv_ntickets * 4, stream) != cudaSuccess ||
+         cudaStreamSynchronize(stream) != cudaSuccess))
+      return UGB_EBACKEND;
+    return UGB_ETIMEOUT;
+  }
   if (b & (ST_NONFINITE_IN | ST_NONFINITE_OUT)) return UGB_ENONFINITE;
   if (b & ST_BADARG) return UGB_ESHAPE;
   return UGB_OK;
